@@ -1,0 +1,69 @@
+// Parameter blocks and launchers of attention.cu (no torch types).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace octo {
+
+struct AttnParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  __nv_bfloat16* o;
+  float* lse;          // [Hq, Tq] natural-log normaliser (may be null)
+  const int32_t* cu_q;     // [nseq + 1] query row ranges
+  const int32_t* cu_k;     // [nseq + 1] ranges into key_idx
+  const int32_t* key_idx;  // gathered key rows
+  const int32_t* tiles;    // [n_tiles, 2] (seq, q0) with q0 a multiple of the CTA's row tile
+  int ldq, ldk, ldo;       // row strides (elements)
+  int Tq, Hq, Hkv;
+  float scale;
+  int causal;
+};
+
+struct AttnBwdParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const __nv_bfloat16* dO;
+  const float* lse;    // [Hq, Tq]
+  const float* delta;  // [Hq, Tq]
+  __nv_bfloat16* dq;   // [Tq, Hq, D]
+  float* dk_acc;       // [rows, Hkv, D] fp32 accumulators (row stride ld_acc)
+  float* dv_acc;
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  const int32_t* key_idx;
+  const int32_t* tiles;   // [n_qtiles, 2] (seq, q0), q0 multiple of 64
+  const int32_t* ktiles;  // [n_ktiles, 2] (seq, k0), k0 multiple of 64
+  int ldq, ldk, lddo, lddq;
+  long ld_acc;
+  int Tq, Hq, Hkv;
+  float scale;
+  int causal;
+};
+
+struct DecodeParams {
+  const __nv_bfloat16* q;  // [B, Hq, D] (row stride ldq)
+  const __nv_bfloat16* k_cache;  // [slots, Hkv, D]
+  const __nv_bfloat16* v_cache;
+  __nv_bfloat16* o;        // [B, Hq, D] (row stride ldo)
+  const int32_t* kv_start;    // [B] first entry of request b in kv_indices
+  const int32_t* kv_len;      // [B] number of keys of request b
+  const int32_t* kv_indices;  // slot ids
+  float* part_o;    // [B, Hq, splits, D] scratch (splits > 1)
+  float* part_lse;  // [B, Hq, splits]
+  int ldq, ldk, ldo;
+  int Hq, Hkv;
+  int num_splits;
+  float scale;
+};
+
+void attn_fwd(const AttnParams& p, int n_tiles, int D, cudaStream_t st);
+void attn_bwd_delta(const __nv_bfloat16* o, int ldo, const __nv_bfloat16* dO, int lddo, float* delta, int Tq, int Hq,
+                    int D, cudaStream_t st);
+void attn_bwd(const AttnBwdParams& p, int n_qtiles, int n_ktiles, int D, cudaStream_t st);
+void attn_decode(const DecodeParams& p, int B, int D, cudaStream_t st);
+
+}  // namespace octo

@@ -1,0 +1,350 @@
+// Persistent warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   C[M, N] = epilogue( sum_k A[m, k] * B[n, k] )
+//
+// Operands are bf16, staged global -> SMEM by TMA (128-byte swizzle, no cluster
+// fan-out), multiplied by tcgen05.mma (M=128, N=BN, K=16) into an fp32 accumulator in
+// TMEM.  Two TMEM accumulators alternate between tiles so the epilogue of tile i runs
+// while the MMAs of tile i+1 are issued.
+//
+// Operand majors:
+//   K-major  : the operand is stored [rows, K] row-major (nn.Linear weight, activations)
+//   MN-major : the operand is stored [K, rows] row-major (dgrad B = W, wgrad A = dY, B = X)
+// so forward (X W^T), dgrad (dY W) and wgrad (dY^T X) all run on the same kernel.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
+// warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4) .. +32, one row per thread).
+//
+// The epilogue is a template functor `Epi` (one copy per thread) with
+//   begin_tile()                                   before the chunks of a tile
+//   apply(row, col0, ncols_valid, float (&v)[32], tile_n)   per valid 32-column chunk
+//   end_tile(row, tile_n)                          after the chunks (rows < M only)
+//   finish()                                       once, after the last tile
+// Each epilogue thread owns one accumulator row per tile; rows >= M are skipped.
+#pragma once
+#include <cuda.h>
+#include "common.cuh"
+#include "octo_api.h"
+
+namespace octo {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kGemmThreads = 192;
+constexpr int kGemmGroupM = 16;  // tile raster: 16 M-blocks share each B tile in L2
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int kABytes = kGemmBM * kGemmBK * 2;
+  static constexpr int kBBytes = BN * kGemmBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = (2 * BN) < 32 ? 32 : 2 * BN;  // BN in {64,128,256}
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+
+__device__ __forceinline__ void gemm_tile_coords(const GemmShape& s, int tile, int& mb, int& nb) {
+  const int group_span = kGemmGroupM * s.n_tiles;
+  const int group = tile / group_span;
+  const int first_m = group * kGemmGroupM;
+  int gm = s.m_tiles - first_m;
+  gm = gm < kGemmGroupM ? gm : kGemmGroupM;
+  const int r = tile - group * group_span;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+template <int BN, bool A_MN, bool B_MN, class Epi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        GemmShape shape, Epi epi, int* status) {
+  // (each thread works on its own copy of the epilogue functor)
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* accf_bar = empty_bar + S;
+  uint64_t* acce_bar = accf_bar + 2;
+  uint64_t* drain_bar = acce_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf_bar[i], 1);
+      mbar_init(&acce_bar[i], 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < shape.num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        gemm_tile_coords(shape, tile, mb, nb);
+        const int m0 = mb * kGemmBM, n0 = nb * BN;
+        for (int kb = 0; kb < shape.k_blocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, 100 + stage)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
+          const int k0 = kb * kGemmBK;
+          uint8_t* a_dst = sA + stage * Cfg::kABytes;
+          uint8_t* b_dst = sB + stage * Cfg::kBBytes;
+          if constexpr (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full_bar[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kGemmBM / 64; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full_bar[stage], m0 + 64 * j, k0);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full_bar[stage], n0 + 64 * j, k0);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: wait (bounded) until every copy this thread issued has landed.
+        const uint64_t t0 = globaltimer_ns();
+        for (int s = 0; s < S; ++s) {
+          if (!(issued_mask & (1u << s))) continue;
+          while (!mbar_try_wait(&full_bar[s], (issued_parity >> s) & 1u)) {
+            if (globaltimer_ns() - t0 > OCTO_WAIT_NS) break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(kGemmBM, BN, A_MN, B_MN, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int tile = blockIdx.x; tile < shape.num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, abort_flag, status, 200 + acc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < shape.k_blocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, status, 300 + stage)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+            uint64_t da, db;
+            if constexpr (!A_MN) {
+              da = umma_smem_desc(a_addr + kk * 32, 16, 1024);
+            } else {
+              da = umma_smem_desc(a_addr + kk * 2048, 8192, 1024);
+            }
+            if constexpr (!B_MN) {
+              db = umma_smem_desc(b_addr + kk * 32, 16, 1024);
+            } else {
+              db = umma_smem_desc(b_addr + kk * 2048, 8192, 1024);
+            }
+            umma_f16_ss(d_tmem, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty_bar[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&accf_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued_any) {
+        // Drain: all MMAs issued so far must finish before TMEM is released.
+        umma_commit(drain_bar);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain_bar, 0)) {
+          if (globaltimer_ns() - t0 > OCTO_WAIT_NS) break;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue warps
+    const int quarter = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < shape.num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(&accf_bar[acc], acc_phase, abort_flag, status, 400 + acc)) break;
+      tc_fence_after();
+      int mb, nb;
+      gemm_tile_coords(shape, tile, mb, nb);
+      const int row = mb * kGemmBM + quarter * 32 + lane;
+      const int n0 = nb * BN;
+      epi.begin_tile();
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_base + static_cast<uint32_t>(acc * BN + c * 32), r);
+        tmem_wait_ld();
+        const int col0 = n0 + c * 32;
+        if (row < shape.M && col0 < shape.N) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          const int nvalid = shape.N - col0 < 32 ? shape.N - col0 : 32;
+          epi.apply(row, col0, nvalid, v, nb);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce_bar[acc]);
+      if (row < shape.M) epi.end_tile(row, nb);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    epi.finish();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+// ---------------------------------------------------------------- epilogues
+
+// C (bf16, row stride ldc) = alpha * acc (+ bias[col]) (+ residual bf16, row stride ldr)
+struct EpiBF16 {
+  __nv_bfloat16* C;
+  int ldc;
+  const __nv_bfloat16* R;
+  int ldr;
+  float alpha;
+  const __nv_bfloat16* bias;
+  __device__ __forceinline__ void apply(int row, int col0, int nvalid, float (&v)[32], int) {
+    __nv_bfloat16* dst = C + static_cast<size_t>(row) * ldc + col0;
+    float a = alpha;  // local: the functor persists across chunks and tiles
+    if (bias != nullptr) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        if (g * 8 < nvalid) {
+          uint4 bv = *reinterpret_cast<const uint4*>(bias + col0 + g * 8);
+          const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&bv);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[g * 8 + i] = v[g * 8 + i] * a + __bfloat162float(bb[i]);
+        }
+      }
+      a = 1.0f;  // already applied
+    }
+    if (R != nullptr) {
+      const __nv_bfloat16* res = R + static_cast<size_t>(row) * ldr + col0;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        if (g * 8 < nvalid) {
+          uint4 rv = *reinterpret_cast<const uint4*>(res + g * 8);
+          const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[g * 8 + i] = a * v[g * 8 + i] + __bfloat162float(rb[i]);
+        }
+      }
+    } else if (a != 1.0f) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= a;
+    }
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (g * 8 < nvalid) {
+        uint4 o;
+        o.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
+        o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
+        o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
+        o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
+        *reinterpret_cast<uint4*>(dst + g * 8) = o;
+      }
+    }
+  }
+  __device__ __forceinline__ void begin_tile() {}
+  __device__ __forceinline__ void end_tile(int, int) {}
+  __device__ __forceinline__ void finish() const {}
+};
+
+// C (fp32) = alpha * acc  (+ C if accumulate)
+struct EpiF32 {
+  float* C;
+  int ldc;
+  float alpha;
+  int accumulate;
+  __device__ __forceinline__ void apply(int row, int col0, int nvalid, float (&v)[32], int) {
+    float* dst = C + static_cast<size_t>(row) * ldc + col0;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      if (g * 4 < nvalid) {
+        float4 o = make_float4(alpha * v[g * 4], alpha * v[g * 4 + 1], alpha * v[g * 4 + 2], alpha * v[g * 4 + 3]);
+        if (accumulate) {
+          const float4 p = *reinterpret_cast<const float4*>(dst + g * 4);
+          o.x += p.x;
+          o.y += p.y;
+          o.z += p.z;
+          o.w += p.w;
+        }
+        *reinterpret_cast<float4*>(dst + g * 4) = o;
+      }
+    }
+  }
+  __device__ __forceinline__ void begin_tile() {}
+  __device__ __forceinline__ void end_tile(int, int) {}
+  __device__ __forceinline__ void finish() const {}
+};
+
+}  // namespace octo

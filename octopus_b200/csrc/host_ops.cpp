@@ -1,0 +1,507 @@
+// Torch-facing host glue of the octopus_b200 extension (compiled by g++, no device code).
+// Every entry point checks devices, dtypes, shapes and strides, then calls a plain
+// launcher from the CUDA translation units on the current stream.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <vector>
+
+#include "attention.h"
+#include "elementwise.h"
+#include "octo_api.h"
+#include "tmap.h"
+
+namespace octo {
+
+static std::mutex g_status_mu;
+static std::vector<torch::Tensor> g_status(64);
+
+torch::Tensor status_tensor(int device) {
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  if (!g_status[device].defined()) {
+    g_status[device] = torch::zeros({2}, torch::dtype(torch::kInt32).device(torch::kCUDA, device));
+  }
+  return g_status[device];
+}
+int* status_ptr(int device) { return status_tensor(device).data_ptr<int>(); }
+
+static cudaStream_t cur_stream(const torch::Tensor& t) {
+  return at::cuda::getCurrentCUDAStream(t.get_device()).stream();
+}
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == torch::kBFloat16, #x " must be bf16")
+#define CHECK_F32(x) TORCH_CHECK((x).scalar_type() == torch::kFloat32, #x " must be fp32")
+#define CHECK_I32(x) TORCH_CHECK((x).scalar_type() == torch::kInt32, #x " must be int32")
+#define CHECK_I64(x) TORCH_CHECK((x).scalar_type() == torch::kInt64, #x " must be int64")
+#define CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+#define BF(x) reinterpret_cast<__nv_bfloat16*>((x).data_ptr())
+#define CBF(x) reinterpret_cast<const __nv_bfloat16*>((x).data_ptr())
+
+// ------------------------------------------------------------------ GEMM
+static int pick_bn(int M, int N, int sms, int hint) {
+  if (hint == 64 || hint == 128 || hint == 256) return hint;
+  const int mt = (M + 127) / 128;
+  auto tiles = [&](int bn) { return mt * ((N + bn - 1) / bn); };
+  if (N >= 256 && tiles(256) >= sms) return 256;
+  if (N >= 128 && tiles(128) >= (sms * 3) / 4) return 128;
+  return 64;
+}
+
+static GemmLaunch make_launch(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int bn_hint) {
+  CHECK_CUDA(A);
+  CHECK_CUDA(B);
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2, "gemm: 2D operands");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm: unit inner stride required");
+  GemmLaunch g{};
+  const int M = a_mn ? A.size(1) : A.size(0);
+  const int K = a_mn ? A.size(0) : A.size(1);
+  const int N = b_mn ? B.size(1) : B.size(0);
+  const int Kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(K == Kb, "gemm: K mismatch ", K, " vs ", Kb);
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && M % 8 == 0, "gemm: M, N, K must be multiples of 8 (got ", M, ", ", N,
+              ", ", K, ")");
+  const int device = A.get_device();
+  const int sms = num_sms(device);
+  const int BN = pick_bn(M, N, sms, bn_hint);
+  g.bn = BN;
+  g.a_mn = a_mn;
+  g.b_mn = b_mn;
+  g.s.M = M;
+  g.s.N = N;
+  g.s.K = K;
+  g.s.m_tiles = (M + 127) / 128;
+  g.s.n_tiles = (N + BN - 1) / BN;
+  g.s.k_blocks = (K + 63) / 64;
+  g.s.num_tiles = g.s.m_tiles * g.s.n_tiles;
+  g.ta = a_mn ? make_tmap_bf16_2d(A.data_ptr(), M, K, A.stride(0), 64, 64)
+              : make_tmap_bf16_2d(A.data_ptr(), K, M, A.stride(0), 64, 128);
+  g.tb = b_mn ? make_tmap_bf16_2d(B.data_ptr(), N, K, B.stride(0), 64, 64)
+              : make_tmap_bf16_2d(B.data_ptr(), K, N, B.stride(0), 64, BN);
+  g.status = status_ptr(device);
+  g.grid = std::min(g.s.num_tiles, sms);
+  g.stream = cur_stream(A);
+  g.alpha = 1.f;
+  g.vocab_limit = N;
+  return g;
+}
+
+// C[M,N] = alpha * A_log[M,K] @ B_log[N,K]^T (+ bias) (+ residual)   or   C += ... (fp32)
+//   a_mn false: A is [M, K];  true: A is [K, M].   b_mn false: B is [N, K];  true: B is [K, N].
+void gemm_out(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, torch::Tensor C, double alpha,
+              c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> bias, bool accumulate,
+              int64_t bn_hint) {
+  c10::cuda::CUDAGuard guard(A.get_device());
+  GemmLaunch g = make_launch(A, a_mn, B, b_mn, static_cast<int>(bn_hint));
+  CHECK_CUDA(C);
+  TORCH_CHECK(C.dim() == 2 && C.size(0) == g.s.M && C.size(1) == g.s.N && C.stride(1) == 1, "gemm: bad output");
+  if (g.s.M == 0 || g.s.N == 0) return;
+  g.alpha = static_cast<float>(alpha);
+  g.C = C.data_ptr();
+  g.ldc = C.stride(0);
+  if (C.scalar_type() == torch::kBFloat16) {
+    TORCH_CHECK(!accumulate, "gemm: accumulate requires an fp32 output");
+    TORCH_CHECK(C.stride(0) % 8 == 0, "gemm: output row stride must be a multiple of 8");
+    g.epi = kEpiBF16;
+    if (residual.has_value() && residual->defined()) {
+      const auto& R = *residual;
+      CHECK_BF16(R);
+      TORCH_CHECK(R.dim() == 2 && R.size(0) == g.s.M && R.size(1) == g.s.N && R.stride(1) == 1 &&
+                      R.stride(0) % 8 == 0,
+                  "gemm: bad residual");
+      g.R = R.data_ptr();
+      g.ldr = R.stride(0);
+    }
+    if (bias.has_value() && bias->defined()) {
+      const auto& b = *bias;
+      CHECK_BF16(b);
+      CHECK_CONTIG(b);
+      TORCH_CHECK(b.numel() == g.s.N, "gemm: bias must have N elements");
+      g.bias = b.data_ptr();
+    }
+  } else {
+    CHECK_F32(C);
+    TORCH_CHECK(C.stride(0) % 4 == 0, "gemm: fp32 output row stride must be a multiple of 4");
+    TORCH_CHECK(!(residual.has_value() && residual->defined()) && !(bias.has_value() && bias->defined()),
+                "gemm: residual/bias only with bf16 output");
+    g.epi = kEpiF32;
+    g.accumulate = accumulate ? 1 : 0;
+  }
+  gemm_launch(g);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Chunked logprob head forward: per row (log p(label), entropy, lse) of softmax(alpha * h W^T)
+// without materialising logits.  labels < 0 mark unscored rows (logp = 0).
+std::vector<torch::Tensor> head_fwd(torch::Tensor h, torch::Tensor W, torch::Tensor labels, double alpha,
+                                    int64_t vocab_limit) {
+  c10::cuda::CUDAGuard guard(h.get_device());
+  CHECK_I32(labels);
+  CHECK_CONTIG(labels);
+  GemmLaunch g = make_launch(h, false, W, false, 256);
+  TORCH_CHECK(labels.numel() == g.s.M, "head_fwd: one label per row");
+  auto f32 = torch::dtype(torch::kFloat32).device(h.device());
+  auto part = torch::empty({g.s.M, g.s.n_tiles, 4}, f32);
+  auto logp = torch::empty({g.s.M}, f32), ent = torch::empty({g.s.M}, f32), lse = torch::empty({g.s.M}, f32);
+  if (g.s.M == 0) return {logp, ent, lse};
+  g.epi = kEpiHeadLse;
+  g.alpha = static_cast<float>(alpha);
+  g.labels = labels.data_ptr<int32_t>();
+  g.partial = part.data_ptr<float>();
+  g.vocab_limit = vocab_limit > 0 ? static_cast<int>(vocab_limit) : g.s.N;
+  gemm_launch(g);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  head_combine(part.data_ptr<float>(), g.s.M, g.s.n_tiles, labels.data_ptr<int32_t>(), logp.data_ptr<float>(),
+               ent.data_ptr<float>(), lse.data_ptr<float>(), g.stream);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {logp, ent, lse};
+}
+
+// d loss / d logits of the head (bf16 [M, N]) recomputed from (lse, entropy).
+void head_grad_logits(torch::Tensor h, torch::Tensor W, torch::Tensor labels, torch::Tensor lse, torch::Tensor ent,
+                      torch::Tensor g_lp, torch::Tensor g_ent, torch::Tensor dz, double alpha, int64_t vocab_limit) {
+  c10::cuda::CUDAGuard guard(h.get_device());
+  GemmLaunch g = make_launch(h, false, W, false, 256);
+  for (auto* t : {&lse, &ent, &g_lp, &g_ent}) {
+    CHECK_F32(*t);
+    CHECK_CONTIG(*t);
+    TORCH_CHECK(t->numel() == g.s.M, "head_grad: per-row vectors");
+  }
+  CHECK_I32(labels);
+  CHECK_BF16(dz);
+  TORCH_CHECK(dz.size(0) == g.s.M && dz.size(1) == g.s.N && dz.stride(1) == 1 && dz.stride(0) % 8 == 0,
+              "head_grad: bad dz");
+  if (g.s.M == 0) return;
+  g.epi = kEpiHeadGrad;
+  g.C = dz.data_ptr();
+  g.ldc = dz.stride(0);
+  g.labels = labels.data_ptr<int32_t>();
+  g.lse = lse.data_ptr<float>();
+  g.ent = ent.data_ptr<float>();
+  g.g_lp = g_lp.data_ptr<float>();
+  g.g_ent = g_ent.data_ptr<float>();
+  g.alpha = static_cast<float>(alpha);
+  g.vocab_limit = vocab_limit > 0 ? static_cast<int>(vocab_limit) : g.s.N;
+  gemm_launch(g);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Fused sampling head: token ~ softmax(alpha * h W^T) by Gumbel-max, plus its logprob.
+std::vector<torch::Tensor> sample_head(torch::Tensor h, torch::Tensor W, double alpha, int64_t seed,
+                                       c10::optional<torch::Tensor> row_stream, int64_t vocab_limit) {
+  c10::cuda::CUDAGuard guard(h.get_device());
+  GemmLaunch g = make_launch(h, false, W, false, 0);
+  auto f32 = torch::dtype(torch::kFloat32).device(h.device());
+  auto part = torch::empty({g.s.M, g.s.n_tiles, 4}, f32);
+  auto tokens = torch::empty({g.s.M}, torch::dtype(torch::kInt64).device(h.device()));
+  auto logprob = torch::empty({g.s.M}, f32);
+  if (g.s.M == 0) return {tokens, logprob};
+  const int64_t* rs = nullptr;
+  if (row_stream.has_value() && row_stream->defined()) {
+    CHECK_I64(*row_stream);
+    CHECK_CONTIG(*row_stream);
+    TORCH_CHECK(row_stream->numel() == g.s.M, "sample_head: one stream id per row");
+    rs = row_stream->data_ptr<int64_t>();
+  }
+  g.epi = kEpiSample;
+  g.alpha = static_cast<float>(alpha);
+  g.partial = part.data_ptr<float>();
+  g.seed = static_cast<uint64_t>(seed);
+  g.row_offset = rs;
+  g.vocab_limit = vocab_limit > 0 ? static_cast<int>(vocab_limit) : g.s.N;
+  gemm_launch(g);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  sample_combine(part.data_ptr<float>(), g.s.M, g.s.n_tiles, g.seed, rs, tokens.data_ptr<int64_t>(),
+                 logprob.data_ptr<float>(), g.stream);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {tokens, logprob};
+}
+
+// ------------------------------------------------------------------ elementwise
+std::vector<torch::Tensor> rmsnorm_fwd_t(torch::Tensor x, torch::Tensor w, double eps, bool plus_one) {
+  c10::cuda::CUDAGuard guard(x.get_device());
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.stride(0) % 8 == 0, "rmsnorm: x [T, H] row-major");
+  const int T = x.size(0), H = x.size(1);
+  TORCH_CHECK(H % 8 == 0 && w.numel() == H, "rmsnorm: H % 8 == 0 and w [H]");
+  auto y = torch::empty({T, H}, x.options());
+  auto rstd = torch::empty({T}, x.options().dtype(torch::kFloat32));
+  rmsnorm_fwd(CBF(x), x.stride(0), CBF(w), BF(y), H, rstd.data_ptr<float>(), T, H, static_cast<float>(eps),
+              plus_one ? 1 : 0, cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {y, rstd};
+}
+
+torch::Tensor rmsnorm_bwd_t(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
+                            c10::optional<torch::Tensor> dres, torch::Tensor dw, bool plus_one) {
+  c10::cuda::CUDAGuard guard(x.get_device());
+  CHECK_BF16(dy);
+  CHECK_CONTIG(dy);
+  CHECK_F32(dw);
+  const int T = x.size(0), H = x.size(1);
+  auto dx = torch::empty({T, H}, x.options());
+  const __nv_bfloat16* dr = nullptr;
+  if (dres.has_value() && dres->defined()) {
+    CHECK_CONTIG(*dres);
+    dr = CBF(*dres);
+  }
+  rmsnorm_bwd(CBF(dy), CBF(x), x.stride(0), CBF(w), rstd.data_ptr<float>(), dr, BF(dx), dw.data_ptr<float>(), T, H,
+              plus_one ? 1 : 0, cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dx;
+}
+
+void rope_t(torch::Tensor qkv, torch::Tensor pos, int64_t Hq, int64_t Hkv, int64_t D, double theta, bool inverse) {
+  c10::cuda::CUDAGuard guard(qkv.get_device());
+  CHECK_BF16(qkv);
+  CHECK_I32(pos);
+  CHECK_CONTIG(pos);
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1, "rope: qkv [T, W]");
+  rope_apply(BF(qkv), qkv.stride(0), pos.data_ptr<int32_t>(), qkv.size(0), Hq, Hkv, D, static_cast<float>(theta),
+             inverse, cur_stream(qkv));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+torch::Tensor swiglu_fwd_t(torch::Tensor gu) {
+  c10::cuda::CUDAGuard guard(gu.get_device());
+  CHECK_BF16(gu);
+  CHECK_CONTIG(gu);
+  const int T = gu.size(0), F = gu.size(1) / 2;
+  TORCH_CHECK(F % 8 == 0, "swiglu: F % 8 == 0");
+  auto out = torch::empty({T, F}, gu.options());
+  swiglu_fwd(CBF(gu), BF(out), T, F, cur_stream(gu));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
+torch::Tensor swiglu_bwd_t(torch::Tensor gu, torch::Tensor dout) {
+  c10::cuda::CUDAGuard guard(gu.get_device());
+  CHECK_CONTIG(gu);
+  CHECK_CONTIG(dout);
+  const int T = gu.size(0), F = gu.size(1) / 2;
+  auto dgu = torch::empty_like(gu);
+  swiglu_bwd(CBF(gu), CBF(dout), BF(dgu), T, F, cur_stream(gu));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dgu;
+}
+
+torch::Tensor embed_fwd_t(torch::Tensor ids, torch::Tensor W) {
+  c10::cuda::CUDAGuard guard(W.get_device());
+  CHECK_I64(ids);
+  CHECK_CONTIG(ids);
+  CHECK_CONTIG(W);
+  const int T = ids.numel(), V = W.size(0), H = W.size(1);
+  auto out = torch::empty({T, H}, W.options());
+  embed_fwd(ids.data_ptr<int64_t>(), CBF(W), BF(out), T, H, V, cur_stream(W));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
+void embed_bwd_t(torch::Tensor ids, torch::Tensor dout, torch::Tensor dW) {
+  c10::cuda::CUDAGuard guard(dW.get_device());
+  CHECK_F32(dW);
+  CHECK_CONTIG(dout);
+  embed_bwd(ids.data_ptr<int64_t>(), CBF(dout), dW.data_ptr<float>(), ids.numel(), dW.size(1), dW.size(0),
+            cur_stream(dW));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void kv_write_t(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, torch::Tensor slots, torch::Tensor kc,
+                torch::Tensor vc) {
+  c10::cuda::CUDAGuard guard(qkv.get_device());
+  CHECK_I64(slots);
+  CHECK_CONTIG(slots);
+  CHECK_CONTIG(kc);
+  CHECK_CONTIG(vc);
+  TORCH_CHECK(qkv.stride(1) == 1, "kv_write: qkv rows");
+  kv_write(CBF(qkv), qkv.stride(0), Hq, Hkv, D, slots.data_ptr<int64_t>(), BF(kc), BF(vc), slots.numel(),
+           cur_stream(qkv));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void sqnorm_accum_t(torch::Tensor g, torch::Tensor out) {
+  c10::cuda::CUDAGuard guard(g.get_device());
+  CHECK_F32(g);
+  CHECK_CONTIG(g);
+  sqnorm_accum(g.data_ptr<float>(), g.numel(), out.data_ptr<float>(), cur_stream(g));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void adamw_t(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, c10::optional<torch::Tensor> p16,
+             double lr, double b1, double b2, double eps, double wd, int64_t step,
+             c10::optional<torch::Tensor> sqnorm, double max_norm, double grad_scale) {
+  c10::cuda::CUDAGuard guard(p.get_device());
+  for (auto* t : {&p, &g, &m, &v}) {
+    CHECK_F32(*t);
+    CHECK_CONTIG(*t);
+    TORCH_CHECK(t->numel() == p.numel(), "adamw: size mismatch");
+  }
+  __nv_bfloat16* w16 = nullptr;
+  if (p16.has_value() && p16->defined()) {
+    CHECK_BF16(*p16);
+    CHECK_CONTIG(*p16);
+    TORCH_CHECK(p16->numel() == p.numel(), "adamw: bf16 copy size");
+    w16 = BF(*p16);
+  }
+  const float* sq = (sqnorm.has_value() && sqnorm->defined()) ? sqnorm->data_ptr<float>() : nullptr;
+  adamw_step(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), w16, p.numel(),
+             lr, b1, b2, eps, wd, static_cast<int>(step), sq, max_norm, grad_scale, cur_stream(p));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------ attention
+std::vector<torch::Tensor> attn_fwd_t(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_q,
+                                      torch::Tensor cu_k, torch::Tensor key_idx, torch::Tensor tiles, int64_t Hq,
+                                      int64_t Hkv, int64_t D, double scale, bool causal, bool want_lse) {
+  c10::cuda::CUDAGuard guard(q.get_device());
+  CHECK_BF16(q);
+  CHECK_BF16(k);
+  CHECK_BF16(v);
+  for (auto* t : {&cu_q, &cu_k, &key_idx, &tiles}) {
+    CHECK_I32(*t);
+    CHECK_CONTIG(*t);
+  }
+  TORCH_CHECK(D == 64 || D == 128, "attention: head dim 64 or 128");
+  TORCH_CHECK(Hq % Hkv == 0, "attention: Hq % Hkv == 0");
+  TORCH_CHECK(q.stride(1) == 1 && k.stride(1) == 1 && v.stride(1) == 1, "attention: rows must be contiguous");
+  TORCH_CHECK(k.stride(0) == v.stride(0), "attention: k and v must share a row stride");
+  TORCH_CHECK(q.stride(0) % 8 == 0 && k.stride(0) % 8 == 0, "attention: row strides multiple of 8");
+  const int Tq = q.size(0);
+  auto o = torch::empty({Tq, Hq * D}, q.options());
+  auto lse = want_lse ? torch::empty({Hq, Tq}, q.options().dtype(torch::kFloat32)) : torch::Tensor();
+  AttnParams p{};
+  p.q = CBF(q);
+  p.k = CBF(k);
+  p.v = CBF(v);
+  p.o = BF(o);
+  p.lse = want_lse ? lse.data_ptr<float>() : nullptr;
+  p.cu_q = cu_q.data_ptr<int32_t>();
+  p.cu_k = cu_k.data_ptr<int32_t>();
+  p.key_idx = key_idx.data_ptr<int32_t>();
+  p.tiles = tiles.data_ptr<int32_t>();
+  p.ldq = q.stride(0);
+  p.ldk = k.stride(0);
+  p.ldo = Hq * D;
+  p.Tq = Tq;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale = static_cast<float>(scale);
+  p.causal = causal ? 1 : 0;
+  attn_fwd(p, tiles.numel() / 2, D, cur_stream(q));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {o, lse};
+}
+
+// Returns dq (bf16 [Tq, Hq*D]); dk/dv are accumulated into the fp32 buffers.
+torch::Tensor attn_bwd_t(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dO,
+                         torch::Tensor lse, torch::Tensor cu_q, torch::Tensor cu_k, torch::Tensor key_idx,
+                         torch::Tensor qtiles, torch::Tensor ktiles, torch::Tensor dk_acc, torch::Tensor dv_acc,
+                         int64_t Hq, int64_t Hkv, int64_t D, double scale, bool causal) {
+  c10::cuda::CUDAGuard guard(q.get_device());
+  CHECK_CONTIG(dO);
+  CHECK_CONTIG(o);
+  CHECK_F32(dk_acc);
+  CHECK_F32(dv_acc);
+  TORCH_CHECK(dk_acc.stride(0) == dv_acc.stride(0), "attn_bwd: accumulators share a row stride");
+  const int Tq = q.size(0);
+  auto delta = torch::empty({Hq, Tq}, q.options().dtype(torch::kFloat32));
+  attn_bwd_delta(CBF(o), o.stride(0), CBF(dO), dO.stride(0), delta.data_ptr<float>(), Tq, Hq, D, cur_stream(q));
+  auto dq = torch::empty({Tq, Hq * D}, q.options());
+  AttnBwdParams p{};
+  p.q = CBF(q);
+  p.k = CBF(k);
+  p.v = CBF(v);
+  p.dO = CBF(dO);
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.dq = BF(dq);
+  p.dk_acc = dk_acc.data_ptr<float>();
+  p.dv_acc = dv_acc.data_ptr<float>();
+  p.cu_q = cu_q.data_ptr<int32_t>();
+  p.cu_k = cu_k.data_ptr<int32_t>();
+  p.key_idx = key_idx.data_ptr<int32_t>();
+  p.tiles = qtiles.data_ptr<int32_t>();
+  p.ktiles = ktiles.data_ptr<int32_t>();
+  p.ldq = q.stride(0);
+  p.ldk = k.stride(0);
+  p.lddo = dO.stride(0);
+  p.lddq = Hq * D;
+  p.ld_acc = dk_acc.stride(0);
+  p.Tq = Tq;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale = static_cast<float>(scale);
+  p.causal = causal ? 1 : 0;
+  attn_bwd(p, qtiles.numel() / 2, ktiles.numel() / 2, D, cur_stream(q));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dq;
+}
+
+void attn_decode_t(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor kv_start,
+                   torch::Tensor kv_len, torch::Tensor kv_indices, torch::Tensor o, torch::Tensor part_o, torch::Tensor part_lse,
+                   int64_t Hq, int64_t Hkv, int64_t D, int64_t num_splits, double scale) {
+  c10::cuda::CUDAGuard guard(q.get_device());
+  CHECK_I32(kv_start);
+  CHECK_I32(kv_len);
+  CHECK_I32(kv_indices);
+  TORCH_CHECK(Hq / Hkv <= 16, "decode: GQA group must be <= 16");
+  TORCH_CHECK(q.stride(1) == 1 && o.stride(1) == 1, "decode: rows contiguous");
+  const int B = q.size(0);
+  TORCH_CHECK(kv_start.numel() >= B && kv_len.numel() >= B, "decode: kv_start/kv_len per request");
+  DecodeParams p{};
+  p.q = CBF(q);
+  p.k_cache = CBF(kc);
+  p.v_cache = CBF(vc);
+  p.o = BF(o);
+  p.kv_start = kv_start.data_ptr<int32_t>();
+  p.kv_len = kv_len.data_ptr<int32_t>();
+  p.kv_indices = kv_indices.data_ptr<int32_t>();
+  p.num_splits = static_cast<int>(num_splits);
+  if (num_splits > 1) {
+    TORCH_CHECK(part_o.numel() >= static_cast<int64_t>(B) * Hq * num_splits * D &&
+                    part_lse.numel() >= static_cast<int64_t>(B) * Hq * num_splits,
+                "decode: scratch too small");
+    p.part_o = part_o.data_ptr<float>();
+    p.part_lse = part_lse.data_ptr<float>();
+  }
+  p.ldq = q.stride(0);
+  p.ldk = Hkv * D;
+  p.ldo = o.stride(0);
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale = static_cast<float>(scale);
+  attn_decode(p, B, D, cur_stream(q));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace octo
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  using namespace octo;
+  m.doc() = "octopus_b200 sm_100a kernels";
+  m.def("status_tensor", [](int64_t d) { return status_tensor(static_cast<int>(d)); });
+  m.def("gemm_out", &gemm_out, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("C"),
+        py::arg("alpha") = 1.0, py::arg("residual") = py::none(), py::arg("bias") = py::none(),
+        py::arg("accumulate") = false, py::arg("bn") = 0);
+  m.def("head_fwd", &head_fwd);
+  m.def("head_grad_logits", &head_grad_logits);
+  m.def("sample_head", &sample_head);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd_t);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd_t);
+  m.def("rope", &rope_t);
+  m.def("swiglu_fwd", &swiglu_fwd_t);
+  m.def("swiglu_bwd", &swiglu_bwd_t);
+  m.def("embed_fwd", &embed_fwd_t);
+  m.def("embed_bwd", &embed_bwd_t);
+  m.def("kv_write", &kv_write_t);
+  m.def("sqnorm_accum", &sqnorm_accum_t);
+  m.def("adamw", &adamw_t);
+  m.def("attn_fwd", &attn_fwd_t);
+  m.def("attn_bwd", &attn_bwd_t);
+  m.def("attn_decode", &attn_decode_t);
+}

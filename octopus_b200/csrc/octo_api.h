@@ -1,0 +1,55 @@
+// Plain C++ interface between the torch-facing host glue (*.cpp, g++) and the CUDA
+// kernel translation units (*.cu, nvcc, no torch headers).  Only POD structs and
+// launch functions live here.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace octo {
+
+struct GemmShape {
+  int M, N, K;
+  int m_tiles, n_tiles, k_blocks, num_tiles;
+};
+
+enum GemmEpiKind : int {
+  kEpiBF16 = 0,     // C bf16 = alpha*acc (+ residual)
+  kEpiF32 = 1,      // C fp32 = alpha*acc (+ C if accumulate)
+  kEpiHeadLse = 2,  // per (row, n-tile) partial (max, sumexp, sum z*exp, label logit)
+  kEpiSample = 3,   // per (row, n-tile) partial (max, sumexp, best gumbel score, argmax)
+  kEpiHeadGrad = 4, // C bf16 = d(loss)/d(logit) of the logprob head, recomputed from lse/entropy
+};
+
+struct GemmLaunch {
+  CUtensorMap ta, tb;
+  GemmShape s;
+  int bn;
+  bool a_mn, b_mn;
+  int epi;
+  void* C;
+  int ldc;
+  const void* R;
+  int ldr;
+  float alpha;
+  int accumulate;
+  // head / sampling epilogue extras
+  const int32_t* labels;   // [M] label per row (head) or unused
+  float* partial;          // [M, n_tiles, 4] fp32 partials
+  uint64_t seed;           // sampling RNG seed
+  const int64_t* row_offset;  // sampling: per-row RNG stream id (may be null)
+  int vocab_limit;         // columns >= vocab_limit are masked (padding)
+  const void* bias;        // bf16 [N] bias added in the bf16 epilogue (may be null)
+  const float* lse;        // head grad: per-row log-normaliser
+  const float* ent;        // head grad: per-row entropy
+  const float* g_lp;       // head grad: d loss / d logp per row
+  const float* g_ent;      // head grad: d loss / d entropy per row
+  int* status;
+  int grid;
+  cudaStream_t stream;
+};
+
+void gemm_launch(const GemmLaunch& g);
+int gemm_smem_bytes(int bn);
+
+}  // namespace octo

@@ -1,0 +1,469 @@
+"""Autograd-aware ops over the sm_100a kernels, with CPU reference fallbacks.
+
+Every op dispatches on the device of its input: CUDA tensors run the hand-written
+kernels of ``octopus_b200._C`` (and raise if the extension is missing), CPU tensors
+run :mod:`octopus_b200.ops.reference` in fp32/fp64 so the whole stack is testable on a
+machine without a GPU.
+
+Weight gradients: a weight tensor may carry an fp32 ``main_grad`` attribute (the
+FSDP / optimizer gradient buffer).  Backward then accumulates straight into it (the
+wgrad GEMM epilogue adds into fp32) and returns no gradient for the weight, so no
+bf16 gradient tensor is ever materialised.
+
+Reference parity: `octopus/rl/lm_head.py:20-153` (chunked head: per-row logprob and
+entropy, recomputed in backward), `octopus/rl/prefix_tree.py:381-413` (tree attention:
+bottom-right causal attention over gathered key lists), `octopus/rl/seq_tiles.py:61-82`
+(rms_norm, silu_mul element-wise blocks).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import reference as ref
+from ._ext import ext
+
+HEAD_CHUNK = 4096  # rows per chunk in the head backward (dz is [chunk, vocab] bf16)
+
+
+def _is_cuda(t: torch.Tensor) -> bool:
+    return t.is_cuda
+
+
+def _accum_wgrad(w: torch.Tensor, dw: torch.Tensor):
+    """Accumulate a weight gradient into w.main_grad if present, else return it."""
+    mg = getattr(w, "main_grad", None)
+    if mg is not None:
+        mg.add_(dw.to(mg.dtype).view_as(mg))
+        return None
+    return dw.to(w.dtype)
+
+
+# ---------------------------------------------------------------------------- GEMM
+def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, out=None,
+         out_dtype=torch.bfloat16, alpha: float = 1.0, residual=None, bias=None, accumulate: bool = False,
+         bn: int = 0) -> torch.Tensor:
+    """C = alpha * A_log @ B_log^T (+bias)(+residual) on the tcgen05 GEMM.
+
+    A_log is `a` ([M, K]) or `a.T` when a_mn ([K, M] storage); B_log is `b` ([N, K]) or
+    `b.T` when b_mn ([K, N] storage).
+    """
+    M = a.shape[1] if a_mn else a.shape[0]
+    N = b.shape[1] if b_mn else b.shape[0]
+    if not _is_cuda(a):
+        A = a.t() if a_mn else a
+        B = b.t() if b_mn else b
+        y = alpha * (ref._f(A) @ ref._f(B).t())
+        if bias is not None:
+            y = y + ref._f(bias)
+        if residual is not None:
+            y = y + ref._f(residual)
+        if out is not None:
+            if accumulate:
+                out.add_(y.to(out.dtype))
+            else:
+                out.copy_(y.to(out.dtype))
+            return out
+        return y.to(out_dtype if a.dtype != torch.float64 else torch.float64)
+    if out is None:
+        out = torch.empty(M, N, dtype=out_dtype, device=a.device)
+    ext().gemm_out(a, a_mn, b, b_mn, out, alpha, residual, bias, accumulate, bn)
+    return out
+
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b, residual):
+        ctx.save_for_backward(x, w)
+        ctx.bias = b
+        ctx.has_res = residual is not None
+        if _is_cuda(x):
+            return gemm(x, w, bias=b, residual=residual)
+        return ref.linear(x, w, b, residual).to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        dres = dy if ctx.has_res else None
+        db = None
+        if ctx.bias is not None:
+            db = _accum_wgrad(ctx.bias, dy.float().sum(0) if dy.dtype != torch.float64 else dy.sum(0))
+        if _is_cuda(x):
+            dx = gemm(dy, w, b_mn=True)  # dy [M,N] @ w [N,K]
+            mg = getattr(w, "main_grad", None)
+            if mg is not None:
+                gemm(dy, x, a_mn=True, b_mn=True, out=mg, accumulate=True)
+                dw = None
+            else:
+                dw = gemm(dy, x, a_mn=True, b_mn=True, out_dtype=torch.float32).to(w.dtype)
+        else:
+            dx = (ref._f(dy) @ ref._f(w)).to(x.dtype)
+            dw = _accum_wgrad(w, ref._f(dy).t() @ ref._f(x))
+        return dx, dw, db, dres
+
+
+def linear(x, w, b=None, residual=None):
+    """y = x W^T (+ b) (+ residual) with fused fp32 weight-gradient accumulation."""
+    return _Linear.apply(x, w, b, residual)
+
+
+# ---------------------------------------------------------------------------- RMSNorm
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps, plus_one):
+        ctx.eps, ctx.plus_one = eps, plus_one
+        if _is_cuda(x):
+            y, rstd = ext().rmsnorm_fwd(x, w, eps, plus_one)
+        else:
+            xf = ref._f(x)
+            rstd = torch.rsqrt(xf.pow(2).mean(-1) + eps)
+            y = ref.rmsnorm(x, w, eps, plus_one).to(x.dtype)
+        ctx.save_for_backward(x, w, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, rstd = ctx.saved_tensors
+        dy = dy.contiguous()
+        if _is_cuda(x):
+            mg = getattr(w, "main_grad", None)
+            dwbuf = mg if mg is not None else torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+            dx = ext().rmsnorm_bwd(dy, x, w, rstd, None, dwbuf, ctx.plus_one)
+            dw = None if mg is not None else dwbuf.to(w.dtype)
+            return dx, dw, None, None
+        xf, dyf, wf = ref._f(x), ref._f(dy), ref._f(w)
+        weff = (1.0 + wf) if ctx.plus_one else wf
+        r = rstd[:, None]
+        xh = xf * r
+        gw = dyf * weff
+        dx = r * (gw - xh * (gw * xh).mean(-1, keepdim=True))
+        dw = _accum_wgrad(w, (dyf * xh).sum(0))
+        return dx.to(x.dtype), dw, None, None
+
+
+def rmsnorm(x, w, eps: float = 1e-6, plus_one: bool = False):
+    return _RMSNorm.apply(x, w, eps, plus_one)
+
+
+# ---------------------------------------------------------------------------- RoPE
+class _Rope(torch.autograd.Function):
+    """In-place rotary embedding on the q and k heads of a fused qkv row."""
+
+    @staticmethod
+    def forward(ctx, qkv, pos, Hq, Hkv, D, theta):
+        ctx.meta = (Hq, Hkv, D, theta)
+        ctx.save_for_backward(pos)
+        _rope_inplace(qkv, pos, Hq, Hkv, D, theta, inverse=False)
+        ctx.mark_dirty(qkv)
+        return qkv
+
+    @staticmethod
+    def backward(ctx, g):
+        (pos,) = ctx.saved_tensors
+        Hq, Hkv, D, theta = ctx.meta
+        g = g.contiguous().clone()
+        _rope_inplace(g, pos, Hq, Hkv, D, theta, inverse=True)
+        return g, None, None, None, None, None
+
+
+def _rope_inplace(qkv, pos, Hq, Hkv, D, theta, inverse):
+    if _is_cuda(qkv):
+        ext().rope(qkv, pos, Hq, Hkv, D, theta, inverse)
+        return
+    T = qkv.shape[0]
+    heads = qkv[:, : (Hq + Hkv) * D].reshape(T, Hq + Hkv, D)
+    heads.copy_(ref.rope(heads, pos, theta, inverse=inverse).to(qkv.dtype))
+
+
+def rope_(qkv, pos, Hq, Hkv, D, theta):
+    return _Rope.apply(qkv, pos, Hq, Hkv, D, theta)
+
+
+# ---------------------------------------------------------------------------- SwiGLU
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu):
+        ctx.save_for_backward(gu)
+        if _is_cuda(gu):
+            return ext().swiglu_fwd(gu)
+        return ref.swiglu(gu).to(gu.dtype)
+
+    @staticmethod
+    def backward(ctx, d):
+        (gu,) = ctx.saved_tensors
+        d = d.contiguous()
+        if _is_cuda(gu):
+            return ext().swiglu_bwd(gu, d)
+        g, u = ref._f(gu).chunk(2, dim=-1)
+        s = torch.sigmoid(g)
+        df = ref._f(d)
+        return torch.cat([df * u * s * (1 + g * (1 - s)), df * g * s], dim=-1).to(gu.dtype)
+
+
+def swiglu(gu):
+    return _SwiGLU.apply(gu)
+
+
+# ---------------------------------------------------------------------------- embedding
+class _Embed(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, W):
+        ctx.save_for_backward(ids, W)
+        if _is_cuda(W):
+            return ext().embed_fwd(ids, W)
+        return W[ids]
+
+    @staticmethod
+    def backward(ctx, d):
+        ids, W = ctx.saved_tensors
+        d = d.contiguous()
+        mg = getattr(W, "main_grad", None)
+        if _is_cuda(W):
+            buf = mg if mg is not None else torch.zeros(W.shape, dtype=torch.float32, device=W.device)
+            ext().embed_bwd(ids, d, buf)
+            return None, (None if mg is not None else buf.to(W.dtype))
+        g = torch.zeros(W.shape, dtype=ref._f(d).dtype)
+        g.index_add_(0, ids, ref._f(d))
+        return None, _accum_wgrad(W, g)
+
+
+def embed(ids, W):
+    return _Embed.apply(ids, W)
+
+
+# ---------------------------------------------------------------------------- attention plan
+@dataclass
+class AttnPlan:
+    """Sequences of query rows with gathered key lists (tree nodes or requests).
+
+    cu_q[s]..cu_q[s+1] are the query rows of sequence s; key_idx[cu_k[s]..cu_k[s+1]]
+    its key rows (own rows last).  Tile tables are precomputed on the host.
+    """
+
+    cu_q: torch.Tensor
+    cu_k: torch.Tensor
+    key_idx: torch.Tensor
+    fwd_tiles: torch.Tensor
+    dq_tiles: torch.Tensor
+    kv_tiles: torch.Tensor
+    host_cu_q: np.ndarray = field(repr=False, default=None)
+    host_cu_k: np.ndarray = field(repr=False, default=None)
+    host_key_idx: np.ndarray = field(repr=False, default=None)
+
+    @staticmethod
+    def build(cu_q, cu_k, key_idx, device="cpu") -> "AttnPlan":
+        cu_q = np.asarray(cu_q, dtype=np.int32)
+        cu_k = np.asarray(cu_k, dtype=np.int32)
+        key_idx = np.asarray(key_idx, dtype=np.int32)
+        nq = np.diff(cu_q)
+        nk = np.diff(cu_k)
+
+        def tiles(lengths, step, mask):
+            out = []
+            for s, n in enumerate(lengths):
+                if n <= 0 or not mask[s]:
+                    continue
+                for o in range(0, int(n), step):
+                    out.append((s, o))
+            return np.asarray(out, dtype=np.int32).reshape(-1, 2)
+
+        has_q = nq > 0
+        ft = tiles(nq, 128, has_q)
+        dt = tiles(nq, 64, has_q)
+        kt = tiles(nk, 64, has_q)
+        dev = torch.device(device)
+
+        def T(a):
+            return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+        return AttnPlan(T(cu_q), T(cu_k), T(key_idx), T(ft.reshape(-1)), T(dt.reshape(-1)), T(kt.reshape(-1)),
+                        cu_q, cu_k, key_idx)
+
+    @staticmethod
+    def causal_packed(lengths, device="cpu") -> "AttnPlan":
+        """Plain packed causal sequences (keys = own rows)."""
+        cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+        return AttnPlan.build(cu, cu, np.arange(cu[-1], dtype=np.int32), device)
+
+
+class _Attention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, plan, Hq, Hkv, D, scale):
+        T, W = qkv.shape
+        q = qkv[:, : Hq * D]
+        k = qkv[:, Hq * D: (Hq + Hkv) * D]
+        v = qkv[:, (Hq + Hkv) * D: (Hq + 2 * Hkv) * D]
+        ctx.meta = (plan, Hq, Hkv, D, scale)
+        if _is_cuda(qkv):
+            o, lse = ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D, scale,
+                                    True, True)
+        else:
+            o3, lse = ref.gather_attention(q.reshape(T, Hq, D), k.reshape(T, Hkv, D), v.reshape(T, Hkv, D),
+                                           plan.host_cu_q, plan.host_cu_k, torch.from_numpy(plan.host_key_idx),
+                                           scale)
+            o = o3.reshape(T, Hq * D).to(qkv.dtype)
+        ctx.save_for_backward(qkv, o, lse)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        qkv, o, lse = ctx.saved_tensors
+        plan, Hq, Hkv, D, scale = ctx.meta
+        T = qkv.shape[0]
+        do = do.contiguous()
+        if _is_cuda(qkv):
+            q = qkv[:, : Hq * D]
+            k = qkv[:, Hq * D: (Hq + Hkv) * D]
+            v = qkv[:, (Hq + Hkv) * D: (Hq + 2 * Hkv) * D]
+            dk = torch.zeros(T, Hkv * D, dtype=torch.float32, device=qkv.device)
+            dv = torch.zeros(T, Hkv * D, dtype=torch.float32, device=qkv.device)
+            dq = ext().attn_bwd(q, k, v, o, do, lse, plan.cu_q, plan.cu_k, plan.key_idx, plan.dq_tiles,
+                                plan.kv_tiles, dk, dv, Hq, Hkv, D, scale, True)
+            dqkv = torch.empty_like(qkv)
+            dqkv[:, : Hq * D] = dq
+            dqkv[:, Hq * D: (Hq + Hkv) * D] = dk
+            dqkv[:, (Hq + Hkv) * D:] = dv
+            return dqkv, None, None, None, None, None
+        # CPU: differentiate the reference with autograd
+        with torch.enable_grad():
+            x = qkv.detach().to(torch.float64 if qkv.dtype == torch.float64 else torch.float32).requires_grad_(True)
+            q = x[:, : Hq * D].reshape(T, Hq, D)
+            k = x[:, Hq * D: (Hq + Hkv) * D].reshape(T, Hkv, D)
+            v = x[:, (Hq + Hkv) * D:].reshape(T, Hkv, D)
+            o3, _ = ref.gather_attention(q, k, v, plan.host_cu_q, plan.host_cu_k,
+                                         torch.from_numpy(plan.host_key_idx), scale)
+            (g,) = torch.autograd.grad(o3.reshape(T, Hq * D), x, ref._f(do).to(x.dtype))
+        return g.to(qkv.dtype), None, None, None, None, None
+
+
+def attention(qkv, plan: AttnPlan, Hq: int, Hkv: int, D: int, scale: float | None = None):
+    """Gathered-key causal attention on a fused qkv [T, (Hq+2Hkv)*D] -> o [T, Hq*D]."""
+    if scale is None:
+        scale = D ** -0.5
+    return _Attention.apply(qkv, plan, Hq, Hkv, D, scale)
+
+
+# ---------------------------------------------------------------------------- logprob head
+class _Head(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h, W, labels, alpha, vocab_limit):
+        M = h.shape[0]
+        ctx.alpha, ctx.vocab_limit = alpha, vocab_limit
+        if _is_cuda(h):
+            pad = (-M) % 8
+            hp = torch.cat([h, h.new_zeros(pad, h.shape[1])]) if pad else h
+            lp = torch.cat([labels, labels.new_full((pad,), -1)]) if pad else labels
+            logp, ent, lse = ext().head_fwd(hp.contiguous(), W, lp.to(torch.int32).contiguous(), alpha,
+                                            vocab_limit or 0)
+            logp, ent, lse = logp[:M], ent[:M], lse[:M]
+        else:
+            logp, ent, lse = ref.logprob_head(h, W, labels, alpha, vocab_limit)
+        ctx.save_for_backward(h, W, labels, lse, ent)
+        return logp, ent
+
+    @staticmethod
+    def backward(ctx, g_lp, g_ent):
+        h, W, labels, lse, ent = ctx.saved_tensors
+        alpha, vocab_limit = ctx.alpha, ctx.vocab_limit
+        M = h.shape[0]
+        if g_lp is None:
+            g_lp = torch.zeros_like(lse)
+        if g_ent is None:
+            g_ent = torch.zeros_like(lse)
+        g_lp = g_lp.float().contiguous()
+        g_ent = g_ent.float().contiguous()
+        if _is_cuda(h):
+            dh = torch.empty_like(h)
+            mg = getattr(W, "main_grad", None)
+            dW = mg if mg is not None else torch.zeros(W.shape, dtype=torch.float32, device=W.device)
+            V = W.shape[0]
+            for a in range(0, M, HEAD_CHUNK):
+                b = min(M, a + HEAD_CHUNK)
+                m = b - a
+                pad = (-m) % 8
+                hc = h[a:b]
+                lc, sc, ec, gl, ge = labels[a:b], lse[a:b], ent[a:b], g_lp[a:b], g_ent[a:b]
+                if pad:
+                    hc = torch.cat([hc, hc.new_zeros(pad, hc.shape[1])])
+                    lc = torch.cat([lc, lc.new_full((pad,), -1)])
+                    z = torch.zeros(pad, dtype=torch.float32, device=h.device)
+                    sc, ec, gl, ge = (torch.cat([t, z]) for t in (sc, ec, gl, ge))
+                hc = hc.contiguous()
+                dz = torch.empty(hc.shape[0], V, dtype=torch.bfloat16, device=h.device)
+                ext().head_grad_logits(hc, W, lc.to(torch.int32).contiguous(), sc.contiguous(), ec.contiguous(),
+                                       gl.contiguous(), ge.contiguous(), dz, alpha, vocab_limit or 0)
+                dh[a:b] = gemm(dz, W, b_mn=True)[:m]
+                gemm(dz, hc, a_mn=True, b_mn=True, out=dW, accumulate=True)
+            dWret = None if mg is not None else dW.to(W.dtype)
+            return dh, dWret, None, None, None
+        with torch.enable_grad():
+            hf = ref._f(h).detach().requires_grad_(True)
+            Wf = ref._f(W).detach().requires_grad_(True)
+            lp, en, _ = ref.logprob_head(hf, Wf, labels, alpha, vocab_limit)
+            gh, gW = torch.autograd.grad((lp * g_lp.to(lp.dtype)).sum() + (en * g_ent.to(en.dtype)).sum(),
+                                         (hf, Wf))
+        return gh.to(h.dtype), _accum_wgrad(W, gW), None, None, None
+
+
+def logprob_head(h, W, labels, alpha: float = 1.0, vocab_limit: int | None = None):
+    """(log p(label), entropy) of softmax(alpha * h W^T) without full logits."""
+    return _Head.apply(h, W, labels, alpha, vocab_limit)
+
+
+# ---------------------------------------------------------------------------- sampling
+def sample(h, W, temperature: float = 1.0, seed: int = 0, row_stream=None, vocab_limit: int | None = None):
+    """Sample one token per row from softmax(h W^T / T) (Gumbel-max); returns (tokens, logprobs)."""
+    alpha = 1.0 / max(temperature, 1e-6)
+    if _is_cuda(h):
+        M = h.shape[0]
+        pad = (-M) % 8
+        hp = torch.cat([h, h.new_zeros(pad, h.shape[1])]) if pad else h
+        rs = row_stream
+        if rs is not None and pad:
+            rs = torch.cat([rs, rs.new_zeros(pad)])
+        tok, lp = ext().sample_head(hp.contiguous(), W, alpha, seed, rs, vocab_limit or 0)
+        return tok[:M], lp[:M]
+    z = (ref._f(h) @ ref._f(W).t()) * alpha
+    if vocab_limit is not None:
+        z = z[:, :vocab_limit]
+    gen = torch.Generator().manual_seed(int(seed))
+    u = torch.rand(z.shape, generator=gen, dtype=z.dtype).clamp_(1e-7, 1 - 1e-7)
+    tok = (z - torch.log(-torch.log(u))).argmax(-1)
+    lp = torch.log_softmax(z, -1).gather(1, tok[:, None])[:, 0]
+    return tok, lp.float()
+
+
+# ---------------------------------------------------------------------------- optimizer
+def adamw_(p32, grad, m, v, p16, *, lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, step=1, sqnorm=None,
+           max_norm=0.0, grad_scale=1.0):
+    """Fused AdamW on flat fp32 buffers (+ bf16 copy), clip factor from a device-side norm."""
+    if _is_cuda(p32):
+        ext().adamw(p32, grad, m, v, p16, lr, betas[0], betas[1], eps, weight_decay, step, sqnorm, max_norm,
+                    grad_scale)
+        return
+    b1, b2 = betas
+    clip = grad_scale
+    if sqnorm is not None and max_norm > 0:
+        nrm = float(sqnorm.sqrt()) * grad_scale
+        if nrm > max_norm:
+            clip *= max_norm / (nrm + 1e-6)
+    g = grad * clip
+    m.mul_(b1).add_(g, alpha=1 - b1)
+    v.mul_(b2).addcmul_(g, g, value=1 - b2)
+    p32.mul_(1 - lr * weight_decay)
+    bc1 = 1 - b1 ** step
+    bc2 = 1 - b2 ** step
+    p32.sub_(lr * (m / bc1) / ((v / bc2).sqrt() + eps))
+    if p16 is not None:
+        p16.copy_(p32.to(p16.dtype))
+
+
+def sqnorm_(g: torch.Tensor, out: torch.Tensor):
+    """out += sum(g^2) (device-side, no sync)."""
+    if _is_cuda(g):
+        ext().sqnorm_accum(g, out)
+    else:
+        out.add_(g.double().pow(2).sum().to(out.dtype))

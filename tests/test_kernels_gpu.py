@@ -1,0 +1,249 @@
+"""GPU numerics of every sm_100a kernel against plain-PyTorch fp32 references."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from octopus_b200 import ops
+from octopus_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / (b.norm() + 1e-12))
+
+
+@pytest.fixture(autouse=True)
+def _status():
+    yield
+    ops.check_status(0)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 1024), (1000, 1536, 1536), (40, 200, 96),
+                                   (4096, 4608, 3584)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm(M, N, K, a_mn, b_mn):
+    torch.manual_seed(0)
+    A = torch.randn(M, K, device=dev).bfloat16()
+    B = torch.randn(N, K, device=dev).bfloat16()
+    a = A.t().contiguous() if a_mn else A
+    b = B.t().contiguous() if b_mn else B
+    C = ops.gemm(a, b, a_mn=a_mn, b_mn=b_mn)
+    R = A.float() @ B.float().t()
+    assert rel_err(C, R) < 1e-2
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_gemm_tiles_and_epilogues(bn):
+    torch.manual_seed(1)
+    M, N, K = 520, 776, 512
+    A = torch.randn(M, K, device=dev).bfloat16()
+    B = torch.randn(N, K, device=dev).bfloat16()
+    bias = torch.randn(N, device=dev).bfloat16()
+    res = torch.randn(M, N, device=dev).bfloat16()
+    C = ops.gemm(A, B, bias=bias, residual=res, alpha=0.5, bn=bn)
+    R = 0.5 * (A.float() @ B.float().t()) + bias.float() + res.float()
+    assert rel_err(C, R) < 1e-2
+    acc = torch.randn(M, N, device=dev)
+    base = acc.clone()
+    ops.gemm(A, B, out=acc, accumulate=True, bn=bn)
+    assert rel_err(acc, base + A.float() @ B.float().t()) < 1e-2
+
+
+def test_linear_autograd():
+    torch.manual_seed(2)
+    x = torch.randn(384, 512, device=dev).bfloat16().requires_grad_(True)
+    w = torch.randn(768, 512, device=dev).bfloat16() * 0.05
+    w.main_grad = torch.zeros(768, 512, device=dev)
+    b = torch.randn(768, device=dev).bfloat16()
+    b.main_grad = torch.zeros(768, device=dev)
+    y = ops.linear(x, w, b)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.float().requires_grad_(True)
+    yr = xr @ wr.t() + b.float()
+    yr.backward(g.float())
+    assert rel_err(y, yr) < 1e-2
+    assert rel_err(x.grad, xr.grad) < 1e-2
+    assert rel_err(w.main_grad, wr.grad) < 1e-2
+    assert rel_err(b.main_grad, g.float().sum(0)) < 1e-3
+
+
+def test_rmsnorm_fwd_bwd():
+    torch.manual_seed(3)
+    for plus_one in (False, True):
+        x = torch.randn(333, 1536, device=dev).bfloat16().requires_grad_(True)
+        w = (torch.rand(1536, device=dev) + 0.5).bfloat16()
+        w.main_grad = torch.zeros(1536, device=dev)
+        y = ops.rmsnorm(x, w, 1e-6, plus_one)
+        g = torch.randn_like(y)
+        y.backward(g)
+        xr = x.detach().float().requires_grad_(True)
+        wr = w.float().requires_grad_(True)
+        yr = ref.rmsnorm(xr, wr, 1e-6, plus_one)
+        yr.backward(g.float())
+        assert rel_err(y, yr) < 1e-2
+        assert rel_err(x.grad, xr.grad) < 2e-2
+        assert rel_err(w.main_grad, wr.grad) < 2e-2
+
+
+def test_rope_roundtrip():
+    torch.manual_seed(4)
+    T, Hq, Hkv, D = 77, 4, 2, 128
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=dev).bfloat16()
+    pos = torch.randint(0, 30000, (T,), device=dev, dtype=torch.int32)
+    x = qkv.clone()
+    ops.ext().rope(x, pos, Hq, Hkv, D, 1e6, False)
+    r = ref.rope(qkv[:, : (Hq + Hkv) * D].reshape(T, Hq + Hkv, D).cpu(), pos.cpu(), 1e6)
+    assert rel_err(x[:, : (Hq + Hkv) * D].reshape(T, Hq + Hkv, D).cpu(), r) < 1e-2
+    assert torch.equal(x[:, (Hq + Hkv) * D:], qkv[:, (Hq + Hkv) * D:])
+    ops.ext().rope(x, pos, Hq, Hkv, D, 1e6, True)
+    assert rel_err(x, qkv) < 2e-2
+
+
+def test_swiglu():
+    torch.manual_seed(5)
+    gu = torch.randn(100, 2 * 688, device=dev).bfloat16().requires_grad_(True)
+    y = ops.swiglu(gu)
+    g = torch.randn_like(y)
+    y.backward(g)
+    gr = gu.detach().float().requires_grad_(True)
+    yr = ref.swiglu(gr)
+    yr.backward(g.float())
+    assert rel_err(y, yr) < 1e-2
+    assert rel_err(gu.grad, gr.grad) < 2e-2
+
+
+def _tree_plan(rng, n_nodes=12, H=64):
+    """Random tree: each node = parent path keys + own rows (own last), rows contiguous."""
+    lens = rng.integers(1, 300, size=n_nodes)
+    parent = [-1] + [int(rng.integers(0, i)) for i in range(1, n_nodes)]
+    starts = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    keys, cu_k, cu_q = [], [0], [0]
+    for i in range(n_nodes):
+        path = []
+        p = parent[i]
+        chain = []
+        while p >= 0:
+            chain.append(p)
+            p = parent[p]
+        for a in reversed(chain):
+            path.extend(range(starts[a], starts[a] + lens[a]))
+        path.extend(range(starts[i], starts[i] + lens[i]))
+        keys.extend(path)
+        cu_k.append(len(keys))
+        cu_q.append(cu_q[-1] + lens[i])
+    return int(lens.sum()), cu_q, cu_k, np.asarray(keys, dtype=np.int32)
+
+
+@pytest.mark.parametrize("D,Hq,Hkv", [(128, 28, 4), (64, 4, 4), (128, 12, 2)])
+def test_tree_attention_fwd_bwd(D, Hq, Hkv):
+    rng = np.random.default_rng(6)
+    torch.manual_seed(6)
+    T, cu_q, cu_k, keys = _tree_plan(rng)
+    plan = ops.AttnPlan.build(cu_q, cu_k, keys, dev)
+    qkv = (torch.randn(T, (Hq + 2 * Hkv) * D, device=dev) * 0.5).bfloat16().requires_grad_(True)
+    o = ops.attention(qkv, plan, Hq, Hkv, D)
+    g = torch.randn_like(o)
+    o.backward(g)
+    x = qkv.detach().float().cpu().requires_grad_(True)
+    q = x[:, : Hq * D].reshape(T, Hq, D)
+    k = x[:, Hq * D: (Hq + Hkv) * D].reshape(T, Hkv, D)
+    v = x[:, (Hq + Hkv) * D:].reshape(T, Hkv, D)
+    orf, _ = ref.gather_attention(q, k, v, cu_q, cu_k, torch.from_numpy(keys), D ** -0.5)
+    orf = orf.reshape(T, Hq * D)
+    orf.backward(g.float().cpu())
+    assert rel_err(o.cpu(), orf) < 2e-2
+    assert rel_err(qkv.grad.cpu(), x.grad) < 3e-2
+
+
+def test_decode_attention():
+    torch.manual_seed(7)
+    B, Hq, Hkv, D = 37, 28, 4, 128
+    slots = 6000
+    kc = torch.randn(slots, Hkv * D, device=dev).bfloat16()
+    vc = torch.randn(slots, Hkv * D, device=dev).bfloat16()
+    lens = torch.randint(1, 1500, (B,))
+    ip = torch.zeros(B + 1, dtype=torch.int32)
+    ip[1:] = torch.cumsum(lens, 0)
+    idx = torch.randint(0, slots, (int(ip[-1]),), dtype=torch.int32)
+    q = torch.randn(B, Hq * D, device=dev).bfloat16()
+    for splits in (1, 4):
+        da = ops.DecodeAttention(Hq, Hkv, D, B, splits, dev)
+        o = da(q, kc, vc, ip.to(dev), idx.to(dev))
+        r = ops.decode.decode_attention_ref(q.cpu().float(), kc.cpu().float(), vc.cpu().float(), ip, idx, Hq, Hkv,
+                                            D, D ** -0.5)
+        assert rel_err(o.cpu(), r) < 2e-2
+
+
+def test_logprob_head_fwd_bwd():
+    torch.manual_seed(8)
+    M, H, V = 1000, 512, 5000
+    h = (torch.randn(M, H, device=dev) * 0.5).bfloat16().requires_grad_(True)
+    W = (torch.randn(V + 120, H, device=dev) * 0.05).bfloat16()
+    W.main_grad = torch.zeros(W.shape, device=dev)
+    labels = torch.randint(0, V, (M,), device=dev)
+    labels[::7] = -1
+    lp, ent = ops.logprob_head(h, W, labels, 0.8, V)
+    glp, gent = torch.randn(M, device=dev), torch.randn(M, device=dev) * 0.1
+    (lp * glp + ent * gent).sum().backward()
+    hr = h.detach().float().requires_grad_(True)
+    Wr = W.float().requires_grad_(True)
+    lpr, entr, _ = ref.logprob_head(hr, Wr, labels, 0.8, V)
+    (lpr * glp + entr * gent).sum().backward()
+    assert rel_err(lp, lpr) < 1e-2
+    assert rel_err(ent, entr) < 1e-2
+    assert rel_err(h.grad, hr.grad) < 3e-2
+    assert rel_err(W.main_grad, Wr.grad) < 3e-2
+
+
+def test_sampling_distribution():
+    torch.manual_seed(9)
+    H, V = 64, 256
+    W = torch.randn(V, H, device=dev).bfloat16() * 0.3
+    h1 = torch.randn(1, H, device=dev).bfloat16()
+    h = h1.repeat(8192, 1)
+    streams = torch.arange(8192, device=dev, dtype=torch.int64)
+    tok, lp = ops.sample(h, W, temperature=1.0, seed=1234, row_stream=streams)
+    p = torch.softmax(h1.float() @ W.float().t(), -1)[0]
+    emp = torch.bincount(tok, minlength=V).float() / tok.numel()
+    assert float((emp - p).abs().sum()) < 0.15
+    assert torch.allclose(lp, torch.log(p[tok]), atol=2e-2)
+    tok2, _ = ops.sample(h, W, temperature=1.0, seed=1234, row_stream=streams)
+    assert torch.equal(tok, tok2)
+
+
+def test_adamw_matches_reference():
+    torch.manual_seed(10)
+    n = 10007
+    p = torch.randn(n, device=dev)
+    g = torch.randn(n, device=dev)
+    m = torch.zeros(n, device=dev)
+    v = torch.zeros(n, device=dev)
+    p16 = torch.empty(n, device=dev, dtype=torch.bfloat16)
+    sq = torch.zeros(1, device=dev)
+    ops.sqnorm_(g, sq)
+    assert abs(float(sq) - float((g * g).sum())) / float((g * g).sum()) < 1e-4
+    pc, gc, mc, vc = p.cpu(), g.cpu(), m.cpu(), v.cpu()
+    ops.adamw_(p, g, m, v, p16, lr=1e-3, weight_decay=0.1, step=1, sqnorm=sq, max_norm=1.0)
+    ops.adamw_(pc, gc, mc, vc, None, lr=1e-3, weight_decay=0.1, step=1, sqnorm=sq.cpu(), max_norm=1.0)
+    assert rel_err(p.cpu(), pc) < 1e-5
+    assert rel_err(p16.float().cpu(), pc) < 1e-2
+
+
+def test_embedding():
+    torch.manual_seed(11)
+    W = torch.randn(1000, 256, device=dev).bfloat16().requires_grad_(True)
+    W.main_grad = torch.zeros(1000, 256, device=dev)
+    ids = torch.randint(0, 1000, (300,), device=dev)
+    y = ops.embed(ids, W)
+    assert torch.equal(y, W.detach()[ids])
+    g = torch.randn_like(y)
+    y.backward(g)
+    r = torch.zeros(1000, 256, device=dev).index_add_(0, ids, g.float())
+    assert rel_err(W.main_grad, r) < 1e-3
