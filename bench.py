@@ -1,0 +1,242 @@
+#!/usr/bin/env python
+"""Headline benchmark: RL step tokens/sec/box (rollout + prefix-tree train + weight sync)
+on the Qwen2.5-7B-shape multi-agent DAG config (planner -> 2 solvers -> verifier, shared
+2048-token prefix mounted zero-copy into every agent, 512-token turns, 32 DAG
+instances x 4 samples), bf16, synthetic tokens, random-init weights.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl octopus|reference]
+
+N > 1 is launched by torchrun (one rank per GPU).  Scaling is strong: the whole config
+(32 x 4 DAG samples) is split across the ranks.  `value` = generated tokens of all ranks
+per second of device time (CUDA events on each rank, max over ranks), every generated
+token is also trained once.  `e2e` = the same metric from the per-step wall clock of the
+public `RLTrainer.step()` API, whose timed region includes the host->device copies of
+each step's inputs (prompts, tree plans) from pinned memory and the device->host reads
+of the results (sampled tokens, logprobs, loss).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "RL step tokens/sec/box (rollout+train+sync), 7B-shape multi-agent, 1/2/4/8 B200"
+BASELINE_VALUE = None  # BASELINE.md publishes no tokens/sec figure for this metric
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="octopus", choices=["octopus", "reference"])
+    ap.add_argument("--model", default="qwen2.5-7b")
+    ap.add_argument("--instances", type=int, default=32)
+    ap.add_argument("--samples", type=int, default=4)
+    ap.add_argument("--prefix", type=int, default=2048)
+    ap.add_argument("--turn", type=int, default=512)
+    ap.add_argument("--role", type=int, default=16)
+    ap.add_argument("--mb-tokens", type=int, default=32768)
+    ap.add_argument("--kv-gb", type=float, default=0.0, help="KV pool size (0: sized from the config)")
+    ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke tests only)")
+    ap.add_argument("--no-graphs", action="store_true")
+    return ap.parse_args()
+
+
+def reference_arm(args):
+    reason = ("reference stack not installable offline: its build backend (hatchling) is not in the wheelhouse, and "
+              "its RL step needs sglang 0.5.19, AReaL and peft, none of which is installed")
+    print(json.dumps({"impl": "reference", "metric": METRIC, "unavailable": reason, "n_gpus": args.gpus}))
+    return 0
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        load = [x for x in sm if smax and x > 0.3 * smax] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+    import torch
+    import torch.distributed as dist
+
+    from octopus_b200 import ops
+    from octopus_b200.envs.dag import DagConfig, MultiAgentDag
+    from octopus_b200.models.config import get_config
+    from octopus_b200.parallel.dp import DataParallel
+    from octopus_b200.rl.actor import Actor
+    from octopus_b200.rl.trainer import RLTrainer, TrainerConfig
+    from octopus_b200.serving.engine import Engine
+    from octopus_b200.utils import iostats
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    n_gpus = world
+
+    over = {"layers": args.layers} if args.layers else {}
+    cfg = get_config(args.model, **over)
+    # strong scaling: this rank's share of the DAG instances
+    inst = [i for i in range(args.instances) if i % world == rank]
+    dcfg = DagConfig(instances=args.instances, samples=args.samples, prefix_len=args.prefix, turn_len=args.turn,
+                     role_len=args.role, seed=1000 + rank)
+    env = MultiAgentDag(cfg.vocab_size, dcfg)
+    actor = Actor(cfg, dev, seed=0)
+    per_inst = args.prefix + args.samples * (4 * (args.turn + args.role) + 2)
+    kv_slots = int(len(inst) * per_inst * 1.15) + 8192
+    if args.kv_gb:
+        kv_slots = int(args.kv_gb * (1 << 30) / (4 * cfg.layers * cfg.kv_width))
+    max_batch = max(8, 1 << (len(inst) * args.samples * 2 - 1).bit_length())
+    engine = Engine(cfg, actor.weights, kv_slots=kv_slots, max_batch=max_batch, device=dev,
+                    use_graphs=not args.no_graphs)
+    dp = DataParallel(actor) if world > 1 else None
+
+    class _Env:
+        def rollout(self, eng):
+            return env.rollout(eng, inst)
+
+    trainer = RLTrainer(actor, engine, _Env(), TrainerConfig(mb_tokens=args.mb_tokens))
+    if dp is not None:
+        dp.attach(trainer)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        trainer.step()
+    torch.cuda.synchronize()
+    ops.check_status(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    iostats.reset()
+    l0 = ops.launches()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gen, wall, stats = 0, [], []
+    start.record()
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        st = trainer.step()
+        torch.cuda.synchronize()
+        wall.append(time.perf_counter() - t0)
+        gen += st["generated_tokens"]
+        stats.append(st)
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    io = iostats.snapshot()
+    launches = ops.launches() - l0
+    ms = start.elapsed_time(end)
+    ops.check_status(local)
+    t = torch.tensor([ms, float(gen), float(launches), io["h2d"], io["d2h"], sum(wall)], dtype=torch.float64,
+                     device=dev)
+    if world > 1:
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms, wall_s = float(mx[0]), float(mx[5])
+        gen, launches, h2d_b, d2h_b = float(sm[1]), int(sm[2]), float(sm[3]), float(sm[4])
+    else:
+        wall_s = sum(wall)
+        h2d_b, d2h_b = float(io["h2d"]), float(io["d2h"])
+    value = gen / (ms / 1000.0)
+    e2e = gen / wall_s
+    if rank == 0:
+        s0 = stats[-1]
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": n_gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 2), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
+            "dtype": "bf16", "data": "synthetic (uniform random tokens, random-init weights, Bernoulli(0.5) rewards)",
+            "config": {"model": args.model + (f"-L{args.layers}" if args.layers else ""),
+                       "global_batch": args.instances * args.samples,
+                       "seq_len": args.prefix + 4 * (args.turn + args.role),
+                       "parallelism": f"dp{n_gpus} (rollout replica + actor per GPU)",
+                       "dag": "planner->2 solvers->verifier, prefix mounted zero-copy",
+                       "instances": args.instances, "samples": args.samples, "prefix": args.prefix,
+                       "turn": args.turn, "tokens_counted": "generated (= trained) tokens per RL step",
+                       "l2": "inputs larger than L2 (7B weights 15 GB, KV > 10 GB per step)"},
+            "clocks": clk,
+            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d_b / args.steps),
+                    "d2h_bytes_per_step": int(d2h_b / args.steps),
+                    "api": "octopus_b200.rl.trainer.RLTrainer.step"},
+            "gpu_launches": int(launches),
+            "phases_s": {"rollout": round(s0["rollout_s"], 3), "train": round(s0["train_s"], 3),
+                         "sync": round(s0["sync_s"], 4)},
+            "tree_tokens": s0.get("tree_tokens"), "flat_tokens": s0.get("flat_tokens"),
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,10 +1,10 @@
 """sm_100a kernels (CUDA tensors) with plain-PyTorch references (CPU tensors)."""
-from ._ext import available, check_status, ext
+from ._ext import add_launches, available, check_status, ext, launches
 from .core import (AttnPlan, adamw_, attention, embed, gemm, linear, logprob_head, rmsnorm, rope_, sample, sqnorm_,
                    swiglu)
 from .decode import DecodeAttention, decode_attention
 
 __all__ = [
-    "AttnPlan", "DecodeAttention", "adamw_", "attention", "available", "check_status", "decode_attention", "embed",
+    "AttnPlan", "DecodeAttention", "adamw_", "add_launches", "launches", "attention", "available", "check_status", "decode_attention", "embed",
     "ext", "gemm", "linear", "logprob_head", "rmsnorm", "rope_", "sample", "sqnorm_", "swiglu",
 ]

@@ -24,15 +24,63 @@ def _load():
     return _C
 
 
+# Kernels launched by each entry point of the extension (for launch accounting).
+KERNELS_PER_CALL = {
+    "gemm_out": 1, "head_fwd": 2, "head_grad_logits": 1, "sample_head": 2, "rmsnorm_fwd": 1, "rmsnorm_bwd": 1,
+    "rope": 1, "swiglu_fwd": 1, "swiglu_bwd": 1, "embed_fwd": 1, "embed_bwd": 1, "kv_write": 1,
+    "sqnorm_accum": 1, "adamw": 1, "attn_fwd": 1, "attn_bwd": 3, "attn_decode": 2,
+}
+LAUNCHES = {"count": 0}
+
+
+class _Counting:
+    """Proxy of the extension module that counts kernel launches per call."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self._cache = {}
+
+    def __getattr__(self, name):
+        fn = self._cache.get(name)
+        if fn is None:
+            target = getattr(self._mod, name)
+            k = KERNELS_PER_CALL.get(name, 0)
+            if not k or not callable(target):
+                return target
+
+            def fn(*a, _t=target, _k=k, **kw):
+                LAUNCHES["count"] += _k
+                return _t(*a, **kw)
+
+            self._cache[name] = fn
+        return fn
+
+
+_PROXY = None
+
+
 def ext():
-    """Return the extension module or raise a clear error."""
+    """Return the (launch-counting) extension module or raise a clear error."""
+    global _PROXY
     mod = _load()
     if mod is None:
         raise RuntimeError(
             "octopus_b200._C (the sm_100a kernels) is not built or failed to load: "
             f"{_ERR!r}. Build it with `python setup.py build_ext --inplace`."
         )
-    return mod
+    if _PROXY is None:
+        _PROXY = _Counting(mod)
+    return _PROXY
+
+
+def launches() -> int:
+    """Kernels of this extension launched from Python so far (graph replays excluded)."""
+    return LAUNCHES["count"]
+
+
+def add_launches(n: int) -> None:
+    """Account kernels launched by CUDA-graph replays of captured extension calls."""
+    LAUNCHES["count"] += int(n)
 
 
 def available() -> bool:

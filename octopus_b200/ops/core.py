@@ -66,7 +66,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
             else:
                 out.copy_(y.to(out.dtype))
             return out
-        return y.to(out_dtype if a.dtype != torch.float64 else torch.float64)
+        return y.to(a.dtype if a.dtype in (torch.float32, torch.float64) else out_dtype)
     if out is None:
         out = torch.empty(M, N, dtype=out_dtype, device=a.device)
     ext().gemm_out(a, a_mn, b, b_mn, out, alpha, residual, bias, accumulate, bn)
@@ -275,9 +275,10 @@ class AttnPlan:
         dt = tiles(nq, 64, has_q)
         kt = tiles(nk, 64, has_q)
         dev = torch.device(device)
+        from ..utils.iostats import h2d
 
         def T(a):
-            return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+            return h2d(np.ascontiguousarray(a), dev)
 
         return AttnPlan(T(cu_q), T(cu_k), T(key_idx), T(ft.reshape(-1)), T(dt.reshape(-1)), T(kt.reshape(-1)),
                         cu_q, cu_k, key_idx)

@@ -1,0 +1,164 @@
+"""Prefix-tree policy actor: micro-batch building, forward/backward, fused AdamW.
+
+`build_microbatch` turns flat sequences (with mounts, loss masks, per-token advantages
+and behaviour logprobs) into a prefix-tree micro-batch: tree tokens and K2 positions,
+the gathered-key attention plan, and per-pair (advantage, loss weight, behaviour
+logprob) obtained by summing the flat tokens that map to each (row, label) pair.
+
+`Actor` owns the flat parameter / gradient / optimizer buffers of one model replica
+and runs a training step over a list of micro-batches: one forward+backward per
+micro-batch (gradients accumulate in fp32 straight from the wgrad GEMM epilogues),
+then a device-side grad-norm and one fused AdamW kernel over the flat buffers that
+also writes the bf16 compute copy (which the colocated rollout engine reads).
+
+Reference parity: `octopus/rl/actor.py:41-351` (ChunkedHeadFSDPPPOActor: prefix-aware
+allocation, scored positions from the rolled loss mask, once-per-call sync,
+optimizer step), `octopus/rl/prefix_tree.py:424-446` (tree_inputs).
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..models.config import ModelConfig
+from ..models.decoder import FlatLayout, TreeBatch, Weights, forward_tree, init_flat
+from ..utils.iostats import h2d
+from .loss import PPOConfig, ppo_loss
+from .prefix_tree import attention_plan, build_tree
+
+
+@dataclass
+class MicroBatch:
+    """Host-side prefix-tree micro-batch."""
+
+    tokens: np.ndarray      # [Tp] int64 (padded)
+    positions: np.ndarray   # [Tp] int32
+    cu_q: np.ndarray
+    cu_k: np.ndarray
+    key_idx: np.ndarray
+    pair_row: np.ndarray
+    pair_label: np.ndarray
+    pair_adv: np.ndarray
+    pair_w: np.ndarray
+    pair_behav: np.ndarray
+    n_tree: int
+    n_flat: int
+    plan_own: tuple | None = None  # (cu_q, cu_k, key_idx) without mounted keys (layer subsets)
+
+    def to_device(self, device) -> "DeviceMicroBatch":
+        d = torch.device(device)
+        T = lambda a, dt: h2d(np.ascontiguousarray(a), d, dt)  # noqa: E731
+        batch = TreeBatch(T(self.tokens, torch.int64), T(self.positions, torch.int32),
+                          ops.AttnPlan.build(self.cu_q, self.cu_k, self.key_idx, d),
+                          T(self.pair_row, torch.int64), T(self.pair_label, torch.int64))
+        return DeviceMicroBatch(batch, T(self.pair_adv, torch.float32), T(self.pair_w, torch.float32),
+                                T(self.pair_behav, torch.float32))
+
+
+@dataclass
+class DeviceMicroBatch:
+    batch: TreeBatch
+    adv: torch.Tensor
+    w: torch.Tensor
+    behav: torch.Tensor
+
+
+def build_microbatch(flat: np.ndarray, cu, mounts: dict | None, loss_mask: np.ndarray, adv: np.ndarray,
+                     behav_logp: np.ndarray, pad_to: int = 128) -> MicroBatch:
+    """loss_mask/adv/behav_logp are per flat token (token p is trained when mask[p])."""
+    flat = np.asarray(flat, dtype=np.int64)
+    n = len(flat)
+    scored = np.zeros(n, dtype=bool)
+    scored[:-1] = loss_mask[1:].astype(bool)
+    tree = build_tree(flat, cu, mounts, scored)
+    plan = attention_plan(tree, True, pad_to)
+    Tp = plan.padded_tokens
+    toks = np.zeros(Tp, np.int64)
+    toks[: tree.num_tokens] = tree.tokens
+    pos = np.zeros(Tp, np.int32)
+    pos[: tree.num_tokens] = tree.positions
+    P = len(tree.pair_row)
+    sel = np.flatnonzero(tree.flat_pair >= 0)
+    pid = tree.flat_pair[sel]
+    nxt = sel + 1  # the trained token of flat position p is p + 1
+    w = np.bincount(pid, minlength=P).astype(np.float32)
+    a = np.bincount(pid, weights=adv[nxt], minlength=P).astype(np.float32)
+    b = np.bincount(pid, weights=behav_logp[nxt], minlength=P).astype(np.float32)
+    nz = np.maximum(w, 1.0)
+    return MicroBatch(toks, pos, plan.cu_q, plan.cu_k, plan.key_idx, tree.pair_row.astype(np.int64),
+                      tree.pair_label.astype(np.int64), a / nz, w, b / nz, tree.num_tokens, n)
+
+
+@dataclass
+class OptimConfig:
+    lr: float = 2e-5
+    betas: tuple = (0.9, 0.999)
+    eps: float = 1e-8
+    weight_decay: float = 0.0
+    max_grad_norm: float = 1.0
+
+
+class Actor:
+    """Single-replica actor over flat buffers (the FSDP actor shards the same layout)."""
+
+    def __init__(self, cfg: ModelConfig, device="cuda", *, optim: OptimConfig | None = None,
+                 ppo: PPOConfig | None = None, seed: int = 0, dtype=torch.bfloat16, ckpt: bool = True,
+                 temperature: float = 1.0):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.optim = optim or OptimConfig()
+        self.ppo = ppo or PPOConfig()
+        self.layout = FlatLayout(cfg)
+        self.flat16 = init_flat(cfg, self.layout, self.device, dtype=dtype, seed=seed)
+        self.master = self.flat16.float() if dtype != torch.float64 else self.flat16.clone()
+        self.grad = torch.zeros(self.layout.total, dtype=torch.float32 if dtype != torch.float64 else dtype,
+                                device=self.device)
+        self.exp_avg = torch.zeros_like(self.master)
+        self.exp_avg_sq = torch.zeros_like(self.master)
+        self.weights = Weights(cfg, self.flat16, self.layout, self.grad)
+        self.step_count = 0
+        self.ckpt = ckpt
+        self.temperature = temperature
+        self.version = 0
+
+    def zero_grad(self):
+        self.grad.zero_()
+
+    def forward_backward(self, mbs: list[MicroBatch], denom: float | None = None) -> dict:
+        denom = denom if denom is not None else float(sum(mb.pair_w.sum() for mb in mbs))
+        stats = {}
+        for mb in mbs:
+            d = mb.to_device(self.device)
+            logp, ent = forward_tree(self.weights, d.batch, self.temperature, ckpt=self.ckpt)
+            loss, st = ppo_loss(logp, ent, d.adv, d.w, d.behav, None, denom, self.ppo)
+            loss.backward()
+            for k, v in st.items():
+                stats[k] = stats.get(k, 0.0) + v.detach() * (1.0 if k == "tokens" else float(mb.pair_w.sum()))
+            stats["loss"] = stats.get("loss", 0.0) + loss.detach()
+        tok = float(sum(mb.pair_w.sum() for mb in mbs)) or 1.0
+        return {k: (v if k in ("tokens", "loss") else v / tok) for k, v in stats.items()}
+
+    def optimizer_step(self) -> torch.Tensor:
+        """Grad-norm clip + AdamW; returns the (device) squared grad norm."""
+        self.step_count += 1
+        sq = torch.zeros(1, dtype=torch.float32, device=self.device)
+        ops.sqnorm_(self.grad, sq)
+        o = self.optim
+        ops.adamw_(self.master, self.grad, self.exp_avg, self.exp_avg_sq, self.flat16, lr=o.lr, betas=o.betas,
+                   eps=o.eps, weight_decay=o.weight_decay, step=self.step_count, sqnorm=sq,
+                   max_norm=o.max_grad_norm)
+        self.version += 1
+        return sq
+
+    def train_step(self, mbs: list[MicroBatch]) -> dict:
+        t0 = time.perf_counter()
+        self.zero_grad()
+        stats = self.forward_backward(mbs)
+        sq = self.optimizer_step()
+        stats["grad_norm"] = sq.sqrt()
+        stats["train_s"] = time.perf_counter() - t0
+        return stats

@@ -1,0 +1,568 @@
+"""Rollout engine: paged (page size 1) KV with zero-copy sharing, cursors, mounts and
+CUDA-graph decode on the sm_100a kernels.
+
+Request model (the wire format of ``/generate``):
+  * ``input_ids``   new tokens to prefill (the delta after ``cursor``, or a full prompt)
+  * ``cursor``      continue from a server-resident reply (its KV is reused zero-copy)
+  * ``mount``       ``[(cursor, start, end), ...]`` splice rows [start, end) of other
+                    cursors into this request's context (zero-copy; rule K2 positions)
+Every request owns the KV slots of its new tokens and of its generated tokens; all
+other rows it attends to are slots shared by reference (radix prefix hits, cursor
+rows, mounted rows).  Refcounts in the native SlotPool free a slot exactly once.
+
+Prefill runs all requests of a batch through one ragged forward: the gathered-key
+attention kernel reads each request's key list (context slots + its own new slots)
+straight from the KV cache.  Decode runs one captured CUDA graph per batch bucket:
+embedding -> 28x(norm, QKV GEMM + bias, RoPE, KV write, split-K paged attention,
+O GEMM + residual, norm, gate/up GEMM, SwiGLU, down GEMM + residual) -> fused
+sampling head (GEMM + Gumbel-max + logprob epilogue), with positions, KV lengths and
+RNG streams advanced on the device, so a decode step needs no host work.
+
+Reference parity: `octopus/serving/kv_mount.py:87-296` (prepare: tokens(B) +
+placeholders + delta, K2 offsets, rebuild/abort semantics), `kv_mount.py:347-383`
+(resolve: append mounted segment pages after B's prefix), `kv_mount.py:585-634`
+(layer-subset views, position offsets), SGLang's scheduler/radix cache (prefix reuse).
+"""
+from __future__ import annotations
+
+import itertools
+import os
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..ops import serve as sv
+from ..models.config import ModelConfig
+from ..models.decoder import Weights
+from ..utils.iostats import d2h, h2d
+from .cursor_store import PLACEHOLDER, Cursor, CursorStore
+
+try:
+    from .. import _native
+except ImportError:  # pragma: no cover - native module not built
+    _native = None
+
+NULL_SLOT = 0  # reserved scratch slot for padding rows
+
+
+class CursorNotFound(KeyError):
+    pass
+
+
+class OutOfKV(RuntimeError):
+    pass
+
+
+def mount_layers_from_env(n_layers: int):
+    v = os.environ.get("OCTOPUS_MOUNT_LAYERS", "").strip()
+    if not v:
+        return None
+    return sorted({int(x) for x in v.replace(" ", "").split(",") if x != ""} & set(range(n_layers)))
+
+
+@dataclass
+class GenInput:
+    input_ids: list
+    cursor: str | None = None
+    mount: list = field(default_factory=list)  # [(cursor_id, start, end)]
+    max_new_tokens: int = 128
+    temperature: float = 1.0
+    stop_ids: tuple = ()
+    rid: int | None = None
+    keep_cursor: bool = True
+    cursor_id: str | None = None  # id to store the reply under (default: generated)
+    prefill_only: bool = False
+
+
+@dataclass
+class GenOutput:
+    output_ids: list
+    output_logprobs: list
+    cursor: str | None
+    prompt_tokens: int          # rows prefilled by this request (placeholders excluded)
+    cached_tokens: int          # rows reused from cache/cursor
+    first_pos: int
+    finish_reason: str = "length"
+
+
+@dataclass
+class _Req:
+    inp: GenInput
+    rid: int
+    ctx_tokens: np.ndarray
+    ctx_slots: np.ndarray
+    ctx_pos: np.ndarray
+    ctx_mounted: np.ndarray
+    new_tokens: np.ndarray
+    first_pos: int
+    own_slots: np.ndarray = None
+    cached: int = 0
+    radix_handle: int = -1
+    out_tok: list = field(default_factory=list)
+    out_lp: list = field(default_factory=list)
+
+
+class Engine:
+    def __init__(self, cfg: ModelConfig, weights: Weights, *, kv_slots: int | None = None,
+                 kv_bytes: int | None = None, max_batch: int = 256, device="cuda", use_graphs: bool = True,
+                 seed: int = 1234, prefill_chunk: int = 16384, num_splits: int | None = None,
+                 mount_layers=None, kv_index_capacity: int = 1 << 25):
+        if _native is None:
+            raise RuntimeError("octopus_b200._native (KV manager) is not built")
+        self.cfg, self.w = cfg, weights
+        self.device = torch.device(device)
+        kvw = cfg.kv_width
+        if kv_slots is None:
+            per = 2 * cfg.layers * kvw * 2
+            kv_slots = max(4096, int((kv_bytes or (8 << 30)) // per))
+        self.kv_slots = kv_slots
+        kv_dtype = weights.flat.dtype
+        self.kc = torch.zeros(cfg.layers, kv_slots, kvw, dtype=kv_dtype, device=self.device)
+        self.vc = torch.zeros(cfg.layers, kv_slots, kvw, dtype=kv_dtype, device=self.device)
+        self.pool = _native.SlotPool(kv_slots)
+        self.null_slot = int(self.pool.alloc(1)[0])  # never freed: padding rows read/write it
+        self.radix = _native.RadixCache(self.pool)
+        self.cursors = CursorStore(self.pool)
+        self.max_batch = max_batch
+        self.seed = seed
+        self.use_graphs = use_graphs and self.device.type == "cuda"
+        self.prefill_chunk = prefill_chunk
+        self.mount_layers = mount_layers if mount_layers is not None else mount_layers_from_env(cfg.layers)
+        self.version = 0
+        self._rid = itertools.count(1)
+        self._cid = itertools.count(1)
+        splits = num_splits or 8
+        self.dec_attn = ops.DecodeAttention(cfg.heads, cfg.kv_heads, cfg.head_dim, max_batch, splits, self.device)
+        # static decode buffers (graph inputs)
+        B = max_batch
+        dev = self.device
+        self.s_tok = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.s_pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.s_start = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.s_len = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.s_start_own = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.s_len_own = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.s_stream = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.s_step = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.kv_index_capacity = kv_index_capacity
+        self.kv_indices = torch.zeros(kv_index_capacity, dtype=torch.int32, device=dev)
+        self.kv_indices_own = torch.zeros(kv_index_capacity if self.mount_layers is not None else 1,
+                                          dtype=torch.int32, device=dev)
+        self.max_steps = 0
+        self.s_out_tok = None
+        self.s_out_lp = None
+        self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._graph_kernels: dict = {}
+        self._graph_pool = None
+        self._graph_steps = 0
+        self.stats = {"prefill_tokens": 0, "cached_tokens": 0, "decode_steps": 0, "requests": 0,
+                      "prefill_s": 0.0, "decode_s": 0.0}
+
+    # ------------------------------------------------------------------ helpers
+    def new_cursor_id(self) -> str:
+        return f"c{next(self._cid)}"
+
+    def _alloc(self, n: int) -> np.ndarray:
+        if n == 0:
+            return np.empty(0, np.int64)
+        s = self.pool.alloc(n)
+        if len(s) < n:
+            self.radix.evict(n - self.pool.free_count() + 1024)
+            s = self.pool.alloc(n)
+            if len(s) < n:
+                raise OutOfKV(f"KV pool exhausted: need {n}, free {self.pool.free_count()}")
+        return np.asarray(s, dtype=np.int64)
+
+    def bump_version(self) -> int:
+        """New weight version: cached KV of older versions is no longer matched."""
+        self.version += 1
+        return self.version
+
+    # ------------------------------------------------------------------ request setup
+    def _resolve(self, inp: GenInput) -> _Req:
+        rid = inp.rid if inp.rid is not None else next(self._rid)
+        new = np.asarray(inp.input_ids, dtype=np.int32)
+        ctx_t, ctx_s, ctx_p, ctx_m = [], [], [], []
+        next_pos = 0
+        cached = 0
+        handle = -1
+        if inp.cursor is not None:
+            cur = self.cursors.get(inp.cursor)
+            if cur is None:
+                raise CursorNotFound(inp.cursor)
+            # rows without KV (a template terminator appended at put) are re-prefilled
+            has_kv = cur.slots >= 0
+            ok = int(np.argmin(has_kv)) if not has_kv.all() else cur.length
+            ctx_t.append(cur.tokens[:ok])
+            ctx_s.append(cur.slots[:ok])
+            ctx_p.append(cur.positions[:ok])
+            ctx_m.append(cur.mounted[:ok])
+            if ok < cur.length:
+                new = np.concatenate([cur.tokens[ok:], new])
+            next_pos = int(cur.positions[ok - 1]) + 1 if ok else 0
+            cached = ok
+        elif len(new) > 1:
+            ln, slots, handle = self.radix.match(self.version, new[:-1])
+            ln = int(ln)
+            if ln > 0:
+                ctx_t.append(new[:ln])
+                ctx_s.append(np.asarray(slots, np.int64))
+                ctx_p.append(np.arange(ln, dtype=np.int64))
+                ctx_m.append(np.zeros(ln, dtype=bool))
+                new = new[ln:]
+                next_pos = ln
+                cached = ln
+                self.radix.lock(handle)
+            else:
+                self.radix.release_handle(handle)
+                handle = -1
+        # mounts: splice rows of other cursors (K2: next = max(own next, last mounted + 1))
+        for (src, a, b) in inp.mount:
+            sc = self.cursors.get(src)
+            if sc is None:
+                raise CursorNotFound(src)
+            a, b = int(a), int(b)
+            if not (0 <= a < b <= sc.length) or (sc.slots[a:b] < 0).any():
+                raise ValueError(f"mount range [{a}, {b}) invalid for cursor {src} of length {sc.length}")
+            ctx_t.append(np.full(b - a, PLACEHOLDER, np.int32))
+            ctx_s.append(sc.slots[a:b])
+            ctx_p.append(sc.positions[a:b])
+            ctx_m.append(np.ones(b - a, dtype=bool))
+            next_pos = max(next_pos, int(sc.positions[b - 1]) + 1)
+        cat = (lambda xs, dt: np.concatenate(xs).astype(dt) if xs else np.empty(0, dt))
+        r = _Req(inp, rid, cat(ctx_t, np.int32), cat(ctx_s, np.int64), cat(ctx_p, np.int64), cat(ctx_m, bool), new,
+                 next_pos, cached=cached, radix_handle=handle)
+        if len(new) == 0:
+            raise ValueError("request has no new tokens to prefill")
+        return r
+
+    # ------------------------------------------------------------------ forward pieces
+    def _layer(self, x, i, pos, write_slots, attn):
+        cfg, w = self.cfg, self.w
+        ln1, qkv_w, qkv_b, o_w, ln2, gu_w, down_w = w.layer(i)
+        h = sv.rms(x, ln1, cfg.rms_eps, cfg.norm_plus_one)
+        qkv = ops.gemm(h, qkv_w, bias=qkv_b).to(x.dtype)
+        sv.rope_(qkv, pos, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.rope_theta)
+        sv.kv_write(qkv, cfg.heads, cfg.kv_heads, cfg.head_dim, write_slots, self.kc[i], self.vc[i])
+        o = attn(qkv[:, : cfg.q_width], i)
+        x = ops.gemm(o, o_w, residual=x).to(x.dtype)
+        h2 = sv.rms(x, ln2, cfg.rms_eps, cfg.norm_plus_one)
+        gu = ops.gemm(h2, gu_w).to(x.dtype)
+        act = sv.swiglu(gu)
+        return ops.gemm(act, down_w, residual=x).to(x.dtype)
+
+    def _final(self, x):
+        return sv.rms(x, self.w["norm"], self.cfg.rms_eps, self.cfg.norm_plus_one)
+
+    # ------------------------------------------------------------------ prefill
+    def _prefill(self, reqs: list[_Req], temperature: float):
+        """Ragged forward of all new tokens; returns first sampled (tokens, logprobs)."""
+        cfg = self.cfg
+        dev = self.device
+        first_tok = np.zeros(len(reqs), np.int64)
+        first_lp = np.zeros(len(reqs), np.float32)
+        # chunk requests so one forward holds <= prefill_chunk tokens
+        groups, cur, cur_n = [], [], 0
+        for j, r in enumerate(reqs):
+            n = len(r.new_tokens)
+            if cur and cur_n + n > self.prefill_chunk:
+                groups.append(cur)
+                cur, cur_n = [], 0
+            cur.append(j)
+            cur_n += n
+        if cur:
+            groups.append(cur)
+        for g in groups:
+            ids, pos, slots, cu_q, cu_k, keys, cu_k_own, keys_own, last = [], [], [], [0], [0], [], [0], [], []
+            for j in g:
+                r = reqs[j]
+                n = len(r.new_tokens)
+                ids.append(r.new_tokens)
+                pos.append(np.arange(r.first_pos, r.first_pos + n))
+                own = r.own_slots[:n]
+                slots.append(own)
+                kk = np.concatenate([r.ctx_slots, own])
+                keys.append(kk)
+                cu_q.append(cu_q[-1] + n)
+                cu_k.append(cu_k[-1] + len(kk))
+                if self.mount_layers is not None:
+                    ko = np.concatenate([r.ctx_slots[~r.ctx_mounted], own])
+                    keys_own.append(ko)
+                    cu_k_own.append(cu_k_own[-1] + len(ko))
+                last.append(cu_q[-1] - 1)
+            T = cu_q[-1]
+            pad = (-T) % 8
+            if pad:
+                ids.append(np.zeros(pad, np.int32))
+                pos.append(np.zeros(pad, np.int64))
+                slots.append(np.full(pad, self.null_slot, np.int64))
+                keys.append(np.full(pad, self.null_slot, np.int64))
+                cu_q.append(cu_q[-1] + pad)
+                cu_k.append(cu_k[-1] + pad)
+                if self.mount_layers is not None:
+                    keys_own.append(np.full(pad, self.null_slot, np.int64))
+                    cu_k_own.append(cu_k_own[-1] + pad)
+            t_ids = h2d(np.concatenate(ids).astype(np.int64), dev)
+            t_pos = h2d(np.concatenate(pos).astype(np.int32), dev)
+            t_slots = h2d(np.concatenate(slots).astype(np.int64), dev)
+            plan = ops.AttnPlan.build(cu_q, cu_k, np.concatenate(keys).astype(np.int32), dev)
+            plan_own = plan if self.mount_layers is None else ops.AttnPlan.build(
+                cu_q, cu_k_own, np.concatenate(keys_own).astype(np.int32), dev)
+            mset = set(self.mount_layers or [])
+            scale = cfg.head_dim ** -0.5
+
+            def attn(q, i):
+                p = plan if (self.mount_layers is None or i in mset) else plan_own
+                return sv.prefill_attn(q, self.kc[i], self.vc[i], p, cfg.heads, cfg.kv_heads, cfg.head_dim, scale)
+
+            x = sv.embed(t_ids, self.w["embed"])
+            for i in range(cfg.layers):
+                x = self._layer(x, i, t_pos, t_slots, attn)
+            rows = h2d(np.asarray(last, np.int64), dev)
+            h = self._final(x.index_select(0, rows))
+            streams = h2d(np.asarray([(reqs[j].rid << 32) | (reqs[j].first_pos + len(reqs[j].new_tokens))
+                                      for j in g], np.int64), dev)
+            tok, lp = ops.sample(h, self.w.head, temperature, self.seed, streams, cfg.vocab_size)
+            tok, lp = d2h(tok).numpy(), d2h(lp).numpy()
+            for k, j in enumerate(g):
+                first_tok[j] = tok[k]
+                first_lp[j] = lp[k]
+            self.stats["prefill_tokens"] += T
+        return first_tok, first_lp
+
+    # ------------------------------------------------------------------ decode
+    def _decode_step(self, B: int, temperature: float):
+        cfg = self.cfg
+        tok = self.s_tok[:B]
+        pos = self.s_pos[:B]
+        start = self.s_start[:B]
+        ln = self.s_len[:B]
+        slot = self.kv_indices.index_select(0, (start + ln).long()).long()
+        att_len = ln + 1
+        mset = set(self.mount_layers or [])
+        if self.mount_layers is not None:
+            start_o = self.s_start_own[:B]
+            len_o = self.s_len_own[:B] + 1
+
+        def attn(q, i):
+            if self.mount_layers is None or i in mset:
+                return self.dec_attn(q, self.kc[i], self.vc[i], start, self.kv_indices, kv_len=att_len)
+            return self.dec_attn(q, self.kc[i], self.vc[i], start_o, self.kv_indices_own, kv_len=len_o)
+
+        x = sv.embed(tok, self.w["embed"])
+        for i in range(cfg.layers):
+            x = self._layer(x, i, pos, slot, attn)
+        h = self._final(x)
+        new_tok, lp = ops.sample(h, self.w.head, temperature, self.seed, self.s_stream[:B], cfg.vocab_size)
+        step = self.s_step.expand(B)[:, None]
+        self.s_out_tok[:B].scatter_(1, step, new_tok[:, None])
+        self.s_out_lp[:B].scatter_(1, step, lp[:, None])
+        self.s_tok[:B].copy_(new_tok)
+        self.s_pos[:B].add_(1)
+        self.s_len[:B].add_(1)
+        if self.mount_layers is not None:
+            self.s_len_own[:B].add_(1)
+        self.s_stream[:B].add_(1)
+        self.s_step.add_(1)
+
+    def _bucket(self, n: int) -> int:
+        b = 8
+        while b < n:
+            b *= 2
+        return min(b, self.max_batch)
+
+    def _ensure_out(self, steps: int):
+        if self.s_out_tok is None or self.s_out_tok.shape[1] < steps:
+            # (re)allocating invalidates captured graphs
+            self.s_out_tok = torch.zeros(self.max_batch, steps, dtype=torch.int64, device=self.device)
+            self.s_out_lp = torch.zeros(self.max_batch, steps, dtype=torch.float32, device=self.device)
+            self._graphs.clear()
+
+    def _graph(self, B: int, temperature: float):
+        key = (B, float(temperature))
+        g = self._graphs.get(key)
+        if g is not None:
+            return g
+        # warm up on a side stream, then capture
+        saved = [t.clone() for t in (self.s_tok, self.s_pos, self.s_len, self.s_len_own, self.s_stream,
+                                     self.s_step)]
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._decode_step(B, temperature)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        for t, v in zip((self.s_tok, self.s_pos, self.s_len, self.s_len_own, self.s_stream, self.s_step), saved):
+            t.copy_(v)
+        if self._graph_pool is None:
+            self._graph_pool = torch.cuda.graph_pool_handle()
+        g = torch.cuda.CUDAGraph()
+        n0 = ops.launches()
+        with torch.cuda.graph(g, pool=self._graph_pool):
+            self._decode_step(B, temperature)
+        self._graph_kernels[key] = ops.launches() - n0
+        for t, v in zip((self.s_tok, self.s_pos, self.s_len, self.s_len_own, self.s_stream, self.s_step), saved):
+            t.copy_(v)
+        self._graphs[key] = g
+        return g
+
+    def _decode(self, reqs: list[_Req], first_tok, steps: int, temperature: float):
+        """Run `steps` decode steps for all requests (batched in buckets of max_batch)."""
+        if steps <= 0:
+            return np.zeros((len(reqs), 0), np.int64), np.zeros((len(reqs), 0), np.float32)
+        out_t = np.zeros((len(reqs), steps), np.int64)
+        out_l = np.zeros((len(reqs), steps), np.float32)
+        self._ensure_out(steps)
+        for b0 in range(0, len(reqs), self.max_batch):
+            chunk = list(range(b0, min(len(reqs), b0 + self.max_batch)))
+            n = len(chunk)
+            B = self._bucket(n)
+            # lay out kv index regions: [ctx slots | own slots (new + generated)]
+            regions, off = [], 0
+            starts = np.zeros(B, np.int32)
+            lens = np.zeros(B, np.int32)
+            starts_o = np.zeros(B, np.int32)
+            lens_o = np.zeros(B, np.int32)
+            regions_o, off_o = [], 0
+            for k, j in enumerate(chunk):
+                r = reqs[j]
+                full = np.concatenate([r.ctx_slots, r.own_slots])
+                regions.append(full)
+                starts[k] = off
+                lens[k] = len(r.ctx_slots) + len(r.new_tokens)
+                off += len(full)
+                if self.mount_layers is not None:
+                    fo = np.concatenate([r.ctx_slots[~r.ctx_mounted], r.own_slots])
+                    regions_o.append(fo)
+                    starts_o[k] = off_o
+                    lens_o[k] = int((~r.ctx_mounted).sum()) + len(r.new_tokens)
+                    off_o += len(fo)
+            # padding rows: a region of one null slot each
+            for k in range(n, B):
+                regions.append(np.full(1 + steps, self.null_slot, np.int64))
+                starts[k] = off
+                lens[k] = 0
+                off += 1 + steps
+                if self.mount_layers is not None:
+                    regions_o.append(np.full(1 + steps, self.null_slot, np.int64))
+                    starts_o[k] = off_o
+                    off_o += 1 + steps
+            if off > self.kv_index_capacity:
+                raise OutOfKV("kv index capacity exceeded; lower the batch or raise kv_index_capacity")
+            dev = self.device
+            self.kv_indices[:off].copy_(h2d(np.concatenate(regions).astype(np.int32), dev))
+            if self.mount_layers is not None:
+                self.kv_indices_own[:off_o].copy_(h2d(np.concatenate(regions_o).astype(np.int32), dev))
+                self.s_start_own[:B].copy_(h2d(starts_o, dev))
+                self.s_len_own[:B].copy_(h2d(lens_o, dev))
+            tok = np.zeros(B, np.int64)
+            pos = np.zeros(B, np.int32)
+            stream = np.zeros(B, np.int64)
+            for k, j in enumerate(chunk):
+                r = reqs[j]
+                tok[k] = first_tok[j]
+                p = r.first_pos + len(r.new_tokens)
+                pos[k] = p
+                stream[k] = (r.rid << 32) | (p + 1)
+            self.s_tok[:B].copy_(h2d(tok, dev))
+            self.s_pos[:B].copy_(h2d(pos, dev))
+            self.s_start[:B].copy_(h2d(starts, dev))
+            self.s_len[:B].copy_(h2d(lens, dev))
+            self.s_stream[:B].copy_(h2d(stream, dev))
+            self.s_step.zero_()
+            if self.use_graphs:
+                g = self._graph(B, temperature)
+                for _ in range(steps):
+                    g.replay()
+                ops.add_launches(self._graph_kernels[(B, float(temperature))] * steps)
+            else:
+                for _ in range(steps):
+                    self._decode_step(B, temperature)
+            ot = d2h(self.s_out_tok[:n, :steps]).numpy()
+            ol = d2h(self.s_out_lp[:n, :steps]).numpy()
+            out_t[b0:b0 + n] = ot
+            out_l[b0:b0 + n] = ol
+            self.stats["decode_steps"] += steps
+        return out_t, out_l
+
+    # ------------------------------------------------------------------ public API
+    @torch.no_grad()
+    def generate(self, inputs: list[GenInput]) -> list[GenOutput]:
+        """Prefill + decode a batch of requests (all share the batch temperature)."""
+        if not inputs:
+            return []
+        temperature = inputs[0].temperature
+        reqs = [self._resolve(inp) for inp in inputs]
+        for r in reqs:
+            r.own_slots = self._alloc(len(r.new_tokens) + (0 if r.inp.prefill_only else r.inp.max_new_tokens))
+        t0 = time.perf_counter()
+        first_tok, first_lp = self._prefill(reqs, temperature)
+        t1 = time.perf_counter()
+        self.stats["prefill_s"] += t1 - t0
+        max_new = max((0 if r.inp.prefill_only else r.inp.max_new_tokens) for r in reqs)
+        out_t, out_l = self._decode(reqs, first_tok, max_new - 1, temperature)
+        self.stats["decode_s"] += time.perf_counter() - t1
+        outs = []
+        for j, r in enumerate(reqs):
+            n_new = len(r.new_tokens)
+            mx = 0 if r.inp.prefill_only else r.inp.max_new_tokens
+            toks = ([int(first_tok[j])] + [int(x) for x in out_t[j]])[:mx]
+            lps = ([float(first_lp[j])] + [float(x) for x in out_l[j]])[:mx]
+            reason = "length"
+            if r.inp.stop_ids:
+                for k, t in enumerate(toks):
+                    if t in r.inp.stop_ids:
+                        toks, lps, reason = toks[:k + 1], lps[:k + 1], "stop"
+                        break
+            # generated rows with KV: all but the last sampled token (its KV is not written)
+            n_kv_gen = max(0, len(toks) - 1)
+            used = n_new + n_kv_gen
+            cid = None
+            if r.inp.keep_cursor:
+                cid = r.inp.cursor_id or self.new_cursor_id()
+                gen_pos = np.arange(r.first_pos + n_new, r.first_pos + n_new + len(toks))
+                slots = np.concatenate([r.ctx_slots, r.own_slots[:used], np.full(len(toks) - n_kv_gen, -1, np.int64)])
+                cur = Cursor(cid, np.concatenate([r.ctx_tokens, r.new_tokens, np.asarray(toks, np.int32)]), slots,
+                             np.concatenate([r.ctx_pos, np.arange(r.first_pos, r.first_pos + n_new), gen_pos]),
+                             prompt_len=len(r.ctx_tokens) + n_new,
+                             mounted=np.concatenate([r.ctx_mounted, np.zeros(n_new + len(toks), bool)]),
+                             version=self.version)
+                held = cur.slots[cur.slots >= 0]
+                self.cursors.put(Cursor(cid, cur.tokens, cur.slots, cur.positions, cur.prompt_len, cur.mounted,
+                                        cur.version), take_ref=False)
+                # the store's reference: ctx slots are borrowed (incref); own used slots transfer ownership
+                if len(r.ctx_slots):
+                    self.pool.incref(r.ctx_slots)
+                del held
+            if r.inp.cursor is None and not r.inp.mount and len(r.new_tokens):
+                full = np.concatenate([r.ctx_tokens, r.new_tokens]).astype(np.int32)
+                sl = np.concatenate([r.ctx_slots, r.own_slots[:n_new]]).astype(np.int64)
+                self.radix.insert(self.version, full, sl)
+            # release what this request owns and did not hand to a cursor
+            if not r.inp.keep_cursor:
+                self.pool.decref(r.own_slots)
+            elif len(r.own_slots) > used:
+                self.pool.decref(r.own_slots[used:])
+            if r.radix_handle >= 0:
+                self.radix.unlock(r.radix_handle)
+                self.radix.release_handle(r.radix_handle)
+            self.stats["cached_tokens"] += r.cached
+            self.stats["requests"] += 1
+            outs.append(GenOutput(toks, lps, cid, n_new, r.cached, r.first_pos, reason))
+        return outs
+
+    def release_cursor(self, cid: str):
+        self.cursors.pop(cid)
+
+    def reset(self):
+        """Drop every cursor and cached prefix (KV memory returns to the pool)."""
+        self.cursors.clear()
+        self.radix.evict(1 << 62)
+
+    def load_stats(self) -> dict:
+        used = self.pool.used_count()
+        return {"token_usage": used / self.kv_slots, "num_used_slots": used, "free_slots": self.pool.free_count(),
+                "cursors": len(self.cursors), "cached_tokens": self.radix.cached_tokens(), **self.stats}
