@@ -43,10 +43,12 @@ __device__ __forceinline__ uint32_t row_key(uint64_t seed, uint64_t stream) {
   return static_cast<uint32_t>(splitmix64(seed ^ splitmix64(stream)) >> 32);
 }
 
-// Uniform in (0, 1) from (row key, column): 24 high bits, offset by half an ulp.
+// Uniform strictly inside (0, 1) from (row key, column): 23 high bits plus half a step,
+// so u is in [2^-24, 1 - 2^-24], both exactly representable in fp32 (a 24-bit
+// variate plus half a step would round its top value to exactly 1.0).
 __device__ __forceinline__ float hash_uniform(uint32_t key, uint32_t col) {
   const uint32_t h = lowbias32(key ^ (col * 0x9E3779B9u));
-  return (static_cast<float>(h >> 8) + 0.5f) * (1.0f / 16777216.0f);
+  return (static_cast<float>(h >> 9) + 0.5f) * (1.0f / 8388608.0f);
 }
 
 // Standard Gumbel noise -log(-log u) (fast log intrinsics; sampling-grade accuracy).

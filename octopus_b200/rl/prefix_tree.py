@@ -212,11 +212,12 @@ def build_tree(flat: np.ndarray, cu, mounts: dict | None = None, scored: np.ndar
     rows = f2t[has_next]
     labels = np.append(flat[1:], 0)[has_next].astype(np.int64)
     if rows.size:
-        packed = rows.astype(np.int64) * (int(labels.max()) + 1) + labels
+        lo = min(int(labels.min()), 0)  # labels are token ids (>= 0); guard negative ids anyway
+        base = int(labels.max()) - lo + 1
+        packed = rows.astype(np.int64) * base + (labels - lo)
         uniq, inv = np.unique(packed, return_inverse=True)
-        base = int(labels.max()) + 1
         tree.pair_row = uniq // base
-        tree.pair_label = uniq % base
+        tree.pair_label = uniq % base + lo
         tree.flat_pair[has_next] = inv
     return tree
 

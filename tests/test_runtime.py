@@ -1,0 +1,150 @@
+"""Agent DAG runtime with a scripted fake chat model (no network, no GPU)."""
+import asyncio
+import json
+
+import pytest
+
+from octopus_b200.runtime import core
+from octopus_b200.runtime.tree import CursorRuntime, WorkspaceProvider, run_episode
+
+
+def call(name, **args):
+    return {"id": f"c-{name}", "type": "function", "function": {"name": name, "arguments": json.dumps(args)}}
+
+
+class Scripted:
+    """Replies per session id from scripts: each entry a (content, [tool calls])."""
+
+    def __init__(self, scripts):
+        self.scripts = {k: list(v) for k, v in scripts.items()}
+        self.bodies = []
+        self.n = 0
+
+    def __call__(self, body):
+        self.bodies.append(body)
+        sid = body["session_id"]
+        key = next(k for k in self.scripts if sid.endswith(k))
+        content, calls = self.scripts[key].pop(0)
+        self.n += 1
+        prompt = sum(len(str(m.get("content", ""))) for m in body["messages"]) // 4 + 10
+        return {"id": f"r{self.n}", "cursor": f"r{self.n}",
+                "choices": [{"message": {"role": "assistant", "content": content, "tool_calls": calls or None}}],
+                "usage": {"prompt_tokens": prompt, "completion_tokens": 20}}
+
+
+def test_fork_join_done(tmp_path):
+    chat = Scripted({
+        "ep": [("plan", [call("fork", tasks=["look left", "look right"])]), ("final", [call("done", answer="42")])],
+        "branch-0": [("ok", [call("commit", branch_id="branch-0", summary="left is clear")])],
+        "branch-1": [("ok", [call("commit", branch_id="branch-1", summary="right has 42")])],
+    })
+    out = run_episode(WorkspaceProvider(), chat, "find the number", log_dir=str(tmp_path))
+    tree = out["tree"]
+    assert tree["main_end"] == "done" and tree["answer"] == "42"
+    (fork,) = tree["forks"]
+    assert [b["branch_id"] for b in fork["branches"]] == ["branch-0", "branch-1"]
+    assert [b["summary"] for b in fork["branches"]] == ["left is clear", "right has 42"]
+    threads = [r["thread"] for r in out["requests"]]
+    assert threads.count("main") == 2 and "fork0/branch-0" in threads and "fork0/branch-1" in threads
+    # the join note reached main's next request
+    last_main = [b for b in chat.bodies if b["session_id"] == "ep"][-1]
+    assert any("right has 42" in str(m.get("content")) for m in last_main["messages"])
+    assert (tmp_path / "tree.json").exists() and (tmp_path / "requests.jsonl").exists()
+
+
+def test_fork_alone_and_remind_once():
+    chat = Scripted({
+        "ep": [("thinking...", []),  # no tool call: reminded once
+               ("both", [call("fork", tasks=["a", "b"]), call("done", answer="x")]),  # done refused
+               ("end", [call("done", answer="y")])],
+        "branch-0": [("", [call("abort", branch_id="branch-0")])],
+        "branch-1": [("", [call("abort", branch_id="branch-1")])],
+    })
+    out = run_episode(WorkspaceProvider(), chat, "t")
+    steps = out["main"]["steps"]
+    assert out["main"]["reminded"] == 1
+    refused = [s for s in steps if s.get("name") == "done" and s.get("rejected")]
+    assert refused and core.FORK_ALONE.format("done") == refused[0]["observed"]
+    assert out["tree"]["answer"] == "y"
+
+
+def test_main_call_cap_and_commit_in_main():
+    chat = Scripted({"ep": [("", [call("commit", branch_id="x", summary="s")])] * 5})
+    out = run_episode(WorkspaceProvider(), chat, "t", max_main_calls=3)
+    assert out["tree"]["main_end"] == "step cap"
+    assert all("no effect in the main thread" in s["observed"] for s in out["main"]["steps"])
+
+
+def test_fork_depth_limit(monkeypatch):
+    monkeypatch.setenv("OCTOPUS_FORK_DEPTH", "1")
+    chat = Scripted({
+        "ep": [("", [call("fork", tasks=["a", "b"])]), ("", [call("done", answer="z")])],
+        "branch-0": [("", [call("fork", tasks=["c", "d"])]), ("", [call("commit", branch_id="branch-0", summary="s")])],
+        "branch-1": [("", [call("commit", branch_id="branch-1", summary="s")])],
+    })
+    out = run_episode(WorkspaceProvider(), chat, "t")
+    b0 = out["tree"]["forks"][0]["branches"][0]
+    assert b0["ended_with"] == "commit"
+    assert any(r["thread"] == "fork0/branch-0" for r in out["requests"])
+
+
+def test_cursor_mode_sends_only_delta(monkeypatch):
+    monkeypatch.setenv("OCTOPUS_CURSOR", "1")
+    chat = Scripted({"ep": [("", [call("fork", tasks=["a", "b"])]), ("", [call("done", answer="q")])],
+                     "branch-0": [("", [call("commit", branch_id="branch-0", summary="s0")])],
+                     "branch-1": [("", [call("commit", branch_id="branch-1", summary="s1")])]})
+    run_episode(WorkspaceProvider(), chat, "t")
+    mains = [b for b in chat.bodies if b["session_id"] == "ep"]
+    assert "cursor" not in mains[0] and mains[1]["cursor"] == "r1"
+    assert mains[1]["messages"][0]["role"] == "tool"  # only the delta after the cursor
+
+
+def test_read_thread_mounts_other_thread(monkeypatch):
+    monkeypatch.setenv("OCTOPUS_READ_TOOL", "1")
+    chat = Scripted({
+        "ep": [("", [call("fork", tasks=["a", "b"])]), ("", [call("done", answer="q")])],
+        "branch-0": [("", [call("commit", branch_id="branch-0", summary="s0")])],
+        "branch-1": [("", [call("read_thread", thread="branch-0")]),
+                     ("", [call("commit", branch_id="branch-1", summary="s1")])],
+    })
+    run_episode(WorkspaceProvider(), chat, "t")
+    b1 = [b for b in chat.bodies if b["session_id"].endswith("branch-1")]
+    assert "mount" not in b1[0]
+    assert b1[1]["mount"] and b1[1]["mount"][0][0].startswith("r")
+
+
+def test_post_chat_retries(monkeypatch):
+    import urllib.error
+    import urllib.request
+
+    calls = {"n": 0}
+
+    class Resp:
+        status = 200
+
+        def __enter__(self):
+            return self
+
+        def __exit__(self, *a):
+            return False
+
+        def read(self):
+            return json.dumps({"id": "ok", "usage": {}}).encode()
+
+    def fake_urlopen(req, timeout=None):
+        calls["n"] += 1
+        if calls["n"] < 3:
+            raise urllib.error.HTTPError(req.full_url, 503, "busy", {}, None)
+        return Resp()
+
+    monkeypatch.setattr(urllib.request, "urlopen", fake_urlopen)
+    out = core.post_chat("http://127.0.0.1:1/v1/chat/completions", {"messages": []}, attempts=4,
+                         sleep=lambda s: None)
+    assert out["id"] == "ok" and calls["n"] == 3
+
+
+def test_fork_task_list_lenient():
+    assert core.fork_task_list('["a\\|b", "c"]') == ["a\\|b", "c"]
+    assert core.fork_task_list('["x",\n "y"] trailing') == ["x", "y"]
+    msg, _ = core.apply_runtime("fork", {"tasks": ["only one"]})
+    assert msg.startswith("fork needs at least two")
