@@ -1,0 +1,370 @@
+// Gathered-key attention forward on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Same contract as attn_fwd in attention.cu (tree nodes / paged prefill: query rows of
+// a sequence attend to a gathered key list, bottom-right causal, GQA), head_dim 128.
+//
+// CTA = 128 query rows of one sequence and one head; 192 threads:
+//   warp 0      producer: cp.async gathers of Q (once) and of 128-key K/V tiles into a
+//               2-stage SMEM ring (128-byte swizzled K-major layout that the UMMA
+//               descriptors read directly); completion via cp.async.mbarrier.arrive
+//   warp 1      TMEM owner and single-thread MMA issuer:
+//                 S_j = Q K_j^T         tcgen05.mma kind::f16, A/B from SMEM, fp32 in TMEM
+//                 O  += P_{j-1} V_{j-1}  tcgen05.mma with A = P read from TMEM (bf16),
+//                                        B = V from SMEM (MN-major)
+//   warps 2..5  softmax: thread = query row (TMEM lane), S row loaded with tcgen05.ld,
+//               online softmax in the exp2 domain with lazy rescaling (O is rescaled in
+//               TMEM only when the running max grows by more than 2^8), P written back
+//               to TMEM as packed bf16; epilogue O / l -> bf16 rows + lse.
+// TMEM columns: S double buffer [0,256), P [256,320), O [384,512).
+// All mbarrier waits are bounded (common.cuh); on timeout the CTA records an error,
+// drains its MMAs and frees TMEM.
+#include <cuda_bf16.h>
+
+#include "attention.h"
+#include "common.cuh"
+
+namespace octo {
+
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kD = 128;
+constexpr int kHalf = 128 * 128;            // bytes of one 64-column half of a 128-row tile
+constexpr int kTileBytes = 2 * kHalf;       // 32 KB: a 128 x 128 bf16 tile
+constexpr int kStages = 2;
+constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;   // log2 units
+
+__device__ __forceinline__ uint32_t toff(int r, int c) {
+  // row r, 16-byte chunk c (0..15) of a 128 x 128 bf16 tile made of two SW128 halves
+  return static_cast<uint32_t>((c >> 3) * kHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void cp_async16z(uint32_t dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + kTileBytes;                   // kStages tiles
+  uint8_t* sV = sK + kStages * kTileBytes;           // kStages tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kStages * kTileBytes);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;                      // [kStages]
+  uint64_t* kv_empty = kv_full + kStages;            // [kStages]
+  uint64_t* s_full = kv_empty + kStages;             // [2]
+  uint64_t* s_empty = s_full + 2;                    // [2]
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* o_done = p_full + 1;
+  uint64_t* drain = o_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int seq = p.tiles[2 * blockIdx.x];
+  const int q0 = p.tiles[2 * blockIdx.x + 1];
+  const int h = blockIdx.y;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const int qbeg = p.cu_q[seq], nq = p.cu_q[seq + 1] - qbeg;
+  const int kbeg = p.cu_k[seq], nk = p.cu_k[seq + 1] - kbeg;
+  const int off = nk - nq;
+  const int mrows = min(kBM, nq - q0);
+  const int n_end = p.causal ? min(nk, q0 + mrows + off) : nk;
+  const int n_tiles = (n_end + kBN - 1) / kBN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 32);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&kv_full[s], 32);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    const __nv_bfloat16* qb = p.q + static_cast<size_t>(h) * kD;
+    const __nv_bfloat16* kb = p.k + static_cast<size_t>(kvh) * kD;
+    const __nv_bfloat16* vb = p.v + static_cast<size_t>(kvh) * kD;
+    const int32_t* kidx = p.key_idx + kbeg;
+    {
+      const uint32_t base = smem_u32(sQ);
+      for (int r = lane; r < kBM; r += 32) {
+        const bool ok = r < mrows;
+        const __nv_bfloat16* src = qb + static_cast<size_t>(qbeg + q0 + (ok ? r : 0)) * p.ldq;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) cp_async16z(base + toff(r, c), src + c * 8, ok);
+      }
+      cp_async_arrive(q_full);
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      if (lane == 0) ok = mbar_wait(&kv_empty[stage], phase ^ 1u, abort_flag, status, 500 + stage);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      const uint32_t kbase = smem_u32(sK + stage * kTileBytes);
+      const uint32_t vbase = smem_u32(sV + stage * kTileBytes);
+      for (int r = lane; r < kBN; r += 32) {
+        const int k = j * kBN + r;
+        const bool valid = k < n_end;
+        const int64_t row = valid ? static_cast<int64_t>(kidx[k]) : 0;
+        const __nv_bfloat16* ks = kb + row * p.ldk;
+        const __nv_bfloat16* vs = vb + row * p.ldk;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          cp_async16z(kbase + toff(r, c), ks + c * 8, valid);
+          cp_async16z(vbase + toff(r, c), vs + c * 8, valid);
+        }
+      }
+      cp_async_arrive(&kv_full[stage]);
+      if (++stage == kStages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_f16(kBM, kBN, false, false, true);
+      constexpr uint32_t idesc_o = umma_idesc_f16(kBM, kD, false, true, true);
+      bool ok = mbar_wait(q_full, 0, abort_flag, status, 600);
+      const uint32_t qaddr = smem_u32(sQ);
+      int stage = 0, prev_stage = 0;
+      uint32_t phase = 0;
+      bool issued = false;
+      auto issue_pv = [&](int jj, int st) {
+        // O += P_jj V_jj  (A = P from TMEM, 8 k-steps of 16 keys)
+        const uint32_t vaddr = smem_u32(sV + st * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bd = umma_smem_desc(vaddr + kk * 2048, kHalf, 1024);
+          umma_f16_ts(tmem + kColO, tmem + kColP + kk * 8, bd, idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(o_done);
+        umma_commit(&kv_empty[st]);
+      };
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int b = j & 1;
+        if (!mbar_wait(&kv_full[stage], phase, abort_flag, status, 610 + stage)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&s_empty[b], ((j >> 1) & 1) ^ 1u, abort_flag, status, 620 + b)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kaddr = smem_u32(sK + stage * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t o16 = (kk >> 2) * kHalf + (kk & 3) * 32;
+          const uint64_t ad = umma_smem_desc(qaddr + o16, 16, 1024);
+          const uint64_t bd = umma_smem_desc(kaddr + o16, 16, 1024);
+          umma_f16_ss(tmem + kColS + b * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[b]);
+        issued = true;
+        if (j > 0) {
+          if (!mbar_wait(p_full, (j - 1) & 1, abort_flag, status, 630)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(j - 1, prev_stage);
+        }
+        prev_stage = stage;
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok && n_tiles > 0) {
+        if (mbar_wait(p_full, (n_tiles - 1) & 1, abort_flag, status, 640)) {
+          tc_fence_after();
+          issue_pv(n_tiles - 1, prev_stage);
+        }
+      }
+      if (issued) {
+        umma_commit(drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0)) {
+          if (globaltimer_ns() - t0 > OCTO_WAIT_NS) break;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue (128 threads)
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;          // TMEM lane = query row in the tile
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const int qi = q0 + r;                      // sequence-relative query index
+    const int lim = p.causal ? min(n_end, qi + off + 1) : n_end;
+    const float sc = p.scale * kLog2e;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag, status, 650 + b)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lane_addr + kColS + b * 128 + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(v[i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[b]);
+      const int kbase = j * kBN;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kBN; ++i) {
+        const float x = (kbase + i < lim) ? s[i] * sc : -INFINITY;
+        s[i] = x;
+        mt = fmaxf(mt, x);
+      }
+      float alpha = 1.f;
+      if (j == 0) {
+        m = mt;
+      } else if (mt > m + kRescaleThreshold) {
+        alpha = exp2f(m - mt);
+        m = mt;
+      }
+      const float mref = m == -INFINITY ? 0.f : m;
+      float rs = 0.f;
+      uint32_t pk[kBN / 2];
+#pragma unroll
+      for (int i = 0; i < kBN / 2; ++i) {
+        const float a = exp2f(s[2 * i] - mref), bb = exp2f(s[2 * i + 1] - mref);
+        rs += a + bb;
+        pk[i] = pack_bf16x2(a, bb);
+      }
+      l = l * alpha + rs;
+      if (j > 0) {
+        // the previous P.V must be complete before P is overwritten or O is rescaled
+        if (!mbar_wait(o_done, (j - 1) & 1, abort_flag, status, 660)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < kD / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tmem + lane_addr + kColO + c * 32, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+            tmem_st_32x32b_x32(tmem + lane_addr + kColO + c * 32, v);
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = pk[c * 32 + i];
+        tmem_st_32x32b_x32(tmem + lane_addr + kColP + c * 32, v);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    // epilogue: O / l
+    if (ok && n_tiles > 0 && mbar_wait(o_done, (n_tiles - 1) & 1, abort_flag, status, 670)) {
+      tc_fence_after();
+      const bool write = r < mrows;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.o + static_cast<size_t>(qbeg + q0 + (write ? r : 0)) * p.ldo + static_cast<size_t>(h) * kD;
+#pragma unroll
+      for (int c = 0; c < kD / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lane_addr + kColO + c * 32, v);
+        tmem_wait_ld();
+        if (write) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 u;
+            u.x = pack_bf16x2(__uint_as_float(v[g * 8 + 0]) * inv, __uint_as_float(v[g * 8 + 1]) * inv);
+            u.y = pack_bf16x2(__uint_as_float(v[g * 8 + 2]) * inv, __uint_as_float(v[g * 8 + 3]) * inv);
+            u.z = pack_bf16x2(__uint_as_float(v[g * 8 + 4]) * inv, __uint_as_float(v[g * 8 + 5]) * inv);
+            u.w = pack_bf16x2(__uint_as_float(v[g * 8 + 6]) * inv, __uint_as_float(v[g * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = u;
+          }
+        }
+      }
+      if (write && p.lse != nullptr)
+        p.lse[static_cast<size_t>(h) * p.Tq + qbeg + q0 + r] = l > 0.f ? (m + log2f(l)) * kLn2 : -INFINITY;
+    } else if (n_tiles == 0 && r < mrows) {
+      __nv_bfloat16* orow = p.o + static_cast<size_t>(qbeg + q0 + r) * p.ldo + static_cast<size_t>(h) * kD;
+      for (int c = 0; c < kD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+      if (p.lse != nullptr) p.lse[static_cast<size_t>(h) * p.Tq + qbeg + q0 + r] = -INFINITY;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+int attn_fwd_tc_smem_bytes() { return (1 + 2 * kStages) * kTileBytes + 1024 + 256; }
+
+void attn_fwd_tc(const AttnParams& p, int n_tiles, int* status, cudaStream_t st) {
+  if (n_tiles == 0) return;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_fwd_tc_smem_bytes());
+    configured = true;
+  }
+  attn_fwd_tc_kernel<<<dim3(n_tiles, p.Hq), 192, attn_fwd_tc_smem_bytes(), st>>>(p, status);
+}
+
+}  // namespace octo

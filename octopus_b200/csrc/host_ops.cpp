@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "attention.h"
+#include "decode_persistent.h"
 #include "elementwise.h"
 #include "octo_api.h"
 #include "tmap.h"
@@ -357,7 +358,8 @@ void adamw_t(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v,
 // ------------------------------------------------------------------ attention
 std::vector<torch::Tensor> attn_fwd_t(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_q,
                                       torch::Tensor cu_k, torch::Tensor key_idx, torch::Tensor tiles, int64_t Hq,
-                                      int64_t Hkv, int64_t D, double scale, bool causal, bool want_lse) {
+                                      int64_t Hkv, int64_t D, double scale, bool causal, bool want_lse,
+                                      bool use_tc) {
   c10::cuda::CUDAGuard guard(q.get_device());
   CHECK_BF16(q);
   CHECK_BF16(k);
@@ -392,7 +394,12 @@ std::vector<torch::Tensor> attn_fwd_t(torch::Tensor q, torch::Tensor k, torch::T
   p.Hkv = Hkv;
   p.scale = static_cast<float>(scale);
   p.causal = causal ? 1 : 0;
-  attn_fwd(p, tiles.numel() / 2, D, cur_stream(q));
+  if (use_tc) {
+    TORCH_CHECK(D == 128, "attention: the tcgen05 forward needs head_dim 128");
+    attn_fwd_tc(p, tiles.numel() / 2, status_ptr(q.get_device()), cur_stream(q));
+  } else {
+    attn_fwd(p, tiles.numel() / 2, D, cur_stream(q));
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {o, lse};
 }
@@ -479,6 +486,49 @@ void attn_decode_t(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::T
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Persistent split-K decode (head_dim 128): grid = min(items, 2 CTAs per SM).
+void attn_decode_persistent_t(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor kv_start,
+                              torch::Tensor kv_len, torch::Tensor kv_indices, torch::Tensor o, torch::Tensor part_o,
+                              torch::Tensor part_lse, int64_t Hq, int64_t Hkv, int64_t num_splits, double scale) {
+  c10::cuda::CUDAGuard guard(q.get_device());
+  CHECK_I32(kv_start);
+  CHECK_I32(kv_len);
+  CHECK_I32(kv_indices);
+  CHECK_BF16(q);
+  CHECK_BF16(kc);
+  CHECK_BF16(vc);
+  TORCH_CHECK(Hq % Hkv == 0 && Hq / Hkv <= 16, "decode: GQA group must be <= 16");
+  TORCH_CHECK(q.stride(1) == 1 && o.stride(1) == 1 && kc.is_contiguous() && vc.is_contiguous(), "decode: layout");
+  TORCH_CHECK(kc.size(-1) == Hkv * 128, "decode_persistent: head_dim 128 only");
+  DecodePersistParams p{};
+  p.q = CBF(q);
+  p.k_cache = CBF(kc);
+  p.v_cache = CBF(vc);
+  p.o = BF(o);
+  p.kv_start = kv_start.data_ptr<int32_t>();
+  p.kv_len = kv_len.data_ptr<int32_t>();
+  p.kv_indices = kv_indices.data_ptr<int32_t>();
+  p.ldq = q.stride(0);
+  p.ldo = o.stride(0);
+  p.B = q.size(0);
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.num_splits = static_cast<int>(num_splits);
+  p.scale = static_cast<float>(scale);
+  if (num_splits > 1) {
+    TORCH_CHECK(part_o.numel() >= static_cast<int64_t>(p.B) * Hq * num_splits * 128 &&
+                    part_lse.numel() >= static_cast<int64_t>(p.B) * Hq * num_splits,
+                "decode: scratch too small");
+    p.part_o = part_o.data_ptr<float>();
+    p.part_lse = part_lse.data_ptr<float>();
+  }
+  const int items = p.B * p.Hkv * p.num_splits;
+  const int grid = std::min(items, 2 * num_sms(q.get_device()));
+  if (p.B == 0) return;
+  decode_persistent_launch(p, grid, status_ptr(q.get_device()), cur_stream(q));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace octo
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -501,7 +551,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_write", &kv_write_t);
   m.def("sqnorm_accum", &sqnorm_accum_t);
   m.def("adamw", &adamw_t);
-  m.def("attn_fwd", &attn_fwd_t);
+  m.def("attn_fwd", &attn_fwd_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu_q"), py::arg("cu_k"),
+        py::arg("key_idx"), py::arg("tiles"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"),
+        py::arg("causal"), py::arg("want_lse"), py::arg("use_tc") = false);
   m.def("attn_bwd", &attn_bwd_t);
   m.def("attn_decode", &attn_decode_t);
+  m.def("attn_decode_persistent", &attn_decode_persistent_t);
 }

@@ -28,6 +28,13 @@ from ._ext import ext
 HEAD_CHUNK = 4096  # rows per chunk in the head backward (dz is [chunk, vocab] bf16)
 
 
+def use_tc_attention(D: int) -> bool:
+    """tcgen05/TMEM attention forward for head_dim 128 (OCTO_ATTN_TC=0 selects the mma.sync kernel)."""
+    import os
+
+    return D == 128 and os.environ.get("OCTO_ATTN_TC", "1") != "0"
+
+
 def _is_cuda(t: torch.Tensor) -> bool:
     return t.is_cuda
 
@@ -300,7 +307,7 @@ class _Attention(torch.autograd.Function):
         ctx.meta = (plan, Hq, Hkv, D, scale)
         if _is_cuda(qkv):
             o, lse = ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D, scale,
-                                    True, True)
+                                    True, True, use_tc_attention(D))
         else:
             o3, lse = ref.gather_attention(q.reshape(T, Hq, D), k.reshape(T, Hkv, D), v.reshape(T, Hkv, D),
                                            plan.host_cu_q, plan.host_cu_k, torch.from_numpy(plan.host_key_idx),

@@ -20,8 +20,11 @@ from ._ext import ext
 class DecodeAttention:
     """Holds the split-K scratch for batches up to ``max_batch`` requests."""
 
-    def __init__(self, Hq: int, Hkv: int, D: int, max_batch: int, num_splits: int = 8, device="cuda"):
+    def __init__(self, Hq: int, Hkv: int, D: int, max_batch: int, num_splits: int = 8, device="cuda",
+                 persistent: bool | None = None):
         self.Hq, self.Hkv, self.D = Hq, Hkv, D
+        # the persistent producer/consumer kernel covers head_dim 128 (all BASELINE models)
+        self.persistent = (D == 128) if persistent is None else persistent
         self.num_splits = num_splits
         self.max_batch = max_batch
         dev = torch.device(device)
@@ -48,9 +51,13 @@ class DecodeAttention:
             start, length = kv_indptr, kv_len
         if q.is_cuda:
             assert B <= self.max_batch, "decode batch exceeds the scratch capacity"
-            ext().attn_decode(q, k_cache, v_cache, start.to(torch.int32).contiguous(),
-                              length.to(torch.int32).contiguous(), kv_indices, out, self.part_o, self.part_lse,
-                              self.Hq, self.Hkv, self.D, self.num_splits, scale)
+            st, ln = start.to(torch.int32).contiguous(), length.to(torch.int32).contiguous()
+            if self.persistent:
+                ext().attn_decode_persistent(q, k_cache, v_cache, st, ln, kv_indices, out, self.part_o,
+                                             self.part_lse, self.Hq, self.Hkv, self.num_splits, scale)
+            else:
+                ext().attn_decode(q, k_cache, v_cache, st, ln, kv_indices, out, self.part_o, self.part_lse,
+                                  self.Hq, self.Hkv, self.D, self.num_splits, scale)
             return out
         return decode_attention_ref(q, k_cache, v_cache, start.cpu(), kv_indices, self.Hq, self.Hkv, self.D, scale,
                                     out, length.cpu())

@@ -557,6 +557,24 @@ class Engine:
     def release_cursor(self, cid: str):
         self.cursors.pop(cid)
 
+    def extend_cursor(self, cid: str, tokens, drop_trailing=()) -> None:
+        """Append tokens without KV yet (e.g. the template's turn terminator) to a cursor,
+        after dropping trailing stop tokens that have no KV; the next continuation
+        prefills them."""
+        cur = self.cursors.get(cid)
+        if cur is None:
+            raise CursorNotFound(cid)
+        n = cur.length
+        drop = set(int(t) for t in drop_trailing)
+        while n > 0 and int(cur.tokens[n - 1]) in drop and cur.slots[n - 1] < 0:
+            n -= 1
+        add = np.asarray(list(tokens), dtype=np.int32)
+        last = int(cur.positions[n - 1]) if n else -1
+        cur.tokens = np.concatenate([cur.tokens[:n], add])
+        cur.slots = np.concatenate([cur.slots[:n], np.full(len(add), -1, np.int64)])
+        cur.positions = np.concatenate([cur.positions[:n], np.arange(last + 1, last + 1 + len(add))])
+        cur.mounted = np.concatenate([cur.mounted[:n], np.zeros(len(add), bool)])
+
     def reset(self):
         """Drop every cursor and cached prefix (KV memory returns to the pool)."""
         self.cursors.clear()

@@ -1,0 +1,187 @@
+"""HTTP serving front-end of the rollout engine (FastAPI).
+
+Endpoints (wire format shared with the reference's patched SGLang):
+  POST /generate               {input_ids, cursor?, mount?, sampling_params{max_new_tokens, temperature},
+                                rid?} -> {output_ids, meta_info{id, cursor, prompt_tokens, cached_tokens,
+                                completion_tokens, output_token_logprobs}}
+  POST /v1/chat/completions    OpenAI chat body + optional ``cursor`` (send only the messages
+                                after that reply) and ``mount`` ([{cursor, start, end}]) -> chat
+                                completion with ``cursor`` (the reply's id) and tool_calls parsed
+  GET  /v1/loads               token usage and queue of this server (router admission)
+  GET  /get_server_info        model and mount capabilities (mount_layers)
+  GET  /health
+  POST /release_cursor         {cursor}
+  POST /flush_cache
+  POST /update_weights_from_disk {model_path}   (HF safetensors; bumps the weight version)
+
+Unknown cursors answer 404 (the client then resends the full history); invalid mounts
+answer 400.  Requests are batched: concurrent requests arriving within a short window
+run as one engine batch (continuous batching at request granularity).
+
+Reference parity: `patches/apply_sglang_cursor.py:1-193` and `patches/apply_sglang_mount.py`
+(cursor/mount fields on /generate and chat, 404 on unknown cursor), `octopus/serving/
+route.py:75` (server_load reads /v1/loads), `octopus/rl/config.py:92-104` (check_mount_layers
+reads /get_server_info).
+"""
+from __future__ import annotations
+
+import asyncio
+import threading
+import time
+import uuid
+
+from .chat import ChatTokenizer, parse_tool_calls
+from .engine import CursorNotFound, Engine, GenInput
+
+
+class BatchingQueue:
+    """Collects concurrent requests for `window` seconds and runs them as one engine batch."""
+
+    def __init__(self, engine: Engine, window: float = 0.005, max_batch: int | None = None):
+        self.engine = engine
+        self.window = window
+        self.max_batch = max_batch or engine.max_batch
+        self.lock = threading.Lock()
+        self.pending: list = []
+        self.inflight = 0
+        self.run_lock = asyncio.Lock()
+
+    async def submit(self, inp: GenInput):
+        loop = asyncio.get_running_loop()
+        fut = loop.create_future()
+        self.pending.append((inp, fut))
+        self.inflight += 1
+        await asyncio.sleep(self.window)
+        async with self.run_lock:
+            batch = [(i, f) for i, f in self.pending if not f.done()][: self.max_batch]
+            if batch and not fut.done():
+                for item in batch:
+                    self.pending.remove(item)
+                # one temperature per engine batch: group by temperature
+                groups: dict = {}
+                for i, f in batch:
+                    groups.setdefault(float(i.temperature), []).append((i, f))
+                for items in groups.values():
+                    try:
+                        outs = await loop.run_in_executor(None, self.engine.generate, [i for i, _ in items])
+                        for (_, f), o in zip(items, outs):
+                            f.set_result(o)
+                    except Exception as e:  # per-request errors (404 cursor, bad mount) fail the whole group
+                        for _, f in items:
+                            if not f.done():
+                                f.set_exception(e)
+        try:
+            return await fut
+        finally:
+            self.inflight -= 1
+
+
+def create_app(engine: Engine, tokenizer: ChatTokenizer | None = None, model_name: str = "octopus-b200"):
+    from fastapi import FastAPI, HTTPException
+    from fastapi.responses import JSONResponse
+
+    app = FastAPI()
+    q = BatchingQueue(engine)
+    state = {"started": time.time()}
+
+    def _mounts(body):
+        out = []
+        for m in body.get("mount") or []:
+            if isinstance(m, dict):
+                out.append((m["cursor"], int(m["start"]), int(m["end"])))
+            else:
+                out.append((m[0], int(m[1]), int(m[2])))
+        return out
+
+    async def _run(inp: GenInput):
+        try:
+            return await q.submit(inp)
+        except CursorNotFound as e:
+            raise HTTPException(404, f"unknown cursor {e}") from None
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from None
+
+    @app.get("/health")
+    async def health():
+        return {"ok": True}
+
+    @app.get("/v1/loads")
+    async def loads():
+        st = engine.load_stats()
+        return {"token_usage": st["token_usage"], "num_used_tokens": st["num_used_slots"],
+                "num_waiting_reqs": len(q.pending), "num_running_reqs": q.inflight, "cursors": st["cursors"]}
+
+    @app.get("/get_server_info")
+    async def server_info():
+        return {"model_path": model_name, "mount_layers": engine.mount_layers, "page_size": 1,
+                "supports_mount": True, "supports_cursor": True, "weight_version": engine.version,
+                "max_batch": engine.max_batch, "kv_slots": engine.kv_slots}
+
+    @app.post("/generate")
+    async def generate(body: dict):
+        sp = body.get("sampling_params") or {}
+        inp = GenInput(list(body.get("input_ids") or []), cursor=body.get("cursor"), mount=_mounts(body),
+                       max_new_tokens=int(sp.get("max_new_tokens", 128)), temperature=float(sp.get("temperature",
+                                                                                                  1.0)),
+                       stop_ids=tuple(sp.get("stop_token_ids") or ()), prefill_only=int(sp.get("max_new_tokens",
+                                                                                              1)) == 0)
+        o = await _run(inp)
+        return {"output_ids": o.output_ids, "text": tokenizer.decode(o.output_ids) if tokenizer else None,
+                "meta_info": {"id": o.cursor, "cursor": o.cursor, "prompt_tokens": o.prompt_tokens,
+                              "cached_tokens": o.cached_tokens, "completion_tokens": len(o.output_ids),
+                              "finish_reason": o.finish_reason, "output_token_logprobs": o.output_logprobs}}
+
+    @app.post("/v1/chat/completions")
+    async def chat(body: dict):
+        if tokenizer is None:
+            raise HTTPException(400, "server started without a tokenizer")
+        msgs = body.get("messages") or []
+        tools = body.get("tools")
+        kwargs = body.get("chat_template_kwargs") or {}
+        cursor = body.get("cursor")
+        if cursor is not None:
+            ids = tokenizer.render_delta(msgs, tools, **kwargs)
+        else:
+            ids = tokenizer.apply(msgs, tools, True, **kwargs)
+        inp = GenInput(ids, cursor=cursor, mount=_mounts(body), max_new_tokens=int(body.get("max_tokens", 1024)),
+                       temperature=float(body.get("temperature", 1.0)), stop_ids=tokenizer.stop_ids)
+        o = await _run(inp)
+        out_ids = [t for t in o.output_ids if t not in tokenizer.stop_ids]
+        text = tokenizer.decode(out_ids)
+        content, calls = parse_tool_calls(text)
+        # the cursor keeps reply tokens + template terminator so the next delta renders right after it
+        if o.cursor is not None and engine.cursors.get(o.cursor) is not None:
+            engine.extend_cursor(o.cursor, tokenizer.terminator(), drop_trailing=tokenizer.stop_ids)
+        rid = o.cursor or f"chatcmpl-{uuid.uuid4().hex[:12]}"
+        return JSONResponse({
+            "id": rid, "object": "chat.completion", "created": int(time.time()), "model": model_name,
+            "cursor": o.cursor,
+            "choices": [{"index": 0, "finish_reason": "tool_calls" if calls else o.finish_reason,
+                         "message": {"role": "assistant", "content": content, "tool_calls": calls or None}}],
+            "usage": {"prompt_tokens": o.prompt_tokens + o.cached_tokens, "completion_tokens": len(o.output_ids),
+                      "prompt_tokens_details": {"cached_tokens": o.cached_tokens}},
+        })
+
+    @app.post("/release_cursor")
+    async def release(body: dict):
+        engine.release_cursor(body["cursor"])
+        return {"ok": True}
+
+    @app.post("/flush_cache")
+    async def flush():
+        engine.reset()
+        return {"ok": True}
+
+    @app.post("/update_weights_from_disk")
+    async def update(body: dict):
+        from ..models.decoder import load_hf
+        load_hf(engine.w, body["model_path"])
+        return {"ok": True, "weight_version": engine.bump_version()}
+
+    return app
+
+
+def serve(engine: Engine, tokenizer=None, host: str = "127.0.0.1", port: int = 30000):
+    import uvicorn
+
+    uvicorn.run(create_app(engine, tokenizer), host=host, port=port, log_level="warning")

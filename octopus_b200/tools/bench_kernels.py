@@ -91,10 +91,14 @@ def main(argv=None):
     qkv = (torch.randn(T, (Hq + 2 * Hkv) * D, device=dev) * 0.5).bfloat16()
     pairs = pre * (pre + 1) / 2 + nseq * (own * pre + own * (own + 1) / 2)
     fl = 4.0 * pairs * Hq * D
-    t = timeit(lambda: ops.attention(qkv, plan, Hq, Hkv, D))
-    r = {"kernel": "tree_attn_fwd", "T": T, "ms": t, "tflops": fl / t / 1e9}
-    res.append(r)
-    print(json.dumps(r), flush=True)
+    q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
+    for tc in (False, True):
+        t = timeit(lambda: ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D,
+                                              D ** -0.5, True, True, tc))
+        r = {"kernel": "tree_attn_fwd_tcgen05" if tc else "tree_attn_fwd_mma_sync", "T": T, "ms": t,
+             "tflops": fl / t / 1e9, "frac_of_measured": fl / t / 1e9 / pk["bf16_tflops"]}
+        res.append(r)
+        print(json.dumps(r), flush=True)
     x = qkv.clone().requires_grad_(True)
     o = ops.attention(x, plan, Hq, Hkv, D)
     g = torch.randn_like(o)
@@ -119,12 +123,28 @@ def main(argv=None):
     ip = torch.arange(0, B + 1, device=dev, dtype=torch.int32) * L
     idx = torch.randperm(B * L, device=dev).to(torch.int32)
     q = torch.randn(B, Hq * D, device=dev).bfloat16()
-    da = ops.DecodeAttention(Hq, Hkv, D, B, 8, dev)
-    t = timeit(lambda: da(q, kc, vc, ip, idx))
     by = 2.0 * B * L * Hkv * D * 2
-    r = {"kernel": "decode_attn", "B": B, "L": L, "ms": t, "gbs": by / t / 1e6, "frac_of_measured": by / t / 1e6 / pk["hbm_gbs"]}
-    res.append(r)
-    print(json.dumps(r), flush=True)
+    for persistent in (False, True):
+        for splits in (4, 8):
+            da = ops.DecodeAttention(Hq, Hkv, D, B, splits, dev, persistent=persistent)
+            t = timeit(lambda: da(q, kc, vc, ip, idx))
+            r = {"kernel": "decode_attn_persistent" if persistent else "decode_attn_splitk", "splits": splits,
+                 "B": B, "L": L, "ms": t, "gbs": by / t / 1e6, "frac_of_measured": by / t / 1e6 / pk["hbm_gbs"]}
+            res.append(r)
+            print(json.dumps(r), flush=True)
+    # shared-prefix case: 8 requests per group share a 2048-slot prefix (mounted task prefix)
+    groups = B // 8
+    pre = torch.randperm(B * L, device=dev)[: groups * 2048].view(groups, 2048).to(torch.int32)
+    own = torch.randperm(B * L, device=dev)[: B * (L - 2048)].view(B, L - 2048).to(torch.int32)
+    idx2 = torch.cat([pre.repeat_interleave(8, 0), own], 1).reshape(-1).contiguous()
+    uniq = (groups * 2048 + B * (L - 2048)) * Hkv * D * 2 * 2
+    for persistent in (False, True):
+        da = ops.DecodeAttention(Hq, Hkv, D, B, 8, dev, persistent=persistent)
+        t = timeit(lambda: da(q, kc, vc, ip, idx2))
+        r = {"kernel": ("decode_attn_persistent" if persistent else "decode_attn_splitk") + "_shared_prefix",
+             "B": B, "L": L, "ms": t, "logical_gbs": by / t / 1e6, "unique_gbs": uniq / t / 1e6}
+        res.append(r)
+        print(json.dumps(r), flush=True)
     ops.check_status(0)
     if args.json:
         with open(args.json, "w") as f:

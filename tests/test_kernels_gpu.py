@@ -260,3 +260,43 @@ def test_sampling_never_nan_over_many_rows():
                              row_stream=torch.arange(512, device=dev, dtype=torch.int64) + 1000 * seed)
         assert torch.isfinite(lp).all()
         assert (tok >= 0).all() and (tok < V).all()
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(28, 4), (12, 2)])
+def test_tcgen05_attention_matches_mma_sync_and_reference(Hq, Hkv):
+    rng = np.random.default_rng(13)
+    torch.manual_seed(13)
+    D = 128
+    T, cu_q, cu_k, keys = _tree_plan(rng, n_nodes=10)
+    plan = ops.AttnPlan.build(cu_q, cu_k, keys, dev)
+    qkv = (torch.randn(T, (Hq + 2 * Hkv) * D, device=dev) * 0.5).bfloat16()
+    q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
+    o_tc, lse_tc = ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D,
+                                      D ** -0.5, True, True, True)
+    o_ms, lse_ms = ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D,
+                                      D ** -0.5, True, True, False)
+    x = qkv.float().cpu()
+    orf, lrf = ref.gather_attention(x[:, : Hq * D].reshape(T, Hq, D), x[:, Hq * D: (Hq + Hkv) * D].reshape(T, Hkv, D),
+                                    x[:, (Hq + Hkv) * D:].reshape(T, Hkv, D), cu_q, cu_k, torch.from_numpy(keys),
+                                    D ** -0.5)
+    assert rel_err(o_tc.cpu(), orf.reshape(T, Hq * D)) < 2e-2
+    assert rel_err(o_tc, o_ms) < 2e-2
+    assert torch.allclose(lse_tc.cpu(), lrf.float(), atol=2e-2)
+
+
+def test_persistent_decode_matches_splitk():
+    torch.manual_seed(14)
+    B, Hq, Hkv, D = 64, 28, 4, 128
+    slots = 20000
+    kc = torch.randn(slots, Hkv * D, device=dev).bfloat16()
+    vc = torch.randn(slots, Hkv * D, device=dev).bfloat16()
+    lens = torch.randint(1, 3000, (B,))
+    ip = torch.zeros(B + 1, dtype=torch.int32)
+    ip[1:] = torch.cumsum(lens, 0)
+    idx = torch.randint(0, slots, (int(ip[-1]),), dtype=torch.int32, device=dev)
+    q = torch.randn(B, Hq * D, device=dev).bfloat16()
+    ipd = ip.to(dev)
+    for splits in (1, 3, 8):
+        a = ops.DecodeAttention(Hq, Hkv, D, B, splits, dev, persistent=True)(q, kc, vc, ipd, idx)
+        b = ops.DecodeAttention(Hq, Hkv, D, B, splits, dev, persistent=False)(q, kc, vc, ipd, idx)
+        assert rel_err(a, b) < 1e-2

@@ -54,7 +54,7 @@ def test_rollout_logprobs_close_to_trainer():
 def test_rl_step_updates_weights():
     cfg, actor, eng = _setup()
     env = MultiAgentDag(cfg.vocab_size, DagConfig(instances=2, samples=2, prefix_len=128, turn_len=16, role_len=8))
-    tr = RLTrainer(actor, eng, env, TrainerConfig(mb_tokens=600))
+    tr = RLTrainer(actor, eng, env, TrainerConfig(mb_tokens=300))
     before = actor.flat16.clone()
     st = tr.step()
     assert np.isfinite(st["loss"]) and st["micro_batches"] >= 2
