@@ -125,13 +125,13 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
     const __nv_bfloat16* kb = p.k + static_cast<size_t>(kvh) * kD;
     const __nv_bfloat16* vb = p.v + static_cast<size_t>(kvh) * kD;
     const int32_t* kidx = p.key_idx + kbeg;
+    const int cl = lane & 15;  // 16 lanes per row: coalesced 256-byte row reads
     {
       const uint32_t base = smem_u32(sQ);
-      for (int r = lane; r < kBM; r += 32) {
+      for (int r = lane >> 4; r < kBM; r += 2) {
         const bool ok = r < mrows;
         const __nv_bfloat16* src = qb + static_cast<size_t>(qbeg + q0 + (ok ? r : 0)) * p.ldq;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) cp_async16z(base + toff(r, c), src + c * 8, ok);
+        cp_async16z(base + toff(r, cl), src + cl * 8, ok);
       }
       cp_async_arrive(q_full);
     }
@@ -144,17 +144,22 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
       if (!ok) break;
       const uint32_t kbase = smem_u32(sK + stage * kTileBytes);
       const uint32_t vbase = smem_u32(sV + stage * kTileBytes);
-      for (int r = lane; r < kBN; r += 32) {
-        const int k = j * kBN + r;
-        const bool valid = k < n_end;
-        const int64_t row = valid ? static_cast<int64_t>(kidx[k]) : 0;
-        const __nv_bfloat16* ks = kb + row * p.ldk;
-        const __nv_bfloat16* vs = vb + row * p.ldk;
+      // the tile's 128 key rows: one coalesced index load per lane per 32 rows, handed
+      // to the copying lanes by shuffle
+      int ix[4];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          cp_async16z(kbase + toff(r, c), ks + c * 8, valid);
-          cp_async16z(vbase + toff(r, c), vs + c * 8, valid);
-        }
+      for (int q = 0; q < 4; ++q) {
+        const int k = j * kBN + q * 32 + lane;
+        ix[q] = k < n_end ? static_cast<int>(kidx[k]) : -1;
+      }
+#pragma unroll
+      for (int i = 0; i < kBN / 2; ++i) {
+        const int r = 2 * i + (lane >> 4);
+        const int src = __shfl_sync(0xffffffffu, ix[i >> 4], r & 31);
+        const bool valid = src >= 0;
+        const int64_t row = valid ? static_cast<int64_t>(src) : 0;
+        cp_async16z(kbase + toff(r, cl), kb + row * p.ldk + cl * 8, valid);
+        cp_async16z(vbase + toff(r, cl), vb + row * p.ldk + cl * 8, valid);
       }
       cp_async_arrive(&kv_full[stage]);
       if (++stage == kStages) {

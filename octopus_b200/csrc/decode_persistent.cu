@@ -118,21 +118,22 @@ __global__ void __launch_bounds__(64, 2) decode_persistent_kernel(DecodePersistP
         }
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
-        // lane l gathers cache rows l and l + 32 of the tile (K and V, all 16 chunks)
+        // the tile's 64 slot indices: one coalesced load per lane (rows lane, lane + 32),
+        // handed to the copying lanes by shuffle (no dependent load per row)
+        const int i0 = t0 + lane < x.k1 ? static_cast<int>(idx[t0 + lane]) : first;
+        const int i1 = t0 + 32 + lane < x.k1 ? static_cast<int>(idx[t0 + 32 + lane]) : first;
+        // 16 lanes per cache row (one 16-byte chunk each): every warp load reads two
+        // whole 256-byte rows, so global reads stay coalesced
         const uint32_t base = smem_u32(smem + stage * kTileBytes);
         const size_t ld = static_cast<size_t>(p.Hkv) * 128;
+        const int c = lane & 15;
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int r = lane + 32 * j;
-          const int k = t0 + r;
-          const int64_t row = k < x.k1 ? static_cast<int64_t>(idx[k]) : static_cast<int64_t>(first);
-          const __nv_bfloat16* ks = p.k_cache + row * ld + x.kvh * 128;
-          const __nv_bfloat16* vs = p.v_cache + row * ld + x.kvh * 128;
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            cp_async16(base + tile_off(r, c), ks + c * 8);
-            cp_async16(base + 2 * kHalfBytes + tile_off(r, c), vs + c * 8);
-          }
+        for (int i = 0; i < kTile / 2; ++i) {
+          const int r = 2 * i + (lane >> 4);
+          const int src = __shfl_sync(0xffffffffu, i < 16 ? i0 : i1, r & 31);
+          const int64_t row = static_cast<int64_t>(src);
+          cp_async16(base + tile_off(r, c), p.k_cache + row * ld + x.kvh * 128 + c * 8);
+          cp_async16(base + 2 * kHalfBytes + tile_off(r, c), p.v_cache + row * ld + x.kvh * 128 + c * 8);
         }
         cp_async_arrive(&full[stage]);
         if (++stage == kStages) {

@@ -529,10 +529,13 @@ void attn_decode_persistent_t(torch::Tensor q, torch::Tensor kc, torch::Tensor v
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void register_comm(py::module& m);
+
 }  // namespace octo
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   using namespace octo;
+  register_comm(m);
   m.doc() = "octopus_b200 sm_100a kernels";
   m.def("status_tensor", [](int64_t d) { return status_tensor(static_cast<int>(d)); });
   m.def("gemm_out", &gemm_out, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("C"),

@@ -26,6 +26,7 @@ from . import reference as ref
 from ._ext import ext
 
 HEAD_CHUNK = 4096  # rows per chunk in the head backward (dz is [chunk, vocab] bf16)
+CPU_VOCAB_CHUNK = 1024  # vocab columns per chunk of the CPU head (online log-sum-exp merge)
 
 
 def use_tc_attention(D: int) -> bool:
@@ -368,7 +369,7 @@ class _Head(torch.autograd.Function):
                                             vocab_limit or 0)
             logp, ent, lse = logp[:M], ent[:M], lse[:M]
         else:
-            logp, ent, lse = ref.logprob_head(h, W, labels, alpha, vocab_limit)
+            logp, ent, lse = ref.logprob_head(h, W, labels, alpha, vocab_limit, vocab_chunk=CPU_VOCAB_CHUNK)
         ctx.save_for_backward(h, W, labels, lse, ent)
         return logp, ent
 

@@ -95,8 +95,14 @@ def gather_attention(q, k, v, cu_q, cu_k, key_idx, scale: float, causal: bool = 
     return o, lse
 
 
-def logprob_head(h, W, labels, alpha: float = 1.0, vocab_limit: int | None = None):
-    """Returns (logp [M], entropy [M], lse [M]); rows with label < 0 get logp 0."""
+def logprob_head(h, W, labels, alpha: float = 1.0, vocab_limit: int | None = None, vocab_chunk: int = 0):
+    """Returns (logp [M], entropy [M], lse [M]); rows with label < 0 get logp 0.
+
+    vocab_chunk > 0 computes the normaliser chunk by chunk over the vocabulary with an
+    online (max, sum exp, sum exp*z) merge, as the fused kernel does per vocab tile.
+    """
+    if vocab_chunk:
+        return _logprob_head_chunked(h, W, labels, alpha, vocab_limit, vocab_chunk)
     z = (_f(h) @ _f(W).t()) * alpha
     if vocab_limit is not None and vocab_limit < z.shape[1]:
         z = z[:, :vocab_limit]
@@ -107,3 +113,30 @@ def logprob_head(h, W, labels, alpha: float = 1.0, vocab_limit: int | None = Non
     lab = labels.long()
     picked = torch.where(lab >= 0, lp.gather(1, lab.clamp(min=0)[:, None])[:, 0], torch.zeros_like(lse))
     return picked, ent, lse
+
+
+def _logprob_head_chunked(h, W, labels, alpha, vocab_limit, chunk):
+    hf = _f(h)
+    V = vocab_limit or W.shape[0]
+    M = hf.shape[0]
+    m = torch.full((M,), -math.inf, dtype=hf.dtype)
+    s = torch.zeros(M, dtype=hf.dtype)
+    t = torch.zeros(M, dtype=hf.dtype)
+    zl = torch.zeros(M, dtype=hf.dtype)
+    lab = labels.long()
+    for a in range(0, V, chunk):
+        b = min(V, a + chunk)
+        z = (hf @ _f(W[a:b]).t()) * alpha
+        cm = z.max(-1).values
+        nm = torch.maximum(m, cm)
+        sc = torch.exp(m - nm)
+        e = torch.exp(z - nm[:, None])
+        s = s * sc + e.sum(-1)
+        t = t * sc + (e * z).sum(-1)
+        m = nm
+        inside = (lab >= a) & (lab < b)
+        zl = torch.where(inside, z.gather(1, (lab - a).clamp(0, b - a - 1)[:, None])[:, 0], zl)
+    lse = m + torch.log(s)
+    logp = torch.where(lab >= 0, zl - lse, torch.zeros_like(lse))
+    ent = lse - t / s
+    return logp, ent, lse

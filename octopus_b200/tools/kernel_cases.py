@@ -1,0 +1,111 @@
+"""Run one kernel case a few times on a small input (for ncu captures and quick timing).
+
+    python -m octopus_b200.tools.kernel_cases <case> [--reps N]
+
+Cases (inputs sized above L2 where DRAM behaviour matters, a few GB at most):
+  gemm_fwd_7b        X[16384, 3584] @ W[18944*2, 3584]^T (gate/up projection)
+  gemm_wgrad_7b      dY^T X for the down projection (MN-major operands)
+  attn_fwd_tc        tree attention forward, tcgen05 kernel (8 x 2048 own + 2048 prefix)
+  attn_fwd_mma       same on the mma.sync kernel
+  attn_bwd           tree attention backward (dq + dkv kernels)
+  decode_splitk      paged decode, 256 requests x 3000 keys (split-K kernel)
+  decode_persistent  same on the persistent producer/consumer kernel
+  head_fwd           fused logprob head, 4096 rows x 152064 vocab
+  sample_head        fused sampling head, 256 rows x 152064 vocab
+"""
+from __future__ import annotations
+
+import argparse
+import time
+
+import numpy as np
+import torch
+
+from octopus_b200 import ops
+
+
+def tree_case(dev):
+    Hq, Hkv, D = 28, 4, 128
+    pre, own, nseq = 2048, 2048, 8
+    T = pre + nseq * own
+    cu_q, cu_k, keys = [0, pre], [0, pre], list(range(pre))
+    for s in range(nseq):
+        a = pre + s * own
+        cu_q.append(cu_q[-1] + own)
+        keys += list(range(pre)) + list(range(a, a + own))
+        cu_k.append(len(keys))
+    plan = ops.AttnPlan.build(cu_q, cu_k, np.asarray(keys, dtype=np.int32), dev)
+    qkv = (torch.randn(T, (Hq + 2 * Hkv) * D, device=dev) * 0.5).bfloat16()
+    return plan, qkv, Hq, Hkv, D
+
+
+def decode_case(dev):
+    B, L, Hq, Hkv, D = 256, 3000, 28, 4, 128
+    kc = torch.randn(B * L, Hkv * D, device=dev).bfloat16()
+    vc = torch.randn(B * L, Hkv * D, device=dev).bfloat16()
+    ip = torch.arange(0, B + 1, device=dev, dtype=torch.int32) * L
+    idx = torch.randperm(B * L, device=dev).to(torch.int32)
+    q = torch.randn(B, Hq * D, device=dev).bfloat16()
+    return q, kc, vc, ip, idx, Hq, Hkv, D, B
+
+
+def build(case: str, dev):
+    if case == "gemm_fwd_7b":
+        A = torch.randn(16384, 3584, device=dev).bfloat16()
+        W = torch.randn(2 * 18944, 3584, device=dev).bfloat16()
+        C = torch.empty(16384, 2 * 18944, device=dev, dtype=torch.bfloat16)
+        return lambda: ops.gemm(A, W, out=C)
+    if case == "gemm_wgrad_7b":
+        dY = torch.randn(16384, 3584, device=dev).bfloat16()
+        X = torch.randn(16384, 18944, device=dev).bfloat16()
+        G = torch.zeros(3584, 18944, device=dev)
+        return lambda: ops.gemm(dY, X, a_mn=True, b_mn=True, out=G, accumulate=True)
+    if case in ("attn_fwd_tc", "attn_fwd_mma"):
+        plan, qkv, Hq, Hkv, D = tree_case(dev)
+        q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
+        tc = case == "attn_fwd_tc"
+        return lambda: ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D,
+                                          D ** -0.5, True, True, tc)
+    if case == "attn_bwd":
+        plan, qkv, Hq, Hkv, D = tree_case(dev)
+        x = qkv.clone().requires_grad_(True)
+        o = ops.attention(x, plan, Hq, Hkv, D)
+        g = torch.randn_like(o)
+        return lambda: torch.autograd.grad(o, x, g, retain_graph=True)
+    if case in ("decode_splitk", "decode_persistent"):
+        q, kc, vc, ip, idx, Hq, Hkv, D, B = decode_case(dev)
+        da = ops.DecodeAttention(Hq, Hkv, D, B, 8, dev, persistent=case == "decode_persistent")
+        return lambda: da(q, kc, vc, ip, idx)
+    if case in ("head_fwd", "sample_head"):
+        M = 4096 if case == "head_fwd" else 256
+        h = torch.randn(M, 3584, device=dev).bfloat16()
+        W = (torch.randn(152064, 3584, device=dev) * 0.02).bfloat16()
+        lab = torch.randint(0, 152064, (M,), device=dev, dtype=torch.int32)
+        if case == "head_fwd":
+            return lambda: ops.ext().head_fwd(h, W, lab, 1.0, 0)
+        st = torch.arange(M, device=dev, dtype=torch.int64)
+        return lambda: ops.ext().sample_head(h, W, 1.0, 1, st, 0)
+    raise SystemExit(f"unknown case {case}")
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case")
+    ap.add_argument("--reps", type=int, default=3)
+    args = ap.parse_args(argv)
+    dev = torch.device("cuda", 0)
+    fn = build(args.case, dev)
+    fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    ops.check_status(0)
+    print(f"{args.case}: {a.elapsed_time(b) / args.reps:.3f} ms/iter")
+
+
+if __name__ == "__main__":
+    main()
