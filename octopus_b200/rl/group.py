@@ -19,6 +19,8 @@ from __future__ import annotations
 import re
 from collections import defaultdict
 
+from ..runtime.core import branch_key
+
 
 def leave_one_out(values: list[float]) -> list[float]:
     """A_i = x_i - mean_{j != i} x_j computed as mean_j (x_i - x_j) over j != i."""
@@ -75,11 +77,6 @@ def code_gate(a: float, branch: dict) -> float:
 def _is_child_thread(parent: str, name: str) -> bool:
     prefix = "" if parent == "main" else parent + "/"
     return re.fullmatch(re.escape(prefix) + r"fork\d+/[^/]+", name) is not None
-
-
-def branch_key(thread: str) -> str:
-    """Stable key of a branch thread (its path without the fork counters)."""
-    return "/".join(p for p in thread.split("/") if not re.fullmatch(r"fork\d+", p)) or "main"
 
 
 def assign_threads(leaf_ids: list[str], episode: dict) -> dict:
