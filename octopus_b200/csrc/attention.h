@@ -20,6 +20,7 @@ struct AttnParams {
   int Tq, Hq, Hkv;
   float scale;
   int causal;
+  unsigned long long* trace;  // optional per-CTA event timestamps (tcgen05 kernel, debugging)
 };
 
 struct AttnBwdParams {

@@ -61,6 +61,11 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// Trace slots (the last CTA of head 0 only, when p.trace != nullptr): [role * 64 + tile] = globaltimer.
+__device__ __forceinline__ void trace_at(const AttnParams& p, int role, int idx) {
+  if (p.trace != nullptr && blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && idx < 64) p.trace[role * 64 + idx] = globaltimer_ns();
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* status) {
@@ -118,6 +123,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) trace_at(p, 9, 0);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -142,6 +148,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
       if (lane == 0) ok = mbar_wait(&kv_empty[stage], phase ^ 1u, abort_flag, status, 500 + stage);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
+      if (lane == 0) trace_at(p, 0, j);
       const uint32_t kbase = smem_u32(sK + stage * kTileBytes);
       const uint32_t vbase = smem_u32(sV + stage * kTileBytes);
       // the tile's 128 key rows: one coalesced index load per lane per 32 rows, handed
@@ -162,6 +169,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
         cp_async16z(vbase + toff(r, cl), vb + row * p.ldk + cl * 8, valid);
       }
       cp_async_arrive(&kv_full[stage]);
+      if (lane == 0) trace_at(p, 1, j);
       if (++stage == kStages) {
         stage = 0;
         phase ^= 1u;
@@ -194,6 +202,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
           ok = false;
           break;
         }
+        trace_at(p, 2, j);
         if (!mbar_wait(&s_empty[b], ((j >> 1) & 1) ^ 1u, abort_flag, status, 620 + b)) {
           ok = false;
           break;
@@ -208,12 +217,14 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
           umma_f16_ss(tmem + kColS + b * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[b]);
+        trace_at(p, 3, j);
         issued = true;
         if (j > 0) {
           if (!mbar_wait(p_full, (j - 1) & 1, abort_flag, status, 630)) {
             ok = false;
             break;
           }
+          trace_at(p, 4, j - 1);
           tc_fence_after();
           issue_pv(j - 1, prev_stage);
         }
@@ -254,6 +265,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
         break;
       }
       tc_fence_after();
+      if (threadIdx.x == 64) trace_at(p, 5, j);
       float s[kBN];
 #pragma unroll
       for (int c = 0; c < kBN / 32; ++c) {
@@ -266,6 +278,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[b]);
+      if (threadIdx.x == 64) trace_at(p, 6, j);
       const int kbase = j * kBN;
       float mt = -INFINITY;
 #pragma unroll
@@ -298,6 +311,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
           break;
         }
         tc_fence_after();
+        if (threadIdx.x == 64) trace_at(p, 7, j);
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
           for (int c = 0; c < kD / 32; ++c) {
@@ -321,6 +335,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
+      if (threadIdx.x == 64) trace_at(p, 8, j);
     }
     // epilogue: O / l
     if (ok && n_tiles > 0 && mbar_wait(o_done, (n_tiles - 1) & 1, abort_flag, status, 670)) {
@@ -357,6 +372,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (threadIdx.x == 0) trace_at(p, 9, 1);
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 

@@ -359,7 +359,7 @@ void adamw_t(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v,
 std::vector<torch::Tensor> attn_fwd_t(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_q,
                                       torch::Tensor cu_k, torch::Tensor key_idx, torch::Tensor tiles, int64_t Hq,
                                       int64_t Hkv, int64_t D, double scale, bool causal, bool want_lse,
-                                      bool use_tc) {
+                                      bool use_tc, c10::optional<torch::Tensor> trace) {
   c10::cuda::CUDAGuard guard(q.get_device());
   CHECK_BF16(q);
   CHECK_BF16(k);
@@ -394,6 +394,8 @@ std::vector<torch::Tensor> attn_fwd_t(torch::Tensor q, torch::Tensor k, torch::T
   p.Hkv = Hkv;
   p.scale = static_cast<float>(scale);
   p.causal = causal ? 1 : 0;
+  p.trace = (trace.has_value() && trace->defined()) ? reinterpret_cast<unsigned long long*>(trace->data_ptr())
+                                                      : nullptr;
   if (use_tc) {
     TORCH_CHECK(D == 128, "attention: the tcgen05 forward needs head_dim 128");
     attn_fwd_tc(p, tiles.numel() / 2, status_ptr(q.get_device()), cur_stream(q));
@@ -556,7 +558,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw", &adamw_t);
   m.def("attn_fwd", &attn_fwd_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu_q"), py::arg("cu_k"),
         py::arg("key_idx"), py::arg("tiles"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"),
-        py::arg("causal"), py::arg("want_lse"), py::arg("use_tc") = false);
+        py::arg("causal"), py::arg("want_lse"), py::arg("use_tc") = false, py::arg("trace") = py::none());
   m.def("attn_bwd", &attn_bwd_t);
   m.def("attn_decode", &attn_decode_t);
   m.def("attn_decode_persistent", &attn_decode_persistent_t);

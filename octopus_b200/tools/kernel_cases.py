@@ -107,5 +107,29 @@ def main(argv=None):
     print(f"{args.case}: {a.elapsed_time(b) / args.reps:.3f} ms/iter")
 
 
+def trace_attn_tc():
+    """Per-event timeline (microseconds from CTA start) of CTA (0, 0) of the tcgen05 attention."""
+    dev = torch.device("cuda", 0)
+    plan, qkv, Hq, Hkv, D = tree_case(dev)
+    q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
+    tr = torch.zeros(10 * 64, dtype=torch.int64, device=dev)
+    for _ in range(2):
+        ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D, D ** -0.5, True,
+                           True, True, tr)
+    torch.cuda.synchronize()
+    t = tr.view(10, 64).cpu().numpy().astype(np.int64)
+    t0 = t[9, 0]
+    names = ["prod_empty_ok", "prod_issued", "mma_kv_full", "mma_S_issued", "mma_p_full", "sm_s_full",
+             "sm_s_loaded", "sm_o_done", "sm_p_stored"]
+    n = int((t[3] > 0).sum())
+    print("CTA total us", (t[9, 1] - t0) / 1e3, "tiles", n)
+    for j in range(min(n, 12)):
+        print(j, " ".join(f"{nm}={(t[r, j] - t0) / 1e3:.2f}" for r, nm in enumerate(names) if t[r, j] > 0))
+
+
 if __name__ == "__main__":
-    main()
+    import sys
+    if len(sys.argv) > 1 and sys.argv[1] == "trace_attn_tc":
+        trace_attn_tc()
+    else:
+        main()
