@@ -3,15 +3,18 @@
 // Same contract as attn_fwd in attention.cu (tree nodes / paged prefill: query rows of
 // a sequence attend to a gathered key list, bottom-right causal, GQA), head_dim 128.
 //
-// CTA = 128 query rows of one sequence and one head; 192 threads:
-//   warp 0      producer: cp.async gathers of Q (once) and of 128-key K/V tiles into a
+// CTA = 128 query rows of one sequence and one head; 224 threads:
+//   warps 0-1   producers: cp.async gathers of Q (once) and of 128-key K/V tiles into a
 //               2-stage SMEM ring (128-byte swizzled K-major layout that the UMMA
-//               descriptors read directly); completion via cp.async.mbarrier.arrive
-//   warp 1      TMEM owner and single-thread MMA issuer:
+//               descriptors read directly), 64 rows per warp; completion via
+//               cp.async.mbarrier.arrive
+//   warp 2      TMEM owner and single-thread MMA issuer, event driven: S_{j+1} is issued
+//               as soon as K_{j+1} has landed and its S buffer is free, P_j V_j as soon as
+//               the softmax has written P_j:
 //                 S_j = Q K_j^T         tcgen05.mma kind::f16, A/B from SMEM, fp32 in TMEM
 //                 O  += P_{j-1} V_{j-1}  tcgen05.mma with A = P read from TMEM (bf16),
 //                                        B = V from SMEM (MN-major)
-//   warps 2..5  softmax: thread = query row (TMEM lane), S row loaded with tcgen05.ld,
+//   warps 3..6  softmax: thread = query row (TMEM lane), S row loaded with tcgen05.ld,
 //               online softmax in the exp2 domain with lazy rescaling (O is rescaled in
 //               TMEM only when the running max grows by more than 2^8), P written back
 //               to TMEM as packed bf16; epilogue O / l -> bf16 rows + lse.
@@ -41,9 +44,8 @@ __device__ __forceinline__ uint32_t toff(int r, int c) {
   return static_cast<uint32_t>((c >> 3) * kHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
-__device__ __forceinline__ void cp_async16z(uint32_t dst, const void* src, bool valid) {
-  const int n = valid ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -68,7 +70,10 @@ __device__ __forceinline__ void trace_at(const AttnParams& p, int role, int idx)
 
 }  // namespace
 
-__global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* status) {
+constexpr int kProducers = 2;  // 64 rows each (register budget: 7 warps keep 255 regs/thread)
+constexpr int kThreads = (kProducers + 1 + 4) * 32;
+
+__global__ void __launch_bounds__(kThreads, 1) attn_fwd_tc_kernel(AttnParams p, int* status) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -100,9 +105,9 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
   const int n_tiles = (n_end + kBN - 1) / kBN;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 32);
+    mbar_init(q_full, 32 * kProducers);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&kv_full[s], 32);
+      mbar_init(&kv_full[s], 32 * kProducers);
       mbar_init(&kv_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -115,7 +120,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == kProducers) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -125,119 +130,119 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) trace_at(p, 9, 0);
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp < kProducers) {
+    // ------------------------------------------------------------ producers (32 rows each)
     const __nv_bfloat16* qb = p.q + static_cast<size_t>(h) * kD;
     const __nv_bfloat16* kb = p.k + static_cast<size_t>(kvh) * kD;
     const __nv_bfloat16* vb = p.v + static_cast<size_t>(kvh) * kD;
     const int32_t* kidx = p.key_idx + kbeg;
-    const int cl = lane & 15;  // 16 lanes per row: coalesced 256-byte row reads
+    const int cl = lane & 15;      // 16 lanes per row: coalesced 256-byte row reads
+    constexpr int kRows = kBM / kProducers;
+    const int rbase = warp * kRows;  // this warp's rows of every tile
     {
       const uint32_t base = smem_u32(sQ);
-      for (int r = lane >> 4; r < kBM; r += 2) {
-        const bool ok = r < mrows;
-        const __nv_bfloat16* src = qb + static_cast<size_t>(qbeg + q0 + (ok ? r : 0)) * p.ldq;
-        cp_async16z(base + toff(r, cl), src + cl * 8, ok);
+#pragma unroll
+      for (int i = 0; i < kRows / 2; ++i) {
+        const int r = rbase + 2 * i + (lane >> 4);
+        const __nv_bfloat16* src = qb + static_cast<size_t>(qbeg + q0 + (r < mrows ? r : 0)) * p.ldq;
+        cp_async16(base + toff(r, cl), src + cl * 8);
       }
       cp_async_arrive(q_full);
     }
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
+    const int32_t first = nk > 0 ? kidx[0] : 0;
     for (int j = 0; j < n_tiles && ok; ++j) {
       if (lane == 0) ok = mbar_wait(&kv_empty[stage], phase ^ 1u, abort_flag, status, 500 + stage);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
-      if (lane == 0) trace_at(p, 0, j);
+      if (warp == 0 && lane == 0) trace_at(p, 0, j);
       const uint32_t kbase = smem_u32(sK + stage * kTileBytes);
       const uint32_t vbase = smem_u32(sV + stage * kTileBytes);
-      // the tile's 128 key rows: one coalesced index load per lane per 32 rows, handed
-      // to the copying lanes by shuffle
-      int ix[4];
+      // this warp's slot indices: one coalesced load per 32 rows, handed out by shuffle;
+      // rows past the key list read a valid row (the softmax masks them)
+      int ix[kRows / 32];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int k = j * kBN + q * 32 + lane;
-        ix[q] = k < n_end ? static_cast<int>(kidx[k]) : -1;
+      for (int q = 0; q < kRows / 32; ++q) {
+        const int kk = j * kBN + rbase + q * 32 + lane;
+        ix[q] = kk < n_end ? static_cast<int>(kidx[kk]) : first;
       }
 #pragma unroll
-      for (int i = 0; i < kBN / 2; ++i) {
-        const int r = 2 * i + (lane >> 4);
-        const int src = __shfl_sync(0xffffffffu, ix[i >> 4], r & 31);
-        const bool valid = src >= 0;
-        const int64_t row = valid ? static_cast<int64_t>(src) : 0;
-        cp_async16z(kbase + toff(r, cl), kb + row * p.ldk + cl * 8, valid);
-        cp_async16z(vbase + toff(r, cl), vb + row * p.ldk + cl * 8, valid);
+      for (int i = 0; i < kRows / 2; ++i) {
+        const int rl = 2 * i + (lane >> 4);
+        const int64_t row = static_cast<int64_t>(__shfl_sync(0xffffffffu, ix[rl >> 5], rl & 31));
+        const int r = rbase + rl;
+        cp_async16(kbase + toff(r, cl), kb + row * p.ldk + cl * 8);
+        cp_async16(vbase + toff(r, cl), vb + row * p.ldk + cl * 8);
       }
       cp_async_arrive(&kv_full[stage]);
-      if (lane == 0) trace_at(p, 1, j);
+      if (warp == 0 && lane == 0) trace_at(p, 1, j);
       if (++stage == kStages) {
         stage = 0;
         phase ^= 1u;
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == kProducers) {
+    // ------------------------------------------------------------ MMA issuer (event loop)
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_f16(kBM, kBN, false, false, true);
       constexpr uint32_t idesc_o = umma_idesc_f16(kBM, kD, false, true, true);
       bool ok = mbar_wait(q_full, 0, abort_flag, status, 600);
+      fence_proxy_async_smem();  // cp.async (generic proxy) writes -> tensor-core reads
       const uint32_t qaddr = smem_u32(sQ);
-      int stage = 0, prev_stage = 0;
-      uint32_t phase = 0;
+      int js = 0, jp = 0;        // next tile whose S / P.V to issue
       bool issued = false;
-      auto issue_pv = [&](int jj, int st) {
-        // O += P_jj V_jj  (A = P from TMEM, 8 k-steps of 16 keys)
-        const uint32_t vaddr = smem_u32(sV + st * kTileBytes);
+      const uint64_t t_start = globaltimer_ns();
+      uint64_t t_last = t_start;
+      while (ok && jp < n_tiles) {
+        bool progressed = false;
+        if (js < n_tiles && js - jp < kStages) {
+          const int st = js % kStages;
+          const uint32_t ph = static_cast<uint32_t>((js / kStages) & 1);
+          const int b = js & 1;
+          if (mbar_try_wait(&kv_full[st], ph) && mbar_try_wait(&s_empty[b], ((js >> 1) & 1) ^ 1u)) {
+            tc_fence_after();
+            fence_proxy_async_smem();
+            trace_at(p, 2, js);
+            const uint32_t kaddr = smem_u32(sK + st * kTileBytes);
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bd = umma_smem_desc(vaddr + kk * 2048, kHalf, 1024);
-          umma_f16_ts(tmem + kColO, tmem + kColP + kk * 8, bd, idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(o_done);
-        umma_commit(&kv_empty[st]);
-      };
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int b = j & 1;
-        if (!mbar_wait(&kv_full[stage], phase, abort_flag, status, 610 + stage)) {
-          ok = false;
-          break;
-        }
-        trace_at(p, 2, j);
-        if (!mbar_wait(&s_empty[b], ((j >> 1) & 1) ^ 1u, abort_flag, status, 620 + b)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t kaddr = smem_u32(sK + stage * kTileBytes);
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t o16 = (kk >> 2) * kHalf + (kk & 3) * 32;
-          const uint64_t ad = umma_smem_desc(qaddr + o16, 16, 1024);
-          const uint64_t bd = umma_smem_desc(kaddr + o16, 16, 1024);
-          umma_f16_ss(tmem + kColS + b * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[b]);
-        trace_at(p, 3, j);
-        issued = true;
-        if (j > 0) {
-          if (!mbar_wait(p_full, (j - 1) & 1, abort_flag, status, 630)) {
-            ok = false;
-            break;
+            for (int kk = 0; kk < kD / 16; ++kk) {
+              const uint32_t o16 = (kk >> 2) * kHalf + (kk & 3) * 32;
+              const uint64_t ad = umma_smem_desc(qaddr + o16, 16, 1024);
+              const uint64_t bd = umma_smem_desc(kaddr + o16, 16, 1024);
+              umma_f16_ss(tmem + kColS + b * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[b]);
+            trace_at(p, 3, js);
+            issued = true;
+            ++js;
+            progressed = true;
           }
-          trace_at(p, 4, j - 1);
-          tc_fence_after();
-          issue_pv(j - 1, prev_stage);
         }
-        prev_stage = stage;
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-      if (ok && n_tiles > 0) {
-        if (mbar_wait(p_full, (n_tiles - 1) & 1, abort_flag, status, 640)) {
+        if (jp < js && mbar_try_wait(p_full, jp & 1)) {
           tc_fence_after();
-          issue_pv(n_tiles - 1, prev_stage);
+          trace_at(p, 4, jp);
+          const int st = jp % kStages;
+          const uint32_t vaddr = smem_u32(sV + st * kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            const uint64_t bd = umma_smem_desc(vaddr + kk * 2048, kHalf, 1024);
+            umma_f16_ts(tmem + kColO, tmem + kColP + kk * 8, bd, idesc_o, (jp > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(o_done);
+          umma_commit(&kv_empty[st]);
+          ++jp;
+          progressed = true;
+        }
+        if (progressed) {
+          t_last = globaltimer_ns();
+        } else if (*abort_flag) {
+          ok = false;
+        } else if (globaltimer_ns() - t_last > OCTO_WAIT_NS) {
+          *abort_flag = 1;
+          record_error(status, kErrMbarTimeout, 610);
+          ok = false;
         }
       }
       if (issued) {
@@ -250,7 +255,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue (128 threads)
-    const int quarter = warp & 3;
+    const int quarter = warp & 3;               // warps 3..6 -> TMEM lane quarters 3, 0, 1, 2
     const int r = quarter * 32 + lane;          // TMEM lane = query row in the tile
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const int qi = q0 + r;                      // sequence-relative query index
@@ -265,7 +270,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
         break;
       }
       tc_fence_after();
-      if (threadIdx.x == 64) trace_at(p, 5, j);
+      if (threadIdx.x == (kProducers + 1) * 32) trace_at(p, 5, j);
       float s[kBN];
 #pragma unroll
       for (int c = 0; c < kBN / 32; ++c) {
@@ -278,7 +283,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[b]);
-      if (threadIdx.x == 64) trace_at(p, 6, j);
+      if (threadIdx.x == (kProducers + 1) * 32) trace_at(p, 6, j);
       const int kbase = j * kBN;
       float mt = -INFINITY;
 #pragma unroll
@@ -311,7 +316,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
           break;
         }
         tc_fence_after();
-        if (threadIdx.x == 64) trace_at(p, 7, j);
+        if (threadIdx.x == (kProducers + 1) * 32) trace_at(p, 7, j);
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
           for (int c = 0; c < kD / 32; ++c) {
@@ -335,7 +340,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
-      if (threadIdx.x == 64) trace_at(p, 8, j);
+      if (threadIdx.x == (kProducers + 1) * 32) trace_at(p, 8, j);
     }
     // epilogue: O / l
     if (ok && n_tiles > 0 && mbar_wait(o_done, (n_tiles - 1) & 1, abort_flag, status, 670)) {
@@ -373,7 +378,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(AttnParams p, int* 
   __syncthreads();
   tc_fence_after();
   if (threadIdx.x == 0) trace_at(p, 9, 1);
-  if (warp == 1) tmem_dealloc(tmem, 512);
+  if (warp == kProducers) tmem_dealloc(tmem, 512);
 }
 
 int attn_fwd_tc_smem_bytes() { return (1 + 2 * kStages) * kTileBytes + 1024 + 256; }
@@ -385,7 +390,7 @@ void attn_fwd_tc(const AttnParams& p, int n_tiles, int* status, cudaStream_t st)
     cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_fwd_tc_smem_bytes());
     configured = true;
   }
-  attn_fwd_tc_kernel<<<dim3(n_tiles, p.Hq), 192, attn_fwd_tc_smem_bytes(), st>>>(p, status);
+  attn_fwd_tc_kernel<<<dim3(n_tiles, p.Hq), kThreads, attn_fwd_tc_smem_bytes(), st>>>(p, status);
 }
 
 }  // namespace octo
