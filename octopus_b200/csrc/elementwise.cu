@@ -11,20 +11,6 @@ namespace octo {
 
 using bf16 = __nv_bfloat16;
 
-__device__ __forceinline__ void load8(const bf16* p, float (&f)[8]) {
-  uint4 u = *reinterpret_cast<const uint4*>(p);
-  const bf16* b = reinterpret_cast<const bf16*>(&u);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) f[i] = __bfloat162float(b[i]);
-}
-__device__ __forceinline__ void store8(bf16* p, const float (&f)[8]) {
-  uint4 u;
-  u.x = pack_bf16x2(f[0], f[1]);
-  u.y = pack_bf16x2(f[2], f[3]);
-  u.z = pack_bf16x2(f[4], f[5]);
-  u.w = pack_bf16x2(f[6], f[7]);
-  *reinterpret_cast<uint4*>(p) = u;
-}
 
 // ----------------------------------------------------------------- head combine
 __global__ void head_combine_kernel(const float* __restrict__ part, int M, int T, const int32_t* __restrict__ labels,

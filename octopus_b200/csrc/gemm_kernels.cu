@@ -17,7 +17,7 @@ static void launch_one(const GemmLaunch& g, const Epi& epi) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     configured = true;
   }
-  kern<<<g.grid, kGemmThreads, Cfg::kSmemBytes, g.stream>>>(g.ta, g.tb, g.s, epi, g.status);
+  kern<<<g.grid, kGemmThreads, Cfg::kSmemBytes, g.stream>>>(ALocal<A_MN>{g.ta}, g.tb, g.s, epi, g.status);
 }
 
 template <int BN, class Epi>
@@ -54,7 +54,7 @@ void gemm_launch(const GemmLaunch& g) {
     if (g.bn == 256) launch_one<256, false, false>(g, e);
     else launch_one<128, false, false>(g, e);
   } else if (g.epi == kEpiSample) {
-    EpiSample e{g.partial, g.s.n_tiles, g.bn, g.alpha, g.vocab_limit, g.seed, g.row_offset};
+    EpiSample e{g.partial, g.s.n_tiles, g.bn, g.alpha, g.vocab_limit, g.seed, g.row_offset, g.col_base};
     if (g.bn == 256) launch_one<256, false, false>(g, e);
     else if (g.bn == 128) launch_one<128, false, false>(g, e);
     else launch_one<64, false, false>(g, e);

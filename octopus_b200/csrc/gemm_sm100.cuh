@@ -55,9 +55,35 @@ __device__ __forceinline__ void gemm_tile_coords(const GemmShape& s, int tile, i
   nb = r / gm;
 }
 
-template <int BN, bool A_MN, bool B_MN, class Epi>
+// ---------------------------------------------------------------- A-operand sources
+//
+// The producer asks its A source for the bytes of an M-block (the stage's expect-tx
+// count) and to issue the TMA loads of one (M-block, K-block) tile.  `signal()` runs
+// once per CTA before any wait, `finish_cta()` once per CTA after the last use.
+
+// One tensor map over a local matrix (K-major: [M, K]; MN-major: [K, M]).
+template <bool A_MN>
+struct ALocal {
+  CUtensorMap m;
+  __device__ __forceinline__ void prefetch() const { tma_prefetch_desc(&m); }
+  __device__ __forceinline__ void signal() const {}
+  __device__ __forceinline__ void finish_cta() const {}
+  __device__ __forceinline__ bool ready(int, uint32_t&, volatile int*, int*) const { return true; }
+  __device__ __forceinline__ uint32_t bytes(int) const { return kGemmBM * kGemmBK * 2; }
+  __device__ __forceinline__ void load(uint8_t* dst, uint64_t* bar, int k0, int mb) const {
+    const int m0 = mb * kGemmBM;
+    if constexpr (!A_MN) {
+      tma_load_2d(dst, &m, bar, k0, m0);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kGemmBM / 64; ++j) tma_load_2d(dst + j * 8192, &m, bar, m0 + 64 * j, k0);
+    }
+  }
+};
+
+template <int BN, bool A_MN, bool B_MN, class Epi, class ASrc = ALocal<A_MN>>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    gemm_tcgen05_kernel(const __grid_constant__ ASrc asrc_param, const __grid_constant__ CUtensorMap tmB,
                         GemmShape shape, Epi epi, int* status) {
   // (each thread works on its own copy of the epilogue functor)
   using Cfg = GemmCfg<BN>;
@@ -90,8 +116,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&tmA);
+    asrc_param.prefetch();
     tma_prefetch_desc(&tmB);
+    asrc_param.signal();
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -105,6 +132,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
+      const ASrc& asrc = asrc_param;
+      uint32_t ready_mask = 0;  // source ranks whose data this CTA has seen published
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
@@ -112,22 +141,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int tile = blockIdx.x; tile < shape.num_tiles && ok; tile += gridDim.x) {
         int mb, nb;
         gemm_tile_coords(shape, tile, mb, nb);
-        const int m0 = mb * kGemmBM, n0 = nb * BN;
+        const int n0 = nb * BN;
         for (int kb = 0; kb < shape.k_blocks; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, 100 + stage)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
           const int k0 = kb * kGemmBK;
           uint8_t* a_dst = sA + stage * Cfg::kABytes;
           uint8_t* b_dst = sB + stage * Cfg::kBBytes;
-          if constexpr (!A_MN) {
-            tma_load_2d(a_dst, &tmA, &full_bar[stage], k0, m0);
-          } else {
-#pragma unroll
-            for (int j = 0; j < kGemmBM / 64; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full_bar[stage], m0 + 64 * j, k0);
+          if (kb == 0 && !asrc.ready(mb, ready_mask, abort_flag, status)) {  // peer data of this M-block published?
+            ok = false;
+            break;
           }
+          mbar_arrive_expect_tx(&full_bar[stage], asrc.bytes(mb) + Cfg::kBBytes);
+          asrc.load(a_dst, &full_bar[stage], k0, mb);
           if constexpr (!B_MN) {
             tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, n0);
           } else {
@@ -260,6 +288,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  if (threadIdx.x == 0) asrc_param.finish_cta();
 }
 
 // ---------------------------------------------------------------- epilogues

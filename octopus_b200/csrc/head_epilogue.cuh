@@ -115,6 +115,7 @@ struct EpiSample {
   int vocab_limit;
   uint64_t seed;
   const int64_t* row_stream;
+  int col_base;    // global vocabulary index of local column 0 (vocab-parallel shards)
   float m, s, best;
   int best_col;
   uint32_t key;
@@ -150,10 +151,10 @@ struct EpiSample {
     for (int i = 0; i < 32; ++i) {
       if (v[i] != -INFINITY) {
         cs += __expf(v[i] - nm);
-        const float g = v[i] + gumbel_noise(key, static_cast<uint32_t>(col0 + i));
+        const float g = v[i] + gumbel_noise(key, static_cast<uint32_t>(col_base + col0 + i));
         if (g > best) {
           best = g;
-          best_col = col0 + i;
+          best_col = col_base + col0 + i;
         }
       }
     }

@@ -42,7 +42,7 @@ static cudaStream_t cur_stream(const torch::Tensor& t) {
 #define CBF(x) reinterpret_cast<const __nv_bfloat16*>((x).data_ptr())
 
 // ------------------------------------------------------------------ GEMM
-static int pick_bn(int M, int N, int sms, int hint) {
+int pick_bn(int M, int N, int sms, int hint) {
   if (hint == 64 || hint == 128 || hint == 256) return hint;
   const int mt = (M + 127) / 128;
   auto tiles = [&](int bn) { return mt * ((N + bn - 1) / bn); };
@@ -532,12 +532,14 @@ void attn_decode_persistent_t(torch::Tensor q, torch::Tensor kc, torch::Tensor v
 }
 
 void register_comm(py::module& m);
+void register_tp(py::module& m);
 
 }  // namespace octo
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   using namespace octo;
   register_comm(m);
+  register_tp(m);
   m.doc() = "octopus_b200 sm_100a kernels";
   m.def("status_tensor", [](int64_t d) { return status_tensor(static_cast<int>(d)); });
   m.def("gemm_out", &gemm_out, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("C"),

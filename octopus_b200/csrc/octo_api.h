@@ -39,6 +39,7 @@ struct GemmLaunch {
   uint64_t seed;           // sampling RNG seed
   const int64_t* row_offset;  // sampling: per-row RNG stream id (may be null)
   int vocab_limit;         // columns >= vocab_limit are masked (padding)
+  int col_base;            // sampling: global vocabulary index of local column 0
   const void* bias;        // bf16 [N] bias added in the bf16 epilogue (may be null)
   const float* lse;        // head grad: per-row log-normaliser
   const float* ent;        // head grad: per-row entropy

@@ -50,6 +50,9 @@ inline int num_sms(int device) {
   return cached[device];
 }
 
+// GEMM N-tile width for an M x N problem on `sms` SMs (hint 64/128/256 forces it).
+int pick_bn(int M, int N, int sms, int hint);
+
 // Status word: int32[2] per device = {code, where}.  Zero means OK.
 int* status_ptr(int device);
 torch::Tensor status_tensor(int device);

@@ -63,6 +63,9 @@ PRESETS = {
     # tiny random-init decoder for exactness tests
     "tiny": ModelConfig("tiny", vocab_size=4096, hidden=256, layers=2, heads=4, kv_heads=4, head_dim=64, ffn=688,
                         rope_theta=10000.0, qkv_bias=False),
+    # small GQA decoder with head_dim 128 for the tensor-parallel engine tests (tp <= 4)
+    "tiny-tp": ModelConfig("tiny-tp", vocab_size=4096, hidden=512, layers=2, heads=8, kv_heads=4, head_dim=128,
+                           ffn=1024, rope_theta=10000.0),
     "qwen2.5-1.5b": ModelConfig("qwen2.5-1.5b", vocab_size=151936, hidden=1536, layers=28, heads=12, kv_heads=2,
                                 head_dim=128, ffn=8960, tie_embeddings=True),
     "qwen2.5-7b": ModelConfig("qwen2.5-7b", vocab_size=152064, hidden=3584, layers=28, heads=28, kv_heads=4,

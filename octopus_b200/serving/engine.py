@@ -114,7 +114,8 @@ class Engine:
             raise RuntimeError("octopus_b200._native (KV manager) is not built")
         self.cfg, self.w = cfg, weights
         self.device = torch.device(device)
-        kvw = cfg.kv_width
+        hq_loc, hkv_loc = self._local_heads()
+        kvw = hkv_loc * cfg.head_dim
         if kv_slots is None:
             per = 2 * cfg.layers * kvw * 2
             kv_slots = max(4096, int((kv_bytes or (8 << 30)) // per))
@@ -135,7 +136,7 @@ class Engine:
         self._rid = itertools.count(1)
         self._cid = itertools.count(1)
         splits = num_splits or 8
-        self.dec_attn = ops.DecodeAttention(cfg.heads, cfg.kv_heads, cfg.head_dim, max_batch, splits, self.device)
+        self.dec_attn = ops.DecodeAttention(hq_loc, hkv_loc, cfg.head_dim, max_batch, splits, self.device)
         # static decode buffers (graph inputs)
         B = max_batch
         dev = self.device
@@ -162,6 +163,14 @@ class Engine:
                       "prefill_s": 0.0, "decode_s": 0.0}
 
     # ------------------------------------------------------------------ helpers
+    def _local_heads(self) -> tuple[int, int]:
+        """(query heads, KV heads) this process computes and caches."""
+        return self.cfg.heads, self.cfg.kv_heads
+
+    def _pad_rows(self, T: int) -> int:
+        """Rows a prefill forward of T tokens is padded to."""
+        return (T + 7) // 8 * 8
+
     def new_cursor_id(self) -> str:
         return f"c{next(self._cid)}"
 
@@ -294,7 +303,7 @@ class Engine:
                     cu_k_own.append(cu_k_own[-1] + len(ko))
                 last.append(cu_q[-1] - 1)
             T = cu_q[-1]
-            pad = (-T) % 8
+            pad = self._pad_rows(T) - T
             if pad:
                 ids.append(np.zeros(pad, np.int32))
                 pos.append(np.zeros(pad, np.int64))
@@ -313,25 +322,41 @@ class Engine:
                 cu_q, cu_k_own, np.concatenate(keys_own).astype(np.int32), dev)
             mset = set(self.mount_layers or [])
             scale = cfg.head_dim ** -0.5
+            hq, hkv = self._local_heads()
 
             def attn(q, i):
                 p = plan if (self.mount_layers is None or i in mset) else plan_own
-                return sv.prefill_attn(q, self.kc[i], self.vc[i], p, cfg.heads, cfg.kv_heads, cfg.head_dim, scale)
+                return sv.prefill_attn(q, self.kc[i], self.vc[i], p, hq, hkv, cfg.head_dim, scale)
 
-            x = sv.embed(t_ids, self.w["embed"])
-            for i in range(cfg.layers):
-                x = self._layer(x, i, t_pos, t_slots, attn)
-            rows = h2d(np.asarray(last, np.int64), dev)
-            h = self._final(x.index_select(0, rows))
-            streams = h2d(np.asarray([(reqs[j].rid << 32) | (reqs[j].first_pos + len(reqs[j].new_tokens))
-                                      for j in g], np.int64), dev)
-            tok, lp = ops.sample(h, self.w.head, temperature, self.seed, streams, cfg.vocab_size)
-            tok, lp = d2h(tok).numpy(), d2h(lp).numpy()
+            streams = np.asarray([(reqs[j].rid << 32) | (reqs[j].first_pos + len(reqs[j].new_tokens)) for j in g],
+                                 np.int64)
+            tok, lp = self._prefill_forward(t_ids, t_pos, t_slots, attn, np.asarray(last, np.int64), streams,
+                                            temperature)
             for k, j in enumerate(g):
                 first_tok[j] = tok[k]
                 first_lp[j] = lp[k]
             self.stats["prefill_tokens"] += T
         return first_tok, first_lp
+
+    def _prefill_forward(self, t_ids, t_pos, t_slots, attn, last: np.ndarray, streams: np.ndarray,
+                         temperature: float):
+        """Forward of a padded prefill batch; samples the rows `last`; host (tokens, logprobs)."""
+        cfg, dev = self.cfg, self.device
+        x = sv.embed(t_ids, self.w["embed"])
+        for i in range(cfg.layers):
+            x = self._layer(x, i, t_pos, t_slots, attn)
+        h = self._final(x.index_select(0, h2d(last, dev)))
+        tok, lp = ops.sample(h, self.w.head, temperature, self.seed, h2d(streams, dev), cfg.vocab_size)
+        return d2h(tok).numpy(), d2h(lp).numpy()
+
+    def _decode_forward(self, tok, pos, slot, attn, B: int, temperature: float):
+        """One decode forward of B rows; returns device (tokens, logprobs)."""
+        cfg = self.cfg
+        x = sv.embed(tok, self.w["embed"])
+        for i in range(cfg.layers):
+            x = self._layer(x, i, pos, slot, attn)
+        h = self._final(x)
+        return ops.sample(h, self.w.head, temperature, self.seed, self.s_stream[:B], cfg.vocab_size)
 
     # ------------------------------------------------------------------ decode
     def _decode_step(self, B: int, temperature: float):
@@ -352,11 +377,7 @@ class Engine:
                 return self.dec_attn(q, self.kc[i], self.vc[i], start, self.kv_indices, kv_len=att_len)
             return self.dec_attn(q, self.kc[i], self.vc[i], start_o, self.kv_indices_own, kv_len=len_o)
 
-        x = sv.embed(tok, self.w["embed"])
-        for i in range(cfg.layers):
-            x = self._layer(x, i, pos, slot, attn)
-        h = self._final(x)
-        new_tok, lp = ops.sample(h, self.w.head, temperature, self.seed, self.s_stream[:B], cfg.vocab_size)
+        new_tok, lp = self._decode_forward(tok, pos, slot, attn, B, temperature)
         step = self.s_step.expand(B)[:, None]
         self.s_out_tok[:B].scatter_(1, step, new_tok[:, None])
         self.s_out_lp[:B].scatter_(1, step, lp[:, None])
@@ -369,10 +390,13 @@ class Engine:
         self.s_step.add_(1)
 
     def _bucket(self, n: int) -> int:
-        b = 8
+        b = self._min_bucket()
         while b < n:
             b *= 2
         return min(b, self.max_batch)
+
+    def _min_bucket(self) -> int:
+        return 8
 
     def _ensure_out(self, steps: int):
         if self.s_out_tok is None or self.s_out_tok.shape[1] < steps:
