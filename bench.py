@@ -7,9 +7,13 @@ instances x 4 samples), bf16, synthetic tokens, random-init weights.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl octopus|reference]
 
 N > 1 is launched by torchrun (one rank per GPU).  Scaling is strong: the whole config
-(32 x 4 DAG samples) is split across the ranks.  `value` = generated tokens of all ranks
-per second of device time (CUDA events on each rank, max over ranks), every generated
-token is also trained once.  `e2e` = the same metric from the per-step wall clock of the
+(32 x 4 DAG samples) is split across N / tp rollout replicas, each a tensor-parallel
+group of `--tp` GPUs (default 2, the config's TP=2) running the fused AG->GEMM /
+GEMM->RS engine; the actor is ZeRO-sharded over all N ranks (fused peer-memory
+reduce-scatter + AdamW + all-gather), and the ranks of a TP group split the training of
+their group's rollout.  `value` = generated tokens of all replicas per second of device
+time (CUDA events on each rank, max over ranks), every generated token is also trained
+once.  `e2e` = the same metric from the per-step wall clock of the
 public `RLTrainer.step()` API, whose timed region includes the host->device copies of
 each step's inputs (prompts, tree plans) from pinned memory and the device->host reads
 of the results (sampled tokens, logprobs, loss).
@@ -48,6 +52,9 @@ def parse():
     ap.add_argument("--kv-gb", type=float, default=0.0, help="KV pool size (0: sized from the config)")
     ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke tests only)")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--tp", type=int, default=0, help="rollout tensor parallelism (0: 2 when N is even, else 1)")
+    ap.add_argument("--actor", default="sharded", choices=["sharded", "dp"],
+                    help="N > 1 actor: ZeRO-sharded with fused peer-memory kernels, or replicated + NCCL all-reduce")
     return ap.parse_args()
 
 
@@ -120,9 +127,11 @@ def main():
     from octopus_b200.envs.dag import DagConfig, MultiAgentDag
     from octopus_b200.models.config import get_config
     from octopus_b200.parallel.dp import DataParallel
+    from octopus_b200.parallel.fsdp import ShardedActor
     from octopus_b200.rl.actor import Actor
     from octopus_b200.rl.trainer import RLTrainer, TrainerConfig
     from octopus_b200.serving.engine import Engine
+    from octopus_b200.serving.tp_engine import TPEngine
     from octopus_b200.utils import iostats
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -137,26 +146,43 @@ def main():
 
     over = {"layers": args.layers} if args.layers else {}
     cfg = get_config(args.model, **over)
-    # strong scaling: this rank's share of the DAG instances
-    inst = [i for i in range(args.instances) if i % world == rank]
+    tp = args.tp or (2 if world % 2 == 0 else 1)
+    if world % tp:
+        raise SystemExit(f"--tp {tp} must divide the {world} GPUs")
+    replicas = world // tp
+    rep, tp_rank = rank // tp, rank % tp
+    tp_group = None
+    if tp > 1:
+        for r in range(replicas):  # every rank creates every group, in the same order
+            g = dist.new_group(list(range(r * tp, (r + 1) * tp)))
+            if r == rep:
+                tp_group = g
+    # strong scaling: this replica's share of the DAG instances
+    inst = [i for i in range(args.instances) if i % replicas == rep]
     dcfg = DagConfig(instances=args.instances, samples=args.samples, prefix_len=args.prefix, turn_len=args.turn,
-                     role_len=args.role, seed=1000 + rank)
+                     role_len=args.role, seed=1000 + rep)
     env = MultiAgentDag(cfg.vocab_size, dcfg)
-    actor = Actor(cfg, dev, seed=0)
+    sharded = world > 1 and args.actor == "sharded"
+    actor = ShardedActor(cfg, dev, seed=0) if sharded else Actor(cfg, dev, seed=0)
     per_inst = args.prefix + args.samples * (4 * (args.turn + args.role) + 2)
     kv_slots = int(len(inst) * per_inst * 1.15) + 8192
     if args.kv_gb:
-        kv_slots = int(args.kv_gb * (1 << 30) / (4 * cfg.layers * cfg.kv_width))
-    max_batch = max(8, 1 << (len(inst) * args.samples * 2 - 1).bit_length())
-    engine = Engine(cfg, actor.weights, kv_slots=kv_slots, max_batch=max_batch, device=dev,
-                    use_graphs=not args.no_graphs)
-    dp = DataParallel(actor) if world > 1 else None
+        kv_slots = int(args.kv_gb * (1 << 30) / (4 * cfg.layers * cfg.kv_width // tp))
+    max_batch = max(8 * tp, 1 << (len(inst) * args.samples * 2 - 1).bit_length())
+    if tp > 1:
+        engine = TPEngine(cfg, actor.weights, group=tp_group, kv_slots=kv_slots, max_batch=max_batch, device=dev,
+                          use_graphs=not args.no_graphs)
+    else:
+        engine = Engine(cfg, actor.weights, kv_slots=kv_slots, max_batch=max_batch, device=dev,
+                        use_graphs=not args.no_graphs)
+    dp = DataParallel(actor) if world > 1 and not sharded else None
 
     class _Env:
         def rollout(self, eng):
             return env.rollout(eng, inst)
 
-    trainer = RLTrainer(actor, engine, _Env(), TrainerConfig(mb_tokens=args.mb_tokens))
+    trainer = RLTrainer(actor, engine, _Env(), TrainerConfig(mb_tokens=args.mb_tokens, mb_shard=(tp_rank, tp)),
+                        sync_fn=engine.sync_weights if tp > 1 else None)
     if dp is not None:
         dp.attach(trainer)
 
@@ -171,6 +197,7 @@ def main():
     barrier()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
+    e0 = dict(engine.stats)
     clocks.start()
     iostats.reset()
     l0 = ops.launches()
@@ -182,7 +209,7 @@ def main():
         st = trainer.step()
         torch.cuda.synchronize()
         wall.append(time.perf_counter() - t0)
-        gen += st["generated_tokens"]
+        gen += st["generated_tokens"] if tp_rank == 0 else 0  # a TP group's rollout counted once
         stats.append(st)
     end.record()
     torch.cuda.synchronize()
@@ -217,7 +244,9 @@ def main():
             "config": {"model": args.model + (f"-L{args.layers}" if args.layers else ""),
                        "global_batch": args.instances * args.samples,
                        "seq_len": args.prefix + 4 * (args.turn + args.role),
-                       "parallelism": f"dp{n_gpus} (rollout replica + actor per GPU)",
+                       "parallelism": (f"rollout tp{tp} x {replicas} replicas (fused AG->GEMM / GEMM->RS), "
+                                       f"actor {'zero-sharded fused' if sharded else 'replicated'} over {n_gpus}"
+                                       if n_gpus > 1 else "single GPU (rollout engine + actor colocated)"),
                        "dag": "planner->2 solvers->verifier, prefix mounted zero-copy",
                        "instances": args.instances, "samples": args.samples, "prefix": args.prefix,
                        "turn": args.turn, "tokens_counted": "generated (= trained) tokens per RL step",
@@ -229,10 +258,19 @@ def main():
             "gpu_launches": int(launches),
             "phases_s": {"rollout": round(s0["rollout_s"], 3), "train": round(s0["train_s"], 3),
                          "sync": round(s0["sync_s"], 4)},
+            "engine_per_step": {k: round((engine.stats[k] - e0[k]) / args.steps, 3)
+                                for k in ("prefill_s", "decode_s", "decode_steps", "prefill_tokens", "cached_tokens")},
             "tree_tokens": s0.get("tree_tokens"), "flat_tokens": s0.get("flat_tokens"),
         }
         print(json.dumps(out), flush=True)
     if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
+        if tp > 1:
+            engine._graphs.clear()
+            engine.close()
+        if sharded:
+            actor.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -2,7 +2,7 @@
 //
 //   AG -> GEMM   the persistent tcgen05 GEMM with an A source that TMA-loads each
 //                128-row block of the sequence-sharded activation straight from the
-//                rank that owns it (peer memory, no multicast, no staging copy).  Every
+//                rank that owns it (plain tiled TMA loads of peer memory, no staging copy).  Every
 //                CTA publishes "my shard is ready" to the peers when it starts and waits
 //                (bounded) for a peer's publication before its first load from that peer,
 //                so the transfer overlaps the MMAs tile by tile.

@@ -139,6 +139,7 @@ class Actor:
             for k, v in st.items():
                 stats[k] = stats.get(k, 0.0) + v.detach() * (1.0 if k == "tokens" else float(mb.pair_w.sum()))
             stats["loss"] = stats.get("loss", 0.0) + loss.detach()
+        stats.setdefault("loss", torch.zeros((), device=self.device))  # a rank with no micro-batch this step
         tok = float(sum(mb.pair_w.sum() for mb in mbs)) or 1.0
         return {k: (v if k in ("tokens", "loss") else v / tok) for k, v in stats.items()}
 

@@ -31,6 +31,9 @@ from .actor import Actor, build_microbatch
 class TrainerConfig:
     mb_tokens: int = 32768      # prefix-tree tokens per micro-batch (flat estimate)
     sync_every: int = 1
+    # (index, count): train every count-th micro-batch starting at index.  Ranks of one
+    # tensor-parallel rollout group hold the same rollout and split its training this way.
+    mb_shard: tuple = (0, 1)
 
 
 class RLTrainer:
@@ -45,6 +48,9 @@ class RLTrainer:
 
     def train_on(self, ro) -> dict:
         mbs = instance_microbatches(ro, self.cfg.mb_tokens, build_microbatch)
+        k, n = self.cfg.mb_shard
+        if n > 1:
+            mbs = mbs[k::n]
         stats = self.actor.train_step(mbs)
         stats["micro_batches"] = len(mbs)
         stats["tree_tokens"] = sum(mb.n_tree for mb in mbs)

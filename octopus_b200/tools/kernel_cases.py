@@ -10,6 +10,10 @@ Cases (inputs sized above L2 where DRAM behaviour matters, a few GB at most):
   attn_bwd           tree attention backward (dq + dkv kernels)
   decode_splitk      paged decode, 256 requests x 3000 keys (split-K kernel)
   decode_persistent  same on the persistent producer/consumer kernel
+  decode_dag         persistent decode with the DAG solver stage's sharing: 32 instances x
+                     8 rows; each row = shared 2048-token prefix + planner segment (shared
+                     by 2 rows) + own 272 tokens
+  decode_dag_flat    same lengths, every row's keys distinct (no sharing)
   head_fwd           fused logprob head, 4096 rows x 152064 vocab
   sample_head        fused sampling head, 256 rows x 152064 vocab
 """
@@ -49,6 +53,36 @@ def decode_case(dev):
     return q, kc, vc, ip, idx, Hq, Hkv, D, B
 
 
+def decode_dag_case(dev, share: bool):
+    Hq, Hkv, D = 28, 4, 128
+    n_inst, per, pre, plan, own = 32, 8, 2048, 528, 272
+    B = n_inst * per
+    rows, nxt = [], 0
+
+    def take(n):
+        nonlocal nxt
+        r = np.arange(nxt, nxt + n)
+        nxt += n
+        return r
+
+    for i in range(n_inst):
+        p = take(pre)
+        for s in range(per // 2):
+            pl = take(plan)
+            for k in range(2):
+                if share:
+                    rows.append(np.concatenate([p, pl, take(own)]))
+                else:
+                    rows.append(take(pre + plan + own))
+    L = len(rows[0])
+    idx = torch.from_numpy(np.concatenate(rows).astype(np.int32)).to(dev)
+    kc = torch.randn(nxt, Hkv * D, device=dev).bfloat16()
+    vc = torch.randn(nxt, Hkv * D, device=dev).bfloat16()
+    ip = torch.arange(0, B + 1, device=dev, dtype=torch.int32) * L
+    q = torch.randn(B, Hq * D, device=dev).bfloat16()
+    return q, kc, vc, ip, idx, Hq, Hkv, D, B
+
+
 def build(case: str, dev):
     if case == "gemm_fwd_7b":
         A = torch.randn(16384, 3584, device=dev).bfloat16()
@@ -75,6 +109,10 @@ def build(case: str, dev):
     if case in ("decode_splitk", "decode_persistent"):
         q, kc, vc, ip, idx, Hq, Hkv, D, B = decode_case(dev)
         da = ops.DecodeAttention(Hq, Hkv, D, B, 8, dev, persistent=case == "decode_persistent")
+        return lambda: da(q, kc, vc, ip, idx)
+    if case in ("decode_dag", "decode_dag_flat"):
+        q, kc, vc, ip, idx, Hq, Hkv, D, B = decode_dag_case(dev, case == "decode_dag")
+        da = ops.DecodeAttention(Hq, Hkv, D, B, 8, dev, persistent=True)
         return lambda: da(q, kc, vc, ip, idx)
     if case in ("head_fwd", "sample_head"):
         M = 4096 if case == "head_fwd" else 256
