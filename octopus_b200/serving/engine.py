@@ -103,6 +103,7 @@ class _Req:
     radix_handle: int = -1
     out_tok: list = field(default_factory=list)
     out_lp: list = field(default_factory=list)
+    mount_at: list = field(default_factory=list)
 
 
 class Engine:
@@ -161,6 +162,10 @@ class Engine:
         self._graph_steps = 0
         self.stats = {"prefill_tokens": 0, "cached_tokens": 0, "decode_steps": 0, "requests": 0,
                       "prefill_s": 0.0, "decode_s": 0.0}
+        # interaction records for training (reply id -> tokens, completion range, behaviour
+        # logprobs, mounts, weight version); enabled by `record_interactions = True`
+        self.record_interactions = False
+        self.records: dict[str, dict] = {}
 
     # ------------------------------------------------------------------ helpers
     def _local_heads(self) -> tuple[int, int]:
@@ -229,7 +234,9 @@ class Engine:
                 self.radix.release_handle(handle)
                 handle = -1
         # mounts: splice rows of other cursors (K2: next = max(own next, last mounted + 1))
+        mount_at = []
         for (src, a, b) in inp.mount:
+            mount_at.append(sum(len(x) for x in ctx_t))
             sc = self.cursors.get(src)
             if sc is None:
                 raise CursorNotFound(src)
@@ -244,6 +251,7 @@ class Engine:
         cat = (lambda xs, dt: np.concatenate(xs).astype(dt) if xs else np.empty(0, dt))
         r = _Req(inp, rid, cat(ctx_t, np.int32), cat(ctx_s, np.int64), cat(ctx_p, np.int64), cat(ctx_m, bool), new,
                  next_pos, cached=cached, radix_handle=handle)
+        r.mount_at = mount_at
         if len(new) == 0:
             raise ValueError("request has no new tokens to prefill")
         return r
@@ -573,6 +581,14 @@ class Engine:
             if r.radix_handle >= 0:
                 self.radix.unlock(r.radix_handle)
                 self.radix.release_handle(r.radix_handle)
+            if self.record_interactions and cid is not None:
+                prompt = np.concatenate([r.ctx_tokens, r.new_tokens]).astype(np.int32)
+                self.records[cid] = {"tokens": np.concatenate([prompt, np.asarray(toks, np.int32)]),
+                                     "prompt_len": len(prompt), "completion": len(toks),
+                                     "logprobs": np.asarray(lps, np.float32), "parent": r.inp.cursor,
+                                     "mounts": [(at, m[0], int(m[1]), int(m[2]))
+                                                for at, m in zip(r.mount_at, r.inp.mount)],
+                                     "version": self.version}
             self.stats["cached_tokens"] += r.cached
             self.stats["requests"] += 1
             outs.append(GenOutput(toks, lps, cid, n_new, r.cached, r.first_pos, reason))
