@@ -53,6 +53,7 @@ __device__ __forceinline__ void gemm_tile_coords(const GemmShape& s, int tile, i
   const int r = tile - group * group_span;
   mb = first_m + r % gm;
   nb = r / gm;
+  if (s.m_shift) mb = (mb + s.m_shift) % s.m_tiles;
 }
 
 // ---------------------------------------------------------------- A-operand sources
@@ -68,6 +69,7 @@ struct ALocal {
   __device__ __forceinline__ void prefetch() const { tma_prefetch_desc(&m); }
   __device__ __forceinline__ void signal() const {}
   __device__ __forceinline__ void finish_cta() const {}
+  __device__ __forceinline__ void prologue(int, volatile int*, int*) const {}
   __device__ __forceinline__ bool ready(int, uint32_t&, volatile int*, int*) const { return true; }
   __device__ __forceinline__ uint32_t bytes(int) const { return kGemmBM * kGemmBK * 2; }
   __device__ __forceinline__ void load(uint8_t* dst, uint64_t* bar, int k0, int mb) const {
@@ -246,6 +248,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue warps
+    asrc_param.prologue(threadIdx.x - 64, abort_flag, status);  // (A-source staging work, if any)
     const int quarter = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     int acc = 0;

@@ -58,9 +58,11 @@ static GemmLaunch base_launch(int M, const torch::Tensor& W, int bn_hint) {
   return g;
 }
 
+// stage: local bf16 [tp * rows_s, K] staging buffer; work: local int32 counters
+// [1 + m_tiles], zero between calls (the kernel's last CTA resets them).
 static AgLaunch ag_launch(const std::vector<int64_t>& x_ptrs, int64_t rows_s, int64_t ldx, const torch::Tensor& W,
                           int64_t me, int64_t sync_local, const std::vector<int64_t>& sync_ptrs, int64_t slot,
-                          int64_t bn_hint) {
+                          int64_t bn_hint, const torch::Tensor& stage, const torch::Tensor& work) {
   check_rows_s(rows_s);
   TORCH_CHECK(x_ptrs.size() == sync_ptrs.size(), "ag_gemm: one shard pointer per rank");
   AgLaunch L{};
@@ -69,8 +71,24 @@ static AgLaunch ag_launch(const std::vector<int64_t>& x_ptrs, int64_t rows_s, in
   L.rows_s = static_cast<int>(rows_s);
   L.box_rows = static_cast<int>(std::min<int64_t>(128, rows_s));
   const int K = W.size(1);
-  for (int r = 0; r < tp; ++r)
-    L.a[r] = make_tmap_bf16_2d(reinterpret_cast<const void*>(x_ptrs[r]), K, rows_s, ldx, 64, L.box_rows);
+  TORCH_CHECK(K % 8 == 0 && ldx % 8 == 0, "ag_gemm: K and the shard row stride must be multiples of 8");
+  TORCH_CHECK(stage.scalar_type() == torch::kBFloat16 && stage.is_contiguous() &&
+                  stage.numel() >= static_cast<int64_t>(tp) * rows_s * K,
+              "ag_gemm: staging buffer too small");
+  TORCH_CHECK(work.scalar_type() == torch::kInt32 && work.is_contiguous() && work.numel() >= 1 + L.g.s.m_tiles,
+              "ag_gemm: work counters too small");
+  auto* st = reinterpret_cast<__nv_bfloat16*>(stage.data_ptr());
+  for (int r = 0; r < tp; ++r) {
+    L.peer_x[r] = reinterpret_cast<const void*>(x_ptrs[r]);
+    if (r == me)
+      L.a[r] = make_tmap_bf16_2d(reinterpret_cast<const void*>(x_ptrs[r]), K, rows_s, ldx, 64, L.box_rows);
+    else
+      L.a[r] = make_tmap_bf16_2d(st + static_cast<size_t>(r) * rows_s * K, K, rows_s, K, 64, L.box_rows);
+  }
+  L.ldx = static_cast<int>(ldx);
+  L.stage = stage.data_ptr();
+  L.work = work.data_ptr<int>();
+  if (rows_s >= 128) L.g.s.m_shift = static_cast<int>(me * rows_s / 128);  // own rows first: no copy to wait for
   L.slot = make_slot(sync_local, sync_ptrs, me, slot);
   L.peer_grid = L.g.grid;  // identical shapes on every rank -> identical grids
   return L;
@@ -79,9 +97,9 @@ static AgLaunch ag_launch(const std::vector<int64_t>& x_ptrs, int64_t rows_s, in
 // C[tp*rows_s, N] (bf16) = AG(x shards)[tp*rows_s, K] @ W[N, K]^T (+ bias)
 void ag_gemm_t(std::vector<int64_t> x_ptrs, int64_t rows_s, int64_t ldx, torch::Tensor W, torch::Tensor C,
                c10::optional<torch::Tensor> bias, int64_t me, int64_t sync_local, std::vector<int64_t> sync_ptrs,
-               int64_t slot, int64_t bn_hint) {
+               int64_t slot, int64_t bn_hint, torch::Tensor stage, torch::Tensor work) {
   c10::cuda::CUDAGuard guard(W.get_device());
-  AgLaunch L = ag_launch(x_ptrs, rows_s, ldx, W, me, sync_local, sync_ptrs, slot, bn_hint);
+  AgLaunch L = ag_launch(x_ptrs, rows_s, ldx, W, me, sync_local, sync_ptrs, slot, bn_hint, stage, work);
   TORCH_CHECK(C.is_cuda() && C.scalar_type() == torch::kBFloat16 && C.dim() == 2 && C.size(0) == L.g.s.M &&
                   C.size(1) == L.g.s.N && C.stride(1) == 1 && C.stride(0) % 8 == 0,
               "ag_gemm: C must be bf16 [tp*rows_s, N]");
@@ -159,9 +177,10 @@ std::vector<torch::Tensor> tp_sample_head_t(std::vector<int64_t> x_ptrs, int64_t
                                             double alpha, int64_t seed, torch::Tensor row_stream, int64_t vocab_limit,
                                             int64_t col_base, int64_t me, int64_t sync_local,
                                             std::vector<int64_t> sync_ptrs, int64_t slot_ag, int64_t slot_smp,
-                                            std::vector<int64_t> xch_ptrs, torch::Tensor xch_local) {
+                                            std::vector<int64_t> xch_ptrs, torch::Tensor xch_local,
+                                            torch::Tensor stage, torch::Tensor work) {
   c10::cuda::CUDAGuard guard(W.get_device());
-  AgLaunch L = ag_launch(x_ptrs, rows_s, ldx, W, me, sync_local, sync_ptrs, slot_ag, 0);
+  AgLaunch L = ag_launch(x_ptrs, rows_s, ldx, W, me, sync_local, sync_ptrs, slot_ag, 0, stage, work);
   const int M = L.g.s.M;
   TORCH_CHECK(row_stream.scalar_type() == torch::kInt64 && row_stream.is_contiguous() && row_stream.numel() == M,
               "tp_sample_head: one stream id per row");

@@ -11,6 +11,7 @@ namespace octo {
 struct GemmShape {
   int M, N, K;
   int m_tiles, n_tiles, k_blocks, num_tiles;
+  int m_shift;  // M-block rotation of the tile order (tensor-parallel: own rows first)
 };
 
 enum GemmEpiKind : int {

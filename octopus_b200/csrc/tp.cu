@@ -78,8 +78,23 @@ __device__ bool wait_peers(const TpSlot& s, int target, int* status, int where) 
 }  // namespace
 
 // ---------------------------------------------------------------- AG -> GEMM A source
+constexpr int kChunkRows = 8;  // staging copy granularity (rows of one peer shard)
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 struct AGather {
   CUtensorMap m[kMaxTp];
+  const __nv_bfloat16* peer_x[kMaxTp];
+  __nv_bfloat16* stage;
+  int* work;
+  int ldx, K, M, m_tiles;
   int rows_s, box_rows;
   TpSlot slot;
   int peer_grid;
@@ -88,7 +103,75 @@ struct AGather {
     for (int r = 0; r < slot.tp; ++r) tma_prefetch_desc(&m[r]);
   }
   __device__ __forceinline__ void signal() const { signal_peers(slot); }
-  __device__ __forceinline__ void finish_cta() const { consume(slot, peer_grid); }
+  // remote rows of M-block mb, in chunks
+  __device__ __forceinline__ int remote_chunks(int mb) const {
+    const int g0 = mb * kGemmBM, g1 = min(M, g0 + kGemmBM);
+    const int o0 = max(g0, slot.me * rows_s), o1 = min(g1, (slot.me + 1) * rows_s);
+    return ((g1 - g0) - max(0, o1 - o0)) / kChunkRows;
+  }
+  // Epilogue warps of every CTA: copy peer chunks into the staging buffer until the work
+  // counter runs out (so the copy never depends on which CTAs are resident).
+  __device__ void prologue(int t, volatile int* abort, int* status) const {
+    const int per_rank = rows_s / kChunkRows;
+    const int total = (slot.tp - 1) * per_rank;
+    const int cpr = K / 8;                       // 16-byte pieces per row
+    __shared__ int chunk;
+    uint32_t seen = 0;
+    for (;;) {
+      if (t == 0) chunk = atomicAdd(work, 1);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const int c = chunk;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (c >= total) break;
+      const int ri = c / per_rank;
+      const int r = ri < slot.me ? ri : ri + 1;
+      const int l0 = (c - ri * per_rank) * kChunkRows;
+      if (!((seen >> r) & 1u)) {
+        // the peer's shard is complete once any of its CTAs has signalled this call
+        if (t == 0 && !wait_ge(slot.flags + r, 1, abort, status, 950 + r)) chunk = -1;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (chunk < 0) return;
+        seen |= 1u << r;
+      }
+      const __nv_bfloat16* src = peer_x[r] + static_cast<size_t>(l0) * ldx;
+      __nv_bfloat16* dst = stage + (static_cast<size_t>(r) * rows_s + l0) * K;
+      for (int p = t; p < kChunkRows * cpr; p += 128) {
+        const int row = p / cpr, col = (p - row * cpr) * 8;
+        *reinterpret_cast<uint4*>(dst + static_cast<size_t>(row) * K + col) =
+            *reinterpret_cast<const uint4*>(src + static_cast<size_t>(row) * ldx + col);
+      }
+      fence_proxy_async_global();  // generic-proxy stores -> the producers' TMA reads
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (t == 0) red_release_gpu_add(work + 1 + (r * rows_s + l0) / kGemmBM, 1);
+    }
+  }
+  __device__ bool ready(int mb, uint32_t&, volatile int* abort, int* status) const {
+    const int need = remote_chunks(mb);
+    if (need == 0) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_gpu(work + 1 + mb) < need) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > OCTO_WAIT_NS) {
+        record_error(status, kErrPeerTimeout, 940);
+        *abort = 1;
+        return false;
+      }
+      __nanosleep(64);
+    }
+    fence_proxy_async_global();
+    return true;
+  }
+  // Last CTA: reset the staging counters and consume the peers' signals of this call.
+  __device__ __forceinline__ void finish_cta() const {
+    if (atomicAdd(slot.done, 1) == static_cast<int>(gridDim.x) - 1) {
+      for (int i = 0; i <= m_tiles; ++i) work[i] = 0;
+      __threadfence();
+      atomicExch(slot.done, 0);
+      for (int r = 0; r < slot.tp; ++r)
+        if (r != slot.me) atomicAdd_system(slot.flags + r, -peer_grid);
+    }
+  }
   // ranks whose rows make up M-block mb: [r0, r1)
   __device__ __forceinline__ void ranks(int mb, int& r0, int& r1) const {
     if (rows_s >= kGemmBM) {
@@ -99,19 +182,6 @@ struct AGather {
       r0 = mb * segs;
       r1 = min(slot.tp, r0 + segs);
     }
-  }
-  __device__ bool ready(int mb, uint32_t& mask, volatile int* abort, int* status) const {
-    int r0, r1;
-    ranks(mb, r0, r1);
-    bool waited = false;
-    for (int r = r0; r < r1; ++r) {
-      if (r == slot.me || (mask >> r) & 1u) continue;
-      if (!wait_ge(slot.flags + r, 1, abort, status, 950 + r)) return false;
-      mask |= 1u << r;
-      waited = true;
-    }
-    if (waited) fence_proxy_async_global();  // acquire (generic proxy) before the TMA reads
-    return true;
   }
   __device__ __forceinline__ uint32_t bytes(int mb) const {
     int r0, r1;
@@ -177,7 +247,16 @@ static void launch_tp(const GemmLaunch& g, const Epi& epi, const ASrc& a) {
 void ag_gemm_launch(const AgLaunch& L) {
   const GemmLaunch& g = L.g;
   AGather a;
-  for (int r = 0; r < kMaxTp; ++r) a.m[r] = L.a[r];
+  for (int r = 0; r < kMaxTp; ++r) {
+    a.m[r] = L.a[r];
+    a.peer_x[r] = static_cast<const __nv_bfloat16*>(L.peer_x[r]);
+  }
+  a.stage = static_cast<__nv_bfloat16*>(L.stage);
+  a.work = L.work;
+  a.ldx = L.ldx;
+  a.K = g.s.K;
+  a.M = g.s.M;
+  a.m_tiles = g.s.m_tiles;
   a.rows_s = L.rows_s;
   a.box_rows = L.box_rows;
   a.slot = L.slot;

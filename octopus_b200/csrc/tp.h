@@ -28,10 +28,18 @@ struct TpSlot {
 };
 
 // AG -> GEMM: C[M = tp * rows_s, N] = concat_r(X_r)[M, K] @ W[N, K]^T (+ bias), with X_r
-// rank r's activation shard read by TMA straight from its memory.
+// rank r's activation shard.  Every remote row crosses NVLink once: the epilogue warps of all CTAs first copy the
+// peers' shards (P2P loads) into a local staging buffer, chunk by chunk from a shared
+// work counter, and count finished chunks per M-block; the TMA producer loads an
+// M-block holding remote rows once its count is complete.  Tiles of the rank's own
+// rows are scheduled first (m_shift) and need no copy.
 struct AgLaunch {
   GemmLaunch g;               // B map, shape, bf16 epilogue, bn, grid, stream, status
-  CUtensorMap a[kMaxTp];      // rank r's shard [rows_s, K] (box 64 x box_rows)
+  CUtensorMap a[kMaxTp];      // rank r's rows [rows_s, K] (own: the shard; peers: staging) box 64 x box_rows
+  const void* peer_x[kMaxTp]; // rank r's shard (peer pointers)
+  int ldx;                    // shard row stride (elements)
+  void* stage;                // local staging [tp * rows_s, K] bf16 (row stride K)
+  int* work;                  // local counters: [0] chunk work counter, [1 + mb] chunks staged of M-block mb
   int rows_s, box_rows;
   TpSlot slot;
   int peer_grid;              // signals one call of a peer delivers (its grid)

@@ -214,6 +214,10 @@ class TPGroup:
         self.xch = PeerBuffers(self.tp * max_m * 16, self.device, group)
         self.max_n = max_n
         self.sync_local = self.sync.ptrs[self.rank]
+        # AG staging: every remote activation row is copied over NVLink once per GEMM
+        max_m = self.tp * max(self.max_rows_s, self.max_sel)
+        self.stage = torch.empty(max_m * hidden, dtype=torch.bfloat16, device=self.device)
+        self.work = torch.zeros(2 + max_m // 128 + 1, dtype=torch.int32, device=self.device)
 
     # ------------------------------------------------------------------ views
     def x_local(self, rows_s: int) -> torch.Tensor:
@@ -233,7 +237,7 @@ class TPGroup:
     def ag_linear(self, rows_s: int, W, out, bias=None, sel: bool = False):
         bufs = self.sel if sel else self.xbuf
         ops.ext().ag_gemm(bufs.ptrs, rows_s, self.hidden, W, out, bias, self.rank, self.sync_local, self.sync.ptrs,
-                          SLOT_AG, 0)
+                          SLOT_AG, 0, self.stage, self.work)
         ops.add_launches(1)
         return out
 
@@ -256,7 +260,7 @@ class TPGroup:
         ops.add_launches(3)
         return ops.ext().tp_sample_head(bufs.ptrs, rows_s, self.hidden, W, alpha, seed, streams, sd.vocab_limit,
                                         sd.col_base, self.rank, self.sync_local, self.sync.ptrs, SLOT_AG, SLOT_SMP,
-                                        self.xch.ptrs, self.xch.local)
+                                        self.xch.ptrs, self.xch.local, self.stage, self.work)
 
     def close(self):
         torch.cuda.synchronize(self.device)

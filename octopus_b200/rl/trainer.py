@@ -47,7 +47,10 @@ class RLTrainer:
         return self.env.rollout(self.engine)
 
     def train_on(self, ro) -> dict:
-        mbs = instance_microbatches(ro, self.cfg.mb_tokens, build_microbatch)
+        if hasattr(ro, "microbatches"):
+            mbs = ro.microbatches(self.cfg.mb_tokens, build_microbatch)
+        else:
+            mbs = instance_microbatches(ro, self.cfg.mb_tokens, build_microbatch)
         k, n = self.cfg.mb_shard
         if n > 1:
             mbs = mbs[k::n]

@@ -119,7 +119,8 @@ class CursorRuntime:
 
     # ------------------------------------------------------------------ transport
     async def _complete(self, thread: str, messages: list, session_id: str) -> dict:
-        body = {"messages": messages, "tools": self.tool_list(thread), "session_id": session_id}
+        body = {"messages": messages, "tools": self.tool_list(thread), "session_id": session_id,
+                "max_tokens": S.max_reply()}
         if self.cursor:
             cur, delta = cursor_delta(messages)
             if cur is not None:

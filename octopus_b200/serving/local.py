@@ -1,0 +1,108 @@
+"""In-process chat service over the engine: request batching, chat rendering with the
+cursor protocol (only the messages after the cursor's reply are rendered), tool-call
+parsing, and the template terminator kept on the reply's cursor.  The HTTP server wraps
+it; the RL agent environment calls it directly as the runtime's completion function
+(no HTTP hop for colocated rollouts).
+
+Reference parity (behaviour): the AReaL proxy the reference runs in-process
+(`octopus/rl/proxy.py:32-78`) and the chat path of `patches/apply_sglang_cursor.py`.
+"""
+from __future__ import annotations
+
+import asyncio
+import threading
+import time
+import uuid
+
+from .chat import ChatTokenizer, parse_tool_calls
+from .engine import Engine, GenInput
+
+
+def mounts_of(body: dict) -> list:
+    out = []
+    for m in body.get("mount") or []:
+        if isinstance(m, dict):
+            out.append((m["cursor"], int(m["start"]), int(m["end"])))
+        else:
+            out.append((m[0], int(m[1]), int(m[2])))
+    return out
+
+
+class BatchingQueue:
+    """Collects concurrent requests for `window` seconds and runs them as one engine batch."""
+
+    def __init__(self, engine: Engine, window: float = 0.005, max_batch: int | None = None):
+        self.engine = engine
+        self.window = window
+        self.max_batch = max_batch or engine.max_batch
+        self.lock = threading.Lock()
+        self.pending: list = []
+        self.inflight = 0
+        self.run_lock = asyncio.Lock()
+
+    async def submit(self, inp: GenInput):
+        loop = asyncio.get_running_loop()
+        fut = loop.create_future()
+        self.pending.append((inp, fut))
+        self.inflight += 1
+        await asyncio.sleep(self.window)
+        async with self.run_lock:
+            batch = [(i, f) for i, f in self.pending if not f.done()][: self.max_batch]
+            if batch and not fut.done():
+                for item in batch:
+                    self.pending.remove(item)
+                # one temperature per engine batch: group by temperature
+                groups: dict = {}
+                for i, f in batch:
+                    groups.setdefault(float(i.temperature), []).append((i, f))
+                for items in groups.values():
+                    try:
+                        outs = await loop.run_in_executor(None, self.engine.generate, [i for i, _ in items])
+                        for (_, f), o in zip(items, outs):
+                            f.set_result(o)
+                    except Exception as e:  # per-request errors (404 cursor, bad mount) fail the whole group
+                        for _, f in items:
+                            if not f.done():
+                                f.set_exception(e)
+        try:
+            return await fut
+        finally:
+            self.inflight -= 1
+
+
+
+class ChatService:
+    """OpenAI-style chat completions (+ cursor / mount) on an engine, batched."""
+
+    def __init__(self, engine: Engine, tokenizer: ChatTokenizer, model_name: str = "octopus-b200",
+                 window: float = 0.005):
+        self.engine, self.tok, self.model_name = engine, tokenizer, model_name
+        self.q = BatchingQueue(engine, window)
+
+    async def chat(self, body: dict) -> dict:
+        tok = self.tok
+        msgs = body.get("messages") or []
+        tools = body.get("tools")
+        kwargs = body.get("chat_template_kwargs") or {}
+        cursor = body.get("cursor")
+        ids = tok.render_delta(msgs, tools, **kwargs) if cursor is not None else tok.apply(msgs, tools, True, **kwargs)
+        inp = GenInput(ids, cursor=cursor, mount=mounts_of(body), max_new_tokens=int(body.get("max_tokens", 1024)),
+                       temperature=float(body.get("temperature", 1.0)), stop_ids=tok.stop_ids)
+        o = await self.q.submit(inp)
+        out_ids = [t for t in o.output_ids if t not in tok.stop_ids]
+        content, calls = parse_tool_calls(tok.decode(out_ids))
+        # the cursor keeps reply tokens + template terminator so the next delta renders right after it
+        eng = self.engine
+        if o.cursor is not None and eng.cursors.get(o.cursor) is not None:
+            eng.extend_cursor(o.cursor, tok.terminator(), drop_trailing=tok.stop_ids)
+        rid = o.cursor or f"chatcmpl-{uuid.uuid4().hex[:12]}"
+        return {
+            "id": rid, "object": "chat.completion", "created": int(time.time()), "model": self.model_name,
+            "cursor": o.cursor,
+            "choices": [{"index": 0, "finish_reason": "tool_calls" if calls else o.finish_reason,
+                         "message": {"role": "assistant", "content": content, "tool_calls": calls or None}}],
+            "usage": {"prompt_tokens": o.prompt_tokens + o.cached_tokens, "completion_tokens": len(o.output_ids),
+                      "prompt_tokens_details": {"cached_tokens": o.cached_tokens}},
+        }
+
+    __call__ = chat

@@ -25,55 +25,11 @@ reads /get_server_info).
 """
 from __future__ import annotations
 
-import asyncio
-import threading
 import time
-import uuid
 
-from .chat import ChatTokenizer, parse_tool_calls
+from .chat import ChatTokenizer
 from .engine import CursorNotFound, Engine, GenInput
-
-
-class BatchingQueue:
-    """Collects concurrent requests for `window` seconds and runs them as one engine batch."""
-
-    def __init__(self, engine: Engine, window: float = 0.005, max_batch: int | None = None):
-        self.engine = engine
-        self.window = window
-        self.max_batch = max_batch or engine.max_batch
-        self.lock = threading.Lock()
-        self.pending: list = []
-        self.inflight = 0
-        self.run_lock = asyncio.Lock()
-
-    async def submit(self, inp: GenInput):
-        loop = asyncio.get_running_loop()
-        fut = loop.create_future()
-        self.pending.append((inp, fut))
-        self.inflight += 1
-        await asyncio.sleep(self.window)
-        async with self.run_lock:
-            batch = [(i, f) for i, f in self.pending if not f.done()][: self.max_batch]
-            if batch and not fut.done():
-                for item in batch:
-                    self.pending.remove(item)
-                # one temperature per engine batch: group by temperature
-                groups: dict = {}
-                for i, f in batch:
-                    groups.setdefault(float(i.temperature), []).append((i, f))
-                for items in groups.values():
-                    try:
-                        outs = await loop.run_in_executor(None, self.engine.generate, [i for i, _ in items])
-                        for (_, f), o in zip(items, outs):
-                            f.set_result(o)
-                    except Exception as e:  # per-request errors (404 cursor, bad mount) fail the whole group
-                        for _, f in items:
-                            if not f.done():
-                                f.set_exception(e)
-        try:
-            return await fut
-        finally:
-            self.inflight -= 1
+from .local import BatchingQueue, ChatService, mounts_of  # noqa: F401  (BatchingQueue re-exported)
 
 
 def create_app(engine: Engine, tokenizer: ChatTokenizer | None = None, model_name: str = "octopus-b200"):
@@ -81,17 +37,9 @@ def create_app(engine: Engine, tokenizer: ChatTokenizer | None = None, model_nam
     from fastapi.responses import JSONResponse
 
     app = FastAPI()
-    q = BatchingQueue(engine)
+    svc = ChatService(engine, tokenizer, model_name)
+    q = svc.q
     state = {"started": time.time()}
-
-    def _mounts(body):
-        out = []
-        for m in body.get("mount") or []:
-            if isinstance(m, dict):
-                out.append((m["cursor"], int(m["start"]), int(m["end"])))
-            else:
-                out.append((m[0], int(m[1]), int(m[2])))
-        return out
 
     async def _run(inp: GenInput):
         try:
@@ -120,7 +68,7 @@ def create_app(engine: Engine, tokenizer: ChatTokenizer | None = None, model_nam
     @app.post("/generate")
     async def generate(body: dict):
         sp = body.get("sampling_params") or {}
-        inp = GenInput(list(body.get("input_ids") or []), cursor=body.get("cursor"), mount=_mounts(body),
+        inp = GenInput(list(body.get("input_ids") or []), cursor=body.get("cursor"), mount=mounts_of(body),
                        max_new_tokens=int(sp.get("max_new_tokens", 128)), temperature=float(sp.get("temperature",
                                                                                                   1.0)),
                        stop_ids=tuple(sp.get("stop_token_ids") or ()), prefill_only=int(sp.get("max_new_tokens",
@@ -135,32 +83,12 @@ def create_app(engine: Engine, tokenizer: ChatTokenizer | None = None, model_nam
     async def chat(body: dict):
         if tokenizer is None:
             raise HTTPException(400, "server started without a tokenizer")
-        msgs = body.get("messages") or []
-        tools = body.get("tools")
-        kwargs = body.get("chat_template_kwargs") or {}
-        cursor = body.get("cursor")
-        if cursor is not None:
-            ids = tokenizer.render_delta(msgs, tools, **kwargs)
-        else:
-            ids = tokenizer.apply(msgs, tools, True, **kwargs)
-        inp = GenInput(ids, cursor=cursor, mount=_mounts(body), max_new_tokens=int(body.get("max_tokens", 1024)),
-                       temperature=float(body.get("temperature", 1.0)), stop_ids=tokenizer.stop_ids)
-        o = await _run(inp)
-        out_ids = [t for t in o.output_ids if t not in tokenizer.stop_ids]
-        text = tokenizer.decode(out_ids)
-        content, calls = parse_tool_calls(text)
-        # the cursor keeps reply tokens + template terminator so the next delta renders right after it
-        if o.cursor is not None and engine.cursors.get(o.cursor) is not None:
-            engine.extend_cursor(o.cursor, tokenizer.terminator(), drop_trailing=tokenizer.stop_ids)
-        rid = o.cursor or f"chatcmpl-{uuid.uuid4().hex[:12]}"
-        return JSONResponse({
-            "id": rid, "object": "chat.completion", "created": int(time.time()), "model": model_name,
-            "cursor": o.cursor,
-            "choices": [{"index": 0, "finish_reason": "tool_calls" if calls else o.finish_reason,
-                         "message": {"role": "assistant", "content": content, "tool_calls": calls or None}}],
-            "usage": {"prompt_tokens": o.prompt_tokens + o.cached_tokens, "completion_tokens": len(o.output_ids),
-                      "prompt_tokens_details": {"cached_tokens": o.cached_tokens}},
-        })
+        try:
+            return JSONResponse(await svc.chat(body))
+        except CursorNotFound as e:
+            raise HTTPException(404, f"unknown cursor {e}") from None
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from None
 
     @app.post("/release_cursor")
     async def release(body: dict):
