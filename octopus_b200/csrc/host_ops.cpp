@@ -10,6 +10,7 @@
 
 #include "attention.h"
 #include "decode_persistent.h"
+#include "decode_shared.h"
 #include "elementwise.h"
 #include "octo_api.h"
 #include "tmap.h"
@@ -40,6 +41,60 @@ static cudaStream_t cur_stream(const torch::Tensor& t) {
 #define CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
 #define BF(x) reinterpret_cast<__nv_bfloat16*>((x).data_ptr())
 #define CBF(x) reinterpret_cast<const __nv_bfloat16*>((x).data_ptr())
+
+// Shared-prefix decode: segment tables from ops.decode.plan_shared (all int32, device).
+void attn_decode_shared_t(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor kv_indices,
+                          torch::Tensor kv_len, torch::Tensor seg_rows, torch::Tensor seg_slot, torch::Tensor seg_start,
+                          torch::Tensor seg_len, torch::Tensor seg_off, torch::Tensor items, torch::Tensor n_items,
+                          torch::Tensor row_nslot, torch::Tensor o, torch::Tensor part_o, torch::Tensor part_lse,
+                          int64_t Hq, int64_t Hkv, int64_t max_slots, int64_t chunk, double scale) {
+  c10::cuda::CUDAGuard guard(q.get_device());
+  for (auto* t : {&kv_indices, &kv_len, &seg_rows, &seg_slot, &seg_start, &seg_len, &seg_off, &items, &n_items,
+                  &row_nslot}) {
+    TORCH_CHECK(t->scalar_type() == torch::kInt32 && t->is_contiguous() && t->is_cuda(),
+                "decode_shared: int32 contiguous CUDA tables");
+  }
+  CHECK_BF16(q);
+  CHECK_BF16(kc);
+  CHECK_BF16(vc);
+  CHECK_BF16(o);
+  TORCH_CHECK(Hq % Hkv == 0 && Hq / Hkv <= 16, "decode_shared: GQA group must be <= 16");
+  TORCH_CHECK(q.stride(1) == 1 && o.stride(1) == 1 && kc.is_contiguous() && vc.is_contiguous(), "decode: layout");
+  TORCH_CHECK(kc.size(-1) == Hkv * 128, "decode_shared: head_dim 128 only");
+  TORCH_CHECK(chunk % 64 == 0 && chunk > 0, "decode_shared: chunk must be a multiple of 64");
+  DecodeSharedParams p{};
+  p.q = CBF(q);
+  p.k_cache = CBF(kc);
+  p.v_cache = CBF(vc);
+  p.o = BF(o);
+  p.kv_indices = kv_indices.data_ptr<int32_t>();
+  p.kv_len = kv_len.data_ptr<int32_t>();
+  p.seg_rows = seg_rows.data_ptr<int32_t>();
+  p.seg_slot = seg_slot.data_ptr<int32_t>();
+  p.seg_start = seg_start.data_ptr<int32_t>();
+  p.seg_len = seg_len.data_ptr<int32_t>();
+  p.seg_off = seg_off.data_ptr<int32_t>();
+  p.items = items.data_ptr<int32_t>();
+  p.n_items = n_items.data_ptr<int32_t>();
+  p.row_nslot = row_nslot.data_ptr<int32_t>();
+  p.ldq = q.stride(0);
+  p.ldo = o.stride(0);
+  p.B = q.size(0);
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.max_slots = static_cast<int>(max_slots);
+  p.chunk = static_cast<int>(chunk);
+  p.scale = static_cast<float>(scale);
+  TORCH_CHECK(row_nslot.numel() >= p.B, "decode_shared: row_nslot too small");
+  TORCH_CHECK(part_o.numel() >= static_cast<int64_t>(p.B) * Hq * max_slots * 128 &&
+                  part_lse.numel() >= static_cast<int64_t>(p.B) * Hq * max_slots,
+              "decode_shared: scratch too small");
+  p.part_o = part_o.data_ptr<float>();
+  p.part_lse = part_lse.data_ptr<float>();
+  if (p.B == 0) return;
+  decode_shared_launch(p, 2 * num_sms(q.get_device()), status_ptr(q.get_device()), cur_stream(q));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 // ------------------------------------------------------------------ GEMM
 int pick_bn(int M, int N, int sms, int hint) {
@@ -564,4 +619,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &attn_bwd_t);
   m.def("attn_decode", &attn_decode_t);
   m.def("attn_decode_persistent", &attn_decode_persistent_t);
+  m.def("attn_decode_shared", &attn_decode_shared_t);
 }

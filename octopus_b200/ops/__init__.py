@@ -2,9 +2,9 @@
 from ._ext import add_launches, available, check_status, ext, launches
 from .core import (AttnPlan, adamw_, attention, embed, gemm, linear, logprob_head, rmsnorm, rope_, sample, sqnorm_,
                    swiglu)
-from .decode import DecodeAttention, decode_attention
+from .decode import DecodeAttention, SharedDecode, decode_attention
 
 __all__ = [
-    "AttnPlan", "DecodeAttention", "adamw_", "add_launches", "launches", "attention", "available", "check_status", "decode_attention", "embed",
+    "AttnPlan", "DecodeAttention", "SharedDecode", "adamw_", "add_launches", "launches", "attention", "available", "check_status", "decode_attention", "embed",
     "ext", "gemm", "linear", "logprob_head", "rmsnorm", "rope_", "sample", "sqnorm_", "swiglu",
 ]

@@ -87,3 +87,117 @@ def decode_attention_ref(q, k_cache, v_cache, kv_start, kv_indices, Hq, Hkv, D, 
 def decode_attention(q, k_cache, v_cache, kv_indptr, kv_indices, Hq, Hkv, D, scale=None, num_splits=8):
     return DecodeAttention(Hq, Hkv, D, q.shape[0], num_splits, q.device)(q, k_cache, v_cache, kv_indptr,
                                                                          kv_indices, scale=scale)
+
+
+class SharedDecode:
+    """Shared-prefix decode (cascade attention) with static device tables.
+
+    `plan()` splits every row's key list into segments: key ranges identical across up
+    to `seg_rows` rows (their contexts agree: a mounted task prefix, a forked parent's
+    context) and each row's own remainder, whose length grows with decoding.  The
+    kernel gathers a shared segment's K/V once for all its rows.  Tables are rewritten
+    in place, so a CUDA graph captured once per batch bucket stays valid across plans.
+    """
+
+    def __init__(self, Hq: int, Hkv: int, D: int, max_batch: int, device="cuda", max_slots: int = 32,
+                 chunk: int = 256, min_shared: int = 64, max_segs: int | None = None):
+        if D != 128:
+            raise ValueError("shared-prefix decode covers head_dim 128")
+        self.Hq, self.Hkv, self.D = Hq, Hkv, D
+        G = Hq // Hkv
+        self.seg_rows = min(8, 2 * (16 // G))
+        self.max_batch, self.max_slots, self.chunk, self.min_shared = max_batch, max_slots, chunk, min_shared
+        self.max_segs = max_segs or 6 * max_batch
+        dev = torch.device(device)
+        i32 = dict(dtype=torch.int32, device=dev)
+        S = self.max_segs
+        self.t_rows = torch.full((S * 8,), -1, **i32)
+        self.t_slot = torch.zeros(S * 8, **i32)
+        self.t_start = torch.zeros(S, **i32)
+        self.t_len = torch.zeros(S, **i32)
+        self.t_off = torch.zeros(S, **i32)
+        self.t_items = torch.zeros(S * 64, **i32)
+        self.t_n = torch.zeros(1, **i32)
+        self.t_nslot = torch.zeros(max_batch, **i32)
+        self.part_o = torch.empty(max_batch * Hq * max_slots * D, dtype=torch.float32, device=dev)
+        self.part_lse = torch.empty(max_batch * Hq * max_slots, dtype=torch.float32, device=dev)
+        self.stats = {}
+
+    def plan(self, lists: list, starts, ctx_len, final_len, B: int) -> bool:
+        """lists[b]: row b's key slots (numpy, >= its final length); starts[b]: offset of that
+        list in the kv index buffer; ctx_len[b]: leading keys that are context (may be
+        shared); final_len[b]: the row's key count at the end of this decode call.  Rows
+        past len(lists) are padding.  Returns False when the tables cannot hold the plan."""
+        import numpy as np
+
+        segs = []  # (rows, start, len (-1 dynamic), off, max_len)
+        n = len(lists)
+
+        def own(b, off):
+            segs.append(([b], int(starts[b]) + off, -1, off, max(0, int(final_len[b]) - off)))
+
+        def rec(rows, off):
+            groups: dict = {}
+            for b in rows:
+                if ctx_len[b] <= off:
+                    own(b, off)
+                else:
+                    groups.setdefault(int(lists[b][off]), []).append(b)
+            for grp in groups.values():
+                if len(grp) == 1:
+                    own(grp[0], off)
+                    continue
+                m = min(int(ctx_len[b]) for b in grp)
+                A = np.stack([np.asarray(lists[b][off:m]) for b in grp])
+                neq = np.nonzero((A != A[0]).any(axis=0))[0]
+                L = int(neq[0]) if len(neq) else m - off
+                if L < self.min_shared:
+                    for b in grp:
+                        own(b, off)
+                    continue
+                for i in range(0, len(grp), self.seg_rows):
+                    part = grp[i:i + self.seg_rows]
+                    segs.append((part, int(starts[part[0]]) + off, L, off, L))
+                rec(grp, off + L)
+
+        rec(list(range(n)), 0)
+        if len(segs) > self.max_segs:
+            return False
+        rows = np.full((self.max_segs, 8), -1, np.int32)
+        slot = np.zeros((self.max_segs, 8), np.int32)
+        nslot = np.zeros(self.max_batch, np.int32)
+        items = []
+        for s, (rr, _, _, _, mx) in enumerate(segs):
+            nch = max(1, -(-mx // self.chunk))
+            if nch > 255:
+                return False
+            for j, b in enumerate(rr):
+                rows[s, j] = b
+                slot[s, j] = nslot[b]
+                nslot[b] += nch
+            items += [(s << 8) | c for c in range(nch)]
+        if nslot.max(initial=0) > self.max_slots or len(items) > self.t_items.numel():
+            return False
+        k = len(segs)
+        dev = self.t_rows.device
+        self.t_rows.copy_(torch.from_numpy(rows.reshape(-1)).to(dev, non_blocking=False))
+        self.t_slot.copy_(torch.from_numpy(slot.reshape(-1)).to(dev))
+        self.t_start[:k].copy_(torch.tensor([x[1] for x in segs], dtype=torch.int32))
+        self.t_len[:k].copy_(torch.tensor([x[2] for x in segs], dtype=torch.int32))
+        self.t_off[:k].copy_(torch.tensor([x[3] for x in segs], dtype=torch.int32))
+        self.t_items[:len(items)].copy_(torch.tensor(items, dtype=torch.int32))
+        self.t_n.fill_(len(items) * self.Hkv)
+        self.t_nslot.copy_(torch.from_numpy(nslot).to(dev))
+        self.stats = {"segments": k, "shared_segments": sum(1 for x in segs if x[2] >= 0), "items": len(items),
+                      "max_slots": int(nslot.max(initial=0))}
+        return True
+
+    def __call__(self, q, k_cache, v_cache, kv_indices, kv_len, out=None, scale=None):
+        B = q.shape[0]
+        if out is None:
+            out = torch.empty(B, self.Hq * self.D, dtype=q.dtype, device=q.device)
+        scale = scale if scale is not None else self.D ** -0.5
+        ext().attn_decode_shared(q, k_cache, v_cache, kv_indices, kv_len.to(torch.int32), self.t_rows, self.t_slot,
+                                 self.t_start, self.t_len, self.t_off, self.t_items, self.t_n, self.t_nslot, out,
+                                 self.part_o, self.part_lse, self.Hq, self.Hkv, self.max_slots, self.chunk, scale)
+        return out

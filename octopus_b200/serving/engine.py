@@ -138,6 +138,13 @@ class Engine:
         self._cid = itertools.count(1)
         splits = num_splits or 8
         self.dec_attn = ops.DecodeAttention(hq_loc, hkv_loc, cfg.head_dim, max_batch, splits, self.device)
+        # shared-prefix decode: rows that share context keys (mounted task prefix, forked parent)
+        # gather them once per group; re-planned per decode call (graph-safe tables)
+        self.shared_decode = None
+        self._shared_active = False
+        if (self.device.type == "cuda" and cfg.head_dim == 128 and self.mount_layers is None
+                and os.environ.get("OCTO_SHARED_DECODE", "1") != "0"):
+            self.shared_decode = ops.SharedDecode(hq_loc, hkv_loc, cfg.head_dim, max_batch, self.device)
         # static decode buffers (graph inputs)
         B = max_batch
         dev = self.device
@@ -381,6 +388,8 @@ class Engine:
             len_o = self.s_len_own[:B] + 1
 
         def attn(q, i):
+            if self._shared_active:
+                return self.shared_decode(q, self.kc[i], self.vc[i], self.kv_indices, att_len)
             if self.mount_layers is None or i in mset:
                 return self.dec_attn(q, self.kc[i], self.vc[i], start, self.kv_indices, kv_len=att_len)
             return self.dec_attn(q, self.kc[i], self.vc[i], start_o, self.kv_indices_own, kv_len=len_o)
@@ -414,7 +423,7 @@ class Engine:
             self._graphs.clear()
 
     def _graph(self, B: int, temperature: float):
-        key = (B, float(temperature))
+        key = (B, float(temperature), self._shared_active)
         g = self._graphs.get(key)
         if g is not None:
             return g
@@ -505,11 +514,14 @@ class Engine:
             self.s_len[:B].copy_(h2d(lens, dev))
             self.s_stream[:B].copy_(h2d(stream, dev))
             self.s_step.zero_()
+            if self.shared_decode is not None:
+                ctx = np.asarray([len(reqs[j].ctx_slots) for j in chunk], np.int64)
+                self._shared_active = self.shared_decode.plan(regions[:n], starts, ctx, lens[:n] + steps + 1, B)
             if self.use_graphs:
                 g = self._graph(B, temperature)
                 for _ in range(steps):
                     g.replay()
-                ops.add_launches(self._graph_kernels[(B, float(temperature))] * steps)
+                ops.add_launches(self._graph_kernels[(B, float(temperature), self._shared_active)] * steps)
             else:
                 for _ in range(steps):
                     self._decode_step(B, temperature)

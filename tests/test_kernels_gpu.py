@@ -300,3 +300,40 @@ def test_persistent_decode_matches_splitk():
         a = ops.DecodeAttention(Hq, Hkv, D, B, splits, dev, persistent=True)(q, kc, vc, ipd, idx)
         b = ops.DecodeAttention(Hq, Hkv, D, B, splits, dev, persistent=False)(q, kc, vc, ipd, idx)
         assert rel_err(a, b) < 1e-2
+
+
+@pytest.mark.gpu
+def test_shared_prefix_decode_matches_persistent():
+    """Rows sharing a task prefix and a planner segment (DAG solver stage) plus unshared
+    rows: the shared-prefix kernel equals the per-row kernel; dynamic lengths advance."""
+    from test_decode_plan import dag_rows
+
+    torch.manual_seed(15)
+    Hq, Hkv, D = 28, 4, 128
+    rows, ctx = dag_rows(n_inst=4, per=8, pre=700, plan=300, own=120)
+    rows += [np.arange(200000, 200000 + 333), np.arange(210000, 210000 + 65)]
+    ctx = np.r_[ctx, 300, 30]
+    B = 40
+    n = len(rows)
+    slots = 220000
+    kc = torch.randn(slots, Hkv * D, device=dev).bfloat16()
+    vc = torch.randn(slots, Hkv * D, device=dev).bfloat16()
+    starts = np.cumsum([0] + [len(r) for r in rows[:-1]]).astype(np.int32)
+    idx = torch.from_numpy(np.concatenate(rows).astype(np.int32)).to(dev)
+    final = np.asarray([len(r) for r in rows])
+    q = torch.randn(B, Hq * D, device=dev).bfloat16()
+    sd = ops.SharedDecode(Hq, Hkv, D, B, dev)
+    assert sd.plan(rows, starts, ctx, final, B)
+    assert sd.stats["shared_segments"] > 0
+    pd = ops.DecodeAttention(Hq, Hkv, D, B, 4, dev, persistent=True)
+    st = torch.zeros(B, dtype=torch.int32, device=dev)
+    st[:n] = torch.from_numpy(starts).to(dev)
+    for shrink in (20, 0):  # an earlier decode step (shorter own parts), then the full lengths
+        ln = torch.zeros(B, dtype=torch.int32, device=dev)
+        ln[:n] = torch.from_numpy(final - shrink).to(dev)
+        a = sd(q, kc, vc, idx, ln)
+        b = pd(q, kc, vc, st, idx, kv_len=ln)
+        torch.cuda.synchronize()
+        ops.check_status(0)
+        assert rel_err(a[:n], b[:n]) < 1e-2
+        assert float(a[n:].float().abs().max()) == 0.0
