@@ -128,6 +128,11 @@ class Actor:
     def zero_grad(self):
         self.grad.zero_()
 
+    def reload_master(self):
+        """fp32 master <- compute weights (after loading a checkpoint into the compute buffer)."""
+        off = getattr(self, "off", 0)
+        self.master.copy_(self.flat16[off: off + self.master.numel()].to(self.master.dtype))
+
     def forward_backward(self, mbs: list[MicroBatch], denom: float | None = None) -> dict:
         denom = denom if denom is not None else float(sum(mb.pair_w.sum() for mb in mbs))
         stats = {}

@@ -1,0 +1,205 @@
+"""RL trainer entry point.
+
+    python -m octopus_b200.rl.train [--config grpo.yaml] [key=value ...]
+    torchrun --nproc-per-node 8 -m octopus_b200.rl.train --config grpo.yaml rollout.tp=2
+
+One process per GPU.  Per step: rollout (colocated engine, or a tensor-parallel group of
+`rollout.tp` GPUs), group credit + prefix-tree micro-batches, the actor update (ZeRO-
+sharded over all ranks with fused peer-memory collectives), weight sync; then a JSON
+step line (`<run>/steps.jsonl` and stdout), a recover checkpoint every
+`checkpoint.recover_every` steps (followed by the rollout spool commit) and HF
+safetensors every `checkpoint.save_every` steps.  A run resumes from its recover
+checkpoint.  `OCTOPUS_LIVE_ENV` (MB_TOKENS, ...) is re-read every step.
+
+Reference parity (behaviour): `octopus/rl/train.py:55-137` (derived settings, episode
+settings snapshot, dataset, trainer with spool commit after the recover checkpoint,
+dynamic filter).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+DEFAULT_CONFIG = os.path.join(os.path.dirname(os.path.abspath(__file__)), "grpo.yaml")
+
+
+def _dist_init(device):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 and not dist.is_initialized():
+        backend = "nccl" if device.type == "cuda" else "gloo"
+        kw = {"device_id": device} if device.type == "cuda" else {}
+        dist.init_process_group(backend, timeout=timedelta(seconds=900), **kw)
+    return world
+
+
+def build(cfg, device):
+    """(trainer, actor, engine, env, spool, tp_rank) for a run config."""
+    import torch
+    import torch.distributed as dist
+
+    from ..envs.dag import DagConfig, MultiAgentDag
+    from ..models.config import get_config
+    from ..models.decoder import load_hf
+    from ..parallel.fsdp import ShardedActor
+    from ..serving.engine import Engine
+    from .actor import Actor, OptimConfig
+    from .loss import PPOConfig
+    from .spool import Spool
+    from .trainer import RLTrainer, TrainerConfig
+
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    mcfg = get_config(cfg.model.preset, **({"layers": cfg.model.layers} if cfg.model.layers else {}))
+    a = cfg.actor
+    optim = OptimConfig(lr=a.lr, betas=(a.beta1, a.beta2), eps=a.eps, weight_decay=a.weight_decay,
+                        max_grad_norm=a.gradient_clipping)
+    ppo = PPOConfig(eps_clip=a.eps_clip, eps_clip_higher=a.eps_clip_higher, behav_imp_weight_cap=a.behav_imp_weight_cap,
+                    reuse_train_logp=a.reuse_train_logp)
+    dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
+    if world > 1 and a.sharded:
+        actor = ShardedActor(mcfg, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype,
+                             ckpt=a.gradient_checkpointing, fused=a.fused_collectives and device.type == "cuda")
+    else:
+        actor = Actor(mcfg, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype, ckpt=a.gradient_checkpointing)
+    if cfg.model.path:
+        load_hf(actor.weights, cfg.model.path)
+        actor.reload_master()
+    tp = max(1, cfg.rollout.tp)
+    rep, tp_rank = rank // tp, rank % tp
+    group = None
+    if tp > 1:
+        for r in range(world // tp):
+            g = dist.new_group(list(range(r * tp, (r + 1) * tp)))
+            if r == rep:
+                group = g
+    kv_slots = int(cfg.rollout.kv_gb * (1 << 30) / (4 * mcfg.layers * mcfg.kv_width // tp))
+    if tp > 1:
+        from ..serving.tp_engine import TPEngine
+
+        engine = TPEngine(mcfg, actor.weights, group=group, kv_slots=kv_slots, max_batch=cfg.rollout.max_batch,
+                          device=device)
+    else:
+        engine = Engine(mcfg, actor.weights, kv_slots=kv_slots, max_batch=cfg.rollout.max_batch, device=device)
+    replicas = world // tp
+    spool = Spool(cfg.rl.spool) if cfg.rl.spool else None
+    if cfg.rl.kind == "dag":
+        inst = [i for i in range(cfg.rl.batch_size) if i % replicas == rep]
+        dag = MultiAgentDag(mcfg.vocab_size, DagConfig(instances=cfg.rl.batch_size, samples=cfg.rl.n_samples,
+                                                       temperature=cfg.rollout.temperature,
+                                                       seed=cfg.seed * 1000 + rep))
+
+        class _Env:
+            def rollout(self, eng):
+                return dag.rollout(eng, inst)
+
+        env = _Env()
+    elif cfg.rl.kind == "search":
+        env = _search_env(cfg, engine, rep, replicas)
+    else:
+        raise SystemExit(f"rl.kind {cfg.rl.kind!r}: dag or search")
+    trainer = RLTrainer(actor, engine, env, TrainerConfig(mb_tokens=a.mb_tokens, mb_shard=(tp_rank, tp)),
+                        sync_fn=engine.sync_weights if tp > 1 else None)
+    return trainer, actor, engine, env, spool, tp_rank
+
+
+def _search_env(cfg, engine, rep, replicas):
+    from ..envs.search.agent import SearchWorkspace, search_defaults
+    from ..envs.search.reward import search_outcome
+    from ..envs.search.service import Retrieval
+    from ..rl.group import search_gate
+    from ..serving.chat import ChatTokenizer
+    from ..serving.local import ChatService
+    from .agent_env import AgentEnv
+
+    if not cfg.rl.search_questions:
+        raise SystemExit("rl.kind=search needs rl.search_questions (JSONL of {qid, question, answer[, corpus]})")
+    rows = [json.loads(x) for x in open(cfg.rl.search_questions) if x.strip()]
+    rows = [r for i, r in enumerate(rows) if i % replicas == rep]
+    corpus_path = os.environ.get("OCTOPUS_SEARCH_CORPUS", "")
+    corpus = [json.loads(x) for x in open(corpus_path)] if corpus_path else [
+        {"docid": r["qid"], "title": r["question"], "text": str(r.get("context", ""))} for r in rows]
+    retrieval = Retrieval(corpus)
+    search_defaults()
+    tok = ChatTokenizer.from_dir(cfg.model.path) if cfg.model.path else ChatTokenizer.tiny()
+    svc = ChatService(engine, tok)
+    return AgentEnv(svc, rows, lambda t: SearchWorkspace(retrieval, t["question"]),
+                    lambda t, ans: search_outcome(ans, t["answer"], t["question"]), n_samples=cfg.rl.n_samples,
+                    batch_size=max(1, cfg.rl.batch_size // replicas), branch_credit=cfg.rl.branch_credit,
+                    gate=search_gate if cfg.rl.branch_credit == "gate" else None,
+                    filter_zero_variance=cfg.rl.filter_zero_variance)
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(prog="python -m octopus_b200.rl.train")
+    ap.add_argument("--config", default=DEFAULT_CONFIG)
+    ap.add_argument("--cpu", action="store_true", help="run on CPU (tiny models, tests)")
+    ap.add_argument("overrides", nargs="*", help="dotted key=value overrides")
+    args = ap.parse_args(argv)
+
+    import torch
+    import torch.distributed as dist
+
+    from . import checkpoint
+    from . import config as C
+    from ..models.decoder import save_hf
+
+    cfg = C.load(args.config, args.overrides)
+    C.set_derived_settings(cfg)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cpu") if args.cpu or not torch.cuda.is_available() else torch.device("cuda", local)
+    if device.type == "cuda":
+        torch.cuda.set_device(device)
+    world = _dist_init(device)
+    rank = dist.get_rank() if world > 1 else 0
+    run_dir = os.path.join(cfg.checkpoint.dir or "runs", cfg.experiment_name, cfg.trial_name)
+    if rank == 0:
+        os.makedirs(run_dir, exist_ok=True)
+        C.save_settings(os.path.join(run_dir, "episode_settings.json"))
+        with open(os.path.join(run_dir, "config.json"), "w") as f:
+            json.dump(cfg.to_dict(), f, indent=1)
+    trainer, actor, engine, env, spool, tp_rank = build(cfg, device)
+    step0 = 0
+    if checkpoint.exists(run_dir):
+        state = checkpoint.load(actor, run_dir)
+        step0 = int(state["step"])
+        engine.bump_version()
+        if hasattr(engine, "sync_weights"):
+            engine.sync_weights()
+    log = open(os.path.join(run_dir, "steps.jsonl"), "a") if rank == 0 else None
+    for step in range(step0, cfg.total_steps):
+        live = C.live_env()
+        if "MB_TOKENS" in live:
+            trainer.cfg.mb_tokens = live["MB_TOKENS"]
+        t0 = time.time()
+        st = trainer.step()
+        row = {"step": step + 1, "time": round(time.time() - t0, 3), "version": actor.version,
+               **{k: (round(v, 6) if isinstance(v, float) else v) for k, v in st.items()
+                  if isinstance(v, (int, float))}}
+        if rank == 0:
+            line = json.dumps(row)
+            print(line, flush=True)
+            log.write(line + "\n")
+            log.flush()
+        if cfg.checkpoint.recover_every and (step + 1) % cfg.checkpoint.recover_every == 0:
+            checkpoint.save(actor, run_dir, step + 1, {"step": step + 1}, spool=spool)
+        if cfg.checkpoint.save_every and (step + 1) % cfg.checkpoint.save_every == 0 and rank == 0:
+            save_hf(actor.weights, os.path.join(run_dir, f"hf-step{step + 1}"))
+    if world > 1:
+        dist.barrier()
+        if hasattr(engine, "close"):
+            engine._graphs.clear()
+            engine.close()
+        if hasattr(actor, "close"):
+            actor.close()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,35 @@
+"""Trainer entry point on CPU: two steps of the tiny DAG run from the shipped grpo.yaml with
+overrides, step log, recover checkpoint, HF save, and resume from the checkpoint."""
+import json
+import os
+
+from octopus_b200.rl import train
+
+
+def _args(tmp, steps):
+    return ["--cpu", "model.preset=tiny", "rl.kind=dag", "rl.batch_size=2", "rl.n_samples=2", "rollout.kv_gb=0.05",
+            "rollout.max_batch=16", "actor.mb_tokens=65536", "actor.gradient_checkpointing=false",
+            f"checkpoint.dir={tmp}", "checkpoint.save_every=2", f"total_steps={steps}"]
+
+
+def test_train_cli_runs_and_resumes(tmp_path, monkeypatch):
+    from octopus_b200.envs import dag
+
+    # a small DAG shape for CPU
+    orig = dag.DagConfig.__init__
+
+    def small(self, *a, **kw):
+        orig(self, *a, **kw)
+        self.prefix_len, self.turn_len, self.role_len = 32, 8, 4
+
+    monkeypatch.setattr(dag.DagConfig, "__init__", small)
+    assert train.main(_args(tmp_path, 2)) == 0
+    run = tmp_path / "octopus-b200" / "run0"
+    rows = [json.loads(x) for x in open(run / "steps.jsonl")]
+    assert [r["step"] for r in rows] == [1, 2]
+    assert (run / "recover" / "state.json").exists() and (run / "hf-step2").exists()
+    assert os.path.exists(run / "episode_settings.json")
+    # resume: continues at step 3
+    assert train.main(_args(tmp_path, 3)) == 0
+    rows = [json.loads(x) for x in open(run / "steps.jsonl")]
+    assert [r["step"] for r in rows] == [1, 2, 3]
