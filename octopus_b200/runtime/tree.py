@@ -125,6 +125,8 @@ class CursorRuntime:
             cur, delta = cursor_delta(messages)
             if cur is not None:
                 body["cursor"], body["messages"] = cur, delta
+                if os.environ.get("OCTOPUS_CURSOR_AUDIT"):
+                    body["audit_messages"] = without_cursors(messages)
         if self.pending_mounts.get(thread):
             body["mount"] = list(self.pending_mounts[thread])
         t0 = time.time()

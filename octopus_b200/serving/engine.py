@@ -136,6 +136,7 @@ class Engine:
         self.version = 0
         self._rid = itertools.count(1)
         self._cid = itertools.count(1)
+        self._uid = os.urandom(3).hex()
         splits = num_splits or 8
         self.dec_attn = ops.DecodeAttention(hq_loc, hkv_loc, cfg.head_dim, max_batch, splits, self.device)
         # shared-prefix decode: rows that share context keys (mounted task prefix, forked parent)
@@ -184,7 +185,8 @@ class Engine:
         return (T + 7) // 8 * 8
 
     def new_cursor_id(self) -> str:
-        return f"c{next(self._cid)}"
+        # unique across engines (clients route by cursor id over a pool of servers)
+        return f"c{self._uid}-{next(self._cid)}"
 
     def _alloc(self, n: int) -> np.ndarray:
         if n == 0:

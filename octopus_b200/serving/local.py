@@ -4,12 +4,17 @@ parsing, and the template terminator kept on the reply's cursor.  The HTTP serve
 it; the RL agent environment calls it directly as the runtime's completion function
 (no HTTP hop for colocated rollouts).
 
-Reference parity (behaviour): the AReaL proxy the reference runs in-process
+OCTOPUS_CURSOR_AUDIT=<path>: for every cursor request that carries the full history in
+``audit_messages``, append a JSONL row comparing the assembled prompt with the oracle.
+
+Reference parity (behaviour): `octopus/serving/cursor_audit.py:30-59` (audit rows); the AReaL proxy the reference runs in-process
 (`octopus/rl/proxy.py:32-78`) and the chat path of `patches/apply_sglang_cursor.py`.
 """
 from __future__ import annotations
 
 import asyncio
+import json
+import os
 import threading
 import time
 import uuid
@@ -78,6 +83,7 @@ class ChatService:
                  window: float = 0.005):
         self.engine, self.tok, self.model_name = engine, tokenizer, model_name
         self.q = BatchingQueue(engine, window)
+        self._audit_lock = threading.Lock()
 
     async def chat(self, body: dict) -> dict:
         tok = self.tok
@@ -86,6 +92,9 @@ class ChatService:
         kwargs = body.get("chat_template_kwargs") or {}
         cursor = body.get("cursor")
         ids = tok.render_delta(msgs, tools, **kwargs) if cursor is not None else tok.apply(msgs, tools, True, **kwargs)
+        audit = os.environ.get("OCTOPUS_CURSOR_AUDIT")
+        if audit and cursor is not None and body.get("audit_messages") and not body.get("mount"):
+            self._audit(audit, body, cursor, ids, tools, kwargs)
         inp = GenInput(ids, cursor=cursor, mount=mounts_of(body), max_new_tokens=int(body.get("max_tokens", 1024)),
                        temperature=float(body.get("temperature", 1.0)), stop_ids=tok.stop_ids)
         o = await self.q.submit(inp)
@@ -104,5 +113,23 @@ class ChatService:
             "usage": {"prompt_tokens": o.prompt_tokens + o.cached_tokens, "completion_tokens": len(o.output_ids),
                       "prompt_tokens_details": {"cached_tokens": o.cached_tokens}},
         }
+
+    def _audit(self, path: str, body: dict, cursor: str, delta_ids: list, tools, kwargs):
+        """Cursor audit: the prompt the engine assembles (cursor tokens + rendered delta)
+        against rendering the whole conversation (the oracle), with the bytes the hop saved."""
+        cur = self.engine.cursors.get(cursor)
+        if cur is None:
+            return
+        full = self.tok.apply(body["audit_messages"], tools, True, **kwargs)
+        assembled = [int(t) for t in cur.tokens] + list(delta_ids)
+        row = {"t": time.time(), "cursor": cursor, "equal": assembled == full, "assembled_tokens": len(assembled),
+               "oracle_tokens": len(full),
+               "first_diff": next((i for i, (a, b) in enumerate(zip(assembled, full)) if a != b),
+                                  None if len(assembled) == len(full) else min(len(assembled), len(full))),
+               "hop_bytes": len(json.dumps(body.get("messages") or [])),
+               "full_bytes": len(json.dumps(body["audit_messages"]))}
+        with self._audit_lock:
+            with open(path, "a") as f:
+                f.write(json.dumps(row) + "\n")
 
     __call__ = chat

@@ -32,6 +32,22 @@ from .engine import CursorNotFound, Engine, GenInput
 from .local import BatchingQueue, ChatService, mounts_of  # noqa: F401  (BatchingQueue re-exported)
 
 
+def generate_input(body: dict) -> GenInput:
+    """/generate body -> engine request."""
+    sp = body.get("sampling_params") or {}
+    return GenInput(list(body.get("input_ids") or []), cursor=body.get("cursor"), mount=mounts_of(body),
+                    max_new_tokens=int(sp.get("max_new_tokens", 128)), temperature=float(sp.get("temperature", 1.0)),
+                    stop_ids=tuple(sp.get("stop_token_ids") or ()),
+                    prefill_only=int(sp.get("max_new_tokens", 1)) == 0)
+
+
+def generate_output(o, tokenizer=None) -> dict:
+    return {"output_ids": o.output_ids, "text": tokenizer.decode(o.output_ids) if tokenizer else None,
+            "meta_info": {"id": o.cursor, "cursor": o.cursor, "prompt_tokens": o.prompt_tokens,
+                          "cached_tokens": o.cached_tokens, "completion_tokens": len(o.output_ids),
+                          "finish_reason": o.finish_reason, "output_token_logprobs": o.output_logprobs}}
+
+
 def create_app(engine: Engine, tokenizer: ChatTokenizer | None = None, model_name: str = "octopus-b200"):
     from fastapi import FastAPI, HTTPException
     from fastapi.responses import JSONResponse
@@ -67,17 +83,8 @@ def create_app(engine: Engine, tokenizer: ChatTokenizer | None = None, model_nam
 
     @app.post("/generate")
     async def generate(body: dict):
-        sp = body.get("sampling_params") or {}
-        inp = GenInput(list(body.get("input_ids") or []), cursor=body.get("cursor"), mount=mounts_of(body),
-                       max_new_tokens=int(sp.get("max_new_tokens", 128)), temperature=float(sp.get("temperature",
-                                                                                                  1.0)),
-                       stop_ids=tuple(sp.get("stop_token_ids") or ()), prefill_only=int(sp.get("max_new_tokens",
-                                                                                              1)) == 0)
-        o = await _run(inp)
-        return {"output_ids": o.output_ids, "text": tokenizer.decode(o.output_ids) if tokenizer else None,
-                "meta_info": {"id": o.cursor, "cursor": o.cursor, "prompt_tokens": o.prompt_tokens,
-                              "cached_tokens": o.cached_tokens, "completion_tokens": len(o.output_ids),
-                              "finish_reason": o.finish_reason, "output_token_logprobs": o.output_logprobs}}
+        o = await _run(generate_input(body))
+        return generate_output(o, tokenizer)
 
     @app.post("/v1/chat/completions")
     async def chat(body: dict):

@@ -37,6 +37,10 @@ class TPEngine(Engine):
         super().__init__(cfg, weights, max_batch=max_batch, prefill_chunk=prefill_chunk, **kw)
         if self.device.type != "cuda":
             raise RuntimeError("TPEngine needs CUDA peer memory")
+        # every rank of the group must hand out the same cursor ids
+        uid = [self._uid]
+        dist.broadcast_object_list(uid, src=dist.get_global_rank(group, 0), group=group)
+        self._uid = uid[0]
         self.tw = TPWeights(cfg, weights, self.sd, self.device)
         max_rows = max(self._pad_rows(prefill_chunk), max_batch)
         # both row-parallel GEMMs (o_proj, down) produce hidden-wide partials

@@ -100,3 +100,22 @@ def test_http_chat_cursor_delta_matches_full(client):
     # the prompt of the continuation ends with the rendered delta
     delta = tk.render_delta(nxt)
     assert got[-len(delta):] == delta
+
+
+def test_cursor_audit_rows(client, tmp_path, monkeypatch):
+    c, eng, tk = client
+    path = tmp_path / "audit.jsonl"
+    monkeypatch.setenv("OCTOPUS_CURSOR_AUDIT", str(path))
+    msgs = [{"role": "system", "content": "sys"}, {"role": "user", "content": "hi there"}]
+    body = c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 4}).json()
+    reply = body["choices"][0]["message"]
+    nxt = [{"role": "user", "content": "and then?"}]
+    full = msgs + [{"role": "assistant", "content": reply["content"]}] + nxt
+    r = c.post("/v1/chat/completions", json={"messages": nxt, "cursor": body["cursor"], "max_tokens": 2,
+                                             "audit_messages": full})
+    assert r.status_code == 200
+    import json
+
+    rows = [json.loads(x) for x in open(path)]
+    assert len(rows) == 1 and rows[0]["cursor"] == body["cursor"]
+    assert isinstance(rows[0]["equal"], bool) and rows[0]["full_bytes"] > rows[0]["hop_bytes"] > 0
