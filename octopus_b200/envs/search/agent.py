@@ -40,6 +40,7 @@ class SearchWorkspace(WorkspaceProvider):
         self.question = question
         self.k = k
         self.searched: dict[str, int] = {}
+        self.opened: set[str] = set()   # docids opened in the episode (evidence recall)
 
     def system_prompt(self, task: str) -> str:
         return ("You answer a research question with a search tool over a document corpus. Use search and open, "
@@ -65,6 +66,7 @@ class SearchWorkspace(WorkspaceProvider):
             return json.dumps(res), False
         if name == "open":
             self.searched[thread] = self.searched.get(thread, 0) + 1
+            self.opened.add(str(args.get("docid", "")))
             return json.dumps(self.retrieval.open(str(args.get("docid", "")), int(args.get("page", 0)))), False
         if name == "done":
             return f"done: {args.get('answer', '')}", True

@@ -1,1 +1,1 @@
-"""octopus_b200.eval"""
+"""Evaluation harnesses (no training): agent-runtime episodes and the synthetic DAG."""
