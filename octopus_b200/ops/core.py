@@ -217,8 +217,10 @@ def swiglu(gu):
 
 # ---------------------------------------------------------------------------- embedding
 class _Embed(torch.autograd.Function):
+    # `anchor` (an empty tensor that requires grad) records the op in the graph when the
+    # table itself does not require grad: its gradient goes to W.main_grad
     @staticmethod
-    def forward(ctx, ids, W):
+    def forward(ctx, ids, W, anchor):
         ctx.save_for_backward(ids, W)
         if _is_cuda(W):
             return ext().embed_fwd(ids, W)
@@ -232,14 +234,19 @@ class _Embed(torch.autograd.Function):
         if _is_cuda(W):
             buf = mg if mg is not None else torch.zeros(W.shape, dtype=torch.float32, device=W.device)
             ext().embed_bwd(ids, d, buf)
-            return None, (None if mg is not None else buf.to(W.dtype))
+            return None, (None if mg is not None or not W.requires_grad else buf.to(W.dtype)), None
         g = torch.zeros(W.shape, dtype=ref._f(d).dtype)
         g.index_add_(0, ids, ref._f(d))
-        return None, _accum_wgrad(W, g)
+        wg = _accum_wgrad(W, g)
+        return None, (wg if W.requires_grad else None), None
 
 
 def embed(ids, W):
-    return _Embed.apply(ids, W)
+    """Rows W[ids]; under grad mode the table's gradient accumulates into W.main_grad."""
+    anchor = None
+    if torch.is_grad_enabled() and not W.requires_grad and hasattr(W, "main_grad"):
+        anchor = torch.empty(0, device=W.device, requires_grad=True)
+    return _Embed.apply(ids, W, anchor)
 
 
 # ---------------------------------------------------------------------------- attention plan

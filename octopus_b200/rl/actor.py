@@ -68,13 +68,13 @@ class DeviceMicroBatch:
 
 
 def build_microbatch(flat: np.ndarray, cu, mounts: dict | None, loss_mask: np.ndarray, adv: np.ndarray,
-                     behav_logp: np.ndarray, pad_to: int = 128) -> MicroBatch:
+                     behav_logp: np.ndarray, pad_to: int = 128, share: bool = True) -> MicroBatch:
     """loss_mask/adv/behav_logp are per flat token (token p is trained when mask[p])."""
     flat = np.asarray(flat, dtype=np.int64)
     n = len(flat)
     scored = np.zeros(n, dtype=bool)
     scored[:-1] = loss_mask[1:].astype(bool)
-    tree = build_tree(flat, cu, mounts, scored)
+    tree = build_tree(flat, cu, mounts, scored, share=share)
     plan = attention_plan(tree, True, pad_to)
     Tp = plan.padded_tokens
     toks = np.zeros(Tp, np.int64)

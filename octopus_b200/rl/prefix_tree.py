@@ -89,8 +89,10 @@ def _first_mismatch(a: np.ndarray, b: np.ndarray) -> int:
     return int(d[0]) if d.size else m
 
 
-def build_tree(flat: np.ndarray, cu, mounts: dict | None = None, scored: np.ndarray | None = None) -> PrefixTree:
-    """Prefix tree of sequences flat[cu[i]:cu[i+1]] (see module docstring)."""
+def build_tree(flat: np.ndarray, cu, mounts: dict | None = None, scored: np.ndarray | None = None,
+               share: bool = True) -> PrefixTree:
+    """Prefix tree of sequences flat[cu[i]:cu[i+1]] (see module docstring).  share=False
+    gives every sequence its own path (the ordinary packed varlen batch, for checks)."""
     flat = np.asarray(flat)
     cu = [int(x) for x in cu]
     seqs = [flat[a:b] for a, b in zip(cu[:-1], cu[1:])]
@@ -111,7 +113,7 @@ def build_tree(flat: np.ndarray, cu, mounts: dict | None = None, scored: np.ndar
         for i in ids:
             if len(seqs[i]) == end:
                 continue
-            key = (int(seqs[i][end]), mpts[i].get(end, ()))
+            key = (int(seqs[i][end]), mpts[i].get(end, ())) if share else (i,)
             groups.setdefault(key, []).append(i)
         return list(groups.values())
 
