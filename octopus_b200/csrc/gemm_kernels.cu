@@ -1,4 +1,6 @@
 // Instantiations and launcher of the tcgen05 GEMM (no torch headers in this unit).
+#include <algorithm>
+
 #include "gemm_sm100.cuh"
 #include "head_epilogue.cuh"
 
@@ -53,12 +55,61 @@ void gemm_launch(const GemmLaunch& g) {
                   g.vocab_limit};
     if (g.bn == 256) launch_one<256, false, false>(g, e);
     else launch_one<128, false, false>(g, e);
+  } else if (g.epi == kEpiSplitK) {
+    EpiSplitK e{reinterpret_cast<float*>(g.C), g.s.M, g.s.N, nullptr};
+    by_bn(g, e);
   } else if (g.epi == kEpiSample) {
     EpiSample e{g.partial, g.s.n_tiles, g.bn, g.alpha, g.vocab_limit, g.seed, g.row_offset, g.col_base};
     if (g.bn == 256) launch_one<256, false, false>(g, e);
     else if (g.bn == 128) launch_one<128, false, false>(g, e);
     else launch_one<64, false, false>(g, e);
   }
+}
+
+// out = sum of the split partials (+ bias) (+ residual), 8 columns per thread
+__global__ void splitk_finish_kernel(const float* __restrict__ ws, int splits, int M, int N,
+                                     const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ res,
+                                     int ldr, __nv_bfloat16* __restrict__ out, int ldc) {
+  const int n8 = N / 8;
+  const size_t total = static_cast<size_t>(M) * n8;
+  const size_t plane = static_cast<size_t>(M) * N;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(i / n8), c = static_cast<int>(i - static_cast<size_t>(row) * n8) * 8;
+    float a[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a[e] = 0.f;
+    const float* p = ws + static_cast<size_t>(row) * N + c;
+    for (int s = 0; s < splits; ++s) {
+      const float4 x = *reinterpret_cast<const float4*>(p + s * plane);
+      const float4 y = *reinterpret_cast<const float4*>(p + s * plane + 4);
+      a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
+      a[4] += y.x; a[5] += y.y; a[6] += y.z; a[7] += y.w;
+    }
+    if (bias != nullptr) {
+      float b[8];
+      load8(bias + c, b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a[e] += b[e];
+    }
+    if (res != nullptr) {
+      float r[8];
+      load8(res + static_cast<size_t>(row) * ldr + c, r);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a[e] += r[e];
+    }
+    store8(out + static_cast<size_t>(row) * ldc + c, a);
+  }
+}
+
+void splitk_finish(const float* ws, int splits, int M, int N, const void* bias, const void* residual, int ldr,
+                   void* out, int ldc, cudaStream_t st) {
+  const size_t total = static_cast<size_t>(M) * (N / 8);
+  if (total == 0) return;
+  const int grid = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 8));
+  splitk_finish_kernel<<<grid, 256, 0, st>>>(ws, splits, M, N, static_cast<const __nv_bfloat16*>(bias),
+                                             static_cast<const __nv_bfloat16*>(residual), ldr,
+                                             static_cast<__nv_bfloat16*>(out), ldc);
 }
 
 }  // namespace octo

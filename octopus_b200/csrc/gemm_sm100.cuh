@@ -44,7 +44,20 @@ struct GemmCfg {
 };
 
 
-__device__ __forceinline__ void gemm_tile_coords(const GemmShape& s, int tile, int& mb, int& nb) {
+// K range of a tile's split: [kb0, kb1) in 64-wide K blocks
+__device__ __forceinline__ void gemm_split_range(const GemmShape& s, int ks, int& kb0, int& kb1) {
+  const int splits = s.k_splits > 1 ? s.k_splits : 1;
+  const int per = (s.k_blocks + splits - 1) / splits;
+  kb0 = min(s.k_blocks, ks * per);
+  kb1 = min(s.k_blocks, kb0 + per);
+}
+
+// tile -> (M-block, N-block, K split); splits are the slowest index so CTAs running at the
+// same time share their K slice of A in L2
+__device__ __forceinline__ void gemm_tile_coords(const GemmShape& s, int tile, int& mb, int& nb, int& ks) {
+  const int per_split = s.m_tiles * s.n_tiles;
+  ks = tile / per_split;
+  tile -= ks * per_split;
   const int group_span = kGemmGroupM * s.n_tiles;
   const int group = tile / group_span;
   const int first_m = group * kGemmGroupM;
@@ -141,10 +154,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < shape.num_tiles && ok; tile += gridDim.x) {
-        int mb, nb;
-        gemm_tile_coords(shape, tile, mb, nb);
+        int mb, nb, ks, kb0, kb1;
+        gemm_tile_coords(shape, tile, mb, nb, ks);
+        gemm_split_range(shape, ks, kb0, kb1);
         const int n0 = nb * BN;
-        for (int kb = 0; kb < shape.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, 100 + stage)) {
             ok = false;
             break;
@@ -152,7 +166,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int k0 = kb * kGemmBK;
           uint8_t* a_dst = sA + stage * Cfg::kABytes;
           uint8_t* b_dst = sB + stage * Cfg::kBBytes;
-          if (kb == 0 && !asrc.ready(mb, ready_mask, abort_flag, status)) {  // peer data of this M-block published?
+          if (kb == kb0 && !asrc.ready(mb, ready_mask, abort_flag, status)) {  // peer data of this M-block published?
             ok = false;
             break;
           }
@@ -200,7 +214,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < shape.k_blocks; ++kb) {
+        int mb_, nb_, ks, kb0, kb1;
+        gemm_tile_coords(shape, tile, mb_, nb_, ks);
+        gemm_split_range(shape, ks, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag, status, 300 + stage)) {
             ok = false;
             break;
@@ -221,7 +238,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             } else {
               db = umma_smem_desc(b_addr + kk * 2048, 8192, 1024);
             }
-            umma_f16_ss(d_tmem, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
+            umma_f16_ss(d_tmem, da, db, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           issued_any = true;
           umma_commit(&empty_bar[stage]);
@@ -256,10 +273,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int tile = blockIdx.x; tile < shape.num_tiles; tile += gridDim.x) {
       if (!mbar_wait(&accf_bar[acc], acc_phase, abort_flag, status, 400 + acc)) break;
       tc_fence_after();
-      int mb, nb;
-      gemm_tile_coords(shape, tile, mb, nb);
+      int mb, nb, ks;
+      gemm_tile_coords(shape, tile, mb, nb, ks);
       const int row = mb * kGemmBM + quarter * 32 + lane;
       const int n0 = nb * BN;
+      epi.begin_split(ks);
       epi.begin_tile();
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -346,6 +364,7 @@ struct EpiBF16 {
       }
     }
   }
+  __device__ __forceinline__ void begin_split(int) {}
   __device__ __forceinline__ void begin_tile() {}
   __device__ __forceinline__ void end_tile(int, int) {}
   __device__ __forceinline__ void finish() const {}
@@ -374,7 +393,25 @@ struct EpiF32 {
       }
     }
   }
+  __device__ __forceinline__ void begin_split(int) {}
   __device__ __forceinline__ void begin_tile() {}
+  __device__ __forceinline__ void end_tile(int, int) {}
+  __device__ __forceinline__ void finish() const {}
+};
+
+// fp32 partial of K split `ks` -> ws[ks][row][col] (row stride N); a finish kernel sums the splits
+struct EpiSplitK {
+  float* ws;
+  int M, N;
+  float* cur;
+  __device__ __forceinline__ void begin_split(int ks) { cur = ws + static_cast<size_t>(ks) * M * N; }
+  __device__ __forceinline__ void begin_tile() {}
+  __device__ __forceinline__ void apply(int row, int col0, int nvalid, float (&v)[32], int) {
+    float* dst = cur + static_cast<size_t>(row) * N + col0;
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      if (g * 4 < nvalid) *reinterpret_cast<float4*>(dst + g * 4) = make_float4(v[g * 4], v[g * 4 + 1], v[g * 4 + 2], v[g * 4 + 3]);
+  }
   __device__ __forceinline__ void end_tile(int, int) {}
   __device__ __forceinline__ void finish() const {}
 };

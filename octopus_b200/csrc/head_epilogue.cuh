@@ -68,6 +68,7 @@ struct EpiHeadLse {
   float m, s, t, zl;
   int label;
 
+  __device__ __forceinline__ void begin_split(int) {}
   __device__ __forceinline__ void begin_tile() {
     m = -INFINITY;
     s = 0.f;
@@ -121,6 +122,7 @@ struct EpiSample {
   uint32_t key;
   bool have_stream;
 
+  __device__ __forceinline__ void begin_split(int) {}
   __device__ __forceinline__ void begin_tile() {
     m = -INFINITY;
     s = 0.f;
@@ -188,6 +190,7 @@ struct EpiHeadGrad {
   const float* g_ent;
   float alpha;
   int vocab_limit;
+  __device__ __forceinline__ void begin_split(int) {}
   __device__ __forceinline__ void begin_tile() {}
   __device__ __forceinline__ void apply(int row, int col0, int nvalid, float (&v)[32], int) {
     const int lab = labels[row];

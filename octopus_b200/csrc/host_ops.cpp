@@ -5,6 +5,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -146,6 +147,27 @@ static GemmLaunch make_launch(const torch::Tensor& A, bool a_mn, const torch::Te
   return g;
 }
 
+// Split-K for decode-sized forward GEMMs (K-major operands, bf16 out, alpha 1): with
+// BN = 256 the N-tiles cannot fill the GPU, so K is split until ~one tile per SM, keeping
+// >= 4 K blocks per split.  Rebuilds the launch's B map for BN = 256.  Returns 1 for none.
+static int splitk_factor(GemmLaunch& g, int64_t bn_hint, int device, const torch::Tensor& B) {
+  if (bn_hint != 0 || g.a_mn || g.b_mn || g.alpha != 1.f || g.s.M > 256 || g.s.N < 256) return 1;
+  if (const char* e = std::getenv("OCTO_SPLITK"); e != nullptr && e[0] == '0') return 1;
+  const int sms = num_sms(device);
+  const int n_tiles = (g.s.N + 255) / 256;
+  const int tiles = g.s.m_tiles * n_tiles;
+  if (tiles * 4 >= sms * 3) return 1;
+  int splits = std::min(sms / tiles, g.s.k_blocks / 4);
+  if (splits < 2) return 1;
+  g.bn = 256;
+  g.s.n_tiles = n_tiles;
+  g.s.k_splits = splits;
+  g.s.num_tiles = tiles * splits;
+  g.grid = std::min(g.s.num_tiles, sms);
+  g.tb = make_tmap_bf16_2d(B.data_ptr(), g.s.K, g.s.N, B.stride(0), 64, 256);
+  return splits;
+}
+
 // C[M,N] = alpha * A_log[M,K] @ B_log[N,K]^T (+ bias) (+ residual)   or   C += ... (fp32)
 //   a_mn false: A is [M, K];  true: A is [K, M].   b_mn false: B is [N, K];  true: B is [K, N].
 void gemm_out(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, torch::Tensor C, double alpha,
@@ -162,6 +184,35 @@ void gemm_out(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, torch::Ten
   if (C.scalar_type() == torch::kBFloat16) {
     TORCH_CHECK(!accumulate, "gemm: accumulate requires an fp32 output");
     TORCH_CHECK(C.stride(0) % 8 == 0, "gemm: output row stride must be a multiple of 8");
+    const int splits = splitk_factor(g, bn_hint, A.get_device(), B);
+    if (splits > 1) {
+      // decode-sized M: wide N tiles (each CTA re-reads fewer activation bytes) split along K so
+      // every SM streams weights; fp32 partials are summed with bias / residual by splitk_finish
+      auto ws = torch::empty({splits, g.s.M, g.s.N}, C.options().dtype(torch::kFloat32));
+      g.epi = kEpiSplitK;
+      g.C = ws.data_ptr();
+      gemm_launch(g);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      const void* rp = nullptr;
+      int ldr = 0;
+      if (residual.has_value() && residual->defined()) {
+        CHECK_BF16(*residual);
+        TORCH_CHECK(residual->size(0) == g.s.M && residual->size(1) == g.s.N && residual->stride(1) == 1 &&
+                        residual->stride(0) % 8 == 0,
+                    "gemm: bad residual");
+        rp = residual->data_ptr();
+        ldr = residual->stride(0);
+      }
+      const void* bp = nullptr;
+      if (bias.has_value() && bias->defined()) {
+        CHECK_BF16(*bias);
+        TORCH_CHECK(bias->is_contiguous() && bias->numel() == g.s.N, "gemm: bias must have N elements");
+        bp = bias->data_ptr();
+      }
+      splitk_finish(ws.data_ptr<float>(), splits, g.s.M, g.s.N, bp, rp, ldr, C.data_ptr(), C.stride(0), g.stream);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      return;
+    }
     g.epi = kEpiBF16;
     if (residual.has_value() && residual->defined()) {
       const auto& R = *residual;

@@ -12,6 +12,7 @@ struct GemmShape {
   int M, N, K;
   int m_tiles, n_tiles, k_blocks, num_tiles;
   int m_shift;  // M-block rotation of the tile order (tensor-parallel: own rows first)
+  int k_splits; // split-K factor (0 or 1: none); tiles = k_splits x m_tiles x n_tiles
 };
 
 enum GemmEpiKind : int {
@@ -20,6 +21,7 @@ enum GemmEpiKind : int {
   kEpiHeadLse = 2,  // per (row, n-tile) partial (max, sumexp, sum z*exp, label logit)
   kEpiSample = 3,   // per (row, n-tile) partial (max, sumexp, best gumbel score, argmax)
   kEpiHeadGrad = 4, // C bf16 = d(loss)/d(logit) of the logprob head, recomputed from lse/entropy
+  kEpiSplitK = 5,   // fp32 partial of one K split -> workspace[split][M][N] (then splitk_finish)
 };
 
 struct GemmLaunch {
@@ -52,6 +54,9 @@ struct GemmLaunch {
 };
 
 void gemm_launch(const GemmLaunch& g);
+// out[M, N] bf16 = sum_s ws[s][M][N] (+ bias[N]) (+ residual[M, N], row stride ldr)
+void splitk_finish(const float* ws, int splits, int M, int N, const void* bias, const void* residual, int ldr,
+                   void* out, int ldc, cudaStream_t st);
 int gemm_smem_bytes(int bn);
 
 }  // namespace octo

@@ -206,6 +206,7 @@ struct EpiRS {
   __nv_bfloat16* dst[kMaxTp];
   int ldc, rows_s;
   TpSlot slot;
+  __device__ __forceinline__ void begin_split(int) {}
   __device__ __forceinline__ void begin_tile() {}
   __device__ __forceinline__ void apply(int row, int col0, int nvalid, float (&v)[32], int) {
     const int owner = row / rows_s;

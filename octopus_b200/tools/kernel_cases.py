@@ -14,6 +14,7 @@ Cases (inputs sized above L2 where DRAM behaviour matters, a few GB at most):
                      8 rows; each row = shared 2048-token prefix + planner segment (shared
                      by 2 rows) + own 272 tokens
   decode_dag_flat    same lengths, every row's keys distinct (no sharing)
+  decode_gemms       the four GEMMs of one 7B decoder layer at 256 decode rows (OCTO_SPLITK=0: no split-K)
   head_fwd           fused logprob head, 4096 rows x 152064 vocab
   sample_head        fused sampling head, 256 rows x 152064 vocab
 """
@@ -110,6 +111,14 @@ def build(case: str, dev):
         q, kc, vc, ip, idx, Hq, Hkv, D, B = decode_case(dev)
         da = ops.DecodeAttention(Hq, Hkv, D, B, 8, dev, persistent=case == "decode_persistent")
         return lambda: da(q, kc, vc, ip, idx)
+    if case == "decode_gemms":
+        M, H, F = 256, 3584, 18944
+        x = torch.randn(M, H, device=dev).bfloat16()
+        ws = [(torch.randn(n, k, device=dev) * 0.02).bfloat16() for n, k in ((4608, H), (H, 3584), (2 * F, H), (H, F))]
+        xa = torch.randn(M, 3584, device=dev).bfloat16()
+        xf = torch.randn(M, F, device=dev).bfloat16()
+        ins = (x, xa, x, xf)
+        return lambda: [ops.gemm(i, w) for i, w in zip(ins, ws)]
     if case in ("decode_dag", "decode_dag_flat"):
         q, kc, vc, ip, idx, Hq, Hkv, D, B = decode_dag_case(dev, case == "decode_dag")
         da = ops.DecodeAttention(Hq, Hkv, D, B, 8, dev, persistent=True)

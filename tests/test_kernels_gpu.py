@@ -337,3 +337,19 @@ def test_shared_prefix_decode_matches_persistent():
         ops.check_status(0)
         assert rel_err(a[:n], b[:n]) < 1e-2
         assert float(a[n:].float().abs().max()) == 0.0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(16, 4608, 3584), (128, 3584, 18944), (256, 3584, 3584), (200, 512, 1024)])
+def test_splitk_decode_gemm(M, N, K):
+    """Decode-sized GEMMs take the split-K path (fp32 partials + finish with bias/residual)."""
+    torch.manual_seed(16)
+    a = (torch.randn(M, K, device=dev) * 0.5).bfloat16()
+    w = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
+    b = (torch.randn(N, device=dev) * 0.1).bfloat16()
+    r = torch.randn(M, N, device=dev).bfloat16()
+    out = ops.gemm(a, w, bias=b, residual=r)
+    torch.cuda.synchronize()
+    ops.check_status(0)
+    ref_ = a.float() @ w.float().t() + b.float() + r.float()
+    assert rel_err(out, ref_) < 1e-2
