@@ -14,6 +14,7 @@ Cases (inputs sized above L2 where DRAM behaviour matters, a few GB at most):
                      8 rows; each row = shared 2048-token prefix + planner segment (shared
                      by 2 rows) + own 272 tokens
   decode_dag_flat    same lengths, every row's keys distinct (no sharing)
+  decode_dag_shared  the decode_dag rows on the shared-prefix kernel (segments planned once)
   decode_gemms       the four GEMMs of one 7B decoder layer at 256 decode rows (OCTO_SPLITK=0: no split-K)
   head_fwd           fused logprob head, 4096 rows x 152064 vocab
   sample_head        fused sampling head, 256 rows x 152064 vocab
@@ -52,6 +53,26 @@ def decode_case(dev):
     idx = torch.randperm(B * L, device=dev).to(torch.int32)
     q = torch.randn(B, Hq * D, device=dev).bfloat16()
     return q, kc, vc, ip, idx, Hq, Hkv, D, B
+
+
+def decode_dag_rows(share: bool):
+    n_inst, per, pre, plan, own = 32, 8, 2048, 528, 272
+    rows, ctx, nxt = [], [], 0
+
+    def take(n):
+        nonlocal nxt
+        r = np.arange(nxt, nxt + n)
+        nxt += n
+        return r
+
+    for i in range(n_inst):
+        p = take(pre)
+        for s in range(per // 2):
+            pl = take(plan)
+            for k in range(2):
+                rows.append(np.concatenate([p, pl, take(own)]) if share else take(pre + plan + own))
+                ctx.append(pre + plan)
+    return rows, np.asarray(ctx), nxt
 
 
 def decode_dag_case(dev, share: bool):
@@ -119,6 +140,19 @@ def build(case: str, dev):
         xf = torch.randn(M, F, device=dev).bfloat16()
         ins = (x, xa, x, xf)
         return lambda: [ops.gemm(i, w) for i, w in zip(ins, ws)]
+    if case == "decode_dag_shared":
+        Hq, Hkv, D = 28, 4, 128
+        rows, ctx, nslots = decode_dag_rows(True)
+        B = len(rows)
+        kc = torch.randn(nslots, Hkv * D, device=dev).bfloat16()
+        vc = torch.randn(nslots, Hkv * D, device=dev).bfloat16()
+        starts = np.cumsum([0] + [len(r) for r in rows[:-1]]).astype(np.int32)
+        idx = torch.from_numpy(np.concatenate(rows).astype(np.int32)).to(dev)
+        ln = torch.tensor([len(r) for r in rows], dtype=torch.int32, device=dev)
+        q = torch.randn(B, Hq * D, device=dev).bfloat16()
+        sd = ops.SharedDecode(Hq, Hkv, D, B, dev)
+        assert sd.plan(rows, starts, ctx, np.asarray([len(r) for r in rows]), B)
+        return lambda: sd(q, kc, vc, idx, ln)
     if case in ("decode_dag", "decode_dag_flat"):
         q, kc, vc, ip, idx, Hq, Hkv, D, B = decode_dag_case(dev, case == "decode_dag")
         da = ops.DecodeAttention(Hq, Hkv, D, B, 8, dev, persistent=True)
@@ -139,15 +173,29 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case")
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--graph", action="store_true", help="time CUDA-graph replays (no host launch overhead)")
     args = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     fn = build(args.case, dev)
     fn()
     torch.cuda.synchronize()
+    run = fn
+    if args.graph:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        run = g.replay
+        run()
+        torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.reps):
-        fn()
+        run()
     b.record()
     torch.cuda.synchronize()
     ops.check_status(0)
