@@ -6,6 +6,7 @@
 #include <torch/extension.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <vector>
 
 #include "tmap.h"
@@ -60,6 +61,26 @@ static GemmLaunch base_launch(int M, const torch::Tensor& W, int bn_hint) {
 
 // stage: local bf16 [tp * rows_s, K] staging buffer; work: local int32 counters
 // [1 + m_tiles], zero between calls (the kernel's last CTA resets them).
+// Split-K for decode-sized tensor-parallel GEMMs (see host_ops.cpp splitk_factor): BN = 256
+// tiles split along K to about one tile per SM; returns 1 for none.  Rebuilds the B map.
+static int tp_splits(GemmLaunch& g, const torch::Tensor& W) {
+  if (g.s.M > 256 || g.s.N < 256) return 1;
+  if (const char* e = std::getenv("OCTO_SPLITK"); e != nullptr && e[0] == '0') return 1;
+  const int sms = num_sms(W.get_device());
+  const int n_tiles = (g.s.N + 255) / 256;
+  const int tiles = g.s.m_tiles * n_tiles;
+  if (tiles * 4 >= sms * 3) return 1;
+  const int splits = std::min(sms / tiles, g.s.k_blocks / 4);
+  if (splits < 2) return 1;
+  g.bn = 256;
+  g.s.n_tiles = n_tiles;
+  g.s.k_splits = splits;
+  g.s.num_tiles = tiles * splits;
+  g.grid = std::min(g.s.num_tiles, sms);
+  g.tb = make_tmap_bf16_2d(W.data_ptr(), g.s.K, g.s.N, W.stride(0), 64, 256);
+  return splits;
+}
+
 static AgLaunch ag_launch(const std::vector<int64_t>& x_ptrs, int64_t rows_s, int64_t ldx, const torch::Tensor& W,
                           int64_t me, int64_t sync_local, const std::vector<int64_t>& sync_ptrs, int64_t slot,
                           int64_t bn_hint, const torch::Tensor& stage, const torch::Tensor& work) {
@@ -103,22 +124,38 @@ void ag_gemm_t(std::vector<int64_t> x_ptrs, int64_t rows_s, int64_t ldx, torch::
   TORCH_CHECK(C.is_cuda() && C.scalar_type() == torch::kBFloat16 && C.dim() == 2 && C.size(0) == L.g.s.M &&
                   C.size(1) == L.g.s.N && C.stride(1) == 1 && C.stride(0) % 8 == 0,
               "ag_gemm: C must be bf16 [tp*rows_s, N]");
-  L.g.epi = kEpiBF16;
-  L.g.C = C.data_ptr();
-  L.g.ldc = C.stride(0);
+  const void* bp = nullptr;
   if (bias.has_value() && bias->defined()) {
     TORCH_CHECK(bias->scalar_type() == torch::kBFloat16 && bias->is_contiguous() && bias->numel() == L.g.s.N,
                 "ag_gemm: bias bf16 [N]");
-    L.g.bias = bias->data_ptr();
+    bp = bias->data_ptr();
   }
+  const int splits = tp_splits(L.g, W);
+  if (splits > 1) {
+    auto ws = torch::empty({splits, L.g.s.M, L.g.s.N}, C.options().dtype(torch::kFloat32));
+    L.g.epi = kEpiSplitK;
+    L.g.C = ws.data_ptr();
+    L.peer_grid = L.g.grid;
+    ag_gemm_launch(L);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    splitk_finish(ws.data_ptr<float>(), splits, L.g.s.M, L.g.s.N, bp, nullptr, 0, C.data_ptr(), C.stride(0),
+                  L.g.stream);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  L.g.epi = kEpiBF16;
+  L.g.C = C.data_ptr();
+  L.g.ldc = C.stride(0);
+  L.g.bias = bp;
   ag_gemm_launch(L);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // Partial A[M, K_loc] @ W[N, K_loc]^T stored into the owners' receive buffers; returns
 // the grid (the number of signals the owners' reduce must wait for).
-int64_t gemm_rs_t(torch::Tensor A, torch::Tensor W, std::vector<int64_t> recv_ptrs, int64_t me, int64_t sync_local,
-                  std::vector<int64_t> sync_ptrs, int64_t slot, int64_t bn_hint) {
+std::vector<int64_t> gemm_rs_t(torch::Tensor A, torch::Tensor W, std::vector<int64_t> recv_ptrs, int64_t recv_elems,
+                               int64_t me, int64_t sync_local, std::vector<int64_t> sync_ptrs, int64_t slot,
+                               int64_t bn_hint) {
   c10::cuda::CUDAGuard guard(A.get_device());
   TORCH_CHECK(A.is_cuda() && A.scalar_type() == torch::kBFloat16 && A.dim() == 2 && A.stride(1) == 1,
               "gemm_rs: A bf16 [M, K] row-major");
@@ -134,24 +171,29 @@ int64_t gemm_rs_t(torch::Tensor A, torch::Tensor W, std::vector<int64_t> recv_pt
   L.ldc = L.g.s.N;
   L.rows_s = M / tp;
   L.slot = make_slot(sync_local, sync_ptrs, me, slot);
+  const int splits = bn_hint == 0 ? tp_splits(L.g, W) : 1;
+  if (splits > 1) L.g.ta = make_tmap_bf16_2d(A.data_ptr(), L.g.s.K, M, A.stride(0), 64, 128);
+  TORCH_CHECK(static_cast<int64_t>(splits) * M * L.g.s.N <= recv_elems,
+              "gemm_rs: receive buffers too small for ", splits, " split partials");
   gemm_rs_launch(L);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return L.g.grid;
+  return {L.g.grid, splits};
 }
 
 // h[rows_s, N] += sum_r recv[r]; x = rmsnorm(h) * w (if w given)
-void tp_reduce_t(torch::Tensor recv, torch::Tensor h, c10::optional<torch::Tensor> w, c10::optional<torch::Tensor> x,
-                 double eps, bool plus_one, int64_t me, int64_t sync_local, std::vector<int64_t> sync_ptrs,
-                 int64_t slot, int64_t peer_grid) {
+void tp_reduce_t(torch::Tensor recv, int64_t splits, torch::Tensor h, c10::optional<torch::Tensor> w,
+                 c10::optional<torch::Tensor> x, double eps, bool plus_one, int64_t me, int64_t sync_local,
+                 std::vector<int64_t> sync_ptrs, int64_t slot, int64_t peer_grid) {
   c10::cuda::CUDAGuard guard(h.get_device());
   const int tp = static_cast<int>(sync_ptrs.size());
   TORCH_CHECK(h.scalar_type() == torch::kBFloat16 && h.dim() == 2 && h.stride(1) == 1 && h.stride(0) % 8 == 0,
               "tp_reduce: h bf16 [rows, N]");
   const int rows_s = h.size(0), N = h.size(1);
   TORCH_CHECK(N % 8 == 0, "tp_reduce: N % 8 == 0");
+  const int parts = static_cast<int>(splits) * tp;
   TORCH_CHECK(recv.scalar_type() == torch::kBFloat16 && recv.is_contiguous() &&
-                  recv.numel() >= static_cast<int64_t>(tp) * rows_s * N,
-              "tp_reduce: recv bf16 [tp, rows, N]");
+                  recv.numel() >= static_cast<int64_t>(parts) * rows_s * N,
+              "tp_reduce: recv bf16 [splits * tp, rows, N]");
   const void* wp = nullptr;
   void* xp = nullptr;
   int ldx = 0;
@@ -165,7 +207,7 @@ void tp_reduce_t(torch::Tensor recv, torch::Tensor h, c10::optional<torch::Tenso
     ldx = x->stride(0);
   }
   TpSlot s = make_slot(sync_local, sync_ptrs, me, slot);
-  tp_reduce(recv.data_ptr(), h.data_ptr(), h.stride(0), N, rows_s, wp, xp, ldx, static_cast<float>(eps),
+  tp_reduce(recv.data_ptr(), parts, h.data_ptr(), h.stride(0), N, rows_s, wp, xp, ldx, static_cast<float>(eps),
             plus_one ? 1 : 0, s, static_cast<int>(peer_grid), status_ptr(h.get_device()),
             at::cuda::getCurrentCUDAStream(h.get_device()).stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -206,12 +206,13 @@ struct EpiRS {
   __nv_bfloat16* dst[kMaxTp];
   int ldc, rows_s;
   TpSlot slot;
-  __device__ __forceinline__ void begin_split(int) {}
+  int part;  // receive slot: split * tp + sending rank (split-K partials are summed by the owner)
+  __device__ __forceinline__ void begin_split(int ks) { part = ks * slot.tp + slot.me; }
   __device__ __forceinline__ void begin_tile() {}
   __device__ __forceinline__ void apply(int row, int col0, int nvalid, float (&v)[32], int) {
     const int owner = row / rows_s;
     __nv_bfloat16* out =
-        dst[owner] + (static_cast<size_t>(slot.me) * rows_s + (row - owner * rows_s)) * ldc + col0;
+        dst[owner] + (static_cast<size_t>(part) * rows_s + (row - owner * rows_s)) * ldc + col0;
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       if (g * 8 < nvalid) {
@@ -264,6 +265,13 @@ void ag_gemm_launch(const AgLaunch& L) {
   a.peer_grid = L.peer_grid;
   EpiBF16 e{reinterpret_cast<__nv_bfloat16*>(g.C), g.ldc, reinterpret_cast<const __nv_bfloat16*>(g.R), g.ldr,
             g.alpha, reinterpret_cast<const __nv_bfloat16*>(g.bias)};
+  if (g.epi == kEpiSplitK) {
+    EpiSplitK es{reinterpret_cast<float*>(g.C), g.s.M, g.s.N, nullptr};
+    if (g.bn == 256) launch_tp<256>(g, es, a);
+    else if (g.bn == 128) launch_tp<128>(g, es, a);
+    else launch_tp<64>(g, es, a);
+    return;
+  }
   if (g.epi == kEpiSample) {
     EpiSample es{g.partial, g.s.n_tiles, g.bn, g.alpha, g.vocab_limit, g.seed, g.row_offset, g.col_base};
     if (g.bn == 256) launch_tp<256>(g, es, a);
@@ -283,6 +291,7 @@ void gemm_rs_launch(const RsLaunch& L) {
   e.ldc = L.ldc;
   e.rows_s = L.rows_s;
   e.slot = L.slot;
+  e.part = L.slot.me;
   ALocal<false> a{g.ta};
   if (g.bn == 256) launch_tp<256>(g, e, a);
   else if (g.bn == 128) launch_tp<128>(g, e, a);
@@ -290,8 +299,8 @@ void gemm_rs_launch(const RsLaunch& L) {
 }
 
 // ---------------------------------------------------------------- reduce (+ RMSNorm)
-__global__ void tp_reduce_kernel(const __nv_bfloat16* __restrict__ recv, __nv_bfloat16* h, int ldh, int N,
-                                 int rows_s, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* x, int ldx,
+__global__ void tp_reduce_kernel(const __nv_bfloat16* __restrict__ recv, int parts, __nv_bfloat16* h, int ldh,
+                                 int N, int rows_s, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* x, int ldx,
                                  float eps, int plus_one, TpSlot slot, int peer_grid, int* status) {
   __shared__ int ok;
   if (threadIdx.x == 0) ok = wait_peers(slot, peer_grid, status, 960) ? 1 : 0;
@@ -304,7 +313,7 @@ __global__ void tp_reduce_kernel(const __nv_bfloat16* __restrict__ recv, __nv_bf
       for (int c = lane * 8; c < N; c += 256) {
         float a[8];
         load8(hr + c, a);
-        for (int r = 0; r < slot.tp; ++r) {
+        for (int r = 0; r < parts; ++r) {
           float b[8];
           load8(recv + (static_cast<size_t>(r) * rows_s + row) * N + c, b);
 #pragma unroll
@@ -345,10 +354,11 @@ __global__ void tp_reduce_kernel(const __nv_bfloat16* __restrict__ recv, __nv_bf
   if (threadIdx.x == 0) consume(slot, peer_grid);
 }
 
-int tp_reduce(const void* recv, void* h, int ldh, int N, int rows_s, const void* w, void* x, int ldx, float eps,
-              int plus_one, const TpSlot& slot, int peer_grid, int* status, cudaStream_t st) {
+int tp_reduce(const void* recv, int parts, void* h, int ldh, int N, int rows_s, const void* w, void* x, int ldx,
+              float eps, int plus_one, const TpSlot& slot, int peer_grid, int* status, cudaStream_t st) {
   const int grid = max(1, min((rows_s + 7) / 8, 148 * 4));
-  tp_reduce_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(recv), static_cast<__nv_bfloat16*>(h),
+  tp_reduce_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(recv), parts,
+                                         static_cast<__nv_bfloat16*>(h),
                                          ldh, N, rows_s, static_cast<const __nv_bfloat16*>(w),
                                          static_cast<__nv_bfloat16*>(x), ldx, eps, plus_one, slot, peer_grid, status);
   return grid;

@@ -47,7 +47,8 @@ struct AgLaunch {
 void ag_gemm_launch(const AgLaunch& a);
 
 // GEMM -> RS: partial C = A[M, K_loc] @ W[N, K_loc]^T; rows of rank p's shard are stored
-// (bf16) into p's receive buffer at [me][row - p * rows_s][:] by peer stores.
+// (bf16) into p's receive buffer at [split * tp + me][row - p * rows_s][:] by peer stores
+// (split-K for decode-sized M: every split's partial goes to its own slot).
 struct RsLaunch {
   GemmLaunch g;
   void* recv[kMaxTp];         // rank r's receive buffer [tp][rows_s][ldc] bf16
@@ -58,8 +59,9 @@ void gemm_rs_launch(const RsLaunch& r);
 
 // h[rows_s, N] += sum_r recv[r][rows_s, N] (fixed rank order), optionally
 // x = rmsnorm(h) * (w or 1 + w).  Waits for every peer's RS signals first.
-int tp_reduce(const void* recv, void* h, int ldh, int N, int rows_s, const void* w, void* x, int ldx, float eps,
-              int plus_one, const TpSlot& slot, int peer_grid, int* status, cudaStream_t st);
+// recv holds `parts` = splits * tp partial slices [parts][rows_s][N].
+int tp_reduce(const void* recv, int parts, void* h, int ldh, int N, int rows_s, const void* w, void* x, int ldx,
+              float eps, int plus_one, const TpSlot& slot, int peer_grid, int* status, cudaStream_t st);
 
 // Vocab-parallel sampling: local combine of the sampling partials, exchange of
 // (max, sum, best score, best column) per row with every rank, then the final merge.

@@ -207,7 +207,9 @@ class TPGroup:
         C = ops.ext()
         self.sync = PeerBuffers(C.tp_sync_bytes(), self.device, group)
         self.xbuf = PeerBuffers(self.max_rows_s * hidden * 2, self.device, group)
-        self.recv = PeerBuffers(self.tp * self.max_rows_s * max_n * 2, self.device, group)
+        # RS receive slots: [splits * tp][rows][N]; decode-sized calls may use up to 8 K splits
+        self.recv_elems = self.tp * max(self.max_rows_s, 8 * 256 // self.tp) * max_n
+        self.recv = PeerBuffers(self.recv_elems * 2, self.device, group)
         self.max_sel = tp_rows(max_sample_rows)
         self.sel = PeerBuffers(self.max_sel * hidden * 2, self.device, group)
         max_m = self.tp * max(self.max_sel, self.max_rows_s)  # rows of one sampling call
@@ -226,8 +228,8 @@ class TPGroup:
     def sel_local(self, rows_s: int) -> torch.Tensor:
         return self.sel.local.view(torch.bfloat16)[: rows_s * self.hidden].view(rows_s, self.hidden)
 
-    def recv_local(self, rows_s: int, n: int) -> torch.Tensor:
-        return self.recv.local.view(torch.bfloat16)[: self.tp * rows_s * n]
+    def recv_local(self, rows_s: int, n: int, splits: int = 1) -> torch.Tensor:
+        return self.recv.local.view(torch.bfloat16)[: splits * self.tp * rows_s * n]
 
     # ------------------------------------------------------------------ kernels
     def barrier(self):
@@ -238,20 +240,24 @@ class TPGroup:
         bufs = self.sel if sel else self.xbuf
         ops.ext().ag_gemm(bufs.ptrs, rows_s, self.hidden, W, out, bias, self.rank, self.sync_local, self.sync.ptrs,
                           SLOT_AG, 0, self.stage, self.work)
-        ops.add_launches(1)
+        ops.add_launches(2 if self.tp * rows_s <= 256 else 1)  # (+ split-K finish for decode sizes)
         return out
 
-    def rs_linear(self, a, W) -> int:
+    def rs_linear(self, a, W):
+        """Returns the call's (grid, splits): what the owners' reduce consumes."""
         n = W.shape[0]
         if n > self.max_n or a.shape[0] > self.tp * self.max_rows_s:
             raise ValueError("gemm_rs: output larger than the receive buffers")
         ops.add_launches(1)
-        return ops.ext().gemm_rs(a, W, self.recv.ptrs, self.rank, self.sync_local, self.sync.ptrs, SLOT_RS, 0)
+        g, sp = ops.ext().gemm_rs(a, W, self.recv.ptrs, self.recv_elems, self.rank, self.sync_local, self.sync.ptrs,
+                                  SLOT_RS, 0)
+        return g, sp
 
-    def reduce(self, h, grid: int, w=None, x=None, eps: float = 1e-6, plus_one: bool = False):
+    def reduce(self, h, call, w=None, x=None, eps: float = 1e-6, plus_one: bool = False):
+        grid, splits = call
         rows_s, n = h.shape
-        ops.ext().tp_reduce(self.recv_local(rows_s, n), h, w, x, eps, plus_one, self.rank, self.sync_local,
-                            self.sync.ptrs, SLOT_RS, grid)
+        ops.ext().tp_reduce(self.recv_local(rows_s, n, splits), splits, h, w, x, eps, plus_one, self.rank,
+                            self.sync_local, self.sync.ptrs, SLOT_RS, grid)
         ops.add_launches(1)
 
     def sample(self, rows_s: int, W, temperature: float, seed: int, streams, sd: ShardDims, sel: bool = False):
