@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke tests only)")
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--tp", type=int, default=0, help="rollout tensor parallelism (0: 2 when N is even, else 1)")
+    ap.add_argument("--profile-step", default="",
+                    help="after the timed steps, run one more step under the PyTorch CUDA trace and write rank 0's "
+                         "per-kernel breakdown (JSON) here; not part of the timed value")
     ap.add_argument("--actor", default="sharded", choices=["sharded", "dp"],
                     help="N > 1 actor: ZeRO-sharded with fused peer-memory kernels, or replicated + NCCL all-reduce")
     return ap.parse_args()
@@ -263,6 +266,21 @@ def main():
             "tree_tokens": s0.get("tree_tokens"), "flat_tokens": s0.get("flat_tokens"),
         }
         print(json.dumps(out), flush=True)
+    if args.profile_step:
+        from torch.profiler import ProfilerActivity, profile
+
+        from octopus_b200.tools.step_profile import breakdown
+
+        if rank == 0:
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                st = trainer.step()
+                torch.cuda.synchronize()
+            out = breakdown(prof, st)
+            with open(args.profile_step, "w") as f:
+                json.dump(out, f, indent=1)
+        else:
+            trainer.step()
+            torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         torch.cuda.synchronize()

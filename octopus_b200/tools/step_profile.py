@@ -18,6 +18,13 @@ from collections import defaultdict
 
 def kernel_group(name: str) -> str:
     n = name
+    if "gemm_tcgen05_kernel" in n:
+        if "AGather" in n:
+            return "ag_gemm (TP all-gather -> GEMM)" + (" split-K" if "EpiSplitK" in n else "")
+        if "EpiRS" in n:
+            return "gemm_rs (TP GEMM -> reduce-scatter)"
+        if "EpiSplitK" in n:
+            return "gemm split-K (decode)"
     for pat, g in ((r"gemm_tcgen05_kernel<(\d+), (?:true|false), (?:true|false), octo::EpiHeadLse", "gemm head lse"),
                    (r"gemm_tcgen05_kernel<(\d+), (?:true|false), (?:true|false), octo::EpiHeadGrad", "gemm head grad"),
                    (r"gemm_tcgen05_kernel<(\d+), (?:true|false), (?:true|false), octo::EpiSample", "gemm sample"),
@@ -76,9 +83,18 @@ def main(argv=None):
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         st = tr.step()
         torch.cuda.synchronize()
+    out = breakdown(prof, st)
+    print(json.dumps(out, indent=1))
+    if args.out:
+        with open(args.out, "w") as f:
+            json.dump(out, f, indent=1)
+
+
+def breakdown(prof, st: dict) -> dict:
+    """Device time per kernel group of a profiled step (+ the step's phase wall times)."""
     tot = defaultdict(float)
     cnt = defaultdict(int)
-    for e in prof.events():
+    for e in prof.events():  # noqa: B007
         if e.device_type.name != "CUDA":
             continue
         g = kernel_group(e.name)
@@ -86,14 +102,10 @@ def main(argv=None):
         cnt[g] += 1
     all_us = sum(tot.values())
     rows = sorted(tot.items(), key=lambda kv: -kv[1])
-    out = {"device_ms_total": round(all_us / 1e3, 1), "phases_s": {k: round(st[k], 3) for k in
-                                                                  ("rollout_s", "train_s", "sync_s")},
-           "kernels": [{"name": k, "ms": round(v / 1e3, 2), "share": round(v / all_us, 4), "launches": cnt[k]}
-                       for k, v in rows[:40]]}
-    print(json.dumps(out, indent=1))
-    if args.out:
-        with open(args.out, "w") as f:
-            json.dump(out, f, indent=1)
+    return {"device_ms_total": round(all_us / 1e3, 1),
+            "phases_s": {k: round(st[k], 3) for k in ("rollout_s", "train_s", "sync_s")},
+            "kernels": [{"name": k, "ms": round(v / 1e3, 2), "share": round(v / all_us, 4), "launches": cnt[k]}
+                        for k, v in rows[:40]]}
 
 
 if __name__ == "__main__":
