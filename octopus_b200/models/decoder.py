@@ -23,7 +23,6 @@ import os
 from dataclasses import dataclass
 
 import torch
-from torch.utils.checkpoint import checkpoint
 
 from .. import ops
 from .config import ModelConfig
@@ -167,19 +166,61 @@ def layer_forward(x, w, cfg: ModelConfig, pos, plan):
     return ops.linear(act, down_w, None, residual=x)
 
 
+class _Ckpt(torch.autograd.Function):
+    """Activation checkpoint of fn(x, *args): forward without a graph, the input saved
+    through autograd's saved-tensor hooks (so host-resident activations apply to it),
+    recompute with a graph in backward.  Weight gradients accumulate into main_grad
+    inside the recompute's backward."""
+
+    @staticmethod
+    def forward(ctx, x, fn, *args):
+        ctx.fn, ctx.args = fn, args
+        ctx.save_for_backward(x)
+        with torch.no_grad():
+            return fn(x, *args)
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x,) = ctx.saved_tensors
+        xr = x.detach().requires_grad_(True)
+        with torch.enable_grad():
+            y = ctx.fn(xr, *ctx.args)
+        torch.autograd.backward(y, dy)
+        return (xr.grad, None) + (None,) * len(ctx.args)
+
+
+def _layers_forward(x, ws, cfg, pos, plan):
+    """Several layers (a checkpoint block); during the block's recompute each layer is
+    checkpointed again, so backward holds one layer's working set at a time."""
+    for w in ws:
+        x = _Ckpt.apply(x, layer_forward, w, cfg, pos, plan) if torch.is_grad_enabled() else \
+            layer_forward(x, w, cfg, pos, plan)
+    return x
+
+
 def forward_tree(weights: Weights, batch: TreeBatch, temperature: float = 1.0, ckpt: bool = True,
-                 layer_hook=None):
-    """Returns (logp [M], entropy [M]) of the scored (row, label) pairs."""
+                 layer_hook=None, ckpt_block: int = 1):
+    """Returns (logp [M], entropy [M]) of the scored (row, label) pairs.
+
+    ckpt: activation checkpointing; ckpt_block = k keeps only every k-th layer input
+    (block checkpoint: the inputs of the layers inside a block are recomputed)."""
     cfg = weights.cfg
     x = ops.embed(batch.ids, weights["embed"])
     if x.requires_grad is False and torch.is_grad_enabled():
         x.requires_grad_(True)
+    if ckpt and ckpt_block > 1 and torch.is_grad_enabled() and layer_hook is None:
+        for i0 in range(0, cfg.layers, ckpt_block):
+            ws = [weights.layer(i) for i in range(i0, min(cfg.layers, i0 + ckpt_block))]
+            x = _Ckpt.apply(x, _layers_forward, ws, cfg, batch.pos, batch.plan)
+        h = ops.rmsnorm(x, weights["norm"], cfg.rms_eps, cfg.norm_plus_one)
+        hp = h.index_select(0, batch.pair_rows)
+        return ops.logprob_head(hp, weights.head, batch.pair_labels, 1.0 / temperature, cfg.vocab_size)
     for i in range(cfg.layers):
         if layer_hook is not None:
             layer_hook(i)
         w = weights.layer(i)
         if ckpt and torch.is_grad_enabled():
-            x = checkpoint(layer_forward, x, w, cfg, batch.pos, batch.plan, use_reentrant=False)
+            x = _Ckpt.apply(x, layer_forward, w, cfg, batch.pos, batch.plan)
         else:
             x = layer_forward(x, w, cfg, batch.pos, batch.plan)
     if layer_hook is not None:

@@ -124,6 +124,16 @@ class Actor:
         self.ckpt = ckpt
         self.temperature = temperature
         self.version = 0
+        self.ckpt_block = 1          # block checkpoint: keep every k-th layer input
+        self.host_acts = None        # HostActivations: saved activations past a GPU budget in pinned host memory
+
+    def set_memory(self, ckpt_block: int = 1, act_gpu_bytes: int | None = None):
+        """Trainer memory knobs: block checkpointing and host-resident saved activations."""
+        from ..utils.pinned_slab import HostActivations, check_checkpointing
+
+        self.ckpt_block = max(1, int(ckpt_block))
+        self.host_acts = HostActivations(act_gpu_bytes) if act_gpu_bytes is not None else None
+        check_checkpointing(self.ckpt, self.host_acts)
 
     def zero_grad(self):
         self.grad.zero_()
@@ -136,10 +146,15 @@ class Actor:
     def forward_backward(self, mbs: list[MicroBatch], denom: float | None = None) -> dict:
         denom = denom if denom is not None else float(sum(mb.pair_w.sum() for mb in mbs))
         stats = {}
+        import contextlib
+
         for mb in mbs:
             d = mb.to_device(self.device)
-            logp, ent = forward_tree(self.weights, d.batch, self.temperature, ckpt=self.ckpt)
-            loss, st = ppo_loss(logp, ent, d.adv, d.w, d.behav, None, denom, self.ppo)
+            host = getattr(self, "host_acts", None)
+            with host if host is not None else contextlib.nullcontext():
+                logp, ent = forward_tree(self.weights, d.batch, self.temperature, ckpt=self.ckpt,
+                                         ckpt_block=getattr(self, "ckpt_block", 1))
+                loss, st = ppo_loss(logp, ent, d.adv, d.w, d.behav, None, denom, self.ppo)
             loss.backward()
             for k, v in st.items():
                 stats[k] = stats.get(k, 0.0) + v.detach() * (1.0 if k == "tokens" else float(mb.pair_w.sum()))
