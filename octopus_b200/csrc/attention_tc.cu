@@ -153,21 +153,32 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_tc_kernel(AttnParams p, 
     uint32_t phase = 0;
     bool ok = true;
     const int32_t first = nk > 0 ? kidx[0] : 0;
+    // this warp's slot indices: one coalesced load per 32 rows, handed out by shuffle;
+    // rows past the key list read a valid row (the softmax masks them).  Loaded one tile
+    // ahead so their latency hides behind the wait and the current tile's copies.
+    int nx[kRows / 32];
+#pragma unroll
+    for (int q = 0; q < kRows / 32; ++q) {
+      const int kk = rbase + q * 32 + lane;
+      nx[q] = kk < n_end ? static_cast<int>(kidx[kk]) : first;
+    }
     for (int j = 0; j < n_tiles && ok; ++j) {
+      int ix[kRows / 32];
+#pragma unroll
+      for (int q = 0; q < kRows / 32; ++q) ix[q] = nx[q];
+      if (j + 1 < n_tiles) {
+#pragma unroll
+        for (int q = 0; q < kRows / 32; ++q) {
+          const int kk = (j + 1) * kBN + rbase + q * 32 + lane;
+          nx[q] = kk < n_end ? static_cast<int>(kidx[kk]) : first;
+        }
+      }
       if (lane == 0) ok = mbar_wait(&kv_empty[stage], phase ^ 1u, abort_flag, status, 500 + stage);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
       if (warp == 0 && lane == 0) trace_at(p, 0, j);
       const uint32_t kbase = smem_u32(sK + stage * kTileBytes);
       const uint32_t vbase = smem_u32(sV + stage * kTileBytes);
-      // this warp's slot indices: one coalesced load per 32 rows, handed out by shuffle;
-      // rows past the key list read a valid row (the softmax masks them)
-      int ix[kRows / 32];
-#pragma unroll
-      for (int q = 0; q < kRows / 32; ++q) {
-        const int kk = j * kBN + rbase + q * 32 + lane;
-        ix[q] = kk < n_end ? static_cast<int>(kidx[kk]) : first;
-      }
 #pragma unroll
       for (int i = 0; i < kRows / 2; ++i) {
         const int rl = 2 * i + (lane >> 4);

@@ -117,6 +117,18 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
+// L2 prefetch of a 2D tile (no SMEM, no barrier); same coordinate rules as the load.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(tmap)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
+// Programmatic dependent launch: wait until the preceding grid's memory is visible /
+// let the next (dependent) grid launch early.  No-ops for launches without the attribute.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // 2D tiled load; coordinates are in elements, innermost first.  The innermost
 // coordinate must keep the start 16-byte aligned (all call sites use multiples of 64
 // elements of a 2-byte type).

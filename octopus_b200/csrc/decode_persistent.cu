@@ -112,16 +112,23 @@ __global__ void __launch_bounds__(64, 2) decode_persistent_kernel(DecodePersistP
       const Item x = item_of(p, it);
       const int32_t* idx = p.kv_indices + p.kv_start[x.b];
       const int first = x.k0 < x.k1 ? static_cast<int>(idx[x.k0]) : 0;
+      // the tile's 64 slot indices: one coalesced load per lane (rows lane, lane + 32),
+      // handed to the copying lanes by shuffle (no dependent load per row); loaded one
+      // tile ahead so their latency hides behind the current tile's wait and copies
+      int n0 = x.k0 + lane < x.k1 ? static_cast<int>(idx[x.k0 + lane]) : first;
+      int n1 = x.k0 + 32 + lane < x.k1 ? static_cast<int>(idx[x.k0 + 32 + lane]) : first;
       for (int t0 = x.k0; t0 < x.k1; t0 += kTile) {
+        const int i0 = n0, i1 = n1;
+        if (t0 + kTile < x.k1) {
+          const int u = t0 + kTile;
+          n0 = u + lane < x.k1 ? static_cast<int>(idx[u + lane]) : first;
+          n1 = u + 32 + lane < x.k1 ? static_cast<int>(idx[u + 32 + lane]) : first;
+        }
         if (lane == 0) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, 700 + stage)) ok = false;
         }
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
-        // the tile's 64 slot indices: one coalesced load per lane (rows lane, lane + 32),
-        // handed to the copying lanes by shuffle (no dependent load per row)
-        const int i0 = t0 + lane < x.k1 ? static_cast<int>(idx[t0 + lane]) : first;
-        const int i1 = t0 + 32 + lane < x.k1 ? static_cast<int>(idx[t0 + 32 + lane]) : first;
         // 16 lanes per cache row (one 16-byte chunk each): every warp load reads two
         // whole 256-byte rows, so global reads stay coalesced
         const uint32_t base = smem_u32(smem + stage * kTileBytes);
@@ -283,6 +290,7 @@ __global__ void __launch_bounds__(64, 2) decode_persistent_kernel(DecodePersistP
 }
 
 __global__ void decode_persistent_combine_kernel(DecodePersistParams p) {
+  grid_dep_launch();
   const int b = blockIdx.x, hq = blockIdx.y;
   const size_t base = (static_cast<size_t>(b) * p.Hq + hq) * p.num_splits;
   float M = -INFINITY;

@@ -115,12 +115,20 @@ __global__ void __launch_bounds__(32 * (1 + kConsumers), 2) decode_shared_kernel
       const SItem x = sitem_of(p, it);
       const int32_t* idx = p.kv_indices + x.start;
       const int first = x.k0 < x.k1 ? static_cast<int>(idx[x.k0]) : 0;
+      // slot indices of the next tile are loaded one tile ahead (their latency hides
+      // behind the current tile's wait and copies)
+      int n0 = x.k0 + lane < x.k1 ? static_cast<int>(idx[x.k0 + lane]) : first;
+      int n1 = x.k0 + 32 + lane < x.k1 ? static_cast<int>(idx[x.k0 + 32 + lane]) : first;
       for (int t0 = x.k0; t0 < x.k1; t0 += kTile) {
+        const int i0 = n0, i1 = n1;
+        if (t0 + kTile < x.k1) {
+          const int u = t0 + kTile;
+          n0 = u + lane < x.k1 ? static_cast<int>(idx[u + lane]) : first;
+          n1 = u + 32 + lane < x.k1 ? static_cast<int>(idx[u + 32 + lane]) : first;
+        }
         if (lane == 0 && !mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, 720 + stage)) ok = false;
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
-        const int i0 = t0 + lane < x.k1 ? static_cast<int>(idx[t0 + lane]) : first;
-        const int i1 = t0 + 32 + lane < x.k1 ? static_cast<int>(idx[t0 + 32 + lane]) : first;
         const uint32_t base = smem_u32(smem + stage * kTileBytes);
 #pragma unroll
         for (int i = 0; i < kTile / 2; ++i) {
@@ -287,6 +295,7 @@ __global__ void __launch_bounds__(32 * (1 + kConsumers), 2) decode_shared_kernel
 
 // o[b, hq] = merge over the row's slots (lse in log2 units)
 __global__ void decode_shared_combine_kernel(DecodeSharedParams p) {
+  grid_dep_launch();
   const int b = blockIdx.x, hq = blockIdx.y;
   const int ns = p.row_nslot[b];
   const size_t base = (static_cast<size_t>(b) * p.Hq + hq) * p.max_slots;

@@ -101,6 +101,7 @@ void sample_combine(const float* part, int M, int T, uint64_t seed, const int64_
 // y = x * rsqrt(mean(x^2) + eps) * (w or 1 + w).  One warp per row, H % 256 == 0 or H % 8 == 0.
 __global__ void rmsnorm_fwd_kernel(const bf16* __restrict__ x, int ldx, const bf16* __restrict__ w, bf16* y,
                                    int ldy, float* rstd_out, int T, int H, float eps, int plus_one) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue and weight prefetch
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -227,6 +228,7 @@ void rope_apply(bf16* qkv, int ld, const int32_t* pos, int T, int Hq, int Hkv, i
 // ----------------------------------------------------------------- SwiGLU
 // gu = [gate | up] along features (each F wide); out = silu(gate) * up
 __global__ void swiglu_fwd_kernel(const bf16* __restrict__ gu, bf16* out, int T, int F) {
+  grid_dep_launch();  // a dependent GEMM may start its prologue and weight prefetch
   const long total = static_cast<long>(T) * F / 8;
   for (long v = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; v < total;
        v += static_cast<long>(gridDim.x) * blockDim.x) {

@@ -19,7 +19,21 @@ static void launch_one(const GemmLaunch& g, const Epi& epi) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     configured = true;
   }
-  kern<<<g.grid, kGemmThreads, Cfg::kSmemBytes, g.stream>>>(ALocal<A_MN>{g.ta}, g.tb, g.s, epi, g.status);
+  if (!g.s.pdl) {
+    kern<<<g.grid, kGemmThreads, Cfg::kSmemBytes, g.stream>>>(ALocal<A_MN>{g.ta}, g.tb, g.s, epi, g.status);
+    return;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(g.grid);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = g.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, ALocal<A_MN>{g.ta}, g.tb, g.s, epi, g.status);
 }
 
 template <int BN, class Epi>
@@ -70,6 +84,7 @@ void gemm_launch(const GemmLaunch& g) {
 __global__ void splitk_finish_kernel(const float* __restrict__ ws, int splits, int M, int N,
                                      const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ res,
                                      int ldr, __nv_bfloat16* __restrict__ out, int ldc) {
+  grid_dep_launch();
   const int n8 = N / 8;
   const size_t total = static_cast<size_t>(M) * n8;
   const size_t plane = static_cast<size_t>(M) * N;

@@ -149,6 +149,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       const ASrc& asrc = asrc_param;
       uint32_t ready_mask = 0;  // source ranks whose data this CTA has seen published
+      if (shape.pdl) {
+        // programmatic dependent launch: the B operand (weights) does not depend on the
+        // preceding kernel, so pull this CTA's first B tiles into L2 while it finishes
+        if (blockIdx.x < shape.num_tiles) {
+          int mb, nb, ks, kb0, kb1;
+          gemm_tile_coords(shape, blockIdx.x, mb, nb, ks);
+          gemm_split_range(shape, ks, kb0, kb1);
+          for (int kb = kb0; kb < kb1 && kb < kb0 + S; ++kb) {
+            if constexpr (!B_MN) {
+              tma_prefetch_l2_2d(&tmB, kb * kGemmBK, nb * BN);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j) tma_prefetch_l2_2d(&tmB, nb * BN + 64 * j, kb * kGemmBK);
+            }
+          }
+        }
+        grid_dep_wait();
+      }
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;

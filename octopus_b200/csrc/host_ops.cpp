@@ -98,6 +98,11 @@ void attn_decode_shared_t(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, t
 }
 
 // ------------------------------------------------------------------ GEMM
+// GEMMs launched while set are programmatic dependents of the preceding kernel (decode
+// graphs of the engine): their prologue and weight prefetch overlap its tail.
+static bool g_pdl = false;
+void set_pdl(bool on) { g_pdl = on; }
+
 int pick_bn(int M, int N, int sms, int hint) {
   if (hint == 64 || hint == 128 || hint == 256) return hint;
   const int mt = (M + 127) / 128;
@@ -144,6 +149,7 @@ static GemmLaunch make_launch(const torch::Tensor& A, bool a_mn, const torch::Te
   g.stream = cur_stream(A);
   g.alpha = 1.f;
   g.vocab_limit = N;
+  g.s.pdl = g_pdl ? 1 : 0;
   return g;
 }
 
@@ -671,4 +677,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_decode", &attn_decode_t);
   m.def("attn_decode_persistent", &attn_decode_persistent_t);
   m.def("attn_decode_shared", &attn_decode_shared_t);
+  m.def("set_pdl", &set_pdl);
 }

@@ -13,6 +13,7 @@ struct GemmShape {
   int m_tiles, n_tiles, k_blocks, num_tiles;
   int m_shift;  // M-block rotation of the tile order (tensor-parallel: own rows first)
   int k_splits; // split-K factor (0 or 1: none); tiles = k_splits x m_tiles x n_tiles
+  int pdl;      // launched as a programmatic dependent: prefetch weights to L2, then wait for the predecessor
 };
 
 enum GemmEpiKind : int {

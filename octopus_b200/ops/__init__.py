@@ -1,10 +1,10 @@
 """sm_100a kernels (CUDA tensors) with plain-PyTorch references (CPU tensors)."""
-from ._ext import add_launches, available, check_status, ext, launches
+from ._ext import add_launches, available, check_status, ext, launches, pdl_launches
 from .core import (AttnPlan, adamw_, attention, embed, gemm, linear, logprob_head, rmsnorm, rope_, sample, sqnorm_,
                    swiglu)
 from .decode import DecodeAttention, SharedDecode, decode_attention
 
 __all__ = [
     "AttnPlan", "DecodeAttention", "SharedDecode", "adamw_", "add_launches", "launches", "attention", "available", "check_status", "decode_attention", "embed",
-    "ext", "gemm", "linear", "logprob_head", "rmsnorm", "rope_", "sample", "sqnorm_", "swiglu",
+    "ext", "gemm", "pdl_launches", "linear", "logprob_head", "rmsnorm", "rope_", "sample", "sqnorm_", "swiglu",
 ]

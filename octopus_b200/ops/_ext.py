@@ -99,3 +99,22 @@ def check_status(device: int = 0, reset: bool = True) -> None:
         names = {1: "pipeline barrier wait timed out", 2: "peer flag wait timed out",
                  3: "bounds check failed", 4: "TMEM allocation failed"}
         raise RuntimeError(f"octopus_b200 kernel error {code} ({names.get(code, '?')}) at site {where}")
+
+
+class pdl_launches:
+    """Context: GEMMs launched inside are programmatic dependents of the preceding kernel
+    (their prologue and weight L2 prefetch overlap its tail).  Used for the engine's
+    decode graphs; OCTO_PDL=0 disables it."""
+
+    def __enter__(self):
+        import os
+
+        self.on = os.environ.get("OCTO_PDL", "1") != "0" and available()
+        if self.on:
+            ext().set_pdl(True)
+        return self
+
+    def __exit__(self, *exc):
+        if self.on:
+            ext().set_pdl(False)
+        return False

@@ -396,7 +396,11 @@ class Engine:
                 return self.dec_attn(q, self.kc[i], self.vc[i], start, self.kv_indices, kv_len=att_len)
             return self.dec_attn(q, self.kc[i], self.vc[i], start_o, self.kv_indices_own, kv_len=len_o)
 
-        new_tok, lp = self._decode_forward(tok, pos, slot, attn, B, temperature)
+        if self.device.type == "cuda":
+            with ops.pdl_launches():
+                new_tok, lp = self._decode_forward(tok, pos, slot, attn, B, temperature)
+        else:
+            new_tok, lp = self._decode_forward(tok, pos, slot, attn, B, temperature)
         step = self.s_step.expand(B)[:, None]
         self.s_out_tok[:B].scatter_(1, step, new_tok[:, None])
         self.s_out_lp[:B].scatter_(1, step, lp[:, None])
