@@ -153,17 +153,20 @@ class TreeBatch:
     pair_labels: torch.Tensor  # [M] int64 label of each pair
 
 
-def layer_forward(x, w, cfg: ModelConfig, pos, plan):
+def layer_forward(x, w, cfg: ModelConfig, pos, plan, lw=None):
+    """One decoder layer; lw: the layer's LoRA adapters (qkv, o, gu, down), each
+    (A, B, scale) or None."""
     ln1, qkv_w, qkv_b, o_w, ln2, gu_w, down_w = w
+    la = lw if lw is not None else (None, None, None, None)
     h = ops.rmsnorm(x, ln1, cfg.rms_eps, cfg.norm_plus_one)
-    qkv = ops.linear(h, qkv_w, qkv_b)
+    qkv = ops.linear(h, qkv_w, qkv_b, lora=la[0])
     qkv = ops.rope_(qkv, pos, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.rope_theta)
     a = ops.attention(qkv, plan, cfg.heads, cfg.kv_heads, cfg.head_dim)
-    x = ops.linear(a, o_w, None, residual=x)
+    x = ops.linear(a, o_w, None, residual=x, lora=la[1])
     h2 = ops.rmsnorm(x, ln2, cfg.rms_eps, cfg.norm_plus_one)
-    gu = ops.linear(h2, gu_w)
+    gu = ops.linear(h2, gu_w, lora=la[2])
     act = ops.swiglu(gu)
-    return ops.linear(act, down_w, None, residual=x)
+    return ops.linear(act, down_w, None, residual=x, lora=la[3])
 
 
 class _Ckpt(torch.autograd.Function):
@@ -189,17 +192,17 @@ class _Ckpt(torch.autograd.Function):
         return (xr.grad, None) + (None,) * len(ctx.args)
 
 
-def _layers_forward(x, ws, cfg, pos, plan):
+def _layers_forward(x, ws, cfg, pos, plan, lws):
     """Several layers (a checkpoint block); during the block's recompute each layer is
     checkpointed again, so backward holds one layer's working set at a time."""
-    for w in ws:
-        x = _Ckpt.apply(x, layer_forward, w, cfg, pos, plan) if torch.is_grad_enabled() else \
-            layer_forward(x, w, cfg, pos, plan)
+    for w, lw in zip(ws, lws):
+        x = _Ckpt.apply(x, layer_forward, w, cfg, pos, plan, lw) if torch.is_grad_enabled() else \
+            layer_forward(x, w, cfg, pos, plan, lw)
     return x
 
 
 def forward_tree(weights: Weights, batch: TreeBatch, temperature: float = 1.0, ckpt: bool = True,
-                 layer_hook=None, ckpt_block: int = 1):
+                 layer_hook=None, ckpt_block: int = 1, lora=None):
     """Returns (logp [M], entropy [M]) of the scored (row, label) pairs.
 
     ckpt: activation checkpointing; ckpt_block = k keeps only every k-th layer input
@@ -210,8 +213,10 @@ def forward_tree(weights: Weights, batch: TreeBatch, temperature: float = 1.0, c
         x.requires_grad_(True)
     if ckpt and ckpt_block > 1 and torch.is_grad_enabled() and layer_hook is None:
         for i0 in range(0, cfg.layers, ckpt_block):
-            ws = [weights.layer(i) for i in range(i0, min(cfg.layers, i0 + ckpt_block))]
-            x = _Ckpt.apply(x, _layers_forward, ws, cfg, batch.pos, batch.plan)
+            idx = range(i0, min(cfg.layers, i0 + ckpt_block))
+            ws = [weights.layer(i) for i in idx]
+            lws = [lora.layer(i) if lora is not None else None for i in idx]
+            x = _Ckpt.apply(x, _layers_forward, ws, cfg, batch.pos, batch.plan, lws)
         h = ops.rmsnorm(x, weights["norm"], cfg.rms_eps, cfg.norm_plus_one)
         hp = h.index_select(0, batch.pair_rows)
         return ops.logprob_head(hp, weights.head, batch.pair_labels, 1.0 / temperature, cfg.vocab_size)
@@ -219,10 +224,11 @@ def forward_tree(weights: Weights, batch: TreeBatch, temperature: float = 1.0, c
         if layer_hook is not None:
             layer_hook(i)
         w = weights.layer(i)
+        lw = lora.layer(i) if lora is not None else None
         if ckpt and torch.is_grad_enabled():
-            x = _Ckpt.apply(x, layer_forward, w, cfg, batch.pos, batch.plan)
+            x = _Ckpt.apply(x, layer_forward, w, cfg, batch.pos, batch.plan, lw)
         else:
-            x = layer_forward(x, w, cfg, batch.pos, batch.plan)
+            x = layer_forward(x, w, cfg, batch.pos, batch.plan, lw)
     if layer_hook is not None:
         layer_hook(cfg.layers)
     h = ops.rmsnorm(x, weights["norm"], cfg.rms_eps, cfg.norm_plus_one)

@@ -99,23 +99,65 @@ class _Linear(torch.autograd.Function):
         db = None
         if ctx.bias is not None:
             db = _accum_wgrad(ctx.bias, dy.float().sum(0) if dy.dtype != torch.float64 else dy.sum(0))
+        mg = getattr(w, "main_grad", None)
+        frozen = mg is None and not ctx.needs_input_grad[1]  # (LoRA base weights: no weight gradient)
         if _is_cuda(x):
             dx = gemm(dy, w, b_mn=True)  # dy [M,N] @ w [N,K]
-            mg = getattr(w, "main_grad", None)
-            if mg is not None:
+            if frozen:
+                dw = None
+            elif mg is not None:
                 gemm(dy, x, a_mn=True, b_mn=True, out=mg, accumulate=True)
                 dw = None
             else:
                 dw = gemm(dy, x, a_mn=True, b_mn=True, out_dtype=torch.float32).to(w.dtype)
         else:
             dx = (ref._f(dy) @ ref._f(w)).to(x.dtype)
-            dw = _accum_wgrad(w, ref._f(dy).t() @ ref._f(x))
+            dw = None if frozen else _accum_wgrad(w, ref._f(dy).t() @ ref._f(x))
         return dx, dw, db, dres
 
 
-def linear(x, w, b=None, residual=None):
-    """y = x W^T (+ b) (+ residual) with fused fp32 weight-gradient accumulation."""
+def linear(x, w, b=None, residual=None, lora=None):
+    """y = x W^T (+ b) (+ residual) with fused fp32 weight-gradient accumulation; with
+    lora = (A [r, in], B [out, r], scale) the adapter term scale * (x A^T) B^T is added."""
+    if lora is not None:
+        return _LoraLinear.apply(x, w, b, residual, lora[0], lora[1], float(lora[2]))
     return _Linear.apply(x, w, b, residual)
+
+
+class _LoraLinear(torch.autograd.Function):
+    """Frozen base W plus a trained low-rank adapter:
+        u = x A^T [M, r];  y = x W^T (+ b) (+ residual) + s u B^T
+    backward (base W gets no gradient):
+        du = s dy B;  dB += s dy^T u;  dA += du^T x;  dx = dy W + du A
+    Adapter gradients accumulate into A.main_grad / B.main_grad (fp32)."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, residual, A, B, s):
+        ctx.s = s
+        ctx.has_res, ctx.bias = residual is not None, b
+        u = gemm(x, A)
+        v = gemm(u, B, alpha=s, residual=residual)
+        y = gemm(x, w, bias=b, residual=v)
+        ctx.save_for_backward(x, w, A, B, u)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, A, B, u = ctx.saved_tensors
+        s = ctx.s
+        dy = dy.contiguous()
+        db = None
+        if ctx.bias is not None and ctx.needs_input_grad[2]:
+            db = _accum_wgrad(ctx.bias, dy.float().sum(0) if dy.dtype != torch.float64 else dy.sum(0))
+        du = gemm(dy, B, b_mn=True, alpha=s)               # [M, r]
+        gB = getattr(B, "main_grad", None)
+        gA = getattr(A, "main_grad", None)
+        if gB is not None:
+            gemm(dy, u, a_mn=True, b_mn=True, alpha=s, out=gB, accumulate=True)
+        if gA is not None:
+            gemm(du, x, a_mn=True, b_mn=True, out=gA, accumulate=True)
+        dx = gemm(dy, w, b_mn=True, residual=gemm(du, A, b_mn=True))
+        return dx, None, db, (dy if ctx.has_res else None), None, None, None
 
 
 # ---------------------------------------------------------------------------- RMSNorm
@@ -391,10 +433,12 @@ class _Head(torch.autograd.Function):
             g_ent = torch.zeros_like(lse)
         g_lp = g_lp.float().contiguous()
         g_ent = g_ent.float().contiguous()
+        mg = getattr(W, "main_grad", None)
+        frozen = mg is None and not ctx.needs_input_grad[1]
         if _is_cuda(h):
             dh = torch.empty_like(h)
-            mg = getattr(W, "main_grad", None)
-            dW = mg if mg is not None else torch.zeros(W.shape, dtype=torch.float32, device=W.device)
+            dW = mg if mg is not None else (None if frozen else
+                                             torch.zeros(W.shape, dtype=torch.float32, device=W.device))
             V = W.shape[0]
             for a in range(0, M, HEAD_CHUNK):
                 b = min(M, a + HEAD_CHUNK)
@@ -412,8 +456,9 @@ class _Head(torch.autograd.Function):
                 ext().head_grad_logits(hc, W, lc.to(torch.int32).contiguous(), sc.contiguous(), ec.contiguous(),
                                        gl.contiguous(), ge.contiguous(), dz, alpha, vocab_limit or 0)
                 dh[a:b] = gemm(dz, W, b_mn=True)[:m]
-                gemm(dz, hc, a_mn=True, b_mn=True, out=dW, accumulate=True)
-            dWret = None if mg is not None else dW.to(W.dtype)
+                if dW is not None:
+                    gemm(dz, hc, a_mn=True, b_mn=True, out=dW, accumulate=True)
+            dWret = None if (mg is not None or dW is None) else dW.to(W.dtype)
             return dh, dWret, None, None, None
         with torch.enable_grad():
             hf = ref._f(h).detach().requires_grad_(True)

@@ -183,3 +183,63 @@ class Actor:
         stats["grad_norm"] = sq.sqrt()
         stats["train_s"] = time.perf_counter() - t0
         return stats
+
+
+class LoRAActor(Actor):
+    """Actor that trains low-rank adapters on a frozen base (octopus_b200.models.lora).
+
+    The base bf16 weights get no gradient (no weight-gradient GEMMs, no fp32 master or
+    optimizer state for them); AdamW runs on the adapters' flat fp32 master.  `serving`
+    holds W + s B A for the rollout engine, refreshed after every optimizer step (the
+    trainer -> rollout weight sync)."""
+
+    def __init__(self, cfg: ModelConfig, device="cuda", *, lora=None, optim: OptimConfig | None = None,
+                 ppo: PPOConfig | None = None, seed: int = 0, dtype=torch.bfloat16, ckpt: bool = True,
+                 temperature: float = 1.0):
+        from ..models.lora import LoRA, merge
+
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.optim = optim or OptimConfig()
+        self.ppo = ppo or PPOConfig()
+        self.layout = FlatLayout(cfg)
+        self.base16 = init_flat(cfg, self.layout, self.device, dtype=dtype, seed=seed)
+        self.base = Weights(cfg, self.base16, self.layout)          # frozen: no main_grad
+        self.lora = LoRA(cfg, lora, self.device, dtype, seed)
+        self.master, self.grad = self.lora.master, self.lora.grad
+        self.exp_avg, self.exp_avg_sq = self.lora.exp_avg, self.lora.exp_avg_sq
+        self.flat16 = self.lora.flat16
+        self.serving = Weights(cfg, self.base16.clone(), self.layout)
+        self._merge = merge
+        self._merge(self.base, self.lora, self.serving)
+        self.weights = self.serving   # what the colocated engine reads
+        self.step_count = 0
+        self.ckpt = ckpt
+        self.temperature = temperature
+        self.version = 0
+        self.ckpt_block = 1
+        self.host_acts = None
+
+    def forward_backward(self, mbs: list[MicroBatch], denom: float | None = None) -> dict:
+        denom = denom if denom is not None else float(sum(mb.pair_w.sum() for mb in mbs))
+        stats = {}
+        for mb in mbs:
+            d = mb.to_device(self.device)
+            logp, ent = forward_tree(self.base, d.batch, self.temperature, ckpt=self.ckpt,
+                                     ckpt_block=self.ckpt_block, lora=self.lora)
+            loss, st = ppo_loss(logp, ent, d.adv, d.w, d.behav, None, denom, self.ppo)
+            loss.backward()
+            for k, v in st.items():
+                stats[k] = stats.get(k, 0.0) + v.detach() * (1.0 if k == "tokens" else float(mb.pair_w.sum()))
+            stats["loss"] = stats.get("loss", 0.0) + loss.detach()
+        stats.setdefault("loss", torch.zeros((), device=self.device))
+        tok = float(sum(mb.pair_w.sum() for mb in mbs)) or 1.0
+        return {k: (v if k in ("tokens", "loss") else v / tok) for k, v in stats.items()}
+
+    def optimizer_step(self) -> torch.Tensor:
+        sq = super().optimizer_step()   # AdamW on the adapters' master -> lora.flat16
+        self._merge(self.base, self.lora, self.serving)
+        return sq
+
+    def reload_master(self):
+        self.lora.master.copy_(self.lora.flat16.to(self.lora.master.dtype))
