@@ -30,6 +30,10 @@ class DataParallel:
         for a in range(0, n, self.bucket):
             dist.all_reduce(g[a: a + self.bucket], group=self.group)
 
+    def attach_actor(self):
+        """Wrap the actor's forward_backward / optimizer_step (no trainer needed)."""
+        return self.attach(None)
+
     def attach(self, trainer):
         actor = self.actor
         fb = actor.forward_backward

@@ -238,8 +238,13 @@ class LoRAActor(Actor):
 
     def optimizer_step(self) -> torch.Tensor:
         sq = super().optimizer_step()   # AdamW on the adapters' master -> lora.flat16
-        self._merge(self.base, self.lora, self.serving)
+        self.optimizer_merge()
         return sq
+
+    def optimizer_merge(self):
+        """serving <- base + s B A (after an update or a base reload)."""
+        self.serving.flat.copy_(self.base16)
+        self._merge(self.base, self.lora, self.serving)
 
     def reload_master(self):
         self.lora.master.copy_(self.lora.flat16.to(self.lora.master.dtype))

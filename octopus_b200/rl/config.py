@@ -60,6 +60,11 @@ class ActorSection:
     gradient_checkpointing: bool = True
     sharded: bool = True        # ZeRO-sharded optimizer state over ranks
     fused_collectives: bool = True
+    lora_rank: int = 0          # > 0: train LoRA adapters on a frozen base (single-replica actor)
+    lora_alpha: float = 32.0
+    lora_targets: str = "all-linear"
+    ckpt_block: int = 1         # block checkpointing: keep every k-th layer input
+    act_gpu_gb: float = -1.0    # >= 0: saved activations past this many GB live in pinned host memory
 
 
 @dataclass

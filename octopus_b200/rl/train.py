@@ -62,14 +62,28 @@ def build(cfg, device):
     ppo = PPOConfig(eps_clip=a.eps_clip, eps_clip_higher=a.eps_clip_higher, behav_imp_weight_cap=a.behav_imp_weight_cap,
                     reuse_train_logp=a.reuse_train_logp)
     dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
-    if world > 1 and a.sharded:
+    if a.lora_rank > 0:
+        from ..models.lora import LoRAConfig, lora_targets
+        from .actor import LoRAActor
+
+        targets = lora_targets(a.lora_targets if "," not in a.lora_targets else a.lora_targets.split(","))
+        actor = LoRAActor(mcfg, device, lora=LoRAConfig(a.lora_rank, a.lora_alpha, targets), optim=optim, ppo=ppo,
+                          seed=cfg.seed, dtype=dtype, ckpt=a.gradient_checkpointing)
+        if world > 1:
+            from ..parallel.dp import DataParallel
+
+            DataParallel(actor).attach_actor()
+    elif world > 1 and a.sharded:
         actor = ShardedActor(mcfg, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype,
                              ckpt=a.gradient_checkpointing, fused=a.fused_collectives and device.type == "cuda")
     else:
         actor = Actor(mcfg, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype, ckpt=a.gradient_checkpointing)
+    actor.set_memory(a.ckpt_block, int(a.act_gpu_gb * (1 << 30)) if a.act_gpu_gb >= 0 else None)
     if cfg.model.path:
-        load_hf(actor.weights, cfg.model.path)
+        load_hf(getattr(actor, "base", actor.weights), cfg.model.path)
         actor.reload_master()
+        if a.lora_rank > 0:
+            actor.optimizer_merge()
     tp = max(1, cfg.rollout.tp)
     rep, tp_rank = rank // tp, rank % tp
     group = None

@@ -33,3 +33,19 @@ def test_train_cli_runs_and_resumes(tmp_path, monkeypatch):
     assert train.main(_args(tmp_path, 3)) == 0
     rows = [json.loads(x) for x in open(run / "steps.jsonl")]
     assert [r["step"] for r in rows] == [1, 2, 3]
+
+
+def test_train_cli_lora(tmp_path, monkeypatch):
+    from octopus_b200.envs import dag
+
+    orig = dag.DagConfig.__init__
+
+    def small(self, *a, **kw):
+        orig(self, *a, **kw)
+        self.prefix_len, self.turn_len, self.role_len = 32, 8, 4
+
+    monkeypatch.setattr(dag.DagConfig, "__init__", small)
+    args = _args(tmp_path, 1) + ["actor.lora_rank=4", "actor.ckpt_block=2", "checkpoint.recover_every=0",
+                                 "checkpoint.save_every=0"]
+    args = [a for a in args if a != "actor.gradient_checkpointing=false"] + ["actor.gradient_checkpointing=true"]
+    assert train.main(args) == 0
