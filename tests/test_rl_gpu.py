@@ -28,6 +28,7 @@ def test_graph_decode_matches_eager():
     prompts = [rng.integers(1, cfg.vocab_size, 100 + 7 * i).tolist() for i in range(5)]
     a = eng.generate([GenInput(p, max_new_tokens=12, rid=100 + i) for i, p in enumerate(prompts)])
     eng.use_graphs = False
+    eng.reset()  # same prefill path (no radix hits): only graph vs eager decode differs
     b = eng.generate([GenInput(p, max_new_tokens=12, rid=100 + i) for i, p in enumerate(prompts)])
     for x, y in zip(a, b):
         assert x.output_ids == y.output_ids
