@@ -645,6 +645,7 @@ void attn_decode_persistent_t(torch::Tensor q, torch::Tensor kc, torch::Tensor v
 
 void register_comm(py::module& m);
 void register_tp(py::module& m);
+void register_recur(py::module& m);
 
 }  // namespace octo
 
@@ -652,6 +653,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   using namespace octo;
   register_comm(m);
   register_tp(m);
+  register_recur(m);
   m.doc() = "octopus_b200 sm_100a kernels";
   m.def("status_tensor", [](int64_t d) { return status_tensor(static_cast<int>(d)); });
   m.def("gemm_out", &gemm_out, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("C"),

@@ -48,6 +48,8 @@ class MicroBatch:
     n_tree: int
     n_flat: int
     plan_own: tuple | None = None  # (cu_q, cu_k, key_idx) without mounted keys (layer subsets)
+    nodes: np.ndarray | None = None  # [n_nodes, 4] (start, end, parent, depth) tree nodes (recurrent layers)
+    path_tail: np.ndarray | None = None  # [n_nodes, 8] last tree rows before each node on its path (-1 pad)
 
     def to_device(self, device) -> "DeviceMicroBatch":
         d = torch.device(device)
@@ -55,6 +57,7 @@ class MicroBatch:
         batch = TreeBatch(T(self.tokens, torch.int64), T(self.positions, torch.int32),
                           ops.AttnPlan.build(self.cu_q, self.cu_k, self.key_idx, d),
                           T(self.pair_row, torch.int64), T(self.pair_label, torch.int64))
+        batch.nodes, batch.path_tail = self.nodes, self.path_tail
         return DeviceMicroBatch(batch, T(self.pair_adv, torch.float32), T(self.pair_w, torch.float32),
                                 T(self.pair_behav, torch.float32))
 
@@ -89,8 +92,18 @@ def build_microbatch(flat: np.ndarray, cu, mounts: dict | None, loss_mask: np.nd
     a = np.bincount(pid, weights=adv[nxt], minlength=P).astype(np.float32)
     b = np.bincount(pid, weights=behav_logp[nxt], minlength=P).astype(np.float32)
     nz = np.maximum(w, 1.0)
+    # tree nodes for recurrent layers (+ one node covering the padding rows)
+    nodes = [(nd.start, nd.end, nd.parent, nd.depth) for nd in tree.nodes]
+    if Tp > tree.num_tokens:
+        nodes.append((tree.num_tokens, Tp, -1, 0))
+    tails = np.full((len(nodes), 8), -1, np.int64)
+    for k, nd in enumerate(tree.nodes):
+        if nd.parent >= 0:
+            pr = tree.path_rows(nd.parent)[-8:]
+            tails[k, 8 - len(pr):] = pr
     return MicroBatch(toks, pos, plan.cu_q, plan.cu_k, plan.key_idx, tree.pair_row.astype(np.int64),
-                      tree.pair_label.astype(np.int64), a / nz, w, b / nz, tree.num_tokens, n)
+                      tree.pair_label.astype(np.int64), a / nz, w, b / nz, tree.num_tokens, n,
+                      nodes=np.asarray(nodes, np.int64).reshape(-1, 4), path_tail=tails)
 
 
 @dataclass
