@@ -171,8 +171,8 @@ std::vector<int64_t> gemm_rs_t(torch::Tensor A, torch::Tensor W, std::vector<int
   L.ldc = L.g.s.N;
   L.rows_s = M / tp;
   L.slot = make_slot(sync_local, sync_ptrs, me, slot);
-  const int splits = bn_hint == 0 ? tp_splits(L.g, W) : 1;
-  if (splits > 1) L.g.ta = make_tmap_bf16_2d(A.data_ptr(), L.g.s.K, M, A.stride(0), 64, 128);
+  // no split-K here: every split's partial would cross NVLink (the owner sums splits x tp slices)
+  const int splits = 1;
   TORCH_CHECK(static_cast<int64_t>(splits) * M * L.g.s.N <= recv_elems,
               "gemm_rs: receive buffers too small for ", splits, " split partials");
   gemm_rs_launch(L);

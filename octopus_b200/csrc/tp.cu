@@ -78,7 +78,7 @@ __device__ bool wait_peers(const TpSlot& s, int target, int* status, int where) 
 }  // namespace
 
 // ---------------------------------------------------------------- AG -> GEMM A source
-constexpr int kChunkRows = 8;  // staging copy granularity (rows of one peer shard)
+constexpr int kChunkRows = 2;  // staging copy granularity (rows of one peer shard)
 
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
@@ -135,10 +135,26 @@ struct AGather {
       }
       const __nv_bfloat16* src = peer_x[r] + static_cast<size_t>(l0) * ldx;
       __nv_bfloat16* dst = stage + (static_cast<size_t>(r) * rows_s + l0) * K;
-      for (int p = t; p < kChunkRows * cpr; p += 128) {
-        const int row = p / cpr, col = (p - row * cpr) * 8;
-        *reinterpret_cast<uint4*>(dst + static_cast<size_t>(row) * K + col) =
-            *reinterpret_cast<const uint4*>(src + static_cast<size_t>(row) * ldx + col);
+      // all loads of the chunk in flight before any store (one NVLink round trip per 8 pieces)
+      constexpr int kPer = 8;
+      for (int p0 = t; p0 < kChunkRows * cpr; p0 += 128 * kPer) {
+        uint4 buf[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+          const int p = p0 + u * 128;
+          if (p < kChunkRows * cpr) {
+            const int row = p / cpr, col = (p - row * cpr) * 8;
+            buf[u] = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(row) * ldx + col);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+          const int p = p0 + u * 128;
+          if (p < kChunkRows * cpr) {
+            const int row = p / cpr, col = (p - row * cpr) * 8;
+            *reinterpret_cast<uint4*>(dst + static_cast<size_t>(row) * K + col) = buf[u];
+          }
+        }
       }
       fence_proxy_async_global();  // generic-proxy stores -> the producers' TMA reads
       __threadfence();
