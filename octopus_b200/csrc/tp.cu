@@ -225,21 +225,41 @@ struct EpiRS {
   int part;  // receive slot: split * tp + sending rank (split-K partials are summed by the owner)
   __device__ __forceinline__ void begin_split(int ks) { part = ks * slot.tp + slot.me; }
   __device__ __forceinline__ void begin_tile() {}
-  __device__ __forceinline__ void apply(int row, int col0, int nvalid, float (&v)[32], int) {
+  __device__ __forceinline__ __nv_bfloat16* row_dst(int row, int col0) const {
     const int owner = row / rows_s;
-    __nv_bfloat16* out =
-        dst[owner] + (static_cast<size_t>(part) * rows_s + (row - owner * rows_s)) * ldc + col0;
+    return dst[owner] + (static_cast<size_t>(part) * rows_s + (row - owner * rows_s)) * ldc + col0;
+  }
+  __device__ __forceinline__ void apply(int row, int col0, int nvalid, float (&v)[32], int) {
+    uint4 o[4];
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      if (g * 8 < nvalid) {
-        uint4 o;
-        o.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
-        o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
-        o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
-        o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
-        *reinterpret_cast<uint4*>(out + g * 8) = o;
-      }
+      o[g].x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
+      o[g].y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
+      o[g].z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
+      o[g].w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
     }
+    const int lane = threadIdx.x & 31;
+    if (__activemask() == 0xffffffffu && __all_sync(0xffffffffu, nvalid == 32)) {
+      // a warp's 32 rows x 32 columns go through shared memory so each store instruction
+      // writes 8 rows x 64 contiguous bytes (peer writes travel in larger NVLink packets)
+      __shared__ uint4 stile[4][32][4];
+      const int w = (threadIdx.x >> 5) & 3;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) stile[w][lane][g] = o[g];
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int rl = it * 8 + (lane >> 2), piece = lane & 3;
+        const int r = __shfl_sync(0xffffffffu, row, rl);
+        *reinterpret_cast<uint4*>(row_dst(r, col0) + piece * 8) = stile[w][rl][piece];
+      }
+      __syncwarp();
+      return;
+    }
+    __nv_bfloat16* out = row_dst(row, col0);
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+      if (g * 8 < nvalid) *reinterpret_cast<uint4*>(out + g * 8) = o[g];
   }
   __device__ __forceinline__ void end_tile(int, int) {}
   __device__ __forceinline__ void finish() {
