@@ -24,3 +24,11 @@ def test_replay_bench_cpu(capsys):
                               "--cpu"]) == 0
     row = json.loads(capsys.readouterr().out.strip())
     assert row["tree_tokens"] < row["flat_tokens"]
+
+
+def test_lora_parity_cpu():
+    from octopus_b200.tools.lora_parity import run
+
+    r = run(preset="tiny", rank=4, randomize=True, device="cpu")
+    # the engine serves the merged adapter: it matches the trainer with the adapter, not without
+    assert r["engine_vs_trainer_lora"] < 1e-3 < r["engine_vs_trainer_base"]
