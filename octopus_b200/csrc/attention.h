@@ -1,5 +1,6 @@
 // Parameter blocks and launchers of attention.cu (no torch types).
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
@@ -68,5 +69,13 @@ void attn_bwd(const AttnBwdParams& p, int n_qtiles, int n_ktiles, int D, cudaStr
 void attn_decode(const DecodeParams& p, int B, int D, cudaStream_t st);
 // tcgen05/TMEM forward (head_dim 128), same contract as attn_fwd with 128-row query tiles
 void attn_fwd_tc(const AttnParams& p, int n_tiles, int* status, cudaStream_t st);
+
+// TMA maps of the two-query-tile forward: q [Tq, Hq*D] box 64 x 128; k, v [rows, Hkv*D]
+// box 64 x 64 (one producer warp's rows), all 128-byte swizzled.
+struct AttnMaps {
+  CUtensorMap q, k, v;
+};
+// head_dim 128; tiles [n_tiles, 2] (seq, q0) with q0 a multiple of 256
+void attn_fwd_pp(const AttnParams& p, const AttnMaps& maps, int n_tiles, int* status, cudaStream_t st);
 
 }  // namespace octo

@@ -29,13 +29,6 @@ constexpr int kStages = 3;       // SMEM ring depth (2 CTAs per SM)
 constexpr int kHalfBytes = kTile * 128;          // 64 rows x 64 cols bf16 (one swizzle column half)
 constexpr int kTileBytes = 4 * kHalfBytes;       // K (2 halves) + V (2 halves) = 32 KB
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-// The mbarrier receives one arrival when all cp.async of this thread issued so far complete.
-__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"

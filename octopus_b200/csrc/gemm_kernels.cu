@@ -6,14 +6,15 @@
 
 namespace octo {
 
-int gemm_smem_bytes(int bn) {
+int gemm_smem_bytes(int bn, int mt) {
+  if (mt == 2) return bn == 256 ? GemmCfg<256, 2>::kSmemBytes : GemmCfg<128, 2>::kSmemBytes;
   return bn == 256 ? GemmCfg<256>::kSmemBytes : (bn == 128 ? GemmCfg<128>::kSmemBytes : GemmCfg<64>::kSmemBytes);
 }
 
-template <int BN, bool A_MN, bool B_MN, class Epi>
+template <int BN, bool A_MN, bool B_MN, class Epi, int MT = 1>
 static void launch_one(const GemmLaunch& g, const Epi& epi) {
-  using Cfg = GemmCfg<BN>;
-  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, Epi>;
+  using Cfg = GemmCfg<BN, MT>;
+  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, Epi, ALocal<A_MN>, MT>;
   static bool configured = false;  // attribute is per function, not per device context
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
@@ -46,6 +47,11 @@ static void by_major(const GemmLaunch& g, const Epi& epi) {
 
 template <class Epi>
 static void by_bn(const GemmLaunch& g, const Epi& epi) {
+  if (g.mt == 2) {  // decode-sized M, K-major operands (chosen by the host)
+    if (g.bn == 256) launch_one<256, false, false, Epi, 2>(g, epi);
+    else launch_one<128, false, false, Epi, 2>(g, epi);
+    return;
+  }
   if (g.bn == 256) by_major<256>(g, epi);
   else if (g.bn == 128) by_major<128>(g, epi);
   else by_major<64>(g, epi);

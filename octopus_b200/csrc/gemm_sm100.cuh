@@ -33,14 +33,24 @@ constexpr int kGemmBK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kGemmThreads = 192;
 constexpr int kGemmGroupM = 16;  // tile raster: 16 M-blocks share each B tile in L2
 
-template <int BN>
+// MT = M-tiles per CTA: with MT = 2 a CTA multiplies two 128-row A tiles by each B tile it
+// loads (decode-sized M), so every weight byte crosses L2 -> SMEM once instead of once per
+// M-tile.  The accumulators take MT * BN TMEM columns; they are double-buffered when two
+// sets fit the 512 columns, else single-buffered (a CTA then waits for its epilogue before
+// the next tile's MMAs, which decode shapes with ~one tile per CTA never do).
+template <int BN, int MT = 1>
 struct GemmCfg {
-  static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr int kABytes = kGemmBM * kGemmBK * 2;
+  static_assert(MT == 1 || MT == 2, "one or two M-tiles per CTA");
+  static constexpr int kAccCols = MT * BN;
+  static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
+  static constexpr int kStages = MT == 1 ? (BN == 256 ? 4 : (BN == 128 ? 6 : 8)) : (BN == 256 ? 3 : (BN == 128 ? 4 : 5));
+  static constexpr int kATileBytes = kGemmBM * kGemmBK * 2;
+  static constexpr int kABytes = MT * kATileBytes;
   static constexpr int kBBytes = BN * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = (2 * BN) < 32 ? 32 : 2 * BN;  // BN in {64,128,256}
+  static constexpr int kTmemCols = kAccBufs * kAccCols < 32 ? 32 : kAccBufs * kAccCols;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(kSmemBytes <= 227 * 1024, "stage ring exceeds shared memory");
 };
 
 
@@ -96,12 +106,14 @@ struct ALocal {
   }
 };
 
-template <int BN, bool A_MN, bool B_MN, class Epi, class ASrc = ALocal<A_MN>>
+template <int BN, bool A_MN, bool B_MN, class Epi, class ASrc = ALocal<A_MN>, int MT = 1>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ ASrc asrc_param, const __grid_constant__ CUtensorMap tmB,
                         GemmShape shape, Epi epi, int* status) {
-  // (each thread works on its own copy of the epilogue functor)
-  using Cfg = GemmCfg<BN>;
+  // (each thread works on its own copy of the epilogue functor; with MT = 2, shape.m_tiles
+  // counts pairs of 128-row M-blocks and tile coordinate mb covers rows 256 mb .. +256)
+  using Cfg = GemmCfg<BN, MT>;
+  static_assert(MT == 1 || !A_MN, "two M-tiles per CTA take a K-major A");
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -149,24 +161,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       const ASrc& asrc = asrc_param;
       uint32_t ready_mask = 0;  // source ranks whose data this CTA has seen published
-      if (shape.pdl) {
-        // programmatic dependent launch: the B operand (weights) does not depend on the
-        // preceding kernel, so pull this CTA's first B tiles into L2 while it finishes
-        if (blockIdx.x < shape.num_tiles) {
-          int mb, nb, ks, kb0, kb1;
-          gemm_tile_coords(shape, blockIdx.x, mb, nb, ks);
-          gemm_split_range(shape, ks, kb0, kb1);
-          for (int kb = kb0; kb < kb1 && kb < kb0 + S; ++kb) {
-            if constexpr (!B_MN) {
-              tma_prefetch_l2_2d(&tmB, kb * kGemmBK, nb * BN);
-            } else {
+      // L2 prefetch cursor over this CTA's (tile, K-block) sequence, kept `ahead` K-blocks in
+      // front of the TMA loads: weight tiles stream from DRAM into L2 with more bytes in flight
+      // than the shared-memory ring holds, so the ring's loads hit L2.
+      const int ahead = shape.b_prefetch > 0 ? shape.b_prefetch : (shape.pdl ? S : 0);
+      int pf_tile = blockIdx.x, pf_nb = 0, pf_kb = 0, pf_kb1 = 0;
+      auto pf_coords = [&]() {
+        int mb_, ks_;
+        gemm_tile_coords(shape, pf_tile, mb_, pf_nb, ks_);
+        gemm_split_range(shape, ks_, pf_kb, pf_kb1);
+      };
+      auto pf_step = [&]() {  // prefetch one K-block of B, then advance the cursor
+        if (pf_tile >= shape.num_tiles) return;
+        if constexpr (!B_MN) {
+          tma_prefetch_l2_2d(&tmB, pf_kb * kGemmBK, pf_nb * BN);
+        } else {
 #pragma unroll
-              for (int j = 0; j < BN / 64; ++j) tma_prefetch_l2_2d(&tmB, nb * BN + 64 * j, kb * kGemmBK);
-            }
-          }
+          for (int j = 0; j < BN / 64; ++j) tma_prefetch_l2_2d(&tmB, pf_nb * BN + 64 * j, pf_kb * kGemmBK);
         }
-        grid_dep_wait();
-      }
+        if (++pf_kb >= pf_kb1) {
+          pf_tile += gridDim.x;
+          if (pf_tile < shape.num_tiles) pf_coords();
+        }
+      };
+      if (pf_tile < shape.num_tiles) pf_coords();
+      // (a programmatic dependent issues these before waiting: B does not depend on the
+      // preceding kernel)
+      for (int i = 0; i < ahead; ++i) pf_step();
+      if (shape.pdl) grid_dep_wait();
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
@@ -188,14 +210,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_bar[stage], asrc.bytes(mb) + Cfg::kBBytes);
-          asrc.load(a_dst, &full_bar[stage], k0, mb);
+          if constexpr (MT == 1) {
+            mbar_arrive_expect_tx(&full_bar[stage], asrc.bytes(mb) + Cfg::kBBytes);
+            asrc.load(a_dst, &full_bar[stage], k0, mb);
+          } else {
+            mbar_arrive_expect_tx(&full_bar[stage], asrc.bytes(MT * mb) * MT + Cfg::kBBytes);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) asrc.load(a_dst + mt * Cfg::kATileBytes, &full_bar[stage], k0, MT * mb + mt);
+          }
           if constexpr (!B_MN) {
             tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, n0);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full_bar[stage], n0 + 64 * j, k0);
           }
+          if (shape.b_prefetch > 0) pf_step();
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == S) {
@@ -231,7 +260,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
         int mb_, nb_, ks, kb0, kb1;
         gemm_tile_coords(shape, tile, mb_, nb_, ks);
         gemm_split_range(shape, ks, kb0, kb1);
@@ -256,7 +285,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             } else {
               db = umma_smem_desc(b_addr + kk * 2048, 8192, 1024);
             }
-            umma_f16_ss(d_tmem, da, db, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+            const uint32_t accum = (kb != kb0 || kk != 0) ? 1u : 0u;
+            umma_f16_ss(d_tmem, da, db, idesc, accum);
+#pragma unroll
+            for (int mt = 1; mt < MT; ++mt)  // further M-tiles reuse the B descriptor (K-major A only)
+              umma_f16_ss(d_tmem + mt * BN, umma_smem_desc(a_addr + mt * Cfg::kATileBytes + kk * 32, 16, 1024), db,
+                          idesc, accum);
           }
           issued_any = true;
           umma_commit(&empty_bar[stage]);
@@ -267,7 +301,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (!ok) break;
         umma_commit(&accf_bar[acc]);
-        if (++acc == 2) {
+        if (++acc == Cfg::kAccBufs) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -293,29 +327,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       int mb, nb, ks;
       gemm_tile_coords(shape, tile, mb, nb, ks);
-      const int row = mb * kGemmBM + quarter * 32 + lane;
       const int n0 = nb * BN;
-      epi.begin_split(ks);
-      epi.begin_tile();
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_base + static_cast<uint32_t>(acc * BN + c * 32), r);
-        tmem_wait_ld();
-        const int col0 = n0 + c * 32;
-        if (row < shape.M && col0 < shape.N) {
-          float v[32];
+      for (int mt = 0; mt < MT; ++mt) {
+        const int row = (MT * mb + mt) * kGemmBM + quarter * 32 + lane;
+        epi.begin_split(ks);
+        epi.begin_tile();
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols + mt * BN + c * 32), r);
+          tmem_wait_ld();
+          const int col0 = n0 + c * 32;
+          if (row < shape.M && col0 < shape.N) {
+            float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          const int nvalid = shape.N - col0 < 32 ? shape.N - col0 : 32;
-          epi.apply(row, col0, nvalid, v, nb);
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            const int nvalid = shape.N - col0 < 32 ? shape.N - col0 : 32;
+            epi.apply(row, col0, nvalid, v, nb);
+          }
         }
+        if (mt == MT - 1) {  // accumulator drained: the MMA warp may reuse it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acce_bar[acc]);
+        }
+        if (row < shape.M) epi.end_tile(row, nb);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acce_bar[acc]);
-      if (row < shape.M) epi.end_tile(row, nb);
-      if (++acc == 2) {
+      if (++acc == Cfg::kAccBufs) {
         acc = 0;
         acc_phase ^= 1u;
       }

@@ -103,6 +103,15 @@ void attn_decode_shared_t(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, t
 static bool g_pdl = false;
 void set_pdl(bool on) { g_pdl = on; }
 
+// L2 prefetch depth of B (K-blocks ahead of the TMA loads) for decode-sized GEMMs.  Off by
+// default: on the 7B decode shapes (M = 256) depths 8 and 16 measured 0-10% slower than none
+// (the weight stream is not bound by the latency of its loads); OCTO_GEMM_PF sets it.
+int gemm_prefetch_depth(int M) {
+  if (M > 256) return 0;
+  const char* e = std::getenv("OCTO_GEMM_PF");
+  return e != nullptr ? std::atoi(e) : 0;
+}
+
 int pick_bn(int M, int N, int sms, int hint) {
   if (hint == 64 || hint == 128 || hint == 256) return hint;
   const int mt = (M + 127) / 128;
@@ -131,6 +140,7 @@ static GemmLaunch make_launch(const torch::Tensor& A, bool a_mn, const torch::Te
   const int sms = num_sms(device);
   const int BN = pick_bn(M, N, sms, bn_hint);
   g.bn = BN;
+  g.mt = 1;
   g.a_mn = a_mn;
   g.b_mn = b_mn;
   g.s.M = M;
@@ -150,24 +160,37 @@ static GemmLaunch make_launch(const torch::Tensor& A, bool a_mn, const torch::Te
   g.alpha = 1.f;
   g.vocab_limit = N;
   g.s.pdl = g_pdl ? 1 : 0;
+  g.s.b_prefetch = gemm_prefetch_depth(M);
   return g;
 }
 
-// Split-K for decode-sized forward GEMMs (K-major operands, bf16 out, alpha 1): with
-// BN = 256 the N-tiles cannot fill the GPU, so K is split until ~one tile per SM, keeping
-// >= 4 K blocks per split.  Rebuilds the launch's B map for BN = 256.  Returns 1 for none.
-static int splitk_factor(GemmLaunch& g, int64_t bn_hint, int device, const torch::Tensor& B) {
+// Decode-sized forward GEMMs (M <= 256, K-major operands, bf16 out, alpha 1): 256-wide N
+// tiles.  When those tiles cannot fill the GPU, K is split until ~one tile per SM (keeping
+// >= 4 K blocks per split).  When they can and M > 128, both 128-row M-blocks go to one CTA
+// (MT = 2) so each weight tile is loaded once.  Rebuilds the launch's B map for BN = 256 and
+// returns the split count (1 for none).  OCTO_SPLITK=0 switches split-K off; OCTO_GEMM_MT=1
+// / =2 force one / two M-tiles per CTA.
+static int decode_shape(GemmLaunch& g, int64_t bn_hint, int device, const torch::Tensor& B) {
   if (bn_hint != 0 || g.a_mn || g.b_mn || g.alpha != 1.f || g.s.M > 256 || g.s.N < 256) return 1;
-  if (const char* e = std::getenv("OCTO_SPLITK"); e != nullptr && e[0] == '0') return 1;
+  const char* e_sk = std::getenv("OCTO_SPLITK");
+  const char* e_mt = std::getenv("OCTO_GEMM_MT");
+  const bool allow_split = !(e_sk != nullptr && e_sk[0] == '0');
+  const int force_mt = e_mt != nullptr ? std::atoi(e_mt) : 0;
   const int sms = num_sms(device);
   const int n_tiles = (g.s.N + 255) / 256;
-  const int tiles = g.s.m_tiles * n_tiles;
-  if (tiles * 4 >= sms * 3) return 1;
-  int splits = std::min(sms / tiles, g.s.k_blocks / 4);
-  if (splits < 2) return 1;
+  const int m1 = (g.s.M + 127) / 128, m2 = (g.s.M + 255) / 256;
+  int mt = 1;
+  if (g.s.M > 128 && force_mt != 1 && (force_mt == 2 || m2 * n_tiles * 4 >= sms * 3)) mt = 2;
+  const int m_tiles = mt == 2 ? m2 : m1;
+  const int tiles = m_tiles * n_tiles;
+  int splits = 1;
+  if (allow_split && tiles * 4 < sms * 3) splits = std::max(1, std::min(sms / tiles, g.s.k_blocks / 4));
+  if (mt == 1 && splits < 2) return 1;  // the default launch
+  g.mt = mt;
   g.bn = 256;
+  g.s.m_tiles = m_tiles;
   g.s.n_tiles = n_tiles;
-  g.s.k_splits = splits;
+  g.s.k_splits = splits > 1 ? splits : 0;
   g.s.num_tiles = tiles * splits;
   g.grid = std::min(g.s.num_tiles, sms);
   g.tb = make_tmap_bf16_2d(B.data_ptr(), g.s.K, g.s.N, B.stride(0), 64, 256);
@@ -190,7 +213,7 @@ void gemm_out(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, torch::Ten
   if (C.scalar_type() == torch::kBFloat16) {
     TORCH_CHECK(!accumulate, "gemm: accumulate requires an fp32 output");
     TORCH_CHECK(C.stride(0) % 8 == 0, "gemm: output row stride must be a multiple of 8");
-    const int splits = splitk_factor(g, bn_hint, A.get_device(), B);
+    const int splits = decode_shape(g, bn_hint, A.get_device(), B);
     if (splits > 1) {
       // decode-sized M: wide N tiles (each CTA re-reads fewer activation bytes) split along K so
       // every SM streams weights; fp32 partials are summed with bias / residual by splitk_finish
@@ -471,7 +494,7 @@ void adamw_t(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v,
 std::vector<torch::Tensor> attn_fwd_t(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_q,
                                       torch::Tensor cu_k, torch::Tensor key_idx, torch::Tensor tiles, int64_t Hq,
                                       int64_t Hkv, int64_t D, double scale, bool causal, bool want_lse,
-                                      bool use_tc, c10::optional<torch::Tensor> trace) {
+                                      int64_t use_tc, c10::optional<torch::Tensor> trace) {
   c10::cuda::CUDAGuard guard(q.get_device());
   CHECK_BF16(q);
   CHECK_BF16(k);
@@ -508,7 +531,15 @@ std::vector<torch::Tensor> attn_fwd_t(torch::Tensor q, torch::Tensor k, torch::T
   p.causal = causal ? 1 : 0;
   p.trace = (trace.has_value() && trace->defined()) ? reinterpret_cast<unsigned long long*>(trace->data_ptr())
                                                       : nullptr;
-  if (use_tc) {
+  if (use_tc == 2) {
+    // two query tiles per CTA; tiles hold q0 multiples of 256
+    TORCH_CHECK(D == 128, "attention: the tcgen05 forward needs head_dim 128");
+    AttnMaps maps;
+    maps.q = make_tmap_bf16_2d(q.data_ptr(), Hq * D, Tq, q.stride(0), 64, 128);
+    maps.k = make_tmap_bf16_2d(k.data_ptr(), Hkv * D, k.size(0), k.stride(0), 64, 64);
+    maps.v = make_tmap_bf16_2d(v.data_ptr(), Hkv * D, v.size(0), v.stride(0), 64, 64);
+    attn_fwd_pp(p, maps, tiles.numel() / 2, status_ptr(q.get_device()), cur_stream(q));
+  } else if (use_tc) {
     TORCH_CHECK(D == 128, "attention: the tcgen05 forward needs head_dim 128");
     attn_fwd_tc(p, tiles.numel() / 2, status_ptr(q.get_device()), cur_stream(q));
   } else {
@@ -674,7 +705,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw", &adamw_t);
   m.def("attn_fwd", &attn_fwd_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu_q"), py::arg("cu_k"),
         py::arg("key_idx"), py::arg("tiles"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"),
-        py::arg("causal"), py::arg("want_lse"), py::arg("use_tc") = false, py::arg("trace") = py::none());
+        py::arg("causal"), py::arg("want_lse"), py::arg("use_tc") = 0, py::arg("trace") = py::none());
   m.def("attn_bwd", &attn_bwd_t);
   m.def("attn_decode", &attn_decode_t);
   m.def("attn_decode_persistent", &attn_decode_persistent_t);

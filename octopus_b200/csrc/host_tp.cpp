@@ -56,12 +56,13 @@ static GemmLaunch base_launch(int M, const torch::Tensor& W, int bn_hint) {
   g.stream = at::cuda::getCurrentCUDAStream(dev).stream();
   g.alpha = 1.f;
   g.vocab_limit = N;
+  g.s.b_prefetch = gemm_prefetch_depth(M);
   return g;
 }
 
 // stage: local bf16 [tp * rows_s, K] staging buffer; work: local int32 counters
 // [1 + m_tiles], zero between calls (the kernel's last CTA resets them).
-// Split-K for decode-sized tensor-parallel GEMMs (see host_ops.cpp splitk_factor): BN = 256
+// Split-K for decode-sized tensor-parallel GEMMs (as decode_shape in host_ops.cpp): BN = 256
 // tiles split along K to about one tile per SM; returns 1 for none.  Rebuilds the B map.
 static int tp_splits(GemmLaunch& g, const torch::Tensor& W) {
   if (g.s.M > 256 || g.s.N < 256) return 1;

@@ -14,6 +14,7 @@ struct GemmShape {
   int m_shift;  // M-block rotation of the tile order (tensor-parallel: own rows first)
   int k_splits; // split-K factor (0 or 1: none); tiles = k_splits x m_tiles x n_tiles
   int pdl;      // launched as a programmatic dependent: prefetch weights to L2, then wait for the predecessor
+  int b_prefetch;  // > 0: the producer keeps L2 prefetches of B this many K-blocks ahead of its loads
 };
 
 enum GemmEpiKind : int {
@@ -29,6 +30,7 @@ struct GemmLaunch {
   CUtensorMap ta, tb;
   GemmShape s;
   int bn;
+  int mt;                  // M-tiles per CTA (1, or 2 for decode-sized M with K-major operands)
   bool a_mn, b_mn;
   int epi;
   void* C;
@@ -58,6 +60,6 @@ void gemm_launch(const GemmLaunch& g);
 // out[M, N] bf16 = sum_s ws[s][M][N] (+ bias[N]) (+ residual[M, N], row stride ldr)
 void splitk_finish(const float* ws, int splits, int M, int N, const void* bias, const void* residual, int ldr,
                    void* out, int ldc, cudaStream_t st);
-int gemm_smem_bytes(int bn);
+int gemm_smem_bytes(int bn, int mt = 1);
 
 }  // namespace octo

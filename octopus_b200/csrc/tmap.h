@@ -52,6 +52,7 @@ inline int num_sms(int device) {
 
 // GEMM N-tile width for an M x N problem on `sms` SMs (hint 64/128/256 forces it).
 int pick_bn(int M, int N, int sms, int hint);
+int gemm_prefetch_depth(int M);  // L2 prefetch distance (K-blocks) of B for an M-row GEMM
 
 // Status word: int32[2] per device = {code, where}.  Zero means OK.
 int* status_ptr(int device);

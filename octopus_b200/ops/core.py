@@ -29,11 +29,14 @@ HEAD_CHUNK = 4096  # rows per chunk in the head backward (dz is [chunk, vocab] b
 CPU_VOCAB_CHUNK = 1024  # vocab columns per chunk of the CPU head (online log-sum-exp merge)
 
 
-def use_tc_attention(D: int) -> bool:
-    """tcgen05/TMEM attention forward for head_dim 128 (OCTO_ATTN_TC=0 selects the mma.sync kernel)."""
+def use_tc_attention(D: int) -> int:
+    """Attention forward kernel: 2 = tcgen05/TMEM with two query tiles per CTA (head_dim 128,
+    the default), 1 = tcgen05 with one query tile per CTA, 0 = mma.sync (OCTO_ATTN_TC)."""
     import os
 
-    return D == 128 and os.environ.get("OCTO_ATTN_TC", "1") != "0"
+    if D != 128:
+        return 0
+    return int(os.environ.get("OCTO_ATTN_TC", "2"))
 
 
 def _is_cuda(t: torch.Tensor) -> bool:
@@ -306,6 +309,7 @@ class AttnPlan:
     fwd_tiles: torch.Tensor
     dq_tiles: torch.Tensor
     kv_tiles: torch.Tensor
+    fwd_tiles_pp: torch.Tensor  # 256-row query tiles, most keys first (two-tile tcgen05 forward)
     host_cu_q: np.ndarray = field(repr=False, default=None)
     host_cu_k: np.ndarray = field(repr=False, default=None)
     host_key_idx: np.ndarray = field(repr=False, default=None)
@@ -329,6 +333,13 @@ class AttnPlan:
 
         has_q = nq > 0
         ft = tiles(nq, 128, has_q)
+        pp = tiles(nq, 256, has_q)
+        if len(pp):
+            # longest CTAs first: keys visible to the tile's last row (bottom-right causal)
+            s_, q0 = pp[:, 0], pp[:, 1]
+            rows = np.minimum(256, nq[s_] - q0)
+            work = np.minimum(nk[s_], q0 + rows + nk[s_] - nq[s_]) * rows
+            pp = pp[np.argsort(-work, kind="stable")]
         dt = tiles(nq, 64, has_q)
         kt = tiles(nk, 64, has_q)
         dev = torch.device(device)
@@ -338,7 +349,11 @@ class AttnPlan:
             return h2d(np.ascontiguousarray(a), dev)
 
         return AttnPlan(T(cu_q), T(cu_k), T(key_idx), T(ft.reshape(-1)), T(dt.reshape(-1)), T(kt.reshape(-1)),
-                        cu_q, cu_k, key_idx)
+                        T(pp.reshape(-1)), cu_q, cu_k, key_idx)
+
+    def tiles_for(self, mode: int) -> torch.Tensor:
+        """Forward tile table of attention kernel `mode` (see use_tc_attention)."""
+        return self.fwd_tiles_pp if mode == 2 else self.fwd_tiles
 
     @staticmethod
     def causal_packed(lengths, device="cpu") -> "AttnPlan":
@@ -356,8 +371,9 @@ class _Attention(torch.autograd.Function):
         v = qkv[:, (Hq + Hkv) * D: (Hq + 2 * Hkv) * D]
         ctx.meta = (plan, Hq, Hkv, D, scale)
         if _is_cuda(qkv):
-            o, lse = ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D, scale,
-                                    True, True, use_tc_attention(D))
+            mode = use_tc_attention(D)
+            o, lse = ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.tiles_for(mode), Hq, Hkv, D,
+                                    scale, True, True, mode)
         else:
             o3, lse = ref.gather_attention(q.reshape(T, Hq, D), k.reshape(T, Hkv, D), v.reshape(T, Hkv, D),
                                            plan.host_cu_q, plan.host_cu_k, torch.from_numpy(plan.host_key_idx),

@@ -37,8 +37,9 @@ def prefill_attn(q, kc, vc, plan, Hq, Hkv, D, scale):
     """q [T, Hq*D] against cache rows plan.key_idx (slot ids), bottom-right causal."""
     if q.is_cuda:
         from .core import use_tc_attention
-        o, _ = ext().attn_fwd(q, kc, vc, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D, scale,
-                              True, False, use_tc_attention(D))
+        mode = use_tc_attention(D)
+        o, _ = ext().attn_fwd(q, kc, vc, plan.cu_q, plan.cu_k, plan.key_idx, plan.tiles_for(mode), Hq, Hkv, D, scale,
+                              True, False, mode)
         return o
     T = q.shape[0]
     o, _ = ref.gather_attention(q.reshape(T, Hq, D), kc.reshape(-1, Hkv, D), vc.reshape(-1, Hkv, D),

@@ -5,7 +5,9 @@
 Cases (inputs sized above L2 where DRAM behaviour matters, a few GB at most):
   gemm_fwd_7b        X[16384, 3584] @ W[18944*2, 3584]^T (gate/up projection)
   gemm_wgrad_7b      dY^T X for the down projection (MN-major operands)
-  attn_fwd_tc        tree attention forward, tcgen05 kernel (8 x 2048 own + 2048 prefix)
+  attn_fwd_pp        tree attention forward, tcgen05 kernel with two query tiles per CTA
+                     (8 x 2048 own + 2048 prefix)
+  attn_fwd_tc        same, tcgen05 kernel with one query tile per CTA
   attn_fwd_mma       same on the mma.sync kernel
   attn_bwd           tree attention backward (dq + dkv kernels)
   decode_splitk      paged decode, 256 requests x 3000 keys (split-K kernel)
@@ -15,7 +17,9 @@ Cases (inputs sized above L2 where DRAM behaviour matters, a few GB at most):
                      by 2 rows) + own 272 tokens
   decode_dag_flat    same lengths, every row's keys distinct (no sharing)
   decode_dag_shared  the decode_dag rows on the shared-prefix kernel (segments planned once)
-  decode_gemms       the four GEMMs of one 7B decoder layer at 256 decode rows (OCTO_SPLITK=0: no split-K)
+  decode_gemms       the four GEMMs of one 7B decoder layer at 256 decode rows (OCTO_SPLITK=0: no split-K,
+                     OCTO_GEMM_MT=1: one M-tile per CTA)
+  decode_gemm_{qkv,o,gu,down}  one of them, over weight copies > 2x L2 (time / copies = per GEMM)
   head_fwd           fused logprob head, 4096 rows x 152064 vocab
   sample_head        fused sampling head, 256 rows x 152064 vocab
 """
@@ -116,12 +120,12 @@ def build(case: str, dev):
         X = torch.randn(16384, 18944, device=dev).bfloat16()
         G = torch.zeros(3584, 18944, device=dev)
         return lambda: ops.gemm(dY, X, a_mn=True, b_mn=True, out=G, accumulate=True)
-    if case in ("attn_fwd_tc", "attn_fwd_mma"):
+    if case in ("attn_fwd_pp", "attn_fwd_tc", "attn_fwd_mma"):
         plan, qkv, Hq, Hkv, D = tree_case(dev)
         q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
-        tc = case == "attn_fwd_tc"
-        return lambda: ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D,
-                                          D ** -0.5, True, True, tc)
+        mode = {"attn_fwd_pp": 2, "attn_fwd_tc": 1, "attn_fwd_mma": 0}[case]
+        return lambda: ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.tiles_for(mode), Hq, Hkv,
+                                          D, D ** -0.5, True, True, mode)
     if case == "attn_bwd":
         plan, qkv, Hq, Hkv, D = tree_case(dev)
         x = qkv.clone().requires_grad_(True)
@@ -140,6 +144,14 @@ def build(case: str, dev):
         xf = torch.randn(M, F, device=dev).bfloat16()
         ins = (x, xa, x, xf)
         return lambda: [ops.gemm(i, w) for i, w in zip(ins, ws)]
+    if case.startswith("decode_gemm_"):
+        # one decode GEMM, rotating over weight copies that together exceed 2x L2 (cold weights)
+        M, H, F = 256, 3584, 18944
+        n, k = {"qkv": (4608, H), "o": (H, 3584), "gu": (2 * F, H), "down": (H, F)}[case[len("decode_gemm_"):]]
+        copies = max(1, -(-(300 << 20) // (n * k * 2)))
+        ws = [(torch.randn(n, k, device=dev) * 0.02).bfloat16() for _ in range(copies)]
+        x = torch.randn(M, k, device=dev).bfloat16()
+        return lambda: [ops.gemm(x, w) for w in ws]
     if case == "decode_dag_shared":
         Hq, Hkv, D = 28, 4, 128
         rows, ctx, nslots = decode_dag_rows(True)
@@ -210,7 +222,7 @@ def trace_attn_tc():
     tr = torch.zeros(10 * 64, dtype=torch.int64, device=dev)
     for _ in range(2):
         ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D, D ** -0.5, True,
-                           True, True, tr)
+                           True, 1, tr)
     torch.cuda.synchronize()
     t = tr.view(10, 64).cpu().numpy().astype(np.int64)
     t0 = t[9, 0]

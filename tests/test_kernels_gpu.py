@@ -262,8 +262,11 @@ def test_sampling_never_nan_over_many_rows():
         assert (tok >= 0).all() and (tok < V).all()
 
 
+@pytest.mark.parametrize("mode", [1, 2])
 @pytest.mark.parametrize("Hq,Hkv", [(28, 4), (12, 2)])
-def test_tcgen05_attention_matches_mma_sync_and_reference(Hq, Hkv):
+def test_tcgen05_attention_matches_mma_sync_and_reference(Hq, Hkv, mode):
+    """tcgen05 forwards (1: one query tile per CTA, 2: two ping-ponging tiles) vs the
+    mma.sync kernel and the fp32 reference on a random tree."""
     rng = np.random.default_rng(13)
     torch.manual_seed(13)
     D = 128
@@ -271,10 +274,12 @@ def test_tcgen05_attention_matches_mma_sync_and_reference(Hq, Hkv):
     plan = ops.AttnPlan.build(cu_q, cu_k, keys, dev)
     qkv = (torch.randn(T, (Hq + 2 * Hkv) * D, device=dev) * 0.5).bfloat16()
     q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
-    o_tc, lse_tc = ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D,
-                                      D ** -0.5, True, True, True)
+    o_tc, lse_tc = ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.tiles_for(mode), Hq, Hkv, D,
+                                      D ** -0.5, True, True, mode)
     o_ms, lse_ms = ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.fwd_tiles, Hq, Hkv, D,
-                                      D ** -0.5, True, True, False)
+                                      D ** -0.5, True, True, 0)
+    torch.cuda.synchronize()
+    ops.check_status(0)
     x = qkv.float().cpu()
     orf, lrf = ref.gather_attention(x[:, : Hq * D].reshape(T, Hq, D), x[:, Hq * D: (Hq + Hkv) * D].reshape(T, Hkv, D),
                                     x[:, (Hq + Hkv) * D:].reshape(T, Hkv, D), cu_q, cu_k, torch.from_numpy(keys),
@@ -282,6 +287,39 @@ def test_tcgen05_attention_matches_mma_sync_and_reference(Hq, Hkv):
     assert rel_err(o_tc.cpu(), orf.reshape(T, Hq * D)) < 2e-2
     assert rel_err(o_tc, o_ms) < 2e-2
     assert torch.allclose(lse_tc.cpu(), lrf.float(), atol=2e-2)
+
+
+@pytest.mark.parametrize("shuffle", [False, True])
+def test_two_tile_attention_long_sequences(shuffle):
+    """Two-tile forward on long sequences (several 256-row CTAs, the ragged last one) with
+    keys in path order (TMA row boxes) or shuffled (cp.async gathers), against fp32."""
+    rng = np.random.default_rng(21)
+    torch.manual_seed(21)
+    Hq, Hkv, D = 8, 2, 128
+    pre, lens = 700, [900, 333, 1]
+    T = pre + sum(lens)
+    perm = rng.permutation(T).astype(np.int32) if shuffle else np.arange(T, dtype=np.int32)
+    keys, cu_q, cu_k, qrows = [], [0], [0], []
+    a = pre
+    for n in lens:
+        keys += list(perm[:pre]) + list(perm[a:a + n])
+        qrows += list(range(a, a + n))
+        cu_q.append(cu_q[-1] + n)
+        cu_k.append(len(keys))
+        a += n
+    keys = np.asarray(keys, dtype=np.int32)
+    plan = ops.AttnPlan.build(cu_q, cu_k, keys, dev)
+    kv = (torch.randn(T, 2 * Hkv * D, device=dev) * 0.5).bfloat16()
+    q = (torch.randn(cu_q[-1], Hq * D, device=dev) * 0.5).bfloat16()
+    k, v = kv[:, : Hkv * D], kv[:, Hkv * D:]
+    o, lse = ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.tiles_for(2), Hq, Hkv, D,
+                                D ** -0.5, True, True, 2)
+    torch.cuda.synchronize()
+    ops.check_status(0)
+    orf, lrf = ref.gather_attention(q.float().cpu().reshape(-1, Hq, D), k.float().cpu().reshape(T, Hkv, D),
+                                    v.float().cpu().reshape(T, Hkv, D), cu_q, cu_k, torch.from_numpy(keys), D ** -0.5)
+    assert rel_err(o.cpu(), orf.reshape(-1, Hq * D)) < 2e-2
+    assert torch.allclose(lse.cpu(), lrf.float(), atol=2e-2)
 
 
 def test_persistent_decode_matches_splitk():
@@ -340,9 +378,11 @@ def test_shared_prefix_decode_matches_persistent():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("M,N,K", [(16, 4608, 3584), (128, 3584, 18944), (256, 3584, 3584), (200, 512, 1024)])
+@pytest.mark.parametrize("M,N,K", [(16, 4608, 3584), (128, 3584, 18944), (256, 3584, 3584), (200, 512, 1024),
+                                   (136, 2048, 4096), (232, 37888, 512), (256, 37888, 3584)])
 def test_splitk_decode_gemm(M, N, K):
-    """Decode-sized GEMMs take the split-K path (fp32 partials + finish with bias/residual)."""
+    """Decode-sized GEMMs: split-K (fp32 partials + finish with bias/residual) and, for
+    128 < M <= 256, two M-tiles per CTA (with and without split-K)."""
     torch.manual_seed(16)
     a = (torch.randn(M, K, device=dev) * 0.5).bfloat16()
     w = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
@@ -353,3 +393,18 @@ def test_splitk_decode_gemm(M, N, K):
     ops.check_status(0)
     ref_ = a.float() @ w.float().t() + b.float() + r.float()
     assert rel_err(out, ref_) < 1e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [144, 256])
+def test_two_mtile_gemm_matches_one_mtile(M, monkeypatch):
+    """MT = 2 (both M-blocks in one CTA) gives the same sums as the one-M-tile launch."""
+    torch.manual_seed(17)
+    a = (torch.randn(M, 3584, device=dev) * 0.5).bfloat16()
+    w = (torch.randn(37888, 3584, device=dev) * 0.02).bfloat16()
+    two = ops.gemm(a, w)
+    monkeypatch.setenv("OCTO_GEMM_MT", "1")
+    one = ops.gemm(a, w)
+    torch.cuda.synchronize()
+    ops.check_status(0)
+    assert torch.equal(one, two)
