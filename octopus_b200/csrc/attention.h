@@ -78,4 +78,14 @@ struct AttnMaps {
 // head_dim 128; tiles [n_tiles, 2] (seq, q0) with q0 a multiple of 256
 void attn_fwd_pp(const AttnParams& p, const AttnMaps& maps, int n_tiles, int* status, cudaStream_t st);
 
+// TMA maps of the tcgen05 backward: q, dO [Tq, Hq*D]; k, v [rows, Hkv*D]; all boxes 64 x 64,
+// 128-byte swizzled.
+struct AttnBwdMaps {
+  CUtensorMap q, dO, k, v;
+};
+// head_dim 128; p.tiles: (seq, q0) with q0 a multiple of 128; p.ktiles: (seq, k0), k0 a
+// multiple of 128 (sequences with queries only).  dk_acc / dv_acc are added to.
+void attn_bwd_tc(const AttnBwdParams& p, const AttnBwdMaps& maps, int n_qtiles, int n_ktiles, int* status,
+                 cudaStream_t st);
+
 }  // namespace octo

@@ -553,7 +553,7 @@ std::vector<torch::Tensor> attn_fwd_t(torch::Tensor q, torch::Tensor k, torch::T
 torch::Tensor attn_bwd_t(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dO,
                          torch::Tensor lse, torch::Tensor cu_q, torch::Tensor cu_k, torch::Tensor key_idx,
                          torch::Tensor qtiles, torch::Tensor ktiles, torch::Tensor dk_acc, torch::Tensor dv_acc,
-                         int64_t Hq, int64_t Hkv, int64_t D, double scale, bool causal) {
+                         int64_t Hq, int64_t Hkv, int64_t D, double scale, bool causal, int64_t use_tc) {
   c10::cuda::CUDAGuard guard(q.get_device());
   CHECK_CONTIG(dO);
   CHECK_CONTIG(o);
@@ -589,7 +589,19 @@ torch::Tensor attn_bwd_t(torch::Tensor q, torch::Tensor k, torch::Tensor v, torc
   p.Hkv = Hkv;
   p.scale = static_cast<float>(scale);
   p.causal = causal ? 1 : 0;
-  attn_bwd(p, qtiles.numel() / 2, ktiles.numel() / 2, D, cur_stream(q));
+  if (use_tc) {
+    // tcgen05 kernels: qtiles / ktiles hold 128-row tiles
+    TORCH_CHECK(D == 128, "attention: the tcgen05 backward needs head_dim 128");
+    TORCH_CHECK(dO.stride(0) % 8 == 0, "attn_bwd: dO row stride multiple of 8");
+    AttnBwdMaps maps;
+    maps.q = make_tmap_bf16_2d(q.data_ptr(), Hq * D, Tq, q.stride(0), 64, 64);
+    maps.dO = make_tmap_bf16_2d(dO.data_ptr(), Hq * D, Tq, dO.stride(0), 64, 64);
+    maps.k = make_tmap_bf16_2d(k.data_ptr(), Hkv * D, k.size(0), k.stride(0), 64, 64);
+    maps.v = make_tmap_bf16_2d(v.data_ptr(), Hkv * D, v.size(0), v.stride(0), 64, 64);
+    attn_bwd_tc(p, maps, qtiles.numel() / 2, ktiles.numel() / 2, status_ptr(q.get_device()), cur_stream(q));
+  } else {
+    attn_bwd(p, qtiles.numel() / 2, ktiles.numel() / 2, D, cur_stream(q));
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dq;
 }
@@ -706,7 +718,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &attn_fwd_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu_q"), py::arg("cu_k"),
         py::arg("key_idx"), py::arg("tiles"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"),
         py::arg("causal"), py::arg("want_lse"), py::arg("use_tc") = 0, py::arg("trace") = py::none());
-  m.def("attn_bwd", &attn_bwd_t);
+  m.def("attn_bwd", &attn_bwd_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dO"),
+        py::arg("lse"), py::arg("cu_q"), py::arg("cu_k"), py::arg("key_idx"), py::arg("qtiles"), py::arg("ktiles"),
+        py::arg("dk_acc"), py::arg("dv_acc"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"),
+        py::arg("causal"), py::arg("use_tc") = 0);
   m.def("attn_decode", &attn_decode_t);
   m.def("attn_decode_persistent", &attn_decode_persistent_t);
   m.def("attn_decode_shared", &attn_decode_shared_t);

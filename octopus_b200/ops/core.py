@@ -39,6 +39,14 @@ def use_tc_attention(D: int) -> int:
     return int(os.environ.get("OCTO_ATTN_TC", "2"))
 
 
+def use_tc_bwd(D: int) -> int:
+    """Attention backward kernels: 1 = tcgen05/TMEM (head_dim 128, the default), 0 = mma.sync
+    (OCTO_ATTN_BWD_TC=0)."""
+    import os
+
+    return int(D == 128 and os.environ.get("OCTO_ATTN_BWD_TC", "1") != "0")
+
+
 def _is_cuda(t: torch.Tensor) -> bool:
     return t.is_cuda
 
@@ -310,6 +318,8 @@ class AttnPlan:
     dq_tiles: torch.Tensor
     kv_tiles: torch.Tensor
     fwd_tiles_pp: torch.Tensor  # 256-row query tiles, most keys first (two-tile tcgen05 forward)
+    dq_tiles_tc: torch.Tensor   # 128-row query tiles, most keys first (tcgen05 backward)
+    kv_tiles_tc: torch.Tensor   # 128-row key tiles of sequences with queries, most work first
     host_cu_q: np.ndarray = field(repr=False, default=None)
     host_cu_k: np.ndarray = field(repr=False, default=None)
     host_key_idx: np.ndarray = field(repr=False, default=None)
@@ -340,6 +350,17 @@ class AttnPlan:
             rows = np.minimum(256, nq[s_] - q0)
             work = np.minimum(nk[s_], q0 + rows + nk[s_] - nq[s_]) * rows
             pp = pp[np.argsort(-work, kind="stable")]
+        dqt = tiles(nq, 128, has_q)
+        if len(dqt):
+            s_, q0 = dqt[:, 0], dqt[:, 1]
+            rows = np.minimum(128, nq[s_] - q0)
+            dqt = dqt[np.argsort(-(np.minimum(nk[s_], q0 + rows + nk[s_] - nq[s_]) * rows), kind="stable")]
+        kvt = tiles(nk, 128, has_q)
+        if len(kvt):
+            # queries that see key tile k0: those from max(0, k0 - (nk - nq)) on
+            s_, k0 = kvt[:, 0], kvt[:, 1]
+            seen = nq[s_] - np.clip(k0 - (nk[s_] - nq[s_]), 0, nq[s_])
+            kvt = kvt[np.argsort(-(seen * np.minimum(128, nk[s_] - k0)), kind="stable")]
         dt = tiles(nq, 64, has_q)
         kt = tiles(nk, 64, has_q)
         dev = torch.device(device)
@@ -349,7 +370,7 @@ class AttnPlan:
             return h2d(np.ascontiguousarray(a), dev)
 
         return AttnPlan(T(cu_q), T(cu_k), T(key_idx), T(ft.reshape(-1)), T(dt.reshape(-1)), T(kt.reshape(-1)),
-                        T(pp.reshape(-1)), cu_q, cu_k, key_idx)
+                        T(pp.reshape(-1)), T(dqt.reshape(-1)), T(kvt.reshape(-1)), cu_q, cu_k, key_idx)
 
     def tiles_for(self, mode: int) -> torch.Tensor:
         """Forward tile table of attention kernel `mode` (see use_tc_attention)."""
@@ -394,8 +415,10 @@ class _Attention(torch.autograd.Function):
             v = qkv[:, (Hq + Hkv) * D: (Hq + 2 * Hkv) * D]
             dk = torch.zeros(T, Hkv * D, dtype=torch.float32, device=qkv.device)
             dv = torch.zeros(T, Hkv * D, dtype=torch.float32, device=qkv.device)
-            dq = ext().attn_bwd(q, k, v, o, do, lse, plan.cu_q, plan.cu_k, plan.key_idx, plan.dq_tiles,
-                                plan.kv_tiles, dk, dv, Hq, Hkv, D, scale, True)
+            tc = use_tc_bwd(D)
+            dq = ext().attn_bwd(q, k, v, o, do, lse, plan.cu_q, plan.cu_k, plan.key_idx,
+                                plan.dq_tiles_tc if tc else plan.dq_tiles, plan.kv_tiles_tc if tc else plan.kv_tiles,
+                                dk, dv, Hq, Hkv, D, scale, True, tc)
             dqkv = torch.empty_like(qkv)
             dqkv[:, : Hq * D] = dq
             dqkv[:, Hq * D: (Hq + Hkv) * D] = dk

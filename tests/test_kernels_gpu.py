@@ -408,3 +408,63 @@ def test_two_mtile_gemm_matches_one_mtile(M, monkeypatch):
     torch.cuda.synchronize()
     ops.check_status(0)
     assert torch.equal(one, two)
+
+
+def _bwd_both(q, k, v, plan, Hq, Hkv, D, seed):
+    """(dq, dk, dv) of the tcgen05 and the mma.sync backward kernels on the same inputs."""
+    torch.manual_seed(seed)
+    T = q.shape[0]
+    o, lse = ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.tiles_for(2), Hq, Hkv, D,
+                                D ** -0.5, True, True, 2)
+    do = (torch.randn_like(o.float()) * 0.5).bfloat16()
+    out = []
+    for tc in (1, 0):
+        dk = torch.zeros(k.shape[0], Hkv * D, dtype=torch.float32, device=dev)
+        dv = torch.zeros_like(dk)
+        dq = ops.ext().attn_bwd(q, k, v, o, do, lse, plan.cu_q, plan.cu_k, plan.key_idx,
+                                plan.dq_tiles_tc if tc else plan.dq_tiles, plan.kv_tiles_tc if tc else plan.kv_tiles,
+                                dk, dv, Hq, Hkv, D, D ** -0.5, True, tc)
+        out.append((dq, dk, dv))
+    torch.cuda.synchronize()
+    ops.check_status(0)
+    return out
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(28, 4), (12, 2)])
+def test_tcgen05_attention_backward_tree(Hq, Hkv):
+    """tcgen05 backward (dq kernel + dkv kernel) vs the mma.sync kernels on a random tree."""
+    rng = np.random.default_rng(31)
+    torch.manual_seed(31)
+    D = 128
+    T, cu_q, cu_k, keys = _tree_plan(rng, n_nodes=10)
+    plan = ops.AttnPlan.build(cu_q, cu_k, keys, dev)
+    qkv = (torch.randn(T, (Hq + 2 * Hkv) * D, device=dev) * 0.5).bfloat16()
+    q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
+    (a, b) = _bwd_both(q, k, v, plan, Hq, Hkv, D, 32)
+    for x, y in zip(a, b):
+        assert rel_err(x.float(), y.float()) < 2e-2
+
+
+@pytest.mark.parametrize("shuffle", [False, True])
+def test_tcgen05_attention_backward_long(shuffle):
+    """Long sequences sharing a prefix (key rows in several lists: fp32 scatter-adds), keys
+    consecutive (TMA boxes) or shuffled (cp.async gathers)."""
+    rng = np.random.default_rng(33)
+    Hq, Hkv, D = 8, 2, 128
+    pre, lens = 700, [900, 333, 1]
+    T = pre + sum(lens)
+    perm = rng.permutation(T).astype(np.int32) if shuffle else np.arange(T, dtype=np.int32)
+    keys, cu_q, cu_k = [], [0], [0]
+    a = pre
+    for n in lens:
+        keys += list(perm[:pre]) + list(perm[a:a + n])
+        cu_q.append(cu_q[-1] + n)
+        cu_k.append(len(keys))
+        a += n
+    plan = ops.AttnPlan.build(cu_q, cu_k, np.asarray(keys, dtype=np.int32), dev)
+    torch.manual_seed(34)
+    kv = (torch.randn(T, 2 * Hkv * D, device=dev) * 0.5).bfloat16()
+    q = (torch.randn(cu_q[-1], Hq * D, device=dev) * 0.5).bfloat16()
+    (a_, b_) = _bwd_both(q, kv[:, : Hkv * D], kv[:, Hkv * D:], plan, Hq, Hkv, D, 35)
+    for x, y in zip(a_, b_):
+        assert rel_err(x.float(), y.float()) < 2e-2
