@@ -14,14 +14,18 @@
 // dQ needs no atomics: it is recomputed per query tile (7 MMAs per tile pair in all
 // instead of 5 plus an fp32 reduction of every dQ partial).
 //
-// Warp roles (both kernels): warp 0 streams the operand whose rows are contiguous (Q/dO,
-// TMA), warp 1 owns TMEM and issues the MMAs from an event loop, warps 2-3 load the
-// gathered key rows (two TMA boxes per 64 rows when consecutive in the key list, cp.async
-// otherwise), warps 4-7 do the elementwise work and the epilogue.
+// Warp roles (both kernels, 384 threads): warp 0 streams the operand whose rows are
+// contiguous (Q/dO, TMA), warp 1 owns TMEM and issues the MMAs from an event loop, warps 2-3
+// load the gathered key rows (two TMA boxes per 64 rows when consecutive in the key list,
+// cp.async otherwise), warps 4-7 and 8-11 (two per SM sub-partition, hiding each other's
+// TMEM and MUFU latency) do the elementwise work on the two column halves and the epilogue.
 //
-// TMEM: dq kernel  S[0] [0,128), S[1] [128,256), dP [256,384), dQ [384,512)
+// TMEM: dq kernel  S[0] [0,128), S[1] [128,256), dP [256,384), dQ [384,512); the bf16 dS
+//                  of key half w goes to S columns [64w, 64w + 32) (inside that half's own S
+//                  range, so neither half overwrites columns the other still reads)
 //       dkv kernel S^T[0] [0,64), S^T[1] [64,128), dP^T[0] [128,192), dP^T[1] [192,256),
-//                  dV [256,384), dK [384,512)
+//                  dV [256,384), dK [384,512); P^T / dS^T of query half w at [32w, 32w + 16)
+//                  of their buffer
 // All waits are bounded (common.cuh); a timed-out CTA records an error, drains and frees TMEM.
 //
 // Reference parity (behaviour): gradients of the tree attention the reference trains through
@@ -41,7 +45,7 @@ constexpr int kHalf = 128 * 128;   // 64-column SW128 half of a 128-row tile
 constexpr int kTile = 2 * kHalf;   // 32 KB
 constexpr int kHalf64 = 64 * 128;  // 64-column half of a 64-row tile
 constexpr int kTile64 = 2 * kHalf64;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ uint32_t toff(int r, int c) {
@@ -103,6 +107,18 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
+// dS = P o (dP - delta) of 32 keys (key index k0 + i; keys >= lim masked), packed bf16 pairs
+__device__ __forceinline__ void ds_chunk(const uint32_t (&sv)[32], const uint32_t (&dv)[32], int k0, int lim,
+                                         float sc, float lse2, float dlt, uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int k = k0 + 2 * i;
+    const float p0 = k < lim ? exp2f(fmaf(__uint_as_float(sv[2 * i]), sc, -lse2)) : 0.f;
+    const float p1 = k + 1 < lim ? exp2f(fmaf(__uint_as_float(sv[2 * i + 1]), sc, -lse2)) : 0.f;
+    pk[i] = pack_bf16x2(p0 * (__uint_as_float(dv[2 * i]) - dlt), p1 * (__uint_as_float(dv[2 * i + 1]) - dlt));
+  }
+}
+
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity))
@@ -131,8 +147,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* dq_done = s_full + 2;    // [2] (per S buffer)
   uint64_t* dp_full = dq_done + 2;
   uint64_t* dp_free = dp_full + 1;
-  uint64_t* ds_full = dp_free + 1;
-  uint64_t* drain = ds_full + 1;
+  uint64_t* ds_full = dp_free + 1;   // [2] (per S buffer)
+  uint64_t* drain = ds_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   constexpr uint32_t kColDP = 256, kColDQ = 384;
@@ -161,8 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&dq_done[s], 1);
     }
     mbar_init(dp_full, 1);
-    mbar_init(dp_free, 4);
-    mbar_init(ds_full, 4);
+    mbar_init(dp_free, 8);
+    mbar_init(&ds_full[0], 8);
+    mbar_init(&ds_full[1], 8);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -235,8 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (ok && jq < nt) {
         bool progressed = false;
         // S(js) = Q K_js^T into S[js & 1]: needs K_js and dQ(js - 2) (the buffer's last reader) complete
-        if (js < nt && mbar_try_wait(&k_full[js & 1], (js >> 1) & 1) &&
-            (js < 2 || mbar_try_wait(&dq_done[js & 1], ((js - 2) >> 1) & 1))) {
+        if (js < nt && mbar_test(&k_full[js & 1], (js >> 1) & 1) &&
+            (js < 2 || mbar_test(&dq_done[js & 1], ((js - 2) >> 1) & 1))) {
           tc_fence_after();
           fence_proxy_async_smem();
           const uint32_t kaddr = smem_u32(sK + (js & 1) * kTile);
@@ -250,9 +267,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++js;
           issued = progressed = true;
         }
-        // dP(jd) = dO V_jd^T: needs V_jd, dP(jd - 1) read by the softmax warps, dQ(jd - 1) issued
-        if (jd < js && jq >= jd && mbar_try_wait(&v_full[jd & 1], (jd >> 1) & 1) &&
-            (jd == 0 || mbar_try_wait(dp_free, (jd - 1) & 1))) {
+        // dP(jd) = dO V_jd^T: needs V_jd and dP(jd - 1) read by the elementwise warps (issued
+        // before the pending dQ so the next tile's elementwise work can start sooner)
+        if (jd < js && mbar_test(&v_full[jd & 1], (jd >> 1) & 1) &&
+            (jd == 0 || mbar_test(dp_free, (jd - 1) & 1))) {
           tc_fence_after();
           fence_proxy_async_smem();
           const uint32_t vaddr = smem_u32(sV + (jd & 1) * kTile);
@@ -267,14 +285,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++jd;
           issued = progressed = true;
         }
-        // dQ += dS(jq) K_jq
-        if (jq < jd && mbar_try_wait(ds_full, jq & 1)) {
+        // dQ += dS(jq) K_jq (dS of key half w at S columns [64w, 64w + 32))
+        if (jq < jd && mbar_test(&ds_full[jq & 1], (jq >> 1) & 1)) {
           tc_fence_after();
           const uint32_t kaddr = smem_u32(sK + (jq & 1) * kTile);
 #pragma unroll
           for (int kk = 0; kk < 128 / 16; ++kk) {
             const uint64_t bd = umma_smem_desc(kaddr + kk * 2048, kHalf, 1024);
-            umma_f16_ts(tmem + kColDQ, tmem + (jq & 1) * 128 + kk * 8, bd, idesc_q, (jq > 0 || kk > 0) ? 1u : 0u);
+            const uint32_t acol = (jq & 1) * 128 + (kk >> 2) * 64 + (kk & 3) * 8;
+            umma_f16_ts(tmem + kColDQ, tmem + acol, bd, idesc_q, (jq > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&dq_done[jq & 1]);
           umma_commit(&k_empty[jq & 1]);
@@ -299,6 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ dS + epilogue (thread = query row)
     const int quarter = warp & 3;
+    const int wh = (warp - 4) >> 2;             // key half of every tile: [64 wh, 64 wh + 64)
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const bool valid = r < mrows;
@@ -309,47 +329,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float dlt = valid ? p.delta[static_cast<size_t>(h) * p.Tq + qbeg + qi] : 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
-      const uint32_t colS = (j & 1) * 128;
+      const uint32_t colS = (j & 1) * 128 + wh * 64;
       if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag, status, 940) ||
           !mbar_wait(dp_full, j & 1, abort_flag, status, 941)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int kbase = j * 128;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dv[32];
-        tmem_ld_32x32b_x32(tmem + lane_addr + colS + c * 32, sv);
-        tmem_ld_32x32b_x32(tmem + lane_addr + kColDP + c * 32, dv);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int k = kbase + c * 32 + 2 * i;
-          const float p0 = k < lim ? exp2f(fmaf(__uint_as_float(sv[2 * i]), sc, -lse2)) : 0.f;
-          const float p1 = k + 1 < lim ? exp2f(fmaf(__uint_as_float(sv[2 * i + 1]), sc, -lse2)) : 0.f;
-          pk[i] = pack_bf16x2(p0 * (__uint_as_float(dv[2 * i]) - dlt), p1 * (__uint_as_float(dv[2 * i + 1]) - dlt));
-        }
-        // dS chunk c -> S columns [16c, 16c + 16): S columns < 32(c + 1) are already read
-        tmem_st_32x32b_x16(tmem + lane_addr + colS + c * 16, pk);
-      }
+      uint32_t d0[32], d1[32], sv[32];
+      tmem_ld_32x32b_x32(tmem + lane_addr + kColDP + wh * 64, d0);
+      tmem_ld_32x32b_x32(tmem + lane_addr + kColDP + wh * 64 + 32, d1);
+      tmem_ld_32x32b_x32(tmem + lane_addr + colS, sv);
+      tmem_wait_ld();
+      // this half of dP is in registers: the next dP may be issued
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(dp_free);  // dP fully read into registers
+      if (lane == 0) mbar_arrive(dp_free);
+      const int kbase = j * 128 + wh * 64;
+      uint32_t pk[16];
+      ds_chunk(sv, d0, kbase, lim, sc, lse2, dlt, pk);
+      // dS chunk c -> columns [16c, 16c + 16) of this half's S range (columns < 32(c + 1) of
+      // the range are already in registers)
+      tmem_st_32x32b_x16(tmem + lane_addr + colS, pk);
+      tmem_ld_32x32b_x32(tmem + lane_addr + colS + 32, sv);
+      tmem_wait_ld();
+      ds_chunk(sv, d1, kbase + 32, lim, sc, lse2, dlt, pk);
+      tmem_st_32x32b_x16(tmem + lane_addr + colS + 16, pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(ds_full);
+      if (lane == 0) mbar_arrive(&ds_full[j & 1]);
     }
     const int last = nt - 1;
-    __nv_bfloat16* dqrow = p.dq + static_cast<size_t>(qbeg + q0 + (valid ? r : 0)) * p.lddq + static_cast<size_t>(h) * kD;
+    __nv_bfloat16* dqrow = p.dq + static_cast<size_t>(qbeg + q0 + (valid ? r : 0)) * p.lddq +
+                           static_cast<size_t>(h) * kD + wh * 64;
     if (ok && nt > 0 && mbar_wait(&dq_done[last & 1], (last >> 1) & 1, abort_flag, status, 950)) {
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < kD / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + lane_addr + kColDQ + c * 32, v);
+        tmem_ld_32x32b_x32(tmem + lane_addr + kColDQ + wh * 64 + c * 32, v);
         tmem_wait_ld();
         if (valid) {
 #pragma unroll
@@ -364,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else if (nt == 0 && valid) {
-      for (int c = 0; c < kD; c += 8) *reinterpret_cast<uint4*>(dqrow + c) = make_uint4(0, 0, 0, 0);
+      for (int c = 0; c < 64; c += 8) *reinterpret_cast<uint4*>(dqrow + c) = make_uint4(0, 0, 0, 0);
     }
   }
 
@@ -425,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sd_full[b], 1);
-      mbar_init(&pd_full[b], 4);
+      mbar_init(&pd_full[b], 8);
       mbar_init(&buf_free[b], 1);
     }
     mbar_init(acc_done, 1);
@@ -512,8 +531,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (ok && ivk < steps) {
         bool progressed = false;
         // S^T(isd) = K Q^T, dP^T(isd) = V dO^T into buffer isd & 1
-        if (isd < steps && isd - ivk < 2 && mbar_try_wait(&st_full[isd % kQStages], (isd / kQStages) & 1) &&
-            (isd < 2 || mbar_try_wait(&buf_free[isd & 1], ((isd - 2) >> 1) & 1))) {
+        if (isd < steps && isd - ivk < 2 && mbar_test(&st_full[isd % kQStages], (isd / kQStages) & 1) &&
+            (isd < 2 || mbar_test(&buf_free[isd & 1], ((isd - 2) >> 1) & 1))) {
           tc_fence_after();
           fence_proxy_async_smem();  // cp.async-gathered K / V rows -> tensor-core reads
           const int b = isd & 1, s = isd % kQStages;
@@ -535,17 +554,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           issued = progressed = true;
         }
         // dV += P^T dO_i, dK += dS^T Q_i
-        if (ivk < isd && mbar_try_wait(&pd_full[ivk & 1], (ivk >> 1) & 1)) {
+        if (ivk < isd && mbar_test(&pd_full[ivk & 1], (ivk >> 1) & 1)) {
           tc_fence_after();
           const int b = ivk & 1, s = ivk % kQStages;
           const uint32_t qaddr = smem_u32(sQ + s * kTile64), doaddr = smem_u32(sdO + s * kTile64);
+          // A columns of query slice kk (16 queries): half kk / 2 at [32 (kk / 2), +16)
 #pragma unroll
           for (int kk = 0; kk < 64 / 16; ++kk)
-            umma_f16_ts(tmem + kColDV, tmem + b * 64 + kk * 8, umma_smem_desc(doaddr + kk * 2048, kHalf64, 1024),
-                        idesc_acc, (ivk > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_ts(tmem + kColDV, tmem + b * 64 + (kk >> 1) * 32 + (kk & 1) * 8,
+                        umma_smem_desc(doaddr + kk * 2048, kHalf64, 1024), idesc_acc, (ivk > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < 64 / 16; ++kk)
-            umma_f16_ts(tmem + kColDK, tmem + kColDPT + b * 64 + kk * 8,
+            umma_f16_ts(tmem + kColDK, tmem + kColDPT + b * 64 + (kk >> 1) * 32 + (kk & 1) * 8,
                         umma_smem_desc(qaddr + kk * 2048, kHalf64, 1024), idesc_acc, (ivk > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&buf_free[b]);
           umma_commit(&st_empty[s]);
@@ -571,6 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ P^T, dS^T + epilogue (thread = key row)
     const int quarter = warp & 3;
+    const int wh = (warp - 4) >> 2;             // query half of every sub-tile: [32 wh, 32 wh + 32)
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const bool kvalid = r < krows;
@@ -579,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int i = 0; i < steps; ++i) {
       const int b = i & 1, s = i % kQStages;
-      const int i0 = qs64 + (i % nqs) * 64;
+      const int i0 = qs64 + (i % nqs) * 64 + wh * 32;
       // (the stage's lse / delta were written by cp.async: observe its barrier directly)
       if (!mbar_wait(&st_full[s], (i / kQStages) & 1, abort_flag, status, 990) ||
           !mbar_wait(&sd_full[b], (i >> 1) & 1, abort_flag, status, 991)) {
@@ -587,57 +608,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const float* lse = sL + s * 64;
-      const float* dl = sDl + s * 64;
-#pragma unroll 1
-      for (int c2 = 0; c2 < 2; ++c2) {
-        uint32_t sv[32], dv[32];
-        tmem_ld_32x32b_x32(tmem + lane_addr + b * 64 + c2 * 32, sv);
-        tmem_ld_32x32b_x32(tmem + lane_addr + kColDPT + b * 64 + c2 * 32, dv);
-        tmem_wait_ld();
-        uint32_t pp[16], dd[16];
+      const float* lse = sL + s * 64 + wh * 32;
+      const float* dl = sDl + s * 64 + wh * 32;
+      const uint32_t colS = b * 64 + wh * 32, colD = kColDPT + b * 64 + wh * 32;
+      uint32_t sv[32], dv[32];
+      tmem_ld_32x32b_x32(tmem + lane_addr + colS, sv);
+      tmem_ld_32x32b_x32(tmem + lane_addr + colD, dv);
+      tmem_wait_ld();
+      uint32_t pp[16], dd[16];
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const int c = c2 * 32 + 2 * t;
-          const int qi = i0 + c;
-          const bool ok0 = kvalid && qi >= qlo && qi < nq;
-          const bool ok1 = kvalid && qi + 1 >= qlo && qi + 1 < nq;
-          const float p0 = ok0 ? exp2f(fmaf(__uint_as_float(sv[2 * t]), sc, -lse[c] * kLog2e)) : 0.f;
-          const float p1 = ok1 ? exp2f(fmaf(__uint_as_float(sv[2 * t + 1]), sc, -lse[c + 1] * kLog2e)) : 0.f;
-          pp[t] = pack_bf16x2(p0, p1);
-          dd[t] = pack_bf16x2(ok0 ? p0 * (__uint_as_float(dv[2 * t]) - dl[c]) : 0.f,
-                              ok1 ? p1 * (__uint_as_float(dv[2 * t + 1]) - dl[c + 1]) : 0.f);
-        }
-        // P^T / dS^T chunk -> columns [16 c2, 16 c2 + 16) of their buffers (already read)
-        tmem_st_32x32b_x16(tmem + lane_addr + b * 64 + c2 * 16, pp);
-        tmem_st_32x32b_x16(tmem + lane_addr + kColDPT + b * 64 + c2 * 16, dd);
+      for (int t = 0; t < 16; ++t) {
+        const int c = 2 * t;
+        const int qi = i0 + c;
+        const bool ok0 = kvalid && qi >= qlo && qi < nq;
+        const bool ok1 = kvalid && qi + 1 >= qlo && qi + 1 < nq;
+        const float p0 = ok0 ? exp2f(fmaf(__uint_as_float(sv[c]), sc, -lse[c] * kLog2e)) : 0.f;
+        const float p1 = ok1 ? exp2f(fmaf(__uint_as_float(sv[c + 1]), sc, -lse[c + 1] * kLog2e)) : 0.f;
+        pp[t] = pack_bf16x2(p0, p1);
+        dd[t] = pack_bf16x2(ok0 ? p0 * (__uint_as_float(dv[c]) - dl[c]) : 0.f,
+                            ok1 ? p1 * (__uint_as_float(dv[c + 1]) - dl[c + 1]) : 0.f);
       }
+      // P^T / dS^T of this half -> the first 16 columns of its (already read) ranges
+      tmem_st_32x32b_x16(tmem + lane_addr + colS, pp);
+      tmem_st_32x32b_x16(tmem + lane_addr + colD, dd);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&pd_full[b]);
     }
+    // epilogue: half 0 adds dV, half 1 adds dK (x scale) into the gathered rows' accumulators
     if (ok && steps > 0 && mbar_wait(acc_done, 0, abort_flag, status, 995)) {
       tc_fence_after();
       const int64_t row = kvalid ? static_cast<int64_t>(kidx[r]) : 0;
-      float* dvr = p.dv_acc + row * p.ld_acc + static_cast<size_t>(kvh) * kD;
-      float* dkr = p.dk_acc + row * p.ld_acc + static_cast<size_t>(kvh) * kD;
+      float* dst = (wh == 0 ? p.dv_acc : p.dk_acc) + row * p.ld_acc + static_cast<size_t>(kvh) * kD;
+      const float mul = wh == 0 ? 1.f : p.scale;
+      const uint32_t col = wh == 0 ? kColDV : kColDK;
 #pragma unroll 1
       for (int c = 0; c < kD / 32; ++c) {
-        uint32_t v[32], k[32];
-        tmem_ld_32x32b_x32(tmem + lane_addr + kColDV + c * 32, v);
-        tmem_ld_32x32b_x32(tmem + lane_addr + kColDK + c * 32, k);
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lane_addr + col + c * 32, v);
         tmem_wait_ld();
         if (kvalid) {
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            atomicAdd(reinterpret_cast<float4*>(dvr + c * 32 + g * 4),
-                      make_float4(__uint_as_float(v[g * 4]), __uint_as_float(v[g * 4 + 1]),
-                                  __uint_as_float(v[g * 4 + 2]), __uint_as_float(v[g * 4 + 3])));
-            atomicAdd(reinterpret_cast<float4*>(dkr + c * 32 + g * 4),
-                      make_float4(__uint_as_float(k[g * 4]) * p.scale, __uint_as_float(k[g * 4 + 1]) * p.scale,
-                                  __uint_as_float(k[g * 4 + 2]) * p.scale, __uint_as_float(k[g * 4 + 3]) * p.scale));
-          }
+          for (int g = 0; g < 8; ++g)
+            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + g * 4),
+                      make_float4(__uint_as_float(v[g * 4]) * mul, __uint_as_float(v[g * 4 + 1]) * mul,
+                                  __uint_as_float(v[g * 4 + 2]) * mul, __uint_as_float(v[g * 4 + 3]) * mul));
         }
       }
     }

@@ -251,8 +251,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int x = 0; x < 2; ++x) {
           // P_x(j) V_j
           const int jp = np[x];
-          if (jp < T.nt[x] && jp < ns[x] && mbar_try_wait(&v_full[jp % kStages], (jp / kStages) & 1) &&
-              mbar_try_wait(&p_full[x], jp & 1)) {
+          if (jp < T.nt[x] && jp < ns[x] && mbar_test(&v_full[jp % kStages], (jp / kStages) & 1) &&
+              mbar_test(&p_full[x], jp & 1)) {
             tc_fence_after();
             fence_proxy_async_smem();  // cp.async-gathered rows -> tensor-core reads
             const uint32_t vaddr = smem_u32(sV + (jp % kStages) * kTile);
@@ -268,8 +268,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           // S_x(j) = Q_x K_j^T
           const int js = ns[x];
-          if (js < T.nt[x] && js == np[x] && mbar_try_wait(&k_full[js % kStages], (js / kStages) & 1) &&
-              (js == 0 || mbar_try_wait(&pv_done[x], (js - 1) & 1))) {
+          if (js < T.nt[x] && js == np[x] && mbar_test(&k_full[js % kStages], (js / kStages) & 1) &&
+              (js == 0 || mbar_test(&pv_done[x], (js - 1) & 1))) {
             tc_fence_after();
             fence_proxy_async_smem();
             const uint32_t qaddr = smem_u32(sQ + x * kTile);

@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_tc_kernel(AttnParams p, 
           const int st = js % kStages;
           const uint32_t ph = static_cast<uint32_t>((js / kStages) & 1);
           const int b = js & 1;
-          if (mbar_try_wait(&kv_full[st], ph) && mbar_try_wait(&s_empty[b], ((js >> 1) & 1) ^ 1u)) {
+          if (mbar_test(&kv_full[st], ph) && mbar_test(&s_empty[b], ((js >> 1) & 1) ^ 1u)) {
             tc_fence_after();
             fence_proxy_async_smem();
             trace_at(p, 2, js);
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_tc_kernel(AttnParams p, 
             progressed = true;
           }
         }
-        if (jp < js && mbar_try_wait(p_full, jp & 1)) {
+        if (jp < js && mbar_test(p_full, jp & 1)) {
           tc_fence_after();
           trace_at(p, 4, jp);
           const int st = jp % kStages;

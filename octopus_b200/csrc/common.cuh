@@ -79,6 +79,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of an mbarrier phase (try_wait may suspend the thread for a while
+// when the phase is incomplete, which would stall an event loop polling several barriers).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase.  `abort_flag` lives in shared memory and is
 // shared by all warps of the CTA: once any wait gives up, all later waits return
 // false immediately so the CTA drains quickly.
