@@ -325,8 +325,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int tile = blockIdx.x; tile < shape.num_tiles; tile += gridDim.x) {
       if (!mbar_wait(&accf_bar[acc], acc_phase, abort_flag, status, 400 + acc)) break;
       tc_fence_after();
-      int mb, nb, ks;
+      int mb, nb, ks, kb0, kb1;
       gemm_tile_coords(shape, tile, mb, nb, ks);
+      gemm_split_range(shape, ks, kb0, kb1);
+      const bool empty_k = kb1 <= kb0;  // no MMA wrote the accumulator: the tile's sum is 0
       const int n0 = nb * BN;
 #pragma unroll 1
       for (int mt = 0; mt < MT; ++mt) {
@@ -342,7 +344,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (row < shape.M && col0 < shape.N) {
             float v[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            for (int i = 0; i < 32; ++i) v[i] = empty_k ? 0.f : __uint_as_float(r[i]);
             const int nvalid = shape.N - col0 < 32 ? shape.N - col0 : 32;
             epi.apply(row, col0, nvalid, v, nb);
           }

@@ -184,7 +184,8 @@ static int decode_shape(GemmLaunch& g, int64_t bn_hint, int device, const torch:
   const int m_tiles = mt == 2 ? m2 : m1;
   const int tiles = m_tiles * n_tiles;
   int splits = 1;
-  if (allow_split && tiles * 4 < sms * 3) splits = std::max(1, std::min(sms / tiles, g.s.k_blocks / 4));
+  if (allow_split && tiles * 4 < sms * 3)
+    splits = nonempty_splits(g.s.k_blocks, std::max(1, std::min(sms / tiles, g.s.k_blocks / 4)));
   if (mt == 1 && splits < 2) return 1;  // the default launch
   g.mt = mt;
   g.bn = 256;

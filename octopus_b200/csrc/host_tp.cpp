@@ -71,7 +71,7 @@ static int tp_splits(GemmLaunch& g, const torch::Tensor& W) {
   const int n_tiles = (g.s.N + 255) / 256;
   const int tiles = g.s.m_tiles * n_tiles;
   if (tiles * 4 >= sms * 3) return 1;
-  const int splits = std::min(sms / tiles, g.s.k_blocks / 4);
+  const int splits = nonempty_splits(g.s.k_blocks, std::min(sms / tiles, g.s.k_blocks / 4));
   if (splits < 2) return 1;
   g.bn = 256;
   g.s.n_tiles = n_tiles;

@@ -52,7 +52,14 @@ inline int num_sms(int device) {
 
 // GEMM N-tile width for an M x N problem on `sms` SMs (hint 64/128/256 forces it).
 int pick_bn(int M, int N, int sms, int hint);
-int gemm_prefetch_depth(int M);  // L2 prefetch distance (K-blocks) of B for an M-row GEMM
+int gemm_prefetch_depth(int M);
+// Split count of `k_blocks` K blocks into about `want` splits with none empty (the kernel
+// gives split s the blocks [s * per, s * per + per) with per = ceil(k_blocks / splits)).
+inline int nonempty_splits(int k_blocks, int want) {
+  if (want <= 1 || k_blocks <= 1) return 1;
+  const int per = (k_blocks + want - 1) / want;
+  return (k_blocks + per - 1) / per;
+}  // L2 prefetch distance (K-blocks) of B for an M-row GEMM
 
 // Status word: int32[2] per device = {code, where}.  Zero means OK.
 int* status_ptr(int device);
