@@ -113,8 +113,8 @@ __device__ __forceinline__ void ds_chunk(const uint32_t (&sv)[32], const uint32_
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const int k = k0 + 2 * i;
-    const float p0 = k < lim ? exp2f(fmaf(__uint_as_float(sv[2 * i]), sc, -lse2)) : 0.f;
-    const float p1 = k + 1 < lim ? exp2f(fmaf(__uint_as_float(sv[2 * i + 1]), sc, -lse2)) : 0.f;
+    const float p0 = k < lim ? exp2_approx(fmaf(__uint_as_float(sv[2 * i]), sc, -lse2)) : 0.f;
+    const float p1 = k + 1 < lim ? exp2_approx(fmaf(__uint_as_float(sv[2 * i + 1]), sc, -lse2)) : 0.f;
     pk[i] = pack_bf16x2(p0 * (__uint_as_float(dv[2 * i]) - dlt), p1 * (__uint_as_float(dv[2 * i + 1]) - dlt));
   }
 }
@@ -622,8 +622,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int qi = i0 + c;
         const bool ok0 = kvalid && qi >= qlo && qi < nq;
         const bool ok1 = kvalid && qi + 1 >= qlo && qi + 1 < nq;
-        const float p0 = ok0 ? exp2f(fmaf(__uint_as_float(sv[c]), sc, -lse[c] * kLog2e)) : 0.f;
-        const float p1 = ok1 ? exp2f(fmaf(__uint_as_float(sv[c + 1]), sc, -lse[c + 1] * kLog2e)) : 0.f;
+        const float p0 = ok0 ? exp2_approx(fmaf(__uint_as_float(sv[c]), sc, -lse[c] * kLog2e)) : 0.f;
+        const float p1 = ok1 ? exp2_approx(fmaf(__uint_as_float(sv[c + 1]), sc, -lse[c + 1] * kLog2e)) : 0.f;
         pp[t] = pack_bf16x2(p0, p1);
         dd[t] = pack_bf16x2(ok0 ? p0 * (__uint_as_float(dv[c]) - dl[c]) : 0.f,
                             ok1 ? p1 * (__uint_as_float(dv[c + 1]) - dl[c + 1]) : 0.f);

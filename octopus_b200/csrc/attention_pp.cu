@@ -21,7 +21,7 @@
 // warps of one tile exponentiate, the MMAs of the other run.  Issue order per tile x:
 //   S_x(j) needs K_j landed and P_x(j-1) V_{j-1} complete
 //   P_x(j) V_j needs S_x(j) issued, V_j landed and the softmax's P_x(j) written
-// Softmax: online, exp2 domain, lazy rescale (O_x rescaled in TMEM only when the running
+// Softmax: online, exp2 domain on the SFU (ex2.approx), lazy rescale (O_x rescaled in TMEM only when the running
 // max grows by more than 2^8; the rescale runs before P_x(j) is published, when
 // P_x(j-1) V_{j-1} is known complete).  Epilogue O / l -> bf16 rows + natural-log lse.
 //
@@ -376,8 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float a = exp2f(fmaf(s[c * 32 + 2 * i], sc, -mref));
-          const float b = exp2f(fmaf(s[c * 32 + 2 * i + 1], sc, -mref));
+          const float a = exp2_approx(fmaf(s[c * 32 + 2 * i], sc, -mref));
+          const float b = exp2_approx(fmaf(s[c * 32 + 2 * i + 1], sc, -mref));
           rs += a + b;
           pk[i] = pack_bf16x2(a, b);
         }

@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_tc_kernel(AttnParams p, 
       uint32_t pk[kBN / 2];
 #pragma unroll
       for (int i = 0; i < kBN / 2; ++i) {
-        const float a = exp2f(s[2 * i] - mref), bb = exp2f(s[2 * i + 1] - mref);
+        const float a = exp2_approx(s[2 * i] - mref), bb = exp2_approx(s[2 * i + 1] - mref);
         rs += a + bb;
         pk[i] = pack_bf16x2(a, bb);
       }

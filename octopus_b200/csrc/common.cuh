@@ -308,6 +308,21 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, bool a_mn_ma
 }
 
 // ---------------------------------------------------------------- small math helpers
+// Rotary angle of dimension pair (i, i + D/2) at position pos: theta^(-2i/D) * pos.  One
+// definition for the rotary kernel and the fused decode finish, so both rotate identically.
+__device__ __forceinline__ void rope_sincos(int pos, int i, int D, float log2_theta, float& sn, float& cs) {
+  const float inv_freq = exp2f(-log2_theta * (2.f * i) / D);
+  sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
+}
+
+// 2^x with the SFU instruction (ex2.approx.ftz: results below 2^-126 flush to 0, which a
+// softmax weight can ignore)
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(64, 2) decode_persistent_kernel(DecodePersistP
           for (int j = 0; j < 8; ++j) {
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const float pv = exp2f(s[j][hr * 2 + e] - mref);
+              const float pv = exp2_approx(s[j][hr * 2 + e] - mref);
               s[j][hr * 2 + e] = pv;
               rs += pv;
             }

@@ -6,7 +6,8 @@
 // list into segments: a segment is a key range [start, start + len) of the index list
 // shared by up to kSegRows rows (the rows' contexts agree on it), or a row's own
 // remainder (dynamic length: grows by one key per decode step, read from kv_len).
-// A work item is (segment, key chunk, kv head).  Its K/V tiles are gathered once into
+// A work item is (segment, key chunk, kv head).  (decode_shared_tc.cu is the tcgen05
+// variant of this kernel with up to 128 / G rows per segment.)  Its K/V tiles are gathered once into
 // SMEM by the producer warp and used by every row of the segment: two consumer warps,
 // each holding the GQA query heads of 16 / G rows in the 16 rows of an mma.sync tile
 // (for G = 7, two rows per warp fill 14 of 16 tile rows instead of 7).  Each item
@@ -229,7 +230,7 @@ __global__ void __launch_bounds__(32 * (1 + kConsumers), 2) decode_shared_kernel
             for (int j = 0; j < 8; ++j) {
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
-                const float pv = exp2f(s[j][hr * 2 + e] - mref);
+                const float pv = exp2_approx(s[j][hr * 2 + e] - mref);
                 s[j][hr * 2 + e] = pv;
                 rs += pv;
               }
@@ -318,6 +319,10 @@ void decode_shared_launch(const DecodeSharedParams& p, int grid, int* status, cu
     configured = true;
   }
   decode_shared_kernel<<<grid, 32 * (1 + kConsumers), decode_shared_smem_bytes(), st>>>(p, status);
+  decode_shared_combine(p, st);
+}
+
+void decode_shared_combine(const DecodeSharedParams& p, cudaStream_t st) {
   decode_shared_combine_kernel<<<dim3(p.B, p.Hq), 128, 0, st>>>(p);
 }
 

@@ -1,12 +1,13 @@
 // Shared-prefix paged decode attention (decode_shared.cu): parameters and launcher.
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
 namespace octo {
 
-constexpr int kSegRows = 8;  // rows one segment may serve
+constexpr int kSegRows = 16;  // rows one segment may serve (table stride)
 
 struct DecodeSharedParams {
   const __nv_bfloat16* q;        // [B, Hq * 128], row stride ldq
@@ -30,9 +31,22 @@ struct DecodeSharedParams {
   int max_slots;
   int chunk;                     // keys per work item
   float scale;
+  unsigned long long* trace;     // optional event timestamps of CTA 0 (tcgen05 kernel; debugging)
 };
 
 int decode_shared_smem_bytes();
 void decode_shared_launch(const DecodeSharedParams& p, int grid, int* status, cudaStream_t st);
+// merges every row's partial slots into p.o
+void decode_shared_combine(const DecodeSharedParams& p, cudaStream_t st);
+
+// tcgen05 variant (decode_shared_tc.cu): TMA maps of the K / V caches [slots, Hkv * 128],
+// box 64 columns x 64 rows, 128-byte swizzle.  Segments may serve up to 128 / G rows.
+struct DecodeSharedMaps {
+  CUtensorMap k, v;
+};
+int decode_shared_tc_smem_bytes();
+// (persistent: the grid is derived from the SM count)
+void decode_shared_tc_launch(const DecodeSharedParams& p, const DecodeSharedMaps& maps, int sms, int* status,
+                             cudaStream_t st);
 
 }  // namespace octo

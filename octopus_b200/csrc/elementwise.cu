@@ -205,9 +205,8 @@ __global__ void rope_kernel(bf16* qkv, int ld, const int32_t* __restrict__ pos, 
     const long th = idx / half;
     const int h = th % heads;
     const int t = th / heads;
-    const float inv_freq = exp2f(-log2_theta * (2.f * i) / D);
     float sn, cs;
-    sincosf(static_cast<float>(pos[t]) * inv_freq, &sn, &cs);
+    rope_sincos(pos[t], i, D, log2_theta, sn, cs);
     sn *= sign;
     bf16* base = qkv + static_cast<size_t>(t) * ld + static_cast<size_t>(h) * D;
     const float a = __bfloat162float(base[i]);

@@ -48,7 +48,8 @@ void attn_decode_shared_t(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, t
                           torch::Tensor kv_len, torch::Tensor seg_rows, torch::Tensor seg_slot, torch::Tensor seg_start,
                           torch::Tensor seg_len, torch::Tensor seg_off, torch::Tensor items, torch::Tensor n_items,
                           torch::Tensor row_nslot, torch::Tensor o, torch::Tensor part_o, torch::Tensor part_lse,
-                          int64_t Hq, int64_t Hkv, int64_t max_slots, int64_t chunk, double scale) {
+                          int64_t Hq, int64_t Hkv, int64_t max_slots, int64_t chunk, double scale, bool use_tc,
+                          c10::optional<torch::Tensor> trace) {
   c10::cuda::CUDAGuard guard(q.get_device());
   for (auto* t : {&kv_indices, &kv_len, &seg_rows, &seg_slot, &seg_start, &seg_len, &seg_off, &items, &n_items,
                   &row_nslot}) {
@@ -92,8 +93,17 @@ void attn_decode_shared_t(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, t
               "decode_shared: scratch too small");
   p.part_o = part_o.data_ptr<float>();
   p.part_lse = part_lse.data_ptr<float>();
+  p.trace = (trace.has_value() && trace->defined()) ? reinterpret_cast<unsigned long long*>(trace->data_ptr())
+                                                      : nullptr;
   if (p.B == 0) return;
-  decode_shared_launch(p, 2 * num_sms(q.get_device()), status_ptr(q.get_device()), cur_stream(q));
+  if (use_tc) {
+    DecodeSharedMaps maps;
+    maps.k = make_tmap_bf16_2d(kc.data_ptr(), Hkv * 128, kc.size(0), Hkv * 128, 64, 64);
+    maps.v = make_tmap_bf16_2d(vc.data_ptr(), Hkv * 128, vc.size(0), Hkv * 128, 64, 64);
+    decode_shared_tc_launch(p, maps, num_sms(q.get_device()), status_ptr(q.get_device()), cur_stream(q));
+  } else {
+    decode_shared_launch(p, 2 * num_sms(q.get_device()), status_ptr(q.get_device()), cur_stream(q));
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -270,6 +280,100 @@ void gemm_out(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, torch::Ten
   }
   gemm_launch(g);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Decode projection fused with what follows it in the layer (engine decode graphs):
+//   (x, h) = (A W^T + bias + residual, RMSNorm(x) * norm_w)
+// Split-K launches (every decode-sized o / down projection) finish in one kernel that also
+// normalises; other shapes run the GEMM and the norm separately.
+std::vector<torch::Tensor> gemm_res_norm_t(torch::Tensor A, torch::Tensor W, torch::Tensor residual,
+                                           torch::Tensor norm_w, double eps, bool plus_one,
+                                           c10::optional<torch::Tensor> bias) {
+  c10::cuda::CUDAGuard guard(A.get_device());
+  GemmLaunch g = make_launch(A, false, W, false, 0);
+  const int M = g.s.M, N = g.s.N;
+  CHECK_BF16(residual);
+  CHECK_BF16(norm_w);
+  CHECK_CONTIG(norm_w);
+  TORCH_CHECK(residual.dim() == 2 && residual.size(0) == M && residual.size(1) == N && residual.stride(1) == 1 &&
+                  residual.stride(0) % 8 == 0,
+              "gemm_res_norm: bad residual");
+  TORCH_CHECK(norm_w.numel() == N && N % 8 == 0 && N / 8 <= 1024, "gemm_res_norm: norm width");
+  const void* bp = nullptr;
+  if (bias.has_value() && bias->defined()) {
+    CHECK_BF16(*bias);
+    TORCH_CHECK(bias->is_contiguous() && bias->numel() == N, "gemm_res_norm: bias must have N elements");
+    bp = bias->data_ptr();
+  }
+  auto x = torch::empty({M, N}, A.options());
+  auto h = torch::empty({M, N}, A.options());
+  if (M == 0) return {x, h};
+  const int splits = decode_shape(g, 0, A.get_device(), W);
+  if (splits > 1) {
+    auto ws = torch::empty({splits, M, N}, A.options().dtype(torch::kFloat32));
+    g.epi = kEpiSplitK;
+    g.C = ws.data_ptr();
+    gemm_launch(g);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    splitk_finish_norm(ws.data_ptr<float>(), splits, M, N, static_cast<const __nv_bfloat16*>(bp), CBF(residual),
+                       residual.stride(0), BF(x), N, CBF(norm_w), static_cast<float>(eps), plus_one, BF(h), N,
+                       g.stream);
+  } else {
+    gemm_out(A, false, W, false, x, 1.0, residual, bias, false, 0);
+    rmsnorm_fwd(CBF(x), N, CBF(norm_w), BF(h), N, nullptr, M, N, static_cast<float>(eps), plus_one ? 1 : 0,
+                g.stream);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {x, h};
+}
+
+// Decode qkv projection fused with the rotary embedding and the KV-cache write:
+//   qkv = A W^T + bias;  rotate the q and k heads at positions pos;  k, v rows -> kc / vc at
+//   slots (negative: not written);  returns the q rows [M, Hq * D].
+torch::Tensor gemm_qkv_rope_t(torch::Tensor A, torch::Tensor W, c10::optional<torch::Tensor> bias, torch::Tensor pos,
+                              double theta, int64_t Hq, int64_t Hkv, int64_t D, torch::Tensor slots, torch::Tensor kc,
+                              torch::Tensor vc) {
+  c10::cuda::CUDAGuard guard(A.get_device());
+  GemmLaunch g = make_launch(A, false, W, false, 0);
+  const int M = g.s.M, N = g.s.N;
+  TORCH_CHECK(N == (Hq + 2 * Hkv) * D && D % 16 == 0, "gemm_qkv_rope: W rows must be (Hq + 2 Hkv) * D");
+  CHECK_I32(pos);
+  CHECK_CONTIG(pos);
+  CHECK_I64(slots);
+  CHECK_CONTIG(slots);
+  CHECK_CONTIG(kc);
+  CHECK_CONTIG(vc);
+  CHECK_BF16(kc);
+  CHECK_BF16(vc);
+  TORCH_CHECK(pos.numel() >= M && slots.numel() >= M, "gemm_qkv_rope: one position and slot per row");
+  TORCH_CHECK(kc.size(-1) == Hkv * D && vc.size(-1) == Hkv * D, "gemm_qkv_rope: cache width");
+  const void* bp = nullptr;
+  if (bias.has_value() && bias->defined()) {
+    CHECK_BF16(*bias);
+    TORCH_CHECK(bias->is_contiguous() && bias->numel() == N, "gemm_qkv_rope: bias must have N elements");
+    bp = bias->data_ptr();
+  }
+  if (M == 0) return torch::empty({0, Hq * D}, A.options());
+  const int splits = decode_shape(g, 0, A.get_device(), W);
+  if (splits > 1) {
+    auto ws = torch::empty({splits, M, N}, A.options().dtype(torch::kFloat32));
+    g.epi = kEpiSplitK;
+    g.C = ws.data_ptr();
+    gemm_launch(g);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    auto q = torch::empty({M, Hq * D}, A.options());
+    splitk_finish_qkv(ws.data_ptr<float>(), splits, M, Hq, Hkv, D, static_cast<const __nv_bfloat16*>(bp),
+                      pos.data_ptr<int32_t>(), static_cast<float>(theta), BF(q), Hq * D, slots.data_ptr<int64_t>(),
+                      BF(kc), BF(vc), g.stream);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return q;
+  }
+  auto qkv = torch::empty({M, N}, A.options());
+  gemm_out(A, false, W, false, qkv, 1.0, c10::nullopt, bias, false, 0);
+  rope_apply(BF(qkv), N, pos.data_ptr<int32_t>(), M, Hq, Hkv, D, static_cast<float>(theta), false, g.stream);
+  kv_write(CBF(qkv), N, Hq, Hkv, D, slots.data_ptr<int64_t>(), BF(kc), BF(vc), M, g.stream);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return qkv.narrow(1, 0, Hq * D);
 }
 
 // Chunked logprob head forward: per row (log p(label), entropy, lse) of softmax(alpha * h W^T)
@@ -714,6 +818,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_fwd", &embed_fwd_t);
   m.def("embed_bwd", &embed_bwd_t);
   m.def("kv_write", &kv_write_t);
+  m.def("gemm_res_norm", &gemm_res_norm_t, py::arg("A"), py::arg("W"), py::arg("residual"), py::arg("norm_w"),
+        py::arg("eps"), py::arg("plus_one"), py::arg("bias") = py::none());
+  m.def("gemm_qkv_rope", &gemm_qkv_rope_t, py::arg("A"), py::arg("W"), py::arg("bias"), py::arg("pos"),
+        py::arg("theta"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("slots"), py::arg("kc"),
+        py::arg("vc"));
   m.def("sqnorm_accum", &sqnorm_accum_t);
   m.def("adamw", &adamw_t);
   m.def("attn_fwd", &attn_fwd_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu_q"), py::arg("cu_k"),
@@ -725,6 +834,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("causal"), py::arg("use_tc") = 0);
   m.def("attn_decode", &attn_decode_t);
   m.def("attn_decode_persistent", &attn_decode_persistent_t);
-  m.def("attn_decode_shared", &attn_decode_shared_t);
+  m.def("attn_decode_shared", &attn_decode_shared_t, py::arg("q"), py::arg("kc"), py::arg("vc"),
+        py::arg("kv_indices"), py::arg("kv_len"), py::arg("seg_rows"), py::arg("seg_slot"), py::arg("seg_start"),
+        py::arg("seg_len"), py::arg("seg_off"), py::arg("items"), py::arg("n_items"), py::arg("row_nslot"),
+        py::arg("o"), py::arg("part_o"), py::arg("part_lse"), py::arg("Hq"), py::arg("Hkv"), py::arg("max_slots"),
+        py::arg("chunk"), py::arg("scale"), py::arg("use_tc") = false, py::arg("trace") = py::none());
   m.def("set_pdl", &set_pdl);
 }

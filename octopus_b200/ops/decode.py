@@ -99,20 +99,30 @@ class SharedDecode:
     in place, so a CUDA graph captured once per batch bucket stays valid across plans.
     """
 
+    SEG_STRIDE = 16  # rows per segment in the device tables (kSegRows)
+
     def __init__(self, Hq: int, Hkv: int, D: int, max_batch: int, device="cuda", max_slots: int = 32,
-                 chunk: int = 256, min_shared: int = 64, max_segs: int | None = None):
+                 chunk: int | None = None, min_shared: int = 64, max_segs: int | None = None,
+                 use_tc: bool | None = None):
+        import os
+
         if D != 128:
             raise ValueError("shared-prefix decode covers head_dim 128")
         self.Hq, self.Hkv, self.D = Hq, Hkv, D
         G = Hq // Hkv
-        self.seg_rows = min(8, 2 * (16 // G))
+        # tcgen05 kernel: one MMA tile holds 128 / G rows' heads; mma.sync kernel: two warps of 16 / G
+        self.use_tc = (os.environ.get("OCTO_DECODE_TC", "1") != "0") if use_tc is None else bool(use_tc)
+        self.seg_rows = min(self.SEG_STRIDE, 128 // G) if self.use_tc else min(8, 2 * (16 // G))
+        # keys per work item: each item pays a descriptor / Q / partial-write overhead, which the
+        # tcgen05 kernel amortises best over 1024 keys (7B DAG solver stage: 121 vs 145 us at 256)
+        chunk = chunk or (1024 if self.use_tc else 256)
         self.max_batch, self.max_slots, self.chunk, self.min_shared = max_batch, max_slots, chunk, min_shared
         self.max_segs = max_segs or 6 * max_batch
         dev = torch.device(device)
         i32 = dict(dtype=torch.int32, device=dev)
         S = self.max_segs
-        self.t_rows = torch.full((S * 8,), -1, **i32)
-        self.t_slot = torch.zeros(S * 8, **i32)
+        self.t_rows = torch.full((S * self.SEG_STRIDE,), -1, **i32)
+        self.t_slot = torch.zeros(S * self.SEG_STRIDE, **i32)
         self.t_start = torch.zeros(S, **i32)
         self.t_len = torch.zeros(S, **i32)
         self.t_off = torch.zeros(S, **i32)
@@ -163,8 +173,8 @@ class SharedDecode:
         rec(list(range(n)), 0)
         if len(segs) > self.max_segs:
             return False
-        rows = np.full((self.max_segs, 8), -1, np.int32)
-        slot = np.zeros((self.max_segs, 8), np.int32)
+        rows = np.full((self.max_segs, self.SEG_STRIDE), -1, np.int32)
+        slot = np.zeros((self.max_segs, self.SEG_STRIDE), np.int32)
         nslot = np.zeros(self.max_batch, np.int32)
         items = []
         for s, (rr, _, _, _, mx) in enumerate(segs):
@@ -175,7 +185,9 @@ class SharedDecode:
                 rows[s, j] = b
                 slot[s, j] = nslot[b]
                 nslot[b] += nch
-            items += [(s << 8) | c for c in range(nch)]
+            items += [((s << 8) | c, min(self.chunk, mx - c * self.chunk)) for c in range(nch)]
+        # longest items first: the persistent CTAs take items round-robin
+        items = [it for it, _ in sorted(items, key=lambda x: -x[1])]
         if nslot.max(initial=0) > self.max_slots or len(items) > self.t_items.numel():
             return False
         k = len(segs)
@@ -199,5 +211,6 @@ class SharedDecode:
         scale = scale if scale is not None else self.D ** -0.5
         ext().attn_decode_shared(q, k_cache, v_cache, kv_indices, kv_len.to(torch.int32), self.t_rows, self.t_slot,
                                  self.t_start, self.t_len, self.t_off, self.t_items, self.t_n, self.t_nslot, out,
-                                 self.part_o, self.part_lse, self.Hq, self.Hkv, self.max_slots, self.chunk, scale)
+                                 self.part_o, self.part_lse, self.Hq, self.Hkv, self.max_slots, self.chunk, scale,
+                                 self.use_tc)
         return out

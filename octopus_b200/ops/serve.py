@@ -47,6 +47,29 @@ def prefill_attn(q, kc, vc, plan, Hq, Hkv, D, scale):
     return o.reshape(T, Hq * D).to(q.dtype)
 
 
+def gemm_res_norm(a, w, residual, norm_w, eps, plus_one=False, bias=None):
+    """(x, h) = (a w^T + bias + residual, RMSNorm(x) * norm_w): on CUDA one split-K GEMM plus
+    one finish kernel for decode-sized rows."""
+    if a.is_cuda:
+        x, h = ext().gemm_res_norm(a, w, residual, norm_w, eps, plus_one, bias)
+        return x, h
+    from .core import gemm
+    x = gemm(a, w, bias=bias, residual=residual).to(residual.dtype)
+    return x, rms(x, norm_w, eps, plus_one)
+
+
+def qkv_rope_kv(h, w, bias, pos, theta, Hq, Hkv, D, slots, kc, vc):
+    """q rows of h w^T + bias after the rotary embedding; the k / v rows go to the cache at
+    `slots` (one GEMM + one finish kernel on CUDA for decode-sized rows)."""
+    if h.is_cuda:
+        return ext().gemm_qkv_rope(h, w, bias, pos, theta, Hq, Hkv, D, slots, kc, vc)
+    from .core import gemm
+    qkv = gemm(h, w, bias=bias).to(h.dtype)
+    rope_(qkv, pos, Hq, Hkv, D, theta)
+    kv_write(qkv, Hq, Hkv, D, slots, kc, vc)
+    return qkv[:, : Hq * D]
+
+
 def swiglu(gu):
     if gu.is_cuda:
         return ext().swiglu_fwd(gu)

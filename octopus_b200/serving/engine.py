@@ -280,6 +280,20 @@ class Engine:
         act = sv.swiglu(gu)
         return ops.gemm(act, down_w, residual=x).to(x.dtype)
 
+    def _layer_decode(self, x, h, i, pos, slots, attn):
+        """One decode layer on (x, h = RMSNorm_ln1(x)); returns (x, the next layer's normed
+        input) with the projections fused into their neighbours (rotary + KV write into the
+        qkv finish, residual + next norm into the o / down finishes)."""
+        cfg, w = self.cfg, self.w
+        _, qkv_w, qkv_b, o_w, ln2, gu_w, down_w = w.layer(i)
+        nxt = w.layer(i + 1)[0] if i + 1 < cfg.layers else w["norm"]
+        q = sv.qkv_rope_kv(h, qkv_w, qkv_b, pos, cfg.rope_theta, cfg.heads, cfg.kv_heads, cfg.head_dim, slots,
+                           self.kc[i], self.vc[i])
+        o = attn(q, i)
+        x, h2 = sv.gemm_res_norm(o, o_w, x, ln2, cfg.rms_eps, cfg.norm_plus_one)
+        act = sv.swiglu(ops.gemm(h2, gu_w).to(x.dtype))
+        return sv.gemm_res_norm(act, down_w, x, nxt, cfg.rms_eps, cfg.norm_plus_one)
+
     def _final(self, x):
         return sv.rms(x, self.w["norm"], self.cfg.rms_eps, self.cfg.norm_plus_one)
 
@@ -370,9 +384,10 @@ class Engine:
         """One decode forward of B rows; returns device (tokens, logprobs)."""
         cfg = self.cfg
         x = sv.embed(tok, self.w["embed"])
+        h = sv.rms(x, self.w.layer(0)[0], cfg.rms_eps, cfg.norm_plus_one)
         for i in range(cfg.layers):
-            x = self._layer(x, i, pos, slot, attn)
-        h = self._final(x)
+            x, h = self._layer_decode(x, h, i, pos, slot, attn)
+        # (h is the final norm's output)
         return ops.sample(h, self.w.head, temperature, self.seed, self.s_stream[:B], cfg.vocab_size)
 
     # ------------------------------------------------------------------ decode

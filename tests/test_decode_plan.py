@@ -2,6 +2,7 @@
 segments in order, shared segments serve rows whose contexts agree, and the slot
 bookkeeping fits the tables."""
 import numpy as np
+import pytest
 
 from octopus_b200.ops.decode import SharedDecode
 
@@ -25,14 +26,15 @@ def dag_rows(n_inst=3, per=8, pre=300, plan=100, own=40, rng=None):
     return rows, np.asarray(ctx)
 
 
-def test_plan_covers_every_row_once():
+@pytest.mark.parametrize("use_tc", [False, True])
+def test_plan_covers_every_row_once(use_tc):
     rows, ctx = dag_rows()
     starts = np.cumsum([0] + [len(r) for r in rows[:-1]])
     final = np.asarray([len(r) for r in rows])
-    sd = SharedDecode(28, 4, 128, 32, device="cpu", chunk=64, min_shared=32)
+    sd = SharedDecode(28, 4, 128, 32, device="cpu", chunk=64, min_shared=32, use_tc=use_tc)
     assert sd.plan(rows, starts, ctx, final, 32)
     S = sd.stats["segments"]
-    seg_rows = sd.t_rows.view(-1, 8)[:S].numpy()
+    seg_rows = sd.t_rows.view(-1, SharedDecode.SEG_STRIDE)[:S].numpy()
     st, ln, off = sd.t_start[:S].numpy(), sd.t_len[:S].numpy(), sd.t_off[:S].numpy()
     flat = np.concatenate(rows)
     for b in range(len(rows)):
@@ -44,9 +46,11 @@ def test_plan_covers_every_row_once():
         got.sort(key=lambda x: x[0])
         keys = np.concatenate([g[1] for g in got])
         assert np.array_equal(keys, rows[b]), b
-    # 3 instances: prefix segments of <= 4 rows (2 per instance), planner pairs, own remainders
-    assert sd.stats["shared_segments"] == 3 * 2 + 12
-    assert sd.stats["segments"] == 3 * 2 + 12 + 24
+    # 3 instances x 8 rows: the prefix is one segment per instance on the tcgen05 kernel (up to
+    # 128 / 7 rows per tile) and two of <= 4 rows on the mma.sync kernel; planner pairs; own remainders
+    per_prefix = 1 if use_tc else 2
+    assert sd.stats["shared_segments"] == 3 * per_prefix + 12
+    assert sd.stats["segments"] == 3 * per_prefix + 12 + 24
     assert int(sd.t_nslot[:24].max()) == sd.stats["max_slots"]
 
 

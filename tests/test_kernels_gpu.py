@@ -341,7 +341,8 @@ def test_persistent_decode_matches_splitk():
 
 
 @pytest.mark.gpu
-def test_shared_prefix_decode_matches_persistent():
+@pytest.mark.parametrize("use_tc", [False, True])
+def test_shared_prefix_decode_matches_persistent(use_tc):
     """Rows sharing a task prefix and a planner segment (DAG solver stage) plus unshared
     rows: the shared-prefix kernel equals the per-row kernel; dynamic lengths advance."""
     from test_decode_plan import dag_rows
@@ -360,7 +361,7 @@ def test_shared_prefix_decode_matches_persistent():
     idx = torch.from_numpy(np.concatenate(rows).astype(np.int32)).to(dev)
     final = np.asarray([len(r) for r in rows])
     q = torch.randn(B, Hq * D, device=dev).bfloat16()
-    sd = ops.SharedDecode(Hq, Hkv, D, B, dev)
+    sd = ops.SharedDecode(Hq, Hkv, D, B, dev, use_tc=use_tc)
     assert sd.plan(rows, starts, ctx, final, B)
     assert sd.stats["shared_segments"] > 0
     pd = ops.DecodeAttention(Hq, Hkv, D, B, 4, dev, persistent=True)
@@ -468,3 +469,37 @@ def test_tcgen05_attention_backward_long(shuffle):
     (a_, b_) = _bwd_both(q, kv[:, : Hkv * D], kv[:, Hkv * D:], plan, Hq, Hkv, D, 35)
     for x, y in zip(a_, b_):
         assert rel_err(x.float(), y.float()) < 2e-2
+
+
+@pytest.mark.parametrize("M", [16, 200, 256, 320])
+def test_fused_decode_finishes_match_unfused(M):
+    """gemm_res_norm / gemm_qkv_rope (split-K finish fused with residual + RMSNorm, and with
+    bias + rotary + KV write) against the separate ops; M = 320 takes the unfused fallback."""
+    from octopus_b200.ops import serve as sv
+
+    torch.manual_seed(40 + M)
+    H, Hq, Hkv, D = 3584, 28, 4, 128
+    a = (torch.randn(M, H, device=dev) * 0.5).bfloat16()
+    w = (torch.randn(H, H, device=dev) * 0.02).bfloat16()
+    res = torch.randn(M, H, device=dev).bfloat16()
+    nw = (torch.rand(H, device=dev) + 0.5).bfloat16()
+    x, h = ops.ext().gemm_res_norm(a, w, res, nw, 1e-6, False, None)
+    x_ref = ops.gemm(a, w, residual=res)
+    h_ref = sv.rms(x_ref, nw, 1e-6, False)
+    assert rel_err(x.float(), x_ref.float()) < 1e-2
+    assert rel_err(h.float(), h_ref.float()) < 1e-2
+    wq = (torch.randn((Hq + 2 * Hkv) * D, H, device=dev) * 0.02).bfloat16()
+    bq = (torch.randn((Hq + 2 * Hkv) * D, device=dev) * 0.1).bfloat16()
+    pos = torch.randint(0, 30000, (M,), device=dev, dtype=torch.int32)
+    slots = torch.randperm(4 * M, device=dev)[:M].long()
+    slots[::7] = -1  # unwritten rows
+    kc, vc = (torch.zeros(4 * M, Hkv * D, device=dev).bfloat16() for _ in range(2))
+    kc2, vc2 = kc.clone(), vc.clone()
+    q = ops.ext().gemm_qkv_rope(a, wq, bq, pos, 1e6, Hq, Hkv, D, slots, kc, vc)
+    qkv = ops.gemm(a, wq, bias=bq)
+    sv.rope_(qkv, pos, Hq, Hkv, D, 1e6)
+    sv.kv_write(qkv, Hq, Hkv, D, slots, kc2, vc2)
+    torch.cuda.synchronize()
+    ops.check_status(0)
+    assert rel_err(q.float(), qkv[:, : Hq * D].float()) < 1e-2
+    assert rel_err(kc.float(), kc2.float()) < 1e-2 and rel_err(vc.float(), vc2.float()) < 1e-2
