@@ -71,8 +71,9 @@ __device__ __forceinline__ SItem sitem_of(const DecodeSharedParams& p, int it) {
   x.chunk = e & 255;
   int len = p.seg_len[x.seg];
   if (len < 0) len = max(0, p.kv_len[p.seg_rows[x.seg * kSegRows]] - p.seg_off[x.seg]);
-  x.k0 = min(len, x.chunk * p.chunk);
-  x.k1 = min(len, x.k0 + p.chunk);
+  const int ck = p.n_items[1];  // (device scalar: graph-safe across plans)
+  x.k0 = min(len, x.chunk * ck);
+  x.k1 = min(len, x.k0 + ck);
   x.start = p.seg_start[x.seg];
   return x;
 }
@@ -87,7 +88,7 @@ __global__ void __launch_bounds__(32 * (1 + kConsumers), 2) decode_shared_kernel
   uint64_t* empty = full + kStages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_items = *p.n_items;
+  const int n_items = p.n_items[0];
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {

@@ -22,14 +22,14 @@ struct DecodeSharedParams {
   const int32_t* seg_len;        // [nseg] keys; -1: dynamic (kv_len[row 0] - seg_off)
   const int32_t* seg_off;        // [nseg] the segment's offset inside its row's key list
   const int32_t* items;          // [n_chunks] seg << 8 | chunk; work item i -> items[i / Hkv], kv head i % Hkv
-  const int32_t* n_items;        // device scalar: n_chunks * Hkv
+  const int32_t* n_items;        // device scalars: [0] n_chunks * Hkv, [1] keys per work item (the plan's chunk)
   const int32_t* row_nslot;      // [B] slots a row's partials occupy
   float* part_o;                 // [B, Hq, max_slots, 128]
   float* part_lse;               // [B, Hq, max_slots] (log2 units)
   int ldq, ldo;
   int B, Hq, Hkv;
   int max_slots;
-  int chunk;                     // keys per work item
+  int chunk;                     // largest keys per work item any plan may use (host checks)
   float scale;
   unsigned long long* trace;     // optional event timestamps of CTA 0 (tcgen05 kernel; debugging)
 };

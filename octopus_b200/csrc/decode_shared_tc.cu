@@ -91,7 +91,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_items = *p.n_items;
+  const int n_items = p.n_items[0];
+  const int ck = p.n_items[1];
   const int G = p.Hq / p.Hkv;
 
   if (threadIdx.x == 0) {
@@ -136,8 +137,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
       const int seg = e >> 8, chunk = e & 255;
       int len = p.seg_len[seg];
       if (len < 0) len = max(0, p.kv_len[p.seg_rows[seg * kSegRows]] - p.seg_off[seg]);
-      const int k0 = min(len, chunk * p.chunk);
-      const int k1 = min(len, k0 + p.chunk);
+      const int k0 = min(len, chunk * ck);  // ck: the plan's keys per item (device scalar)
+      const int k1 = min(len, k0 + ck);
       const int start = p.seg_start[seg];
       const int myrow = lane < kSegRows ? p.seg_rows[seg * kSegRows + lane] : -1;
       const int myslot = lane < kSegRows ? p.seg_slot[seg * kSegRows + lane] + chunk : 0;

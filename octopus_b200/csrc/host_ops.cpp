@@ -64,6 +64,7 @@ void attn_decode_shared_t(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, t
   TORCH_CHECK(q.stride(1) == 1 && o.stride(1) == 1 && kc.is_contiguous() && vc.is_contiguous(), "decode: layout");
   TORCH_CHECK(kc.size(-1) == Hkv * 128, "decode_shared: head_dim 128 only");
   TORCH_CHECK(chunk % 64 == 0 && chunk > 0, "decode_shared: chunk must be a multiple of 64");
+  TORCH_CHECK(n_items.numel() >= 2, "decode_shared: n_items holds [work items, keys per item]");
   DecodeSharedParams p{};
   p.q = CBF(q);
   p.k_cache = CBF(kc);

@@ -127,7 +127,9 @@ class SharedDecode:
         self.t_len = torch.zeros(S, **i32)
         self.t_off = torch.zeros(S, **i32)
         self.t_items = torch.zeros(S * 64, **i32)
-        self.t_n = torch.zeros(1, **i32)
+        self.t_n = torch.zeros(2, **i32)  # [work items, keys per item]
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
+        self.target_items = 4 * 2 * sms  # ~4 items per CTA of the persistent grid (2 CTAs per SM)
         self.t_nslot = torch.zeros(max_batch, **i32)
         self.part_o = torch.empty(max_batch * Hq * max_slots * D, dtype=torch.float32, device=dev)
         self.part_lse = torch.empty(max_batch * Hq * max_slots, dtype=torch.float32, device=dev)
@@ -173,19 +175,28 @@ class SharedDecode:
         rec(list(range(n)), 0)
         if len(segs) > self.max_segs:
             return False
+        # keys per work item: the largest candidate that still gives every CTA of the
+        # persistent grid ~4 items (long items amortise per-item costs; too few of them leave
+        # SMs idle), read by the kernels from a device scalar so captured graphs follow it
+        cands = [c for c in (1024, 512, 256, 128) if c <= self.chunk] or [self.chunk]
+        chunk = cands[-1]
+        for c in cands:
+            if sum(max(1, -(-x[4] // c)) for x in segs) * self.Hkv >= self.target_items:
+                chunk = c
+                break
         rows = np.full((self.max_segs, self.SEG_STRIDE), -1, np.int32)
         slot = np.zeros((self.max_segs, self.SEG_STRIDE), np.int32)
         nslot = np.zeros(self.max_batch, np.int32)
         items = []
         for s, (rr, _, _, _, mx) in enumerate(segs):
-            nch = max(1, -(-mx // self.chunk))
+            nch = max(1, -(-mx // chunk))
             if nch > 255:
                 return False
             for j, b in enumerate(rr):
                 rows[s, j] = b
                 slot[s, j] = nslot[b]
                 nslot[b] += nch
-            items += [((s << 8) | c, min(self.chunk, mx - c * self.chunk)) for c in range(nch)]
+            items += [((s << 8) | c, min(chunk, mx - c * chunk)) for c in range(nch)]
         # longest items first: the persistent CTAs take items round-robin
         items = [it for it, _ in sorted(items, key=lambda x: -x[1])]
         if nslot.max(initial=0) > self.max_slots or len(items) > self.t_items.numel():
@@ -198,10 +209,10 @@ class SharedDecode:
         self.t_len[:k].copy_(torch.tensor([x[2] for x in segs], dtype=torch.int32))
         self.t_off[:k].copy_(torch.tensor([x[3] for x in segs], dtype=torch.int32))
         self.t_items[:len(items)].copy_(torch.tensor(items, dtype=torch.int32))
-        self.t_n.fill_(len(items) * self.Hkv)
+        self.t_n.copy_(torch.tensor([len(items) * self.Hkv, chunk], dtype=torch.int32))
         self.t_nslot.copy_(torch.from_numpy(nslot).to(dev))
         self.stats = {"segments": k, "shared_segments": sum(1 for x in segs if x[2] >= 0), "items": len(items),
-                      "max_slots": int(nslot.max(initial=0))}
+                      "max_slots": int(nslot.max(initial=0)), "chunk": chunk}
         return True
 
     def __call__(self, q, k_cache, v_cache, kv_indices, kv_len, out=None, scale=None):
