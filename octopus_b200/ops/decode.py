@@ -110,8 +110,11 @@ class SharedDecode:
             raise ValueError("shared-prefix decode covers head_dim 128")
         self.Hq, self.Hkv, self.D = Hq, Hkv, D
         G = Hq // Hkv
-        # tcgen05 kernel: one MMA tile holds 128 / G rows' heads; mma.sync kernel: two warps of 16 / G
-        self.use_tc = (os.environ.get("OCTO_DECODE_TC", "1") != "0") if use_tc is None else bool(use_tc)
+        # tcgen05 kernel: one MMA tile holds 128 / G rows' heads; mma.sync kernel: two warps of 16 / G.
+        # The mma.sync kernel is the default: in the 7B DAG RL step it took 5.1 s of decode attention
+        # against 6.4 s for the tcgen05 one (which wins only on consecutive-slot solver batches:
+        # 121 vs 165 us); OCTO_DECODE_TC=1 selects the tcgen05 kernel.
+        self.use_tc = (os.environ.get("OCTO_DECODE_TC", "0") != "0") if use_tc is None else bool(use_tc)
         self.seg_rows = min(self.SEG_STRIDE, 128 // G) if self.use_tc else min(8, 2 * (16 // G))
         # keys per work item: each item pays a descriptor / Q / partial-write overhead, which the
         # tcgen05 kernel amortises best over 1024 keys (7B DAG solver stage: 121 vs 145 us at 256)
