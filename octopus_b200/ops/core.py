@@ -436,6 +436,56 @@ class _Attention(torch.autograd.Function):
         return g.to(qkv.dtype), None, None, None, None, None
 
 
+class _AttentionKV(torch.autograd.Function):
+    """Gathered-key attention with separate q [Tq, Hq*D] and k, v [rows, Hkv*D]: the key
+    rows may extend past the query rows (chunk-major training appends the kept k / v of
+    earlier chunks after a chunk's own rows)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, plan, Hq, Hkv, D, scale):
+        ctx.meta = (plan, Hq, Hkv, D, scale)
+        if _is_cuda(q):
+            mode = use_tc_attention(D)
+            o, lse = ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.tiles_for(mode), Hq, Hkv, D,
+                                    scale, True, True, mode)
+            ctx.save_for_backward(q, k, v, o, lse)
+            return o
+        o3, _ = ref.gather_attention(q.reshape(q.shape[0], Hq, D), k.reshape(k.shape[0], Hkv, D),
+                                     v.reshape(v.shape[0], Hkv, D), plan.host_cu_q, plan.host_cu_k,
+                                     torch.from_numpy(plan.host_key_idx), scale)
+        ctx.save_for_backward(q, k, v)
+        return o3.reshape(q.shape[0], Hq * D).to(q.dtype)
+
+    @staticmethod
+    def backward(ctx, do):
+        plan, Hq, Hkv, D, scale = ctx.meta
+        do = do.contiguous()
+        if _is_cuda(do):
+            q, k, v, o, lse = ctx.saved_tensors
+            dk = torch.zeros(k.shape[0], Hkv * D, dtype=torch.float32, device=k.device)
+            dv = torch.zeros_like(dk)
+            tc = use_tc_bwd(D)
+            dq = ext().attn_bwd(q, k, v, o, do, lse, plan.cu_q, plan.cu_k, plan.key_idx,
+                                plan.dq_tiles_tc if tc else plan.dq_tiles, plan.kv_tiles_tc if tc else plan.kv_tiles,
+                                dk, dv, Hq, Hkv, D, scale, True, tc)
+            return dq, dk.to(k.dtype), dv.to(v.dtype), None, None, None, None, None
+        q, k, v = ctx.saved_tensors
+        with torch.enable_grad():
+            ins = [t.detach().requires_grad_(True) for t in (q, k, v)]
+            o3, _ = ref.gather_attention(ins[0].reshape(q.shape[0], Hq, D), ins[1].reshape(k.shape[0], Hkv, D),
+                                         ins[2].reshape(v.shape[0], Hkv, D), plan.host_cu_q, plan.host_cu_k,
+                                         torch.from_numpy(plan.host_key_idx), scale)
+            g = torch.autograd.grad(o3.reshape(q.shape[0], Hq * D), ins, ref._f(do).to(o3.dtype))
+        return g[0].to(q.dtype), g[1].to(k.dtype), g[2].to(v.dtype), None, None, None, None, None
+
+
+def attention_kv(q, k, v, plan: AttnPlan, Hq: int, Hkv: int, D: int, scale: float | None = None):
+    """Gathered-key causal attention of q rows against k / v rows (key_idx indexes k / v)."""
+    if scale is None:
+        scale = D ** -0.5
+    return _AttentionKV.apply(q, k, v, plan, Hq, Hkv, D, scale)
+
+
 def attention(qkv, plan: AttnPlan, Hq: int, Hkv: int, D: int, scale: float | None = None):
     """Gathered-key causal attention on a fused qkv [T, (Hq+2Hkv)*D] -> o [T, Hq*D]."""
     if scale is None:

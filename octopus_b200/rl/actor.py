@@ -26,6 +26,7 @@ import torch
 from .. import ops
 from ..models.config import ModelConfig
 from ..models.decoder import FlatLayout, TreeBatch, Weights, forward_tree, init_flat
+from .chunk_major import chunk_major_forward
 from ..utils.iostats import h2d
 from .loss import PPOConfig, ppo_loss
 from .prefix_tree import attention_plan, build_tree
@@ -138,13 +139,17 @@ class Actor:
         self.temperature = temperature
         self.version = 0
         self.ckpt_block = 1          # block checkpoint: keep every k-th layer input
+        self.chunk_tokens = 0        # chunk-major training of micro-batches larger than this (0: off)
         self.host_acts = None        # HostActivations: saved activations past a GPU budget in pinned host memory
 
-    def set_memory(self, ckpt_block: int = 1, act_gpu_bytes: int | None = None):
-        """Trainer memory knobs: block checkpointing and host-resident saved activations."""
+    def set_memory(self, ckpt_block: int = 1, act_gpu_bytes: int | None = None, chunk_tokens: int = 0):
+        """Trainer memory knobs: block checkpointing, host-resident saved activations and
+        chunk-major training (micro-batches of more than chunk_tokens tree rows run through
+        the model chunk by chunk: rl.chunk_major)."""
         from ..utils.pinned_slab import HostActivations, check_checkpointing
 
         self.ckpt_block = max(1, int(ckpt_block))
+        self.chunk_tokens = max(0, int(chunk_tokens))
         self.host_acts = HostActivations(act_gpu_bytes) if act_gpu_bytes is not None else None
         check_checkpointing(self.ckpt, self.host_acts)
 
@@ -165,8 +170,11 @@ class Actor:
             d = mb.to_device(self.device)
             host = getattr(self, "host_acts", None)
             with host if host is not None else contextlib.nullcontext():
-                logp, ent = forward_tree(self.weights, d.batch, self.temperature, ckpt=self.ckpt,
-                                         ckpt_block=getattr(self, "ckpt_block", 1))
+                if self._chunked(mb):
+                    logp, ent = chunk_major_forward(self.weights, mb, self.chunk_tokens, self.temperature)
+                else:
+                    logp, ent = forward_tree(self.weights, d.batch, self.temperature, ckpt=self.ckpt,
+                                             ckpt_block=getattr(self, "ckpt_block", 1))
                 loss, st = ppo_loss(logp, ent, d.adv, d.w, d.behav, None, denom, self.ppo)
             loss.backward()
             for k, v in st.items():
@@ -175,6 +183,10 @@ class Actor:
         stats.setdefault("loss", torch.zeros((), device=self.device))  # a rank with no micro-batch this step
         tok = float(sum(mb.pair_w.sum() for mb in mbs)) or 1.0
         return {k: (v if k in ("tokens", "loss") else v / tok) for k, v in stats.items()}
+
+    def _chunked(self, mb) -> bool:
+        ct = getattr(self, "chunk_tokens", 0)
+        return bool(ct) and self.ckpt and mb.n_tree > ct
 
     def optimizer_step(self) -> torch.Tensor:
         """Grad-norm clip + AdamW; returns the (device) squared grad norm."""
@@ -231,6 +243,7 @@ class LoRAActor(Actor):
         self.temperature = temperature
         self.version = 0
         self.ckpt_block = 1
+        self.chunk_tokens = 0
         self.host_acts = None
 
     def forward_backward(self, mbs: list[MicroBatch], denom: float | None = None) -> dict:
@@ -238,8 +251,11 @@ class LoRAActor(Actor):
         stats = {}
         for mb in mbs:
             d = mb.to_device(self.device)
-            logp, ent = forward_tree(self.base, d.batch, self.temperature, ckpt=self.ckpt,
-                                     ckpt_block=self.ckpt_block, lora=self.lora)
+            if self._chunked(mb):
+                logp, ent = chunk_major_forward(self.base, mb, self.chunk_tokens, self.temperature, lora=self.lora)
+            else:
+                logp, ent = forward_tree(self.base, d.batch, self.temperature, ckpt=self.ckpt,
+                                         ckpt_block=self.ckpt_block, lora=self.lora)
             loss, st = ppo_loss(logp, ent, d.adv, d.w, d.behav, None, denom, self.ppo)
             loss.backward()
             for k, v in st.items():

@@ -65,6 +65,7 @@ class ActorSection:
     lora_targets: str = "all-linear"
     ckpt_block: int = 1         # block checkpointing: keep every k-th layer input
     act_gpu_gb: float = -1.0    # >= 0: saved activations past this many GB live in pinned host memory
+    chunk_tokens: int = 0       # > 0: micro-batches with more tree rows train chunk-major in chunks of this size
 
 
 @dataclass

@@ -78,7 +78,11 @@ def build(cfg, device):
                              ckpt=a.gradient_checkpointing, fused=a.fused_collectives and device.type == "cuda")
     else:
         actor = Actor(mcfg, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype, ckpt=a.gradient_checkpointing)
-    actor.set_memory(a.ckpt_block, int(a.act_gpu_gb * (1 << 30)) if a.act_gpu_gb >= 0 else None)
+    chunk_tokens = a.chunk_tokens
+    if not chunk_tokens and os.environ.get("OCTOPUS_CHUNK_MAJOR", "0") == "1":  # the reference's host switch
+        chunk_tokens = int(os.environ.get("OCTOPUS_CHUNK_TOKENS", "32768"))
+    actor.set_memory(a.ckpt_block, int(a.act_gpu_gb * (1 << 30)) if a.act_gpu_gb >= 0 else None,
+                     chunk_tokens=chunk_tokens)
     if cfg.model.path:
         load_hf(getattr(actor, "base", actor.weights), cfg.model.path)
         actor.reload_master()
