@@ -169,6 +169,60 @@ def layer_forward(x, w, cfg: ModelConfig, pos, plan, lw=None):
     return ops.linear(act, down_w, None, residual=x, lora=la[3])
 
 
+def _mlp_part(x, a, w, cfg, lw):
+    """The row-wise rest of a layer after attention: o-projection + residual, RMSNorm,
+    SwiGLU MLP + residual."""
+    _, _, _, o_w, ln2, gu_w, down_w = w
+    la = lw if lw is not None else (None, None, None, None)
+    x = ops.linear(a, o_w, None, residual=x, lora=la[1])
+    h2 = ops.rmsnorm(x, ln2, cfg.rms_eps, cfg.norm_plus_one)
+    act = ops.swiglu(ops.linear(h2, gu_w, lora=la[2]))
+    return ops.linear(act, down_w, None, residual=x, lora=la[3])
+
+
+class _TileCkpt(torch.autograd.Function):
+    """Checkpoint of _mlp_part on one row tile (inputs x, a): backward recomputes the tile,
+    so only one tile's MLP activations exist at a time."""
+
+    @staticmethod
+    def forward(ctx, x, a, w, cfg, lw):
+        ctx.args = (w, cfg, lw)
+        ctx.save_for_backward(x, a)
+        with torch.no_grad():
+            return _mlp_part(x, a, w, cfg, lw)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, a = ctx.saved_tensors
+        xr, ar = x.detach().requires_grad_(True), a.detach().requires_grad_(True)
+        with torch.enable_grad():
+            y = _mlp_part(xr, ar, *ctx.args)
+        torch.autograd.backward(y, dy)
+        return xr.grad, ar.grad, None, None, None
+
+
+def layer_forward_tiled(x, w, cfg: ModelConfig, pos, plan, lw=None, tile: int = 16384):
+    """layer_forward with the row-wise part in tiles of `tile` rows, each checkpointed: the
+    q / k / v projection and attention see the whole tree (keys come from any row), the
+    o-projection and MLP run tile by tile, so their activations follow the tile, not the
+    tree."""
+    ln1, qkv_w, qkv_b = w[0], w[1], w[2]
+    la = lw if lw is not None else (None, None, None, None)
+    h = ops.rmsnorm(x, ln1, cfg.rms_eps, cfg.norm_plus_one)
+    qkv = ops.linear(h, qkv_w, qkv_b, lora=la[0])
+    qkv = ops.rope_(qkv, pos, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.rope_theta)
+    a = ops.attention(qkv, plan, cfg.heads, cfg.kv_heads, cfg.head_dim)
+    T = x.shape[0]
+    tile = max(8, tile // 8 * 8)
+    if T <= tile:
+        return _mlp_part(x, a, w, cfg, lw)
+    outs = []
+    for r0 in range(0, T, tile):
+        xt, at = x[r0:r0 + tile], a[r0:r0 + tile]
+        outs.append(_TileCkpt.apply(xt, at, w, cfg, lw) if torch.is_grad_enabled() else _mlp_part(xt, at, w, cfg, lw))
+    return torch.cat(outs)
+
+
 class _Ckpt(torch.autograd.Function):
     """Activation checkpoint of fn(x, *args): forward without a graph, the input saved
     through autograd's saved-tensor hooks (so host-resident activations apply to it),
@@ -192,22 +246,27 @@ class _Ckpt(torch.autograd.Function):
         return (xr.grad, None) + (None,) * len(ctx.args)
 
 
-def _layers_forward(x, ws, cfg, pos, plan, lws):
+def _layers_forward(x, ws, cfg, pos, plan, lws, lf=layer_forward):
     """Several layers (a checkpoint block); during the block's recompute each layer is
     checkpointed again, so backward holds one layer's working set at a time."""
     for w, lw in zip(ws, lws):
-        x = _Ckpt.apply(x, layer_forward, w, cfg, pos, plan, lw) if torch.is_grad_enabled() else \
-            layer_forward(x, w, cfg, pos, plan, lw)
+        x = _Ckpt.apply(x, lf, w, cfg, pos, plan, lw) if torch.is_grad_enabled() else lf(x, w, cfg, pos, plan, lw)
     return x
 
 
 def forward_tree(weights: Weights, batch: TreeBatch, temperature: float = 1.0, ckpt: bool = True,
-                 layer_hook=None, ckpt_block: int = 1, lora=None):
+                 layer_hook=None, ckpt_block: int = 1, lora=None, seq_tile: int = 0):
     """Returns (logp [M], entropy [M]) of the scored (row, label) pairs.
 
     ckpt: activation checkpointing; ckpt_block = k keeps only every k-th layer input
-    (block checkpoint: the inputs of the layers inside a block are recomputed)."""
+    (block checkpoint: the inputs of the layers inside a block are recomputed); seq_tile > 0:
+    each layer's o-projection and MLP run in checkpointed tiles of that many rows
+    (layer_forward_tiled)."""
     cfg = weights.cfg
+    if seq_tile and seq_tile < batch.ids.shape[0]:
+        lf = lambda *a: layer_forward_tiled(*a, tile=seq_tile)  # noqa: E731
+    else:
+        lf = layer_forward
     x = ops.embed(batch.ids, weights["embed"])
     if x.requires_grad is False and torch.is_grad_enabled():
         x.requires_grad_(True)
@@ -216,7 +275,7 @@ def forward_tree(weights: Weights, batch: TreeBatch, temperature: float = 1.0, c
             idx = range(i0, min(cfg.layers, i0 + ckpt_block))
             ws = [weights.layer(i) for i in idx]
             lws = [lora.layer(i) if lora is not None else None for i in idx]
-            x = _Ckpt.apply(x, _layers_forward, ws, cfg, batch.pos, batch.plan, lws)
+            x = _Ckpt.apply(x, _layers_forward, ws, cfg, batch.pos, batch.plan, lws, lf)
         h = ops.rmsnorm(x, weights["norm"], cfg.rms_eps, cfg.norm_plus_one)
         hp = h.index_select(0, batch.pair_rows)
         return ops.logprob_head(hp, weights.head, batch.pair_labels, 1.0 / temperature, cfg.vocab_size)
@@ -226,9 +285,9 @@ def forward_tree(weights: Weights, batch: TreeBatch, temperature: float = 1.0, c
         w = weights.layer(i)
         lw = lora.layer(i) if lora is not None else None
         if ckpt and torch.is_grad_enabled():
-            x = _Ckpt.apply(x, layer_forward, w, cfg, batch.pos, batch.plan, lw)
+            x = _Ckpt.apply(x, lf, w, cfg, batch.pos, batch.plan, lw)
         else:
-            x = layer_forward(x, w, cfg, batch.pos, batch.plan, lw)
+            x = lf(x, w, cfg, batch.pos, batch.plan, lw)
     if layer_hook is not None:
         layer_hook(cfg.layers)
     h = ops.rmsnorm(x, weights["norm"], cfg.rms_eps, cfg.norm_plus_one)

@@ -142,14 +142,17 @@ class Actor:
         self.chunk_tokens = 0        # chunk-major training of micro-batches larger than this (0: off)
         self.host_acts = None        # HostActivations: saved activations past a GPU budget in pinned host memory
 
-    def set_memory(self, ckpt_block: int = 1, act_gpu_bytes: int | None = None, chunk_tokens: int = 0):
+    def set_memory(self, ckpt_block: int = 1, act_gpu_bytes: int | None = None, chunk_tokens: int = 0,
+                   seq_tile: int = 0):
         """Trainer memory knobs: block checkpointing, host-resident saved activations and
         chunk-major training (micro-batches of more than chunk_tokens tree rows run through
-        the model chunk by chunk: rl.chunk_major)."""
+        the model chunk by chunk: rl.chunk_major) and sequence tiles (each layer's
+        o-projection and MLP in checkpointed tiles of seq_tile rows)."""
         from ..utils.pinned_slab import HostActivations, check_checkpointing
 
         self.ckpt_block = max(1, int(ckpt_block))
         self.chunk_tokens = max(0, int(chunk_tokens))
+        self.seq_tile = max(0, int(seq_tile))  # o-projection + MLP in checkpointed row tiles (0: off)
         self.host_acts = HostActivations(act_gpu_bytes) if act_gpu_bytes is not None else None
         check_checkpointing(self.ckpt, self.host_acts)
 
@@ -174,7 +177,8 @@ class Actor:
                     logp, ent = chunk_major_forward(self.weights, mb, self.chunk_tokens, self.temperature)
                 else:
                     logp, ent = forward_tree(self.weights, d.batch, self.temperature, ckpt=self.ckpt,
-                                             ckpt_block=getattr(self, "ckpt_block", 1))
+                                             ckpt_block=getattr(self, "ckpt_block", 1),
+                                             seq_tile=getattr(self, "seq_tile", 0))
                 loss, st = ppo_loss(logp, ent, d.adv, d.w, d.behav, None, denom, self.ppo)
             loss.backward()
             for k, v in st.items():
@@ -255,7 +259,8 @@ class LoRAActor(Actor):
                 logp, ent = chunk_major_forward(self.base, mb, self.chunk_tokens, self.temperature, lora=self.lora)
             else:
                 logp, ent = forward_tree(self.base, d.batch, self.temperature, ckpt=self.ckpt,
-                                         ckpt_block=self.ckpt_block, lora=self.lora)
+                                         ckpt_block=self.ckpt_block, lora=self.lora,
+                                         seq_tile=getattr(self, "seq_tile", 0))
             loss, st = ppo_loss(logp, ent, d.adv, d.w, d.behav, None, denom, self.ppo)
             loss.backward()
             for k, v in st.items():

@@ -66,6 +66,7 @@ class ActorSection:
     ckpt_block: int = 1         # block checkpointing: keep every k-th layer input
     act_gpu_gb: float = -1.0    # >= 0: saved activations past this many GB live in pinned host memory
     chunk_tokens: int = 0       # > 0: micro-batches with more tree rows train chunk-major in chunks of this size
+    seq_tile: int = 0           # > 0: each layer's o-projection + MLP run in checkpointed tiles of this many rows
 
 
 @dataclass

@@ -82,7 +82,7 @@ def build(cfg, device):
     if not chunk_tokens and os.environ.get("OCTOPUS_CHUNK_MAJOR", "0") == "1":  # the reference's host switch
         chunk_tokens = int(os.environ.get("OCTOPUS_CHUNK_TOKENS", "32768"))
     actor.set_memory(a.ckpt_block, int(a.act_gpu_gb * (1 << 30)) if a.act_gpu_gb >= 0 else None,
-                     chunk_tokens=chunk_tokens)
+                     chunk_tokens=chunk_tokens, seq_tile=a.seq_tile)
     if cfg.model.path:
         load_hf(getattr(actor, "base", actor.weights), cfg.model.path)
         actor.reload_master()

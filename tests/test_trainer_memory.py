@@ -56,3 +56,13 @@ def test_host_activations_context_and_slab():
     assert s.take(4000) is not None
     with pytest.raises(ValueError):
         check_checkpointing(False, HostActivations(0))
+
+
+def test_sequence_tiles_match_whole_layer():
+    """o-projection + MLP in checkpointed row tiles: same logprobs and gradients as the
+    untiled layer (tiles of 8 and 24 rows, with block checkpointing too)."""
+    w, grad, d = _setup()
+    lp1, g1 = _run(w, grad, d)
+    for kw in ({"seq_tile": 8}, {"seq_tile": 24}, {"seq_tile": 16, "ckpt_block": 2}):
+        lp2, g2 = _run(w, grad, d, **kw)
+        assert torch.allclose(lp1, lp2, rtol=1e-12, atol=1e-12) and torch.allclose(g1, g2, rtol=1e-9, atol=1e-12)
