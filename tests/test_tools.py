@@ -36,3 +36,16 @@ def test_embedding_gets_gradient():
     lp, _ = forward_tree(w, d.batch, ckpt=True)
     lp.sum().backward()
     assert float(w["embed"].main_grad[torch.as_tensor(toks[:-1])].norm()) > 0
+
+
+def test_act_gpu_bench_settings_agree():
+    """Every memory setting gives the first one's gradients (float64 on CPU), LoRA too."""
+    from octopus_b200.tools.act_gpu_bench import parse_setting, run
+
+    assert parse_setting("chunk:64+tile:16") == {"ckpt_block": 1, "act_gpu_bytes": None, "chunk_tokens": 64,
+                                                   "seq_tile": 16}
+    for lora in (0, 4):
+        rows = run(["layer", "block:2", "chunk:40", "tile:16", "chunk:40+tile:8"], 150, preset="tiny", layers=2,
+                   lora=lora, group=3, device="cpu")
+        assert len(rows) == 5 and rows[0]["tree_tokens"] > 0
+        assert all(r["grad_rel_l2"] < 1e-9 for r in rows), rows
