@@ -49,3 +49,34 @@ def test_act_gpu_bench_settings_agree():
                    lora=lora, group=3, device="cpu")
         assert len(rows) == 5 and rows[0]["tree_tokens"] > 0
         assert all(r["grad_rel_l2"] < 1e-9 for r in rows), rows
+
+
+def test_rollout_and_mount_load_run_on_the_engine():
+    """rollout_load runs DAG rollouts with weight-version switches; mount_load runs fork
+    pairs whose forced reads mount the sibling's own rows (tiny CPU engine)."""
+    import io
+    import json
+
+    import torch
+
+    from octopus_b200.envs.dag import DagConfig, MultiAgentDag
+    from octopus_b200.models.config import get_config
+    from octopus_b200.models.decoder import FlatLayout, Weights, init_flat
+    from octopus_b200.serving.engine import Engine
+    from octopus_b200.tools import mount_load, rollout_load
+
+    cfg = get_config("tiny", vocab_size=512, layers=2)
+    lay = FlatLayout(cfg)
+    w = Weights(cfg, init_flat(cfg, lay, "cpu", dtype=torch.float32, seed=3, std=0.05), lay)
+    eng = Engine(cfg, w, kv_slots=60000, max_batch=16, device="cpu")
+    env = MultiAgentDag(cfg.vocab_size, DagConfig(instances=1, samples=2, prefix_len=32, turn_len=4, role_len=4))
+    buf = io.StringIO()
+    s = rollout_load.run(eng, env, rollouts=2, duration=600, switch=1e-9, out=buf)
+    assert s["rollouts"] == 2 and s["generated_tokens"] > 0 and s["version_switches"] == 1
+    assert len(buf.getvalue().splitlines()) == 2
+    buf = io.StringIO()
+    st = mount_load.run(eng, cfg.vocab_size, pairs=2, duration=600, turns=(6, 8), root=40, tool=12, reply=(3, 6),
+                        mount=10, seed=1, out=buf)
+    rows = [json.loads(x) for x in buf.getvalue().splitlines()]
+    assert st["pairs"] == 2 and st["reads"] > 0 and st["mounted_tokens"] > 0 and st["not_found"] == 0
+    assert any(r["kind"] == "read" and r["mounted"] > 0 for r in rows)
