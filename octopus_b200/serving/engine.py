@@ -75,6 +75,11 @@ class GenInput:
     keep_cursor: bool = True
     cursor_id: str | None = None  # id to store the reply under (default: generated)
     prefill_only: bool = False
+    # positions of mounted keys: K2 (default) keeps their positions and continues at
+    # max(own next, last mounted + 1); K1 keeps their positions and continues at its own
+    # next; K3 relocates them to the request's next positions (copies whose keys are
+    # re-rotated by the offset) and continues after them
+    mount_rule: str = "K2"
 
 
 @dataclass
@@ -104,6 +109,7 @@ class _Req:
     out_tok: list = field(default_factory=list)
     out_lp: list = field(default_factory=list)
     mount_at: list = field(default_factory=list)
+    extra_slots: list = field(default_factory=list)  # K3 relocated copies this request allocated
 
 
 class Engine:
@@ -176,6 +182,53 @@ class Engine:
         self.records: dict[str, dict] = {}
 
     # ------------------------------------------------------------------ helpers
+    def _mount_rows(self, inp, ctx_t, ctx_s, ctx_p, ctx_m, mount_at, extra, next_pos: int) -> int:
+        """Append the rows of inp.mount to the context lists under inp.mount_rule; returns
+        the request's next position."""
+        for (src, a, b) in inp.mount:
+            mount_at.append(sum(len(x) for x in ctx_t))
+            sc = self.cursors.get(src)
+            if sc is None:
+                raise CursorNotFound(src)
+            a, b = int(a), int(b)
+            if not (0 <= a < b <= sc.length) or (sc.slots[a:b] < 0).any():
+                raise ValueError(f"mount range [{a}, {b}) invalid for cursor {src} of length {sc.length}")
+            rule = inp.mount_rule
+            if rule not in ("K1", "K2", "K3"):
+                raise ValueError(f"unknown mount rule {rule!r} (K1, K2, K3)")
+            ctx_t.append(np.full(b - a, PLACEHOLDER, np.int32))
+            ctx_m.append(np.ones(b - a, dtype=bool))
+            if rule == "K3":
+                pos = next_pos + np.arange(b - a, dtype=np.int64)
+                ctx_s.append(self._relocated(sc.slots[a:b], pos - sc.positions[a:b], extra))
+                ctx_p.append(pos)
+                next_pos += b - a
+                continue
+            ctx_s.append(sc.slots[a:b])
+            ctx_p.append(sc.positions[a:b])
+            if rule == "K2":
+                next_pos = max(next_pos, int(sc.positions[b - 1]) + 1)
+        return next_pos
+
+    def _relocated(self, src: np.ndarray, delta: np.ndarray, owned: list) -> np.ndarray:
+        """Copies of KV slots `src` in every layer with the keys re-rotated by `delta`
+        positions (rotary angles add: R(p + d) = R(d) R(p)); the new slots are appended to
+        `owned` (the request holds one reference until it ends)."""
+        new = self._alloc(len(src))
+        owned.append(new)
+        cfg = self.cfg
+        _, hkv = self._local_heads()
+        dev = self.kc.device
+        si = torch.as_tensor(np.asarray(src, np.int64), device=dev)
+        ni = torch.as_tensor(np.asarray(new, np.int64), device=dev)
+        d = torch.as_tensor(np.asarray(delta, np.int32), device=dev)
+        for layer in range(cfg.layers):
+            k = self.kc[layer].index_select(0, si)
+            sv.rope_(k, d, 0, hkv, cfg.head_dim, cfg.rope_theta)
+            self.kc[layer].index_copy_(0, ni, k)
+            self.vc[layer].index_copy_(0, ni, self.vc[layer].index_select(0, si))
+        return new
+
     def _local_heads(self) -> tuple[int, int]:
         """(query heads, KV heads) this process computes and caches."""
         return self.cfg.heads, self.cfg.kv_heads
@@ -243,24 +296,21 @@ class Engine:
                 self.radix.release_handle(handle)
                 handle = -1
         # mounts: splice rows of other cursors (K2: next = max(own next, last mounted + 1))
-        mount_at = []
-        for (src, a, b) in inp.mount:
-            mount_at.append(sum(len(x) for x in ctx_t))
-            sc = self.cursors.get(src)
-            if sc is None:
-                raise CursorNotFound(src)
-            a, b = int(a), int(b)
-            if not (0 <= a < b <= sc.length) or (sc.slots[a:b] < 0).any():
-                raise ValueError(f"mount range [{a}, {b}) invalid for cursor {src} of length {sc.length}")
-            ctx_t.append(np.full(b - a, PLACEHOLDER, np.int32))
-            ctx_s.append(sc.slots[a:b])
-            ctx_p.append(sc.positions[a:b])
-            ctx_m.append(np.ones(b - a, dtype=bool))
-            next_pos = max(next_pos, int(sc.positions[b - 1]) + 1)
+        mount_at, extra = [], []
+        try:
+            next_pos = self._mount_rows(inp, ctx_t, ctx_s, ctx_p, ctx_m, mount_at, extra, next_pos)
+        except Exception:
+            for ex in extra:  # K3 copies made before the failing mount
+                self.pool.decref(ex)
+            if handle >= 0:
+                self.radix.unlock(handle)
+                self.radix.release_handle(handle)
+            raise
         cat = (lambda xs, dt: np.concatenate(xs).astype(dt) if xs else np.empty(0, dt))
         r = _Req(inp, rid, cat(ctx_t, np.int32), cat(ctx_s, np.int64), cat(ctx_p, np.int64), cat(ctx_m, bool), new,
                  next_pos, cached=cached, radix_handle=handle)
         r.mount_at = mount_at
+        r.extra_slots = extra
         if len(new) == 0:
             raise ValueError("request has no new tokens to prefill")
         return r
@@ -611,6 +661,8 @@ class Engine:
                 self.pool.decref(r.own_slots)
             elif len(r.own_slots) > used:
                 self.pool.decref(r.own_slots[used:])
+            for ex in r.extra_slots:  # K3 copies: a kept cursor holds its own reference
+                self.pool.decref(ex)
             if r.radix_handle >= 0:
                 self.radix.unlock(r.radix_handle)
                 self.radix.release_handle(r.radix_handle)
