@@ -54,3 +54,25 @@ def test_probe_runs_every_condition_without_leaking_slots():
     eng.radix.evict(1 << 62)  # prompts the probe prefilled stay in the prefix cache until evicted
     assert eng.pool.free_count() == free0
     eng.pool.check_invariants()
+
+
+def test_route_a_conditions_and_report():
+    """Route A on the tiny engine: every condition runs; without a layer subset kvcomm_sel is
+    K3; on a subset engine whose subset is every layer, K2 / kvcomm_sel equal the full
+    engine's K2 / K3; the report pairs conditions with bootstrap intervals."""
+    from octopus_b200.baselines.route_a import CONDITIONS as RA, parse_layers, report as ra_report, run_one
+    from octopus_b200.serving.engine import Engine
+
+    cfg, w, eng = tiny_engine()
+    probes = synthetic_probes(3, 500, a_len=30, turn_len=20, b_len=30, cue_len=4, answer_len=3)
+    req = [7, 8, 9, 10]
+    rows = [{"probe": i, "conditions": run_one(eng, None, p, RA, f"r{i}", req, 5)} for i, p in enumerate(probes)]
+    c0 = rows[0]["conditions"]
+    assert set(c0) == set(RA) and c0["kvcomm_sel"]["same_as"] == "K3" and c0["summary"]["summary_tokens"] == 5
+    rep = ra_report(rows)
+    assert rep["pairs"]["K2 - K3"]["n"] == 3 and len(rep["pairs"]["K2 - K3"]["ci95"]) == 2
+    assert parse_layers("0-1", cfg.layers) == [0, 1] and parse_layers("all", cfg.layers) is None
+    sub = Engine(cfg, w, kv_slots=20000, max_batch=16, device="cpu", mount_layers=[0, 1])
+    r = run_one(eng, sub, probes[0], ("K2", "K3", "kvcomm_sel"), "s", req, 5)
+    assert r["K2"]["layers"] == "subset" and r["kvcomm_sel"]["output"] == c0["K3"]["output"]
+    assert r["K2"]["output"] == c0["K2"]["output"]
