@@ -1,6 +1,7 @@
 """SWE workspace: a git repository the agent edits and tests, with per-branch copies.
 
-Tools: view, edit (exact-match replace), write, shell, test, done (main), commit / abort
+Tools: view, edit (exact-match replace), write, shell, test, reproduce (a hypothesis and a
+Python reproducer, kept per thread) / rerun_reproduction, done (main), commit / abort
 (branches).  Every branch (fork) works in its own copy of its parent's tree; a branch
 that commits hands back its patch (git diff against the copy's base), which the parent
 applies with a 3-way merge when the fork joins.  snapshot / restore (rewinds) use
@@ -17,8 +18,10 @@ from __future__ import annotations
 
 import json
 import os
+import shlex
 import shutil
 import subprocess
+import sys
 import tempfile
 
 from ...runtime.core import DONE_TOOL, _tool
@@ -34,6 +37,9 @@ WRITE = _tool("write", "Write a whole file.", {"path": {"type": "string"}, "cont
               ["path", "content"])
 SHELL = _tool("shell", "Run a shell command in the repository.", {"cmd": {"type": "string"}}, ["cmd"])
 TEST = _tool("test", "Run the task's tests.", {}, [])
+REPRODUCE = _tool("reproduce", "State a hypothesis about the bug and run Python code that reproduces it.",
+                  {"hypothesis": {"type": "string"}, "code": {"type": "string"}}, ["hypothesis", "code"])
+RERUN = _tool("rerun_reproduction", "Run the last reproducer again (after a change).", {}, [])
 COMMIT = _tool("commit", "Finish this branch and hand its changes to the parent.",
                {"summary": {"type": "string"}}, ["summary"])
 ABORT = _tool("abort", "Finish this branch without changes.", {"reason": {"type": "string"}}, ["reason"])
@@ -50,10 +56,14 @@ def _git(args, cwd, check=True, inp: bytes | None = None) -> subprocess.Complete
 class GitWorkspace(WorkspaceProvider):
     report = "what you changed and whether the tests pass"
 
-    def __init__(self, repo: str, test_cmd: str, executor=None, timeout: float = 120.0, max_output: int = 8000):
+    def __init__(self, repo: str, test_cmd: str, executor=None, timeout: float = 120.0, max_output: int = 8000,
+                 python: str | None = None):
         self.root = repo
         self.test_cmd = test_cmd
         self.exec = executor or LocalExec()
+        # the interpreter reproducers run with (in a container: the image's python3)
+        self.python = python or (sys.executable if type(self.exec) is LocalExec else "python3")
+        self.repro: dict[str, dict] = {}  # thread -> {"hypothesis", "code"} (a fork inherits its parent's)
         self.timeout, self.max_output = timeout, max_output
         self.dirs = {"main": repo}
         self.base = {"main": _git(["rev-parse", "HEAD"], repo).stdout.decode().strip()}
@@ -65,7 +75,7 @@ class GitWorkspace(WorkspaceProvider):
         return SYSTEM
 
     def tools(self):
-        return [VIEW, EDIT, WRITE, SHELL, TEST, DONE_TOOL, COMMIT, ABORT]
+        return [VIEW, EDIT, WRITE, SHELL, TEST, REPRODUCE, RERUN, DONE_TOOL, COMMIT, ABORT]
 
     def _dir(self, thread: str) -> str:
         return self.dirs.get(thread, self.root)
@@ -110,6 +120,18 @@ class GitWorkspace(WorkspaceProvider):
             if name == "test":
                 r = self.exec.run(self.test_cmd, self._dir(thread), self.timeout)
                 return self._clip(f"tests {'passed' if r.code == 0 else 'failed'} (exit {r.code})\n{r.output}"), False
+            if name in ("reproduce", "rerun_reproduction"):
+                if name == "reproduce":
+                    code, hyp = args.get("code"), args.get("hypothesis")
+                    if not (isinstance(code, str) and code.strip() and isinstance(hyp, str) and hyp.strip()):
+                        return "reproduce needs hypothesis and code", False
+                    self.repro[thread] = {"hypothesis": hyp, "code": code}
+                rep = self.repro.get(thread)
+                if not rep:
+                    return "Define and execute a reproducer first.", False
+                r = self.exec.run(f"{self.python} -c {shlex.quote(rep['code'])}", self._dir(thread), self.timeout)
+                tag = " (timed out)" if r.timed_out else ""
+                return self._clip(f"exit {r.code}{tag}\n{r.output}"), False
             if name == "done":
                 return f"done: {args.get('answer', '')}", True
             if name == "commit":
@@ -130,6 +152,8 @@ class GitWorkspace(WorkspaceProvider):
               f"fork {child}"], dst)
         self.dirs[child] = dst
         self.base[child] = _git(["rev-parse", "HEAD"], dst).stdout.decode().strip()
+        if parent in self.repro:
+            self.repro[child] = dict(self.repro[parent])
 
     async def snapshot(self, thread: str):
         d = self._dir(thread)
@@ -159,16 +183,27 @@ class GitWorkspace(WorkspaceProvider):
         d = self._dir(thread)
         lines = []
         for res in results:
-            if res.get("ended_with") != "commit" or not res.get("patch"):
+            # a runtime branch record carries capture()'s output under "result"
+            patch = res.get("patch") or (res.get("result") or {}).get("patch")
+            if res.get("ended_with") != "commit" or not patch:
                 continue
-            r = _git(["apply", "--3way", "--whitespace=nowarn", "-"], d, check=False, inp=res["patch"].encode())
+            r = _git(["apply", "--3way", "--whitespace=nowarn", "-"], d, check=False, inp=patch.encode())
             status = "merged" if r.returncode == 0 else "conflict"
             res["merge"] = status
-            lines.append(f"{res.get('branch', '?')}: {status}")
+            lines.append(f"{res.get('branch') or res.get('thread', '?')}: {status}")
         return "\n".join(lines)
 
     async def close(self) -> None:
+        if getattr(self, "defer_close", False):  # kept for grading; discard() removes them
+            return
+        self.discard()
+
+    def discard(self) -> None:
+        """Remove the branch copies (and a prepared task's copy of the repository)."""
         shutil.rmtree(self.tmp, ignore_errors=True)
+        d = getattr(self, "task_dir", None)
+        if d:
+            shutil.rmtree(d, ignore_errors=True)
 
     def state(self) -> dict:
         return {"dirs": self.dirs, "results": {k: {kk: v for kk, v in r.items() if kk != "patch"}

@@ -38,9 +38,12 @@ class AgentRollout:
 class AgentEnv:
     def __init__(self, chat, tasks: list[dict], make_workspace, grade, *, n_samples: int = 4, batch_size: int = 8,
                  branch_credit: str = "outcome", gate=None, filter_zero_variance: bool = True,
-                 max_main_calls: int | None = None, branch_turns: int | None = None):
+                 max_main_calls: int | None = None, branch_turns: int | None = None, grade_workspace: bool = False):
         """chat: async completion function (serving.local.ChatService); tasks: dicts with at
-        least "question"; make_workspace(task) -> WorkspaceProvider; grade(task, answer) -> y."""
+        least "question"; make_workspace(task) -> WorkspaceProvider; grade(task, answer) -> y,
+        or with grade_workspace grade(task, answer, workspace, branch records) -> y (the
+        episode's final tree decides, e.g. SWE tests; the grader may add fields to the branch
+        records, which credit reads); a workspace with discard() is discarded after grading."""
         self.chat = chat
         self.tasks = tasks
         self._it = itertools.cycle(range(len(tasks)))
@@ -48,6 +51,7 @@ class AgentEnv:
         self.n, self.batch = n_samples, batch_size
         self.branch_credit, self.gate, self.filter = branch_credit, gate, filter_zero_variance
         self.max_main_calls, self.branch_turns = max_main_calls, branch_turns
+        self.grade_workspace = grade_workspace
         self.step = 0
 
     async def _episodes(self, picked):
@@ -57,6 +61,11 @@ class AgentEnv:
             rt = CursorRuntime(ws, self.chat, session_id=f"r{self.step}-t{ti}-s{s}",
                                max_main_calls=self.max_main_calls, branch_turns=self.branch_turns)
             res = await rt.run(task["question"])
+            if self.grade_workspace:
+                branches = [br for _, _, br in tree_branches(res["tree"].get("forks") or [])]
+                res["y"] = float(self.grade(task, res["tree"].get("answer"), ws, branches))
+            if hasattr(ws, "discard"):
+                ws.discard()
             return ti, res
 
         return await asyncio.gather(*[one(ti, s) for ti in picked for s in range(self.n)])
@@ -72,7 +81,8 @@ class AgentEnv:
         for ti, res in results:
             tree = res["tree"]
             branches = [{**br, "key": branch_key(name)} for name, _, br in tree_branches(tree.get("forks") or [])]
-            ep = {"y": float(self.grade(self.tasks[ti], tree.get("answer"))), "requests": res["requests"],
+            y = res["y"] if "y" in res else float(self.grade(self.tasks[ti], tree.get("answer")))
+            ep = {"y": y, "requests": res["requests"],
                   "branches": branches, "task": ti}
             groups.setdefault(ti, []).append(ep)
             out.episodes.append(ep)
