@@ -82,6 +82,31 @@ def evaluate(svc, retrieval, questions, samples: int = 1, judge=None, max_main_c
     return {"summary": summary, "rows": rows}
 
 
+def build_service(preset: str, model_path: str = "", kv_gb: float = 8.0, cpu: bool = False):
+    """(ChatService, Engine) on cuda:0 (CPU with `cpu` or without a GPU): Hugging Face
+    weights from `model_path`, else random-init weights of `preset` with the tiny tokenizer."""
+    import torch
+
+    from ..models.config import get_config
+    from ..models.decoder import FlatLayout, Weights, init_flat, load_hf
+    from ..serving.chat import ChatTokenizer
+    from ..serving.engine import Engine
+    from ..serving.local import ChatService
+
+    dev = torch.device("cpu") if cpu or not torch.cuda.is_available() else torch.device("cuda", 0)
+    tok = ChatTokenizer.from_dir(model_path) if model_path else ChatTokenizer.tiny()
+    cfg = get_config(preset)
+    if not model_path and cfg.vocab_size < tok.vocab_size:
+        cfg = cfg.with_(vocab_size=(tok.vocab_size + 127) // 128 * 128)
+    lay = FlatLayout(cfg)
+    w = Weights(cfg, init_flat(cfg, lay, dev, dtype=torch.bfloat16 if dev.type == "cuda" else torch.float32), lay)
+    if model_path:
+        load_hf(w, model_path)
+    kv_slots = int(kv_gb * (1 << 30) / (4 * cfg.layers * cfg.kv_width))
+    eng = Engine(cfg, w, kv_slots=kv_slots, max_batch=64, device=dev)
+    return ChatService(eng, tok), eng
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="python -m octopus_b200.eval.search_eval")
     ap.add_argument("--questions", required=True)
@@ -97,32 +122,14 @@ def main(argv=None) -> int:
     ap.add_argument("--out", default="")
     args = ap.parse_args(argv)
 
-    import torch
-
     from ..envs.search.agent import search_defaults
     from ..envs.search.service import Retrieval
-    from ..models.config import get_config
-    from ..models.decoder import FlatLayout, Weights, init_flat, load_hf
     from ..rl.config import run_episode_settings
-    from ..serving.chat import ChatTokenizer
-    from ..serving.engine import Engine
-    from ..serving.local import ChatService
 
     if args.settings:
         run_episode_settings(args.settings)
     search_defaults()
-    dev = torch.device("cpu") if args.cpu or not torch.cuda.is_available() else torch.device("cuda", 0)
-    tok = ChatTokenizer.from_dir(args.model_path) if args.model_path else ChatTokenizer.tiny()
-    cfg = get_config(args.preset)
-    if not args.model_path and cfg.vocab_size < tok.vocab_size:
-        cfg = cfg.with_(vocab_size=(tok.vocab_size + 127) // 128 * 128)
-    lay = FlatLayout(cfg)
-    w = Weights(cfg, init_flat(cfg, lay, dev, dtype=torch.bfloat16 if dev.type == "cuda" else torch.float32), lay)
-    if args.model_path:
-        load_hf(w, args.model_path)
-    kv_slots = int(args.kv_gb * (1 << 30) / (4 * cfg.layers * cfg.kv_width))
-    eng = Engine(cfg, w, kv_slots=kv_slots, max_batch=64, device=dev)
-    svc = ChatService(eng, tok)
+    svc, eng = build_service(args.preset, args.model_path, args.kv_gb, args.cpu)
     questions = [json.loads(x) for x in open(args.questions) if x.strip()]
     corpus = [json.loads(x) for x in open(args.corpus) if x.strip()]
     judge = judge_via_http(args.judge_url) if args.judge_url else None
