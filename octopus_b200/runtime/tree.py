@@ -39,6 +39,8 @@ FORK_BRANCHES_REFUSAL = "Forking is not available: this episode has made all the
 ONE_FORK = "fork refused: one fork per reply, this reply's first fork call; put every task in that one fork's tasks."
 MAIN_CLOSE = "{} has no effect in the main thread: a branch commits or aborts itself. End the main thread with done."
 FORK_FLOOR = 8192
+# a read that mounted: the source thread's full name, its steps (reply indices) and the rows mounted
+MOUNT_RESULT = "read_thread: mounted {src} steps {a}-{b} ({n} tokens) into your attention from your next reply on"
 
 
 class BranchCopyError(RuntimeError):
@@ -198,7 +200,9 @@ class CursorRuntime:
         target = args.get("thread")
         names = {t: t for t in self.threads} | {t.rsplit("/", 1)[-1]: t for t in self.threads if t != "main"}
         src = names.get(target)
-        if src is None or src == reader:
+        if src == reader:
+            return "read_thread: a thread reads other threads, never itself"
+        if src is None:
             return f"read_thread: no other thread named {target!r}"
         replies = self.threads[src]["replies"]
         if not replies or replies[-1][3] is None:
@@ -216,7 +220,7 @@ class CursorRuntime:
         if end_tok <= start_tok:
             return "read_thread: nothing readable in that range"
         self.pending_mounts.setdefault(reader, []).append((cursor, start_tok, end_tok))
-        return f"read {target} steps {a}-{b}: mounted into your attention from your next reply on"
+        return MOUNT_RESULT.format(src=src, a=a, b=b, n=end_tok - start_tok)
 
     async def _run_thread(self, thread: str, start: dict, depth: int) -> dict:
         port = RuntimePort(owner=None if thread == "main" else start["branch_id"])
@@ -252,9 +256,10 @@ class CursorRuntime:
                           "task": br["task"], "messages": hist + [{"role": "user", "content": msg}],
                           "step": start.get("step")}
                 self.running += 1
-                tasks.append((br, child, asyncio.ensure_future(self._run_thread(child, bstart, depth + 1))))
+                tasks.append((br, child, len(bstart["messages"]),
+                              asyncio.ensure_future(self._run_thread(child, bstart, depth + 1))))
             results = []
-            for br, child, t in tasks:
+            for br, child, prefix_len, t in tasks:
                 try:
                     res = await t
                 finally:
@@ -263,7 +268,10 @@ class CursorRuntime:
                 out = {"branch_id": br["branch_id"], "task": br["task"], "thread": child,
                        "ended_with": closing_name(res["steps"]) if cl else "stopped",
                        "summary": handed(cl), "end_time": time.time(), "forks": self.forks.get(child, []),
-                       "result": await self.ws.capture(child)}
+                       "result": await self.ws.capture(child),
+                       # the branch's history (inherited prefix + its own turns) for offline analysis
+                       "messages": without_cursors(res["messages"]), "prefix_len": prefix_len,
+                       "rewinds": len(res.get("rewinds") or []), "tools": self.tool_list(child)}
                 record["branches"].append(out)
                 results.append(out)
             record["join_response_id"] = record["response_id"]
@@ -292,7 +300,8 @@ class CursorRuntime:
                  "messages": [{"role": "system", "content": self.ws.system_prompt(task)},
                               {"role": "user", "content": task}]}
         res = await self._run_thread("main", start, 0)
-        tree = {"task": task, "forks": self.forks.get("main", []), "main_end": self._main_end(res["steps"]),
+        tree = {"task": task, "tools": self.tool_list("main"), "forks": self.forks.get("main", []),
+                "main_end": self._main_end(res["steps"]),
                 "answer": handed(closing_step(res["steps"])), "requests": len(self.requests),
                 "budget": self.ws.budget(), "used": self.used, "reminded": res["reminded"]}
         if self.log_dir:
@@ -315,7 +324,8 @@ class CursorRuntime:
     def _write(self, tree: dict, res: dict) -> None:
         d = self.log_dir
         d.mkdir(parents=True, exist_ok=True)
-        (d / "tree.json").write_text(json.dumps(without_cursors(tree), indent=1, default=str))
+        (d / "tree.json").write_text(json.dumps(without_cursors({**tree, "main": res["messages"]}), indent=1,
+                                                default=str))
         (d / "trajectory.json").write_text(json.dumps(without_cursors(res["messages"]), indent=1, default=str))
         with open(d / "requests.jsonl", "w") as f:
             for r in self.requests:
