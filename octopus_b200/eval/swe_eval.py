@@ -20,16 +20,23 @@ from __future__ import annotations
 import argparse
 import asyncio
 import json
+import os
 import statistics
 
 
-async def run_episodes(svc, specs, samples: int, executor=None, timeout: float = 120.0, max_main_calls=None):
+def _episode_dir(log_dir, spec, s):
+    return os.path.join(log_dir, spec.instance_id, str(s)) if log_dir else None
+
+
+async def run_episodes(svc, specs, samples: int, executor=None, timeout: float = 120.0, max_main_calls=None,
+                       log_dir=None):
     from ..envs.swe.taskset import prepare_workspace
     from ..runtime.tree import CursorRuntime
 
     async def one(spec, s):
         ws = prepare_workspace(spec, executor, timeout)
-        rt = CursorRuntime(ws, svc.chat, session_id=f"swe-{spec.instance_id}-{s}", max_main_calls=max_main_calls)
+        rt = CursorRuntime(ws, svc.chat, session_id=f"swe-{spec.instance_id}-{s}", max_main_calls=max_main_calls,
+                           log_dir=_episode_dir(log_dir, spec, s))
         res = await rt.run(spec.statement)
         return spec, s, res, ws
 
@@ -37,12 +44,14 @@ async def run_episodes(svc, specs, samples: int, executor=None, timeout: float =
 
 
 def evaluate(svc, specs, samples: int = 1, executor=None, timeout: float = 120.0, max_main_calls=None,
-             engine=None) -> dict:
+             engine=None, log_dir=None) -> dict:
+    """Per-episode rows and a summary; with log_dir each episode's logs (tree.json, ...) go to
+    log_dir/<instance_id>/<sample>/ with its grade in result.json."""
     from ..envs.swe.rl import grade_episode
     from ..rl.group import critical_path
     from ..runtime.core import tree_branches
 
-    results = asyncio.run(run_episodes(svc, specs, samples, executor, timeout, max_main_calls))
+    results = asyncio.run(run_episodes(svc, specs, samples, executor, timeout, max_main_calls, log_dir))
     rows, by_t = [], {}
     for spec, s, res, ws in results:
         try:
@@ -57,6 +66,11 @@ def evaluate(svc, specs, samples: int = 1, executor=None, timeout: float = 120.0
                "requests": len(res["requests"]), "critical_path": critical_path(res["requests"])}
         rows.append(row)
         by_t.setdefault(spec.instance_id, []).append(row["resolved"])
+        d = _episode_dir(log_dir, spec, s)
+        if d:
+            os.makedirs(d, exist_ok=True)
+            with open(os.path.join(d, "result.json"), "w") as f:
+                json.dump({**row, "reward": y, "task": spec.instance_id}, f)
         if engine is not None:
             for r in res["requests"]:
                 if engine.cursors.get(r["id"]) is not None:
@@ -84,6 +98,7 @@ def main(argv=None) -> int:
     ap.add_argument("--max-main-calls", type=int, default=None)
     ap.add_argument("--kv-gb", type=float, default=8.0)
     ap.add_argument("--cpu", action="store_true")
+    ap.add_argument("--log-dir", default="", help="per-episode logs (tree.json, result.json) for tree SFT")
     ap.add_argument("--out", default="")
     args = ap.parse_args(argv)
 
@@ -97,7 +112,8 @@ def main(argv=None) -> int:
     if args.bundle > 1:
         specs = build_bundles(specs, args.bundle)
     svc, eng = build_service(args.preset, args.model_path, args.kv_gb, args.cpu)
-    out = evaluate(svc, specs, args.samples, timeout=args.timeout, max_main_calls=args.max_main_calls, engine=eng)
+    out = evaluate(svc, specs, args.samples, timeout=args.timeout, max_main_calls=args.max_main_calls, engine=eng,
+                   log_dir=args.log_dir or None)
     if args.out:
         with open(args.out, "w") as f:
             for r in out["rows"]:

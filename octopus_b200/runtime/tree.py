@@ -238,7 +238,8 @@ class CursorRuntime:
             if not forks_this_turn:
                 return None
             fork = forks_this_turn[0]
-            record = {"response_id": self.threads[thread]["replies"][-1][0], "branches": []}
+            record = {"response_id": self.threads[thread]["replies"][-1][0], "branches": [],
+                      "prefix_len": len(messages)}  # the parent's history at the fork (its join note follows)
             my_forks.append(record)
             k = len(my_forks) - 1
             tasks = []
