@@ -136,9 +136,11 @@ def linear_layer_forward(x, hw: HybridWeights, i: int, tree):
     rows = torch.as_tensor(tails[:, 8 - (W - 1):], device=x.device)
     ok = (rows >= 0).unsqueeze(-1)
     ctx = qkv.index_select(0, rows.clamp_min(0).reshape(-1)).view(len(nodes), W - 1, -1)
-    ctx = torch.where(ok, ctx.float(), torch.zeros((), device=x.device))
+    cdt = torch.float64 if x.dtype == torch.float64 else torch.float32  # conv context: fp32 (exact for bf16)
+    ctx = torch.where(ok, ctx.to(cdt), torch.zeros((), device=x.device, dtype=cdt))
     segs = [(int(s), int(e) - int(s)) for s, e, _, _ in nodes]
-    qkv = causal_conv(qkv, hw.fp32[f"layers.{i}.conv_w"].float(), None, segs, ctx=ctx, ctx_idx=list(range(len(nodes))))
+    qkv = causal_conv(qkv, hw.fp32[f"layers.{i}.conv_w"].to(cdt), None, segs, ctx=ctx,
+                      ctx_idx=list(range(len(nodes))))
     C, Hh, d = hc.lin_width, hc.lin_heads, hc.lin_dim
     T = x.shape[0]
     q = torch.nn.functional.normalize(qkv[:, :C].float().view(T, Hh, d), dim=-1).to(x.dtype).reshape(T, C)

@@ -104,3 +104,86 @@ def test_chunk_major_gpu_matches_whole_tree():
     rel = lambda a, b: float((a.float() - b.float()).norm() / (b.float().norm() + 1e-12))  # noqa: E731
     assert rel(lp2, lp.detach()) < 1e-2 and rel(ent2, ent.detach()) < 1e-2
     assert rel(grad, g_ref) < 3e-2
+
+
+def _hybrid_setup(kind, mounts):
+    from octopus_b200.models.hybrid import HybridConfig, HybridWeights
+
+    base = get_config("tiny", layers=4, vocab_size=512)
+    hw = HybridWeights(HybridConfig(base, kind=kind, pattern="LLAL", lin_heads=2, lin_dim=32), "cpu",
+                       dtype=torch.float64, seed=4, std=0.05)
+    rng = np.random.default_rng(5)
+    root = rng.integers(1, 512, 21)
+    a = np.r_[root, rng.integers(1, 512, 13)]
+    b = np.r_[root, rng.integers(1, 512, 18)]
+    c = np.r_[a, rng.integers(1, 512, 9)]  # below a's node: depth 2
+    e = rng.integers(1, 512, 17)            # mounts a[3:9] at its row 6
+    seqs = [a, b, c, e]
+    flat = np.concatenate(seqs)
+    cu = np.r_[0, np.cumsum([len(x) for x in seqs])]
+    n = len(flat)
+    m = {3: [(6, 0, 3, 9)]} if mounts else None
+    mb = build_microbatch(flat, cu, m, np.ones(n, np.float32), rng.normal(size=n).astype(np.float32),
+                          np.zeros(n, np.float32), pad_to=8)
+    return hw, mb
+
+
+def _hybrid_grads(hw):
+    return torch.cat([hw.grad] + [t.main_grad.reshape(-1) for t in hw.t.values()] +
+                     [p.grad.reshape(-1) for p in hw.fp32.values()])
+
+
+def _hybrid_zero(hw):
+    hw.grad.zero_()
+    for t in hw.t.values():
+        t.main_grad.zero_()
+    for p in hw.fp32.values():
+        p.grad = None
+
+
+@pytest.mark.parametrize("tokens", [8, 13, 24, 1000])
+@pytest.mark.parametrize("kind,mounts", [("gdn", False), ("gdn", True), ("gla", False)])
+def test_hybrid_chunk_major_matches_whole_tree(kind, mounts, tokens):
+    """Linear layers keep states and conv input rows across chunks: chunks of a few rows
+    (nodes split into parts, parents in earlier chunks) give the whole-tree logprobs and
+    every parameter gradient (dense, linear-layer and fp32 gate / conv parameters)."""
+    from octopus_b200.models.hybrid import hybrid_forward
+
+    hw, mb = _hybrid_setup(kind, mounts)
+    assert mb.nodes[:, 3].max() >= 2
+    d = mb.to_device("cpu")
+    _hybrid_zero(hw)
+    lp, ent = hybrid_forward(hw, d.batch)
+    _loss(lp, ent, d).backward()
+    g_ref = _hybrid_grads(hw).clone()
+    _hybrid_zero(hw)
+    lp2, ent2 = chunk_major_forward(hw, mb, tokens)
+    _loss(lp2, ent2, d).backward()
+    assert torch.allclose(lp2, lp.detach(), rtol=1e-9, atol=1e-10)
+    assert torch.allclose(ent2, ent.detach(), rtol=1e-9, atol=1e-10)
+    g = _hybrid_grads(hw)
+    assert torch.allclose(g, g_ref, rtol=1e-7, atol=1e-10), float((g - g_ref).abs().max())
+
+
+@pytest.mark.gpu
+def test_hybrid_chunk_major_gpu_matches_whole_tree():
+    """bf16 on the sm_100a kernels (7B attention shapes, GDN layers with 2 heads of 128):
+    hybrid chunk-major with 16-row chunks against the whole-tree forward / backward."""
+    from octopus_b200.models.hybrid import HybridConfig, HybridWeights, hybrid_forward
+
+    dev = torch.device("cuda", 0)
+    _, mb = _hybrid_setup("gdn", True)
+    hw = HybridWeights(HybridConfig(get_config("qwen2.5-7b", layers=4), kind="gdn", pattern="LLAL", lin_heads=2,
+                                    lin_dim=128), dev, dtype=torch.bfloat16, seed=4)
+    d = mb.to_device(dev)
+    _hybrid_zero(hw)
+    lp, ent = hybrid_forward(hw, d.batch)
+    _loss(lp, ent, d).backward()
+    g_ref = _hybrid_grads(hw).clone()
+    _hybrid_zero(hw)
+    lp2, ent2 = chunk_major_forward(hw, mb, 16)
+    _loss(lp2, ent2, d).backward()
+    torch.cuda.synchronize()
+    rel = lambda a, b: float((a.float() - b.float()).norm() / (b.float().norm() + 1e-12))  # noqa: E731
+    assert rel(lp2, lp.detach()) < 1e-2 and rel(ent2, ent.detach()) < 1e-2
+    assert rel(_hybrid_grads(hw), g_ref) < 3e-2
