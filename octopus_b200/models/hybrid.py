@@ -69,11 +69,18 @@ class HybridConfig:
     def lin_width(self) -> int:
         return self.lin_heads * self.lin_dim
 
+    @property
+    def ba_rows(self) -> int:
+        """Rows of the beta / gate projection: 2 * heads, padded with zero rows to a multiple
+        of 8 (the GEMM's tile granularity; the padding rows' outputs are never read, so their
+        gradients and values stay zero)."""
+        return (2 * self.lin_heads + 7) // 8 * 8
+
 
 def _lin_specs(hc: HybridConfig, i: int):
     H, C = hc.base.hidden, hc.lin_width
     return [(f"layers.{i}.ln1", (H,), "ones"), (f"layers.{i}.lin_qkv", (3 * C, H), "normal"),
-            (f"layers.{i}.lin_z", (C, H), "normal"), (f"layers.{i}.lin_ba", (2 * hc.lin_heads, H), "normal"),
+            (f"layers.{i}.lin_z", (C, H), "normal"), (f"layers.{i}.lin_ba", (hc.ba_rows, H), "ba"),
             (f"layers.{i}.lin_out", (H, C), "normal"),
             (f"layers.{i}.lin_norm", (hc.lin_dim,), "ones"), (f"layers.{i}.ln2", (H,), "ones"),
             (f"layers.{i}.gu_w", (2 * hc.base.ffn, H), "normal"), (f"layers.{i}.down_w", (H, hc.base.ffn), "normal")]
@@ -102,6 +109,8 @@ class HybridWeights:
                     w = torch.ones(shape, dtype=torch.float32)
                 else:
                     w = torch.randn(shape, generator=g) * std
+                    if init == "ba":
+                        w[2 * hc.lin_heads:] = 0.0
                 w = w.to(dtype).to(device)
                 w.main_grad = torch.zeros(shape, dtype=grad_dt, device=device)
                 self.t[name] = w
@@ -129,8 +138,8 @@ def linear_layer_forward(x, hw: HybridWeights, i: int, tree):
     h = ops.rmsnorm(x, t[f"layers.{i}.ln1"], cfg.rms_eps, cfg.norm_plus_one)
     qkv = ops.linear(h, t[f"layers.{i}.lin_qkv"])
     z = ops.linear(h, t[f"layers.{i}.lin_z"])
-    ba = ops.linear(h, t[f"layers.{i}.lin_ba"])  # [T, 2 * heads]: beta logits | gate inputs
-    bb, aa = ba[:, :hc.lin_heads], ba[:, hc.lin_heads:]
+    ba = ops.linear(h, t[f"layers.{i}.lin_ba"])  # [T, ba_rows]: beta logits | gate inputs | zero padding
+    bb, aa = ba[:, :hc.lin_heads], ba[:, hc.lin_heads:2 * hc.lin_heads]
     W = hc.conv_width
     # conv context: the W - 1 rows before each node on its ancestor path (zeros when absent)
     rows = torch.as_tensor(tails[:, 8 - (W - 1):], device=x.device)

@@ -86,6 +86,10 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
                 out.copy_(y.to(out.dtype))
             return out
         return y.to(a.dtype if a.dtype in (torch.float32, torch.float64) else out_dtype)
+    K = a.shape[0] if a_mn else a.shape[1]
+    if M % 8 or N % 8 or K % 8:
+        # the tcgen05 GEMM's granularity; checked here so the extension never sees such a shape
+        raise ValueError(f"gemm: M, N, K must be multiples of 8 on the GPU (got {M}, {N}, {K})")
     if out is None:
         out = torch.empty(M, N, dtype=out_dtype, device=a.device)
     ext().gemm_out(a, a_mn, b, b_mn, out, alpha, residual, bias, accumulate, bn)

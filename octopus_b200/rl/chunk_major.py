@@ -302,7 +302,7 @@ def _chunk_linear_layer(x, st_ext, cx_ext, hw, i, L):
     qkv = ops.linear(h, t[f"layers.{i}.lin_qkv"])
     z = ops.linear(h, t[f"layers.{i}.lin_z"])
     ba = ops.linear(h, t[f"layers.{i}.lin_ba"])
-    bb, aa = ba[:, :hc.lin_heads], ba[:, hc.lin_heads:]
+    bb, aa = ba[:, :hc.lin_heads], ba[:, hc.lin_heads:2 * hc.lin_heads]
     W, U = hc.conv_width, len(L.segs)
     srcrows = torch.cat([qkv, cx_ext.to(qkv.dtype)]) if cx_ext is not None else qkv
     ok = (L.ctx_idx >= 0).unsqueeze(-1)
