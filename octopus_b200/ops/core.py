@@ -568,9 +568,73 @@ def logprob_head(h, W, labels, alpha: float = 1.0, vocab_limit: int | None = Non
 
 
 # ---------------------------------------------------------------------------- sampling
-def sample(h, W, temperature: float = 1.0, seed: int = 0, row_stream=None, vocab_limit: int | None = None):
-    """Sample one token per row from softmax(h W^T / T) (Gumbel-max); returns (tokens, logprobs)."""
+def _uniform(seed: int, stream: torch.Tensor, V: int) -> torch.Tensor:
+    """Counter-based uniforms in (0, 1), [rows, V]: a 32-bit integer hash (Wellons' "lowbias32"
+    finaliser) of (seed, row stream, token), so a row's draws do not depend on the batch."""
+    M32 = 0xFFFFFFFF
+    tok = torch.arange(V, device=stream.device, dtype=torch.int64)
+    x = ((stream.to(torch.int64)[:, None] * 0x9E3779B1 + (int(seed) & M32) * 0x85EBCA77) & M32)
+    x = (x ^ ((tok[None, :] * 0xC2B2AE3D) & M32)) & M32
+    x = x ^ (x >> 16)
+    x = (x * 0x7FEB352D) & M32
+    x = x ^ (x >> 15)
+    x = (x * 0x846CA68B) & M32
+    x = x ^ (x >> 16)
+    return (x.to(torch.float64) + 0.5) / 4294967296.0
+
+
+def filter_logits(z: torch.Tensor, top_p: float = 1.0, top_k: int = 0) -> torch.Tensor:
+    """Mask of the tokens kept by top-k (k <= 0 or k >= vocab: no top-k), then top-p on the
+    renormalised distribution (the smallest set of highest-probability tokens whose mass
+    reaches p; the top token is always kept)."""
+    V = z.shape[-1]
+    keep = torch.ones_like(z, dtype=torch.bool)
+    if 0 < top_k < V:
+        kth = z.topk(int(top_k), dim=-1).values[:, -1:]
+        keep &= z >= kth
+    if top_p < 1.0:
+        zs, idx = z.masked_fill(~keep, float("-inf")).sort(dim=-1, descending=True)
+        p = torch.softmax(zs, dim=-1)
+        before = p.cumsum(-1) - p  # mass of the higher-ranked tokens
+        drop = before >= top_p
+        drop[:, 0] = False
+        keep &= ~torch.zeros_like(drop).scatter(1, idx, drop)
+    return keep
+
+
+def _sample_filtered(h, W, alpha, seed, row_stream, vocab_limit, top_p, top_k):
+    """Sampling with top-p / top-k: logits of the rows (one GEMM), the filter, Gumbel-max over
+    the kept tokens.  The logprob is under the full tempered distribution (what the trainer
+    recomputes)."""
+    V = vocab_limit or W.shape[0]
+    if _is_cuda(h):
+        M = h.shape[0]
+        pad = (-M) % 8
+        hp = torch.cat([h, h.new_zeros(pad, h.shape[1])]) if pad else h
+        z = gemm(hp.contiguous(), W, out_dtype=torch.float32)[:M, :V] * alpha
+    else:
+        z = (ref._f(h) @ ref._f(W).t())[:, :V] * alpha
+    rs = row_stream if row_stream is not None else torch.arange(z.shape[0], device=z.device)
+    toks, lps = [], []
+    for a in range(0, z.shape[0], 32):  # row blocks bound the [rows, vocab] temporaries
+        zb = z[a:a + 32]
+        keep = filter_logits(zb, top_p, top_k)
+        g = -torch.log(-torch.log(_uniform(seed, rs[a:a + 32], V))).to(zb.dtype)
+        tok = (zb + g).masked_fill(~keep, float("-inf")).argmax(-1)
+        toks.append(tok)
+        lps.append(torch.log_softmax(zb, -1).gather(1, tok[:, None])[:, 0])
+    return torch.cat(toks), torch.cat(lps).float()
+
+
+def sample(h, W, temperature: float = 1.0, seed: int = 0, row_stream=None, vocab_limit: int | None = None,
+           top_p: float = 1.0, top_k: int = 0):
+    """Sample one token per row from softmax(h W^T / T) (Gumbel-max); returns (tokens, logprobs).
+    With top_p < 1 or 0 < top_k < vocab the distribution is filtered first (_sample_filtered);
+    otherwise the fused head samples without materialising logits."""
     alpha = 1.0 / max(temperature, 1e-6)
+    V = vocab_limit or W.shape[0]
+    if top_p < 1.0 or 0 < top_k < V:
+        return _sample_filtered(h, W, alpha, seed, row_stream, vocab_limit, float(top_p), int(top_k))
     if _is_cuda(h):
         M = h.shape[0]
         pad = (-M) % 8

@@ -80,6 +80,10 @@ class GenInput:
     # next; K3 relocates them to the request's next positions (copies whose keys are
     # re-rotated by the offset) and continues after them
     mount_rule: str = "K2"
+    # nucleus / top-k filtering (1.0 / 0: off; top_k >= vocab: off); shared by the batch like
+    # the temperature
+    top_p: float = 1.0
+    top_k: int = 0
 
 
 @dataclass
@@ -149,6 +153,7 @@ class Engine:
         # gather them once per group; re-planned per decode call (graph-safe tables)
         self.shared_decode = None
         self._shared_active = False
+        self._filter = (1.0, 0)  # the batch's (top_p, top_k)
         if (self.device.type == "cuda" and cfg.head_dim == 128 and self.mount_layers is None
                 and os.environ.get("OCTO_SHARED_DECODE", "1") != "0"):
             self.shared_decode = ops.SharedDecode(hq_loc, hkv_loc, cfg.head_dim, max_batch, self.device)
@@ -427,7 +432,8 @@ class Engine:
         for i in range(cfg.layers):
             x = self._layer(x, i, t_pos, t_slots, attn)
         h = self._final(x.index_select(0, h2d(last, dev)))
-        tok, lp = ops.sample(h, self.w.head, temperature, self.seed, h2d(streams, dev), cfg.vocab_size)
+        tp_, tk_ = self._filter
+        tok, lp = ops.sample(h, self.w.head, temperature, self.seed, h2d(streams, dev), cfg.vocab_size, tp_, tk_)
         return d2h(tok).numpy(), d2h(lp).numpy()
 
     def _decode_forward(self, tok, pos, slot, attn, B: int, temperature: float):
@@ -438,7 +444,8 @@ class Engine:
         for i in range(cfg.layers):
             x, h = self._layer_decode(x, h, i, pos, slot, attn)
         # (h is the final norm's output)
-        return ops.sample(h, self.w.head, temperature, self.seed, self.s_stream[:B], cfg.vocab_size)
+        tp_, tk_ = self._filter
+        return ops.sample(h, self.w.head, temperature, self.seed, self.s_stream[:B], cfg.vocab_size, tp_, tk_)
 
     # ------------------------------------------------------------------ decode
     def _decode_step(self, B: int, temperature: float):
@@ -493,8 +500,11 @@ class Engine:
             self.s_out_lp = torch.zeros(self.max_batch, steps, dtype=torch.float32, device=self.device)
             self._graphs.clear()
 
+    def _graph_key(self, B: int, temperature: float):
+        return (B, float(temperature), self._shared_active, self._filter)
+
     def _graph(self, B: int, temperature: float):
-        key = (B, float(temperature), self._shared_active)
+        key = self._graph_key(B, temperature)
         g = self._graphs.get(key)
         if g is not None:
             return g
@@ -592,7 +602,7 @@ class Engine:
                 g = self._graph(B, temperature)
                 for _ in range(steps):
                     g.replay()
-                ops.add_launches(self._graph_kernels[(B, float(temperature), self._shared_active)] * steps)
+                ops.add_launches(self._graph_kernels[self._graph_key(B, temperature)] * steps)
             else:
                 for _ in range(steps):
                     self._decode_step(B, temperature)
@@ -610,6 +620,7 @@ class Engine:
         if not inputs:
             return []
         temperature = inputs[0].temperature
+        self._filter = (float(inputs[0].top_p), int(inputs[0].top_k))
         reqs = [self._resolve(inp) for inp in inputs]
         for r in reqs:
             r.own_slots = self._alloc(len(r.new_tokens) + (0 if r.inp.prefill_only else r.inp.max_new_tokens))

@@ -56,10 +56,10 @@ class BatchingQueue:
             if batch and not fut.done():
                 for item in batch:
                     self.pending.remove(item)
-                # one temperature per engine batch: group by temperature
+                # one sampling setting per engine batch: group by (temperature, top_p, top_k)
                 groups: dict = {}
                 for i, f in batch:
-                    groups.setdefault(float(i.temperature), []).append((i, f))
+                    groups.setdefault((float(i.temperature), float(i.top_p), int(i.top_k)), []).append((i, f))
                 for items in groups.values():
                     try:
                         outs = await loop.run_in_executor(None, self.engine.generate, [i for i, _ in items])
@@ -74,6 +74,11 @@ class BatchingQueue:
         finally:
             self.inflight -= 1
 
+
+
+def _top_k(v) -> int:
+    """OpenAI / SGLang top_k: absent, None, 0 or -1 mean no top-k."""
+    return 0 if v is None or int(v) < 0 else int(v)
 
 
 class ChatService:
@@ -96,7 +101,8 @@ class ChatService:
         if audit and cursor is not None and body.get("audit_messages") and not body.get("mount"):
             self._audit(audit, body, cursor, ids, tools, kwargs)
         inp = GenInput(ids, cursor=cursor, mount=mounts_of(body), max_new_tokens=int(body.get("max_tokens", 1024)),
-                       temperature=float(body.get("temperature", 1.0)), stop_ids=tok.stop_ids)
+                       temperature=float(body.get("temperature", 1.0)), stop_ids=tok.stop_ids,
+                       top_p=float(body.get("top_p", 1.0)), top_k=_top_k(body.get("top_k")))
         o = await self.q.submit(inp)
         out_ids = [t for t in o.output_ids if t not in tok.stop_ids]
         content, calls = parse_tool_calls(tok.decode(out_ids))

@@ -1,7 +1,8 @@
 """HTTP serving front-end of the rollout engine (FastAPI).
 
 Endpoints (wire format shared with the reference's patched SGLang):
-  POST /generate               {input_ids, cursor?, mount?, sampling_params{max_new_tokens, temperature},
+  POST /generate               {input_ids, cursor?, mount?, sampling_params{max_new_tokens, temperature,
+                                top_p, top_k, stop_token_ids},
                                 rid?} -> {output_ids, meta_info{id, cursor, prompt_tokens, cached_tokens,
                                 completion_tokens, output_token_logprobs}}
   POST /v1/chat/completions    OpenAI chat body + optional ``cursor`` (send only the messages
@@ -29,7 +30,7 @@ import time
 
 from .chat import ChatTokenizer
 from .engine import CursorNotFound, Engine, GenInput
-from .local import BatchingQueue, ChatService, mounts_of  # noqa: F401  (BatchingQueue re-exported)
+from .local import BatchingQueue, ChatService, _top_k, mounts_of  # noqa: F401  (BatchingQueue re-exported)
 
 
 def generate_input(body: dict) -> GenInput:
@@ -38,7 +39,8 @@ def generate_input(body: dict) -> GenInput:
     return GenInput(list(body.get("input_ids") or []), cursor=body.get("cursor"), mount=mounts_of(body),
                     max_new_tokens=int(sp.get("max_new_tokens", 128)), temperature=float(sp.get("temperature", 1.0)),
                     stop_ids=tuple(sp.get("stop_token_ids") or ()),
-                    prefill_only=int(sp.get("max_new_tokens", 1)) == 0)
+                    prefill_only=int(sp.get("max_new_tokens", 1)) == 0,
+                    top_p=float(sp.get("top_p", 1.0)), top_k=_top_k(sp.get("top_k")))
 
 
 def generate_output(o, tokenizer=None) -> dict:

@@ -87,7 +87,14 @@ class TPEngine(Engine):
             c.reduce(h, g, w=nw, x=x, eps=cfg.rms_eps, plus_one=cfg.norm_plus_one)
         return x
 
+    def _no_filter(self):
+        tp_, tk_ = self._filter
+        if tp_ < 1.0 or 0 < tk_ < self.cfg.vocab_size:
+            raise ValueError("top_p / top_k sampling runs on single-GPU engines; the tensor-parallel engine "
+                             "samples from the full tempered distribution (vocab-parallel fused head)")
+
     def _prefill_forward(self, t_ids, t_pos, t_slots, attn, last, streams, temperature):
+        self._no_filter()
         M = t_ids.shape[0]
         rows_s = M // self.tp
         r0 = self.tp_rank * rows_s
@@ -115,6 +122,7 @@ class TPEngine(Engine):
         return tok[rank_pos], lp[rank_pos]
 
     def _decode_forward(self, tok, pos, slot, attn, B: int, temperature: float):
+        self._no_filter()
         rows_s = B // self.tp
         r0 = self.tp_rank * rows_s
         self._tp_forward(tok[r0:r0 + rows_s], pos, slot, attn, rows_s)

@@ -62,3 +62,30 @@ def test_rl_step_updates_weights():
     assert not torch.equal(before, actor.flat16)
     assert eng.version == 1
     ops.check_status(0)
+
+
+def test_filtered_sampling_graph_and_eager():
+    """top-p / top-k sampling on the GPU: graph-captured decode gives the eager tokens, top_k = 1
+    is greedy (the fp32 argmax of the head), and tokens stay inside the top-k set."""
+    cfg, actor, eng = _setup()
+    rng = np.random.default_rng(1)
+    prompts = [rng.integers(1, cfg.vocab_size, 60 + 5 * i).tolist() for i in range(3)]
+    mk = lambda **kw: [GenInput(p, max_new_tokens=8, rid=300 + i, keep_cursor=False, **kw)  # noqa: E731
+                       for i, p in enumerate(prompts)]
+    a = eng.generate(mk(top_p=0.9, top_k=50))
+    eng.use_graphs = False
+    eng.reset()
+    b = eng.generate(mk(top_p=0.9, top_k=50))
+    for x, y in zip(a, b):
+        assert x.output_ids == y.output_ids
+    h = torch.randn(24, cfg.hidden, device=dev).bfloat16()
+    W = actor.weights.head
+    z = (h.float() @ W.float().t())[:, :cfg.vocab_size]
+    t1, lp1 = ops.sample(h, W, 1.0, 0, None, cfg.vocab_size, top_k=1)
+    gap = z.topk(2).values
+    clear = (gap[:, 0] - gap[:, 1]) > 1e-2  # rows whose argmax is not a bf16 near-tie
+    assert torch.equal(t1[clear], z.argmax(-1)[clear])
+    t5, _ = ops.sample(h, W, 1.0, 1, None, cfg.vocab_size, top_k=5)
+    assert bool((z.topk(8).indices == t5[:, None]).any(-1).all())
+    assert torch.isfinite(lp1).all()
+    ops.check_status(0)
