@@ -21,8 +21,6 @@ from __future__ import annotations
 
 import json
 import os
-import re
-import uuid
 
 STUB = [{"role": "user", "content": "stub"}, {"role": "assistant", "content": "stub"}]
 
@@ -156,22 +154,9 @@ class ChatTokenizer:
         return out + self.terminator()
 
 
-TOOL_CALL = re.compile(r"<tool_call>\s*(\{.*?\})\s*</tool_call>", re.S)
+def parse_tool_calls(text: str, fmt: str = "qwen25", tools=None) -> tuple[str, list[dict]]:
+    """Split a completion into (content, OpenAI tool_calls) for tool-call format `fmt`
+    (serving.tool_parsers; hermes / qwen25 by default)."""
+    from .tool_parsers import parse
 
-
-def parse_tool_calls(text: str) -> tuple[str, list[dict]]:
-    """Split a completion into (content, OpenAI tool_calls) for the hermes/qwen25 format."""
-    calls = []
-    for m in TOOL_CALL.finditer(text):
-        try:
-            obj = json.loads(m.group(1))
-        except json.JSONDecodeError:
-            continue
-        if not isinstance(obj, dict) or not isinstance(obj.get("name"), str):
-            continue
-        args = obj.get("arguments", {})
-        calls.append({"id": f"call_{uuid.uuid4().hex[:9]}", "type": "function",
-                      "function": {"name": obj["name"],
-                                   "arguments": args if isinstance(args, str) else json.dumps(args)}})
-    content = TOOL_CALL.sub("", text).strip() if calls else text
-    return content, calls
+    return parse(text, fmt, tools)

@@ -85,8 +85,12 @@ class ChatService:
     """OpenAI-style chat completions (+ cursor / mount) on an engine, batched."""
 
     def __init__(self, engine: Engine, tokenizer: ChatTokenizer, model_name: str = "octopus-b200",
-                 window: float = 0.005):
+                 window: float = 0.005, tool_format: str | None = None):
+        from .tool_parsers import detect_format
+
         self.engine, self.tok, self.model_name = engine, tokenizer, model_name
+        # the tool-call markup the model emits: given, else the chat template's family
+        self.tool_format = tool_format or detect_format(tokenizer.template_src)
         self.q = BatchingQueue(engine, window)
         self._audit_lock = threading.Lock()
 
@@ -105,7 +109,7 @@ class ChatService:
                        top_p=float(body.get("top_p", 1.0)), top_k=_top_k(body.get("top_k")))
         o = await self.q.submit(inp)
         out_ids = [t for t in o.output_ids if t not in tok.stop_ids]
-        content, calls = parse_tool_calls(tok.decode(out_ids))
+        content, calls = parse_tool_calls(tok.decode(out_ids), self.tool_format, tools)
         # the cursor keeps reply tokens + template terminator so the next delta renders right after it
         eng = self.engine
         if o.cursor is not None and eng.cursors.get(o.cursor) is not None:
