@@ -154,6 +154,7 @@ class Engine:
         self.shared_decode = None
         self._shared_active = False
         self._filter = (1.0, 0)  # the batch's (top_p, top_k)
+        self._use_radix = True   # prefix reuse across requests (hybrid models: off, their states are per cursor)
         if (self.device.type == "cuda" and cfg.head_dim == 128 and self.mount_layers is None
                 and os.environ.get("OCTO_SHARED_DECODE", "1") != "0"):
             self.shared_decode = ops.SharedDecode(hq_loc, hkv_loc, cfg.head_dim, max_batch, self.device)
@@ -285,7 +286,7 @@ class Engine:
                 new = np.concatenate([cur.tokens[ok:], new])
             next_pos = int(cur.positions[ok - 1]) + 1 if ok else 0
             cached = ok
-        elif len(new) > 1:
+        elif len(new) > 1 and self._use_radix:
             ln, slots, handle = self.radix.match(self.version, new[:-1])
             ln = int(ln)
             if ln > 0:
@@ -319,6 +320,22 @@ class Engine:
         if len(new) == 0:
             raise ValueError("request has no new tokens to prefill")
         return r
+
+    # ------------------------------------------------------------------ model-family hooks
+    def _prefill_group(self, reqs, g, cu_q):
+        """Before one prefill forward of requests g (rows cu_q, padding after the last)."""
+
+    def _prefill_group_done(self, reqs, g):
+        """After that forward."""
+
+    def _decode_begin(self, reqs, chunk, B: int, steps: int):
+        """Before the decode steps of requests `chunk` (rows 0..len-1 of a B-row batch)."""
+
+    def _decode_end(self, reqs, chunk):
+        """After them."""
+
+    def _on_cursor(self, r, cid: str):
+        """A request's reply was stored as cursor `cid`."""
 
     # ------------------------------------------------------------------ forward pieces
     def _layer(self, x, i, pos, write_slots, attn):
@@ -416,8 +433,10 @@ class Engine:
 
             streams = np.asarray([(reqs[j].rid << 32) | (reqs[j].first_pos + len(reqs[j].new_tokens)) for j in g],
                                  np.int64)
+            self._prefill_group(reqs, g, cu_q)
             tok, lp = self._prefill_forward(t_ids, t_pos, t_slots, attn, np.asarray(last, np.int64), streams,
                                             temperature)
+            self._prefill_group_done(reqs, g)
             for k, j in enumerate(g):
                 first_tok[j] = tok[k]
                 first_lp[j] = lp[k]
@@ -598,6 +617,7 @@ class Engine:
             if self.shared_decode is not None:
                 ctx = np.asarray([len(reqs[j].ctx_slots) for j in chunk], np.int64)
                 self._shared_active = self.shared_decode.plan(regions[:n], starts, ctx, lens[:n] + steps + 1, B)
+            self._decode_begin(reqs, chunk, B, steps)
             if self.use_graphs:
                 g = self._graph(B, temperature)
                 for _ in range(steps):
@@ -606,6 +626,7 @@ class Engine:
             else:
                 for _ in range(steps):
                     self._decode_step(B, temperature)
+            self._decode_end(reqs, chunk)
             ot = d2h(self.s_out_tok[:n, :steps]).numpy()
             ol = d2h(self.s_out_lp[:n, :steps]).numpy()
             out_t[b0:b0 + n] = ot
@@ -659,11 +680,12 @@ class Engine:
                 held = cur.slots[cur.slots >= 0]
                 self.cursors.put(Cursor(cid, cur.tokens, cur.slots, cur.positions, cur.prompt_len, cur.mounted,
                                         cur.version), take_ref=False)
+                self._on_cursor(r, cid)
                 # the store's reference: ctx slots are borrowed (incref); own used slots transfer ownership
                 if len(r.ctx_slots):
                     self.pool.incref(r.ctx_slots)
                 del held
-            if r.inp.cursor is None and not r.inp.mount and len(r.new_tokens):
+            if r.inp.cursor is None and not r.inp.mount and len(r.new_tokens) and self._use_radix:
                 full = np.concatenate([r.ctx_tokens, r.new_tokens]).astype(np.int32)
                 sl = np.concatenate([r.ctx_slots, r.own_slots[:n_new]]).astype(np.int64)
                 self.radix.insert(self.version, full, sl)
