@@ -28,13 +28,20 @@ def exact_match(response: str, gold: str) -> bool:
 
 
 def grade(question: str, response: str, gold: str, judge=None) -> dict:
-    """{correct, by}: exact match first, then judge(question, response, gold) -> bool if given."""
+    """{correct, by}: exact match first, then judge(question, response, gold) -> bool | None
+    (given, else the BrowseComp-Plus judge configured by OCTOPUS_JUDGE_*: envs.search.judge);
+    a judge without a verdict grades incorrect ("judge_unparsed")."""
     if response is None or not str(response).strip():
         return {"correct": False, "by": "empty"}
     if exact_match(response, gold):
         return {"correct": True, "by": "exact"}
+    if judge is None:
+        from .judge import env_judge
+
+        judge = env_judge()
     if judge is not None:
-        return {"correct": bool(judge(question, response, gold)), "by": "judge"}
+        v = judge(question, response, gold)
+        return {"correct": False, "by": "judge_unparsed"} if v is None else {"correct": bool(v), "by": "judge"}
     return {"correct": False, "by": "exact"}
 
 

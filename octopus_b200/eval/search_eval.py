@@ -2,7 +2,7 @@
 
     python -m octopus_b200.eval.search_eval --questions q.jsonl --corpus corpus.jsonl
         [--model-path HF_DIR] [--preset qwen2.5-7b] [--samples 1] [--settings episode_settings.json]
-        [--judge-url http://host:port/v1/chat/completions] [--out results.jsonl]
+        [--judge-url http://host:port/v1 --judge-model NAME] [--out results.jsonl]
 
 Questions: JSONL {qid, question, answer[, evidence: [docid, ...]]}; corpus: JSONL
 {docid, title, text}.  Each question runs `samples` episodes on the in-process engine
@@ -23,17 +23,14 @@ import json
 import statistics
 
 
-def judge_via_http(url: str, model: str = "judge"):
-    """judge(question, response, gold) -> bool through an OpenAI-compatible chat endpoint."""
-    from ..runtime.core import post_chat
+def judge_via_http(url: str, model: str = "judge", key: str | None = None, temperature: float = 0.0,
+                   cache: str | None = None):
+    """judge(question, response, gold) -> bool | None: the BrowseComp-Plus grader
+    (envs.search.judge) on an OpenAI-compatible endpoint (base URL ending in /v1)."""
+    from ..envs.search.judge import judge as bcp_judge
 
     def judge(question, response, gold):
-        prompt = (f"Question: {question}\nGold answer: {gold}\nResponse: {response}\n"
-                  "Is the response correct? Answer yes or no.")
-        out = post_chat(url, {"model": model, "temperature": 0, "max_tokens": 4,
-                              "messages": [{"role": "user", "content": prompt}]})
-        text = (out["choices"][0]["message"].get("content") or "").strip().lower()
-        return text.startswith("yes")
+        return bcp_judge(question, response, gold, url, model, key, temperature, cache)[0]
 
     return judge
 
@@ -116,6 +113,7 @@ def main(argv=None) -> int:
     ap.add_argument("--samples", type=int, default=1)
     ap.add_argument("--settings", default="")
     ap.add_argument("--judge-url", default="")
+    ap.add_argument("--judge-model", default="judge")
     ap.add_argument("--max-main-calls", type=int, default=None)
     ap.add_argument("--kv-gb", type=float, default=8.0)
     ap.add_argument("--cpu", action="store_true")
@@ -132,7 +130,7 @@ def main(argv=None) -> int:
     svc, eng = build_service(args.preset, args.model_path, args.kv_gb, args.cpu)
     questions = [json.loads(x) for x in open(args.questions) if x.strip()]
     corpus = [json.loads(x) for x in open(args.corpus) if x.strip()]
-    judge = judge_via_http(args.judge_url) if args.judge_url else None
+    judge = judge_via_http(args.judge_url, args.judge_model) if args.judge_url else None
     res = evaluate(svc, Retrieval(corpus), questions, args.samples, judge, args.max_main_calls, eng)
     print(json.dumps(res["summary"]))
     if args.out:
