@@ -71,13 +71,16 @@ class ActorSection:
 
 @dataclass
 class RLSection:
-    kind: str = "dag"           # dag | search | plan
+    kind: str = "dag"           # dag | search | swe
     n_samples: int = 4
     batch_size: int = 32        # prompts (DAG instances) per step
     branch_credit: str = "outcome"
     filter_zero_variance: bool = True
     spool: str = ""             # rollout spool dir ("" = off)
     search_questions: str = ""
+    swe_tasks: str = ""         # kind=swe: JSONL task rows (envs.swe.taskset), or a directory of them
+    swe_bundle: int = 0         # > 1: bundles of this many tasks of one repository per episode
+    swe_timeout: float = 120.0  # seconds per tool / test command
     episodes_per_server: int = 8
 
 

@@ -119,8 +119,10 @@ def build(cfg, device):
         env = _Env()
     elif cfg.rl.kind == "search":
         env = _search_env(cfg, engine, rep, replicas)
+    elif cfg.rl.kind == "swe":
+        env = _swe_env(cfg, engine, rep, replicas)
     else:
-        raise SystemExit(f"rl.kind {cfg.rl.kind!r}: dag or search")
+        raise SystemExit(f"rl.kind {cfg.rl.kind!r}: dag, search or swe")
     trainer = RLTrainer(actor, engine, env, TrainerConfig(mb_tokens=a.mb_tokens, mb_shard=(tp_rank, tp)),
                         sync_fn=engine.sync_weights if tp > 1 else None)
     return trainer, actor, engine, env, spool, tp_rank
@@ -151,6 +153,29 @@ def _search_env(cfg, engine, rep, replicas):
                     batch_size=max(1, cfg.rl.batch_size // replicas), branch_credit=cfg.rl.branch_credit,
                     gate=search_gate if cfg.rl.branch_credit == "gate" else None,
                     filter_zero_variance=cfg.rl.filter_zero_variance)
+
+
+def _swe_env(cfg, engine, rep, replicas):
+    """SWE plan episodes (envs.swe.rl): the task rows of this replica, bundled when asked,
+    graded by their hidden tests in local sandboxed copies."""
+    from ..envs.swe.containers import LocalExec
+    from ..envs.swe.rl import swe_agent_env
+    from ..envs.swe.taskset import build_bundles, load_rows, select_task_specs
+    from ..serving.chat import ChatTokenizer
+    from ..serving.local import ChatService
+
+    if not cfg.rl.swe_tasks:
+        raise SystemExit("rl.kind=swe needs rl.swe_tasks (JSONL task rows or a directory of them)")
+    specs = select_task_specs(load_rows(cfg.rl.swe_tasks))
+    if cfg.rl.swe_bundle > 1:
+        specs = build_bundles(specs, cfg.rl.swe_bundle, seed=cfg.seed)
+    specs = [s for i, s in enumerate(specs) if i % replicas == rep]
+    if not specs:
+        raise SystemExit(f"rl.swe_tasks {cfg.rl.swe_tasks}: no task with a local repository for this replica")
+    tok = ChatTokenizer.from_dir(cfg.model.path) if cfg.model.path else ChatTokenizer.tiny()
+    return swe_agent_env(ChatService(engine, tok), specs, LocalExec(sandbox=True), n_samples=cfg.rl.n_samples,
+                         batch_size=max(1, cfg.rl.batch_size // replicas), branch_credit=cfg.rl.branch_credit,
+                         timeout=cfg.rl.swe_timeout, filter_zero_variance=cfg.rl.filter_zero_variance)
 
 
 def main(argv=None) -> int:

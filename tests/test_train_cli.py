@@ -49,3 +49,34 @@ def test_train_cli_lora(tmp_path, monkeypatch):
                                  "checkpoint.save_every=0"]
     args = [a for a in args if a != "actor.gradient_checkpointing=false"] + ["actor.gradient_checkpointing=true"]
     assert train.main(args) == 0
+
+
+def test_train_cli_swe(tmp_path, monkeypatch):
+    """rl.kind=swe: plan episodes on a local task set (tiny random policy, short replies),
+    graded by hidden tests, one trained step."""
+    import platform
+    import sys
+
+    import pytest
+
+    if platform.machine() != "x86_64":
+        pytest.skip("x86_64 guard")
+    from dataclasses import asdict
+
+    from octopus_b200.envs.swe.taskset import TaskSpec
+    from test_swe_taskset import HIDDEN, _repo
+
+    repo = _repo(tmp_path)
+    rows = tmp_path / "tasks.jsonl"
+    rows.write_text("".join(json.dumps(asdict(TaskSpec(f"org__calc-{i}", repo, "HEAD", "add() subtracts; fix it.", "",
+                                                       f"{sys.executable} test_hidden.py",
+                                                       {"test_hidden.py": HIDDEN}))) + "\n" for i in range(2)))
+    monkeypatch.setenv("OCTOPUS_MAX_TOKENS", "6")
+    monkeypatch.setenv("OCTOPUS_MAIN_MAX_CALLS", "2")
+    args = [a for a in _args(tmp_path, 1) if a != "rl.kind=dag"] + [
+        "rl.kind=swe", f"rl.swe_tasks={rows}", "rl.filter_zero_variance=false", "rl.swe_timeout=30",
+        "checkpoint.recover_every=0", "checkpoint.save_every=0"]
+    assert train.main(args) == 0
+    run = tmp_path / "octopus-b200" / "run0"
+    (row,) = [json.loads(x) for x in open(run / "steps.jsonl")]
+    assert row["step"] == 1
