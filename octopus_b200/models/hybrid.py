@@ -77,6 +77,19 @@ class HybridConfig:
         return (2 * self.lin_heads + 7) // 8 * 8
 
 
+def hybrid_config(preset: str, layers: int = 0) -> HybridConfig | None:
+    """Hybrid presets (None for a dense preset): "tiny-hybrid" (tests) and "hybrid-7b" (the 7B
+    decoder's shape with three linear layers per attention layer, as Qwen3-Next / Qwen3.5)."""
+    from .config import get_config
+
+    kw = {"layers": layers} if layers else {}
+    if preset == "tiny-hybrid":
+        return HybridConfig(get_config("tiny", **kw), kind="gdn", pattern="LLLA", lin_heads=4, lin_dim=64)
+    if preset == "hybrid-7b":
+        return HybridConfig(get_config("qwen2.5-7b", **kw), kind="gdn", pattern="LLLA", lin_heads=16, lin_dim=128)
+    return None
+
+
 def _lin_specs(hc: HybridConfig, i: int):
     H, C = hc.base.hidden, hc.lin_width
     return [(f"layers.{i}.ln1", (H,), "ones"), (f"layers.{i}.lin_qkv", (3 * C, H), "normal"),
@@ -219,4 +232,5 @@ def hybrid_sequence_reference(hw: HybridWeights, tokens: np.ndarray):
     return hybrid_forward(hw, d.batch)[0], mb
 
 
-__all__ = ["FAMILIES", "HybridConfig", "HybridWeights", "family_kind", "hybrid_forward", "linear_layer_forward"]
+__all__ = ["FAMILIES", "HybridConfig", "HybridWeights", "family_kind", "hybrid_config", "hybrid_forward",
+           "linear_layer_forward"]

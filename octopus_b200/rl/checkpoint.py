@@ -55,9 +55,11 @@ def save(actor, root: str, step: int, dataloader_state: dict | None = None, spoo
         save_hf(actor.weights, os.path.join(tmp, "weights"))
     if dist:
         dist.barrier()
-    torch.save({"master": actor.master.cpu(), "exp_avg": actor.exp_avg.cpu(), "exp_avg_sq": actor.exp_avg_sq.cpu(),
-                "step_count": actor.step_count, "layout": _layout_hash(actor)},
-               os.path.join(tmp, f"optim-rank{rank}.pt"))
+    opt = {"master": actor.master.cpu(), "exp_avg": actor.exp_avg.cpu(), "exp_avg_sq": actor.exp_avg_sq.cpu(),
+           "step_count": actor.step_count, "layout": _layout_hash(actor)}
+    if hasattr(actor, "extra_state"):  # parameters and optimizer state outside the flat layout (hybrid layers)
+        opt["extra"] = actor.extra_state()
+    torch.save(opt, os.path.join(tmp, f"optim-rank{rank}.pt"))
     if dist:
         dist.barrier()
     if rank == 0:
@@ -96,6 +98,8 @@ def load(actor, root: str) -> dict:
     actor.master.copy_(opt["master"].to(actor.master.device))
     actor.exp_avg.copy_(opt["exp_avg"].to(actor.exp_avg.device))
     actor.exp_avg_sq.copy_(opt["exp_avg_sq"].to(actor.exp_avg_sq.device))
+    if hasattr(actor, "load_extra_state"):
+        actor.load_extra_state(opt["extra"])
     actor.step_count = int(opt["step_count"])
     actor.version = int(state["version"])
     return state

@@ -55,14 +55,24 @@ def build(cfg, device):
 
     world = dist.get_world_size() if dist.is_initialized() else 1
     rank = dist.get_rank() if dist.is_initialized() else 0
-    mcfg = get_config(cfg.model.preset, **({"layers": cfg.model.layers} if cfg.model.layers else {}))
+    from ..models.hybrid import hybrid_config
+
+    hc = hybrid_config(cfg.model.preset, cfg.model.layers)
+    mcfg = hc.base if hc is not None else get_config(cfg.model.preset,
+                                                     **({"layers": cfg.model.layers} if cfg.model.layers else {}))
     a = cfg.actor
     optim = OptimConfig(lr=a.lr, betas=(a.beta1, a.beta2), eps=a.eps, weight_decay=a.weight_decay,
                         max_grad_norm=a.gradient_clipping)
     ppo = PPOConfig(eps_clip=a.eps_clip, eps_clip_higher=a.eps_clip_higher, behav_imp_weight_cap=a.behav_imp_weight_cap,
                     reuse_train_logp=a.reuse_train_logp)
     dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
-    if a.lora_rank > 0:
+    if hc is not None:
+        if a.lora_rank > 0 or world > 1 or cfg.rollout.tp > 1:
+            raise SystemExit("hybrid presets train full-parameter on one replica (no LoRA, DP or TP yet)")
+        from .hybrid_actor import HybridActor
+
+        actor = HybridActor(hc, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype, ckpt=a.gradient_checkpointing)
+    elif a.lora_rank > 0:
         from ..models.lora import LoRAConfig, lora_targets
         from .actor import LoRAActor
 
@@ -85,6 +95,8 @@ def build(cfg, device):
                      chunk_tokens=chunk_tokens, seq_tile=a.seq_tile)
     if cfg.model.path:
         load_hf(getattr(actor, "base", actor.weights), cfg.model.path)
+        if hc is not None:
+            _load_hybrid_linear(actor, cfg.model.path)
         actor.reload_master()
         if a.lora_rank > 0:
             actor.optimizer_merge()
@@ -97,7 +109,11 @@ def build(cfg, device):
             if r == rep:
                 group = g
     kv_slots = int(cfg.rollout.kv_gb * (1 << 30) / (4 * mcfg.layers * mcfg.kv_width // tp))
-    if tp > 1:
+    if hc is not None:
+        from ..serving.hybrid_engine import HybridEngine
+
+        engine = HybridEngine(actor.hw, kv_slots=kv_slots, max_batch=cfg.rollout.max_batch, device=device)
+    elif tp > 1:
         from ..serving.tp_engine import TPEngine
 
         engine = TPEngine(mcfg, actor.weights, group=group, kv_slots=kv_slots, max_batch=cfg.rollout.max_batch,
@@ -153,6 +169,21 @@ def _search_env(cfg, engine, rep, replicas):
                     batch_size=max(1, cfg.rl.batch_size // replicas), branch_credit=cfg.rl.branch_credit,
                     gate=search_gate if cfg.rl.branch_credit == "gate" else None,
                     filter_zero_variance=cfg.rl.filter_zero_variance)
+
+
+def _load_hybrid_linear(actor, path):
+    """Linear-layer tensors of a hybrid checkpoint written by HybridActor.save_hf."""
+    f = os.path.join(path, "hybrid_linear.safetensors")
+    if not os.path.exists(f):
+        raise SystemExit(f"{path}: no hybrid_linear.safetensors for the hybrid preset's linear layers")
+    from safetensors.torch import load_file
+
+    st = load_file(f)
+    import torch
+
+    with torch.no_grad():
+        for k, t in list(actor.hw.t.items()) + list(actor.hw.fp32.items()):
+            t.copy_(st[k].to(t.dtype))
 
 
 def _swe_env(cfg, engine, rep, replicas):
@@ -232,7 +263,8 @@ def main(argv=None) -> int:
         if cfg.checkpoint.recover_every and (step + 1) % cfg.checkpoint.recover_every == 0:
             checkpoint.save(actor, run_dir, step + 1, {"step": step + 1}, spool=spool)
         if cfg.checkpoint.save_every and (step + 1) % cfg.checkpoint.save_every == 0 and rank == 0:
-            save_hf(actor.weights, os.path.join(run_dir, f"hf-step{step + 1}"))
+            out_dir = os.path.join(run_dir, f"hf-step{step + 1}")
+            actor.save_hf(out_dir) if hasattr(actor, "save_hf") else save_hf(actor.weights, out_dir)
     if world > 1:
         dist.barrier()
         if hasattr(engine, "close"):
