@@ -122,3 +122,70 @@ def serve(engine: Engine, tokenizer=None, host: str = "127.0.0.1", port: int = 3
     import uvicorn
 
     uvicorn.run(create_app(engine, tokenizer), host=host, port=port, log_level="warning")
+
+
+def build_engine(preset: str, model_path: str = "", kv_gb: float = 8.0, max_batch: int = 256, layers: int = 0,
+                 device=None):
+    """(engine, tokenizer) for a preset: dense presets get the paged engine, hybrid presets
+    (models.hybrid.hybrid_config) the hybrid engine; weights from an HF directory (the
+    hybrid linear layers from its hybrid_linear.safetensors) or random init."""
+    import os
+
+    import torch
+
+    from ..models.config import get_config
+    from ..models.decoder import FlatLayout, Weights, init_flat, load_hf
+    from ..models.hybrid import HybridWeights, hybrid_config
+
+    dev = torch.device(device or ("cuda" if torch.cuda.is_available() else "cpu"))
+    dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
+    has_tok = bool(model_path) and os.path.exists(os.path.join(model_path, "tokenizer.json"))
+    tok = ChatTokenizer.from_dir(model_path) if has_tok else ChatTokenizer.tiny()
+    hc = hybrid_config(preset, layers)
+    cfg = hc.base if hc is not None else get_config(preset, **({"layers": layers} if layers else {}))
+    kv_slots = max(4096, int(kv_gb * (1 << 30) / (4 * cfg.layers * cfg.kv_width)))
+    if hc is not None:
+        from .hybrid_engine import HybridEngine
+
+        hw = HybridWeights(hc, dev, dtype=dtype)
+        if model_path:
+            load_hf(hw.dense, model_path)
+            from safetensors.torch import load_file
+
+            st = load_file(os.path.join(model_path, "hybrid_linear.safetensors"))
+            with torch.no_grad():
+                for k, t in list(hw.t.items()) + list(hw.fp32.items()):
+                    t.copy_(st[k].to(t.dtype))
+        return HybridEngine(hw, kv_slots=kv_slots, max_batch=max_batch, device=dev), tok
+    lay = FlatLayout(cfg)
+    w = Weights(cfg, init_flat(cfg, lay, dev, dtype=dtype), lay)
+    if model_path:
+        load_hf(w, model_path)
+    return Engine(cfg, w, kv_slots=kv_slots, max_batch=max_batch, device=dev), tok
+
+
+def main(argv=None) -> int:
+    import argparse
+
+    ap = argparse.ArgumentParser(prog="python -m octopus_b200.serving.server")
+    ap.add_argument("--preset", default="qwen2.5-7b", help="dense preset or hybrid preset (tiny-hybrid, hybrid-7b)")
+    ap.add_argument("--model-path", default="", help="HF checkpoint directory (weights, tokenizer, chat template)")
+    ap.add_argument("--layers", type=int, default=0)
+    ap.add_argument("--kv-gb", type=float, default=24.0)
+    ap.add_argument("--max-batch", type=int, default=256)
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=30000)
+    ap.add_argument("--device", default=None)
+    ap.add_argument("--check", action="store_true", help="build the engine and app, then exit (no listening)")
+    args = ap.parse_args(argv)
+    eng, tok = build_engine(args.preset, args.model_path, args.kv_gb, args.max_batch, args.layers, args.device)
+    if args.check:
+        create_app(eng, tok)
+        print(f"ok: {type(eng).__name__} {args.preset} on {eng.device}")
+        return 0
+    serve(eng, tok, args.host, args.port)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -131,3 +131,20 @@ def test_hybrid_actor_gpu_step():
 
 
 test_hybrid_actor_gpu_step = __import__("pytest").mark.gpu(test_hybrid_actor_gpu_step)
+
+
+def test_server_cli_builds_from_hybrid_checkpoint(tmp_path):
+    """A hybrid checkpoint written by the actor loads into the server's hybrid engine; the
+    server CLI builds a dense engine and its app."""
+    from octopus_b200.serving.server import build_engine, main
+
+    act = HybridActor(hybrid_config("tiny-hybrid"), "cpu", dtype=torch.float32, seed=4)
+    act.train_step([_mb(5, V=4096)])
+    act.save_hf(str(tmp_path / "ck"))
+    eng, _ = build_engine("tiny-hybrid", str(tmp_path / "ck"), kv_gb=0.01, max_batch=8, device="cpu")
+    assert type(eng).__name__ == "HybridEngine"
+    for k in ("layers.0.lin_qkv", "layers.1.lin_ba"):
+        assert torch.equal(eng.hw.t[k], act.hw.t[k])
+    assert torch.equal(eng.hw.fp32["layers.0.A_log"].detach(), act.hw.fp32["layers.0.A_log"].detach())
+    assert torch.equal(eng.w.flat, act.flat16)
+    assert main(["--preset", "tiny", "--kv-gb", "0.01", "--max-batch", "8", "--device", "cpu", "--check"]) == 0
