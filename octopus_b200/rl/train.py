@@ -171,6 +171,31 @@ def _search_env(cfg, engine, rep, replicas):
                     filter_zero_variance=cfg.rl.filter_zero_variance)
 
 
+def _observability(engine, before: dict, device) -> dict:
+    """Per-step serving and memory figures for the step log: prefix-cache hit rate (rows
+    reused from the radix cache or cursors / rows prefilled or reused), requests, KV pool
+    usage, peak device memory and host RSS."""
+    import torch
+
+    d = {k: engine.stats.get(k, 0) - before.get(k, 0) for k in ("cached_tokens", "prefill_tokens", "requests")}
+    tot = d["cached_tokens"] + d["prefill_tokens"]
+    out = {"cache_hit_rate": round(d["cached_tokens"] / tot, 4) if tot else None, "requests": d["requests"]}
+    try:
+        ls = engine.load_stats()
+        out["kv_usage"] = round(float(ls.get("token_usage", 0.0)), 4)
+    except Exception:  # noqa: BLE001  (engines without a pool report)
+        pass
+    if device.type == "cuda":
+        out["peak_gpu_gb"] = round(torch.cuda.max_memory_allocated(device) / 2**30, 3)
+    try:
+        import psutil
+
+        out["host_rss_gb"] = round(psutil.Process().memory_info().rss / 2**30, 3)
+    except ImportError:
+        pass
+    return out
+
+
 def _load_hybrid_linear(actor, path):
     """Linear-layer tensors of a hybrid checkpoint written by HybridActor.save_hf."""
     f = os.path.join(path, "hybrid_linear.safetensors")
@@ -251,10 +276,13 @@ def main(argv=None) -> int:
         if "MB_TOKENS" in live:
             trainer.cfg.mb_tokens = live["MB_TOKENS"]
         t0 = time.time()
+        seen = dict(engine.stats)
+        if device.type == "cuda":
+            torch.cuda.reset_peak_memory_stats(device)
         st = trainer.step()
         row = {"step": step + 1, "time": round(time.time() - t0, 3), "version": actor.version,
                **{k: (round(v, 6) if isinstance(v, float) else v) for k, v in st.items()
-                  if isinstance(v, (int, float))}}
+                  if isinstance(v, (int, float))}, **_observability(engine, seen, device)}
         if rank == 0:
             line = json.dumps(row)
             print(line, flush=True)

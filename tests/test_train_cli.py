@@ -27,6 +27,8 @@ def test_train_cli_runs_and_resumes(tmp_path, monkeypatch):
     run = tmp_path / "octopus-b200" / "run0"
     rows = [json.loads(x) for x in open(run / "steps.jsonl")]
     assert [r["step"] for r in rows] == [1, 2]
+    assert all({"cache_hit_rate", "requests", "kv_usage", "host_rss_gb"} <= set(r) for r in rows)
+    assert rows[0]["requests"] > 0
     assert (run / "recover" / "state.json").exists() and (run / "hf-step2").exists()
     assert os.path.exists(run / "episode_settings.json")
     # resume: continues at step 3
