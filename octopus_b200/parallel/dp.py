@@ -29,6 +29,10 @@ class DataParallel:
         n = g.numel()
         for a in range(0, n, self.bucket):
             dist.all_reduce(g[a: a + self.bucket], group=self.group)
+        # gradients outside the flat buffer (hybrid models' linear layers and gate / conv
+        # parameters), the same list in the same order on every rank
+        for t in getattr(self.actor, "extra_grads", lambda: [])():
+            dist.all_reduce(t, group=self.group)
 
     def attach_actor(self):
         """Wrap the actor's forward_backward / optimizer_step (no trainer needed)."""

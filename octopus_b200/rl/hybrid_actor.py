@@ -77,6 +77,14 @@ class HybridActor:
         for p in self.hw.fp32.values():
             p.grad = None
 
+    def extra_grads(self) -> list:
+        """Gradient tensors outside the flat buffer, in a fixed order (data-parallel reduce);
+        absent fp32 parameter gradients are created as zeros."""
+        for p in self.hw.fp32.values():
+            if p.grad is None:
+                p.grad = torch.zeros_like(p)
+        return [t.main_grad for t in self.hw.t.values()] + [p.grad for p in self.hw.fp32.values()]
+
     def reload_master(self):
         self.master.copy_(self.flat16.to(self.master.dtype))
         for k, t in self.hw.t.items():

@@ -67,11 +67,15 @@ def build(cfg, device):
                     reuse_train_logp=a.reuse_train_logp)
     dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
     if hc is not None:
-        if a.lora_rank > 0 or world > 1 or cfg.rollout.tp > 1:
-            raise SystemExit("hybrid presets train full-parameter on one replica (no LoRA, DP or TP yet)")
+        if a.lora_rank > 0 or cfg.rollout.tp > 1:
+            raise SystemExit("hybrid presets train full-parameter replicas (no LoRA or rollout TP)")
         from .hybrid_actor import HybridActor
 
         actor = HybridActor(hc, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype, ckpt=a.gradient_checkpointing)
+        if world > 1:  # replicated data parallelism: one all-reduce of every gradient per step
+            from ..parallel.dp import DataParallel
+
+            DataParallel(actor).attach_actor()
     elif a.lora_rank > 0:
         from ..models.lora import LoRAConfig, lora_targets
         from .actor import LoRAActor

@@ -148,3 +148,56 @@ def test_server_cli_builds_from_hybrid_checkpoint(tmp_path):
     assert torch.equal(eng.hw.fp32["layers.0.A_log"].detach(), act.hw.fp32["layers.0.A_log"].detach())
     assert torch.equal(eng.w.flat, act.flat16)
     assert main(["--preset", "tiny", "--kv-gb", "0.01", "--max-batch", "8", "--device", "cpu", "--check"]) == 0
+
+
+def _dp_rank(rank, world, port, q):
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from octopus_b200.parallel.dp import DataParallel
+
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        act = _actor()
+        DataParallel(act).attach_actor()
+        act.zero_grad()
+        act.forward_backward([_mb(10 + rank)])
+        act.optimizer_step()
+        q.put((rank, act.flat16.clone().numpy(), {k: t.clone().numpy() for k, t in act.hw.t.items()},
+               {k: p.detach().clone().numpy() for k, p in act.hw.fp32.items()}))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_hybrid_data_parallel_matches_one_process():
+    """Two gloo ranks, one micro-batch each, equal the one-process step over both."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    ref = _actor()
+    ref.zero_grad()
+    ref.forward_backward([_mb(10), _mb(11)])
+    ref.optimizer_step()
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_dp_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict((r, rest) for r, *rest in (q.get(timeout=300) for _ in procs))
+    for p in procs:
+        p.join(timeout=60)
+    for r in (0, 1):
+        flat, lin, fp = got[r]
+        assert np.allclose(flat, ref.flat16.numpy(), rtol=1e-9, atol=1e-12)
+        for k, t in ref.hw.t.items():
+            assert np.allclose(lin[k], t.numpy(), rtol=1e-9, atol=1e-12), k
+        for k, p in ref.hw.fp32.items():
+            assert np.allclose(fp[k], p.detach().numpy(), rtol=1e-9, atol=1e-12), k
