@@ -1,8 +1,10 @@
 """Linear recurrences (gated delta rule / simple GLA) and the causal depthwise conv1d of
 hybrid models, as autograd ops over variable-length segments with initial / final states.
 
-CUDA tensors run the sm_100a kernels of csrc/recurrence.cu; CPU tensors run token-by-
-token references (the test oracle, as in the reference's tests).
+CUDA tensors run the sm_100a kernels of csrc/recurrence.cu (or, with
+OCTO_RECURRENCE_CHUNKED=1, the chunked tensor-op form); CPU tensors run the chunked form
+(`recurrence_chunked`, autograd through its tensor ops).  `recurrence_ref` is the
+token-by-token oracle (as in the reference's tests).
 
   recurrence(q, k, v, g, beta, segs, scale, delta, init_state, init_idx) -> (o, final)
       q, k, v [rows, H * d]; g, beta [rows, H] fp32; segs: host [(start, len)];
@@ -61,6 +63,61 @@ def recurrence_ref(q, k, v, g, beta, segs, scale, delta, init_state=None, init_i
     return o.view(rows, Hd), (torch.stack(finals) if finals else torch.zeros(0, H, d, d, dtype=q.dtype))
 
 
+def recurrence_chunked(q, k, v, g, beta, segs, scale, delta, init_state=None, init_idx=None, chunk: int = 64):
+    """The same recurrence in chunks of `chunk` tokens (the chunked gated delta rule of
+    Yang et al., "Gated Delta Networks", 2024, via its UT transform; GLA without the delta
+    term), differentiable with plain tensor ops.
+
+    Per head, a chunk with state S0 [d_v, d_k], cumulative log decay b_t (gamma_t = exp b_t)
+    and R[t, s] = exp(b_t - b_s):
+        A = strictly-lower(beta_t (k_t . k_s) R[t, s]),  (I + A) U = beta V,  (I + A) W = beta gamma K
+        V' = U - W S0^T                                  (delta rule; GLA: V' = V)
+        O  = scale ((gamma Q) S0^T + ((Q K^T) * lower-incl(R)) V')
+        S  = gamma_L S0 + (V' * R[L, :])^T K
+    Returns (o [rows, H*d], final [n_seg, H, d, d]) like recurrence_ref."""
+    rows, Hd = q.shape
+    H = g.shape[1]
+    d = Hd // H
+    dt = q.dtype if q.dtype == torch.float64 else torch.float32
+    qh, kh, vh = (t.view(rows, H, d).to(dt) for t in (q, k, v))
+    gh, bh = g.to(dt), beta.to(dt)
+    out = torch.zeros(rows, H, d, dtype=dt, device=q.device)
+    finals = []
+    for s_idx, (t0, T) in enumerate(segs):
+        t0, T = int(t0), int(T)
+        if init_state is not None and init_idx is not None and int(init_idx[s_idx]) >= 0:
+            S = init_state[int(init_idx[s_idx])].to(dt)
+        else:
+            S = torch.zeros(H, d, d, dtype=dt, device=q.device)
+        for c0 in range(t0, t0 + T, chunk):
+            c1 = min(t0 + T, c0 + chunk)
+            L = c1 - c0
+            Q, K, V = (x[c0:c1].transpose(0, 1) for x in (qh, kh, vh))   # [H, L, d]
+            b = gh[c0:c1].transpose(0, 1).cumsum(-1)                     # [H, L]
+            incl = torch.ones(L, L, dtype=torch.bool, device=q.device).tril()
+            # the exponent is masked before exp: above the diagonal b_t - b_s > 0 can overflow,
+            # and an inf there would turn the masked entries' gradients into NaN
+            diff = (b[:, :, None] - b[:, None, :]).masked_fill(~incl, float("-inf"))
+            R = torch.exp(diff)                                         # [H, L, L], 0 above the diagonal
+            gam = torch.exp(b)                                           # [H, L]
+            if delta:
+                be = bh[c0:c1].transpose(0, 1)                           # [H, L]
+                A = (be[:, :, None] * (K @ K.transpose(1, 2)) * R).tril(-1)
+                I = torch.eye(L, dtype=dt, device=q.device).expand(H, L, L)
+                U = torch.linalg.solve_triangular(I + A, be[:, :, None] * V, upper=False, unitriangular=True)
+                W = torch.linalg.solve_triangular(I + A, (be * gam)[:, :, None] * K, upper=False,
+                                                  unitriangular=True)
+                Vp = U - W @ S.transpose(1, 2)
+            else:
+                Vp = V
+            O = (gam[:, :, None] * Q) @ S.transpose(1, 2) + ((Q @ K.transpose(1, 2)) * R) @ Vp
+            out[c0:c1] = (scale * O).transpose(0, 1)
+            S = gam[:, -1, None, None] * S + (Vp * R[:, -1, :, None]).transpose(1, 2) @ K
+        finals.append(S)
+    fin = torch.stack(finals) if finals else torch.zeros(0, H, d, d, dtype=dt, device=q.device)
+    return out.view(rows, Hd).to(q.dtype), fin
+
+
 def conv_ref(x, w, bias, segs, ctx=None, ctx_idx=None, silu=True):
     rows, C = x.shape
     W = w.shape[1]
@@ -84,11 +141,11 @@ class _Recurrence(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, g, beta, init_state, segs, scale, delta, init_idx):
         ctx.segs, ctx.scale, ctx.delta, ctx.init_idx = segs, scale, delta, init_idx
-        if not q.is_cuda:
-            o, fin = recurrence_ref(q, k, v, g, beta, segs, scale, delta, init_state, init_idx)
+        if not q.is_cuda or _chunked_on_gpu():
+            o, fin = recurrence_chunked(q, k, v, g, beta, segs, scale, delta, init_state, init_idx)
             ctx.save_for_backward(q, k, v, g, beta, init_state)
             ctx.cpu = True
-            return o, fin
+            return o, fin.to(torch.float64 if q.dtype == torch.float64 else torch.float32)
         ctx.cpu = False
         dev = q.device
         seg_t = _seg_tensor(segs, dev)
@@ -108,7 +165,7 @@ class _Recurrence(torch.autograd.Function):
             with torch.enable_grad():
                 ins = [t.detach().requires_grad_(True) if t is not None else None
                        for t in (q, k, v, g, beta, init_state)]
-                o, fin = recurrence_ref(*ins[:5], ctx.segs, ctx.scale, ctx.delta, ins[5], ctx.init_idx)
+                o, fin = recurrence_chunked(*ins[:5], ctx.segs, ctx.scale, ctx.delta, ins[5], ctx.init_idx)
                 outs, grads = [o], [do]
                 if dfin is not None:
                     outs.append(fin)
@@ -131,6 +188,14 @@ class _Recurrence(torch.autograd.Function):
             ok = ii >= 0
             d_init_state.index_add_(0, ii[ok], dinit[ok])
         return dq, dk, dv, dg, (dbeta if ctx.delta else None), d_init_state, None, None, None, None
+
+
+def _chunked_on_gpu() -> bool:
+    """OCTO_RECURRENCE_CHUNKED=1: CUDA tensors take the chunked tensor-op form (batched GEMMs
+    and triangular solves) instead of the token-serial kernels."""
+    import os
+
+    return os.environ.get("OCTO_RECURRENCE_CHUNKED", "0") == "1"
 
 
 def recurrence(q, k, v, g, beta, segs, scale: float, delta: bool, init_state=None, init_idx=None):

@@ -102,3 +102,67 @@ def test_conv_cuda_matches_reference():
     assert float((y.float().cpu() - yr).abs().max()) < 5e-2
     for a, r in ((x, xr), (w, wr), (b, br), (ctx, cr)):
         assert float((a.grad.float().cpu() - r.grad).abs().max() / r.grad.abs().max()) < 2e-2
+
+
+def _rand(rows, H, d, dtype, seed, decay=0.5):
+    gen = torch.Generator().manual_seed(seed)
+    nq = lambda: torch.nn.functional.normalize(torch.randn(rows, H, d, generator=gen, dtype=dtype), dim=-1)  # noqa
+    q, k = nq().reshape(rows, H * d), nq().reshape(rows, H * d)
+    v = torch.randn(rows, H * d, generator=gen, dtype=dtype)
+    g = -torch.rand(rows, H, generator=gen, dtype=dtype) * decay
+    beta = torch.rand(rows, H, generator=gen, dtype=dtype)
+    init = torch.randn(2, H, d, d, generator=gen, dtype=dtype) * 0.3
+    return q, k, v, g, beta, init
+
+
+@pytest.mark.parametrize("delta", [True, False])
+@pytest.mark.parametrize("chunk", [1, 7, 16, 64])
+def test_chunked_equals_token_serial(delta, chunk):
+    """The chunked (UT-transform) form equals the token-by-token recurrence: outputs, final
+    states and every input gradient (initial states included), over ragged segments."""
+    from octopus_b200.ops.recurrence import recurrence_chunked
+
+    rows, H, d = 150, 2, 8
+    segs = [(0, 1), (1, 63), (64, 65), (129, 21)]
+    idx = [1, -1, 0, 1]
+    base = _rand(rows, H, d, torch.float64, 0)
+    res = []
+    for fn in (recurrence_ref, lambda *a: recurrence_chunked(*a, chunk=chunk)):
+        ins = [t.clone().requires_grad_(True) for t in base]
+        o, fin = fn(*ins[:5], segs, d ** -0.5, delta, ins[5], idx)
+        gen = torch.Generator().manual_seed(1)
+        (o * torch.randn(o.shape, generator=gen, dtype=o.dtype)).sum().backward(retain_graph=True)
+        (fin * 0.37).sum().backward()
+        res.append((o.detach(), fin.detach(), [t.grad for t in ins]))
+    (o1, f1, g1), (o2, f2, g2) = res
+    assert torch.allclose(o1, o2, atol=1e-12) and torch.allclose(f1, f2, atol=1e-12)
+    for a, b in zip(g1, g2):
+        if a is None or b is None:
+            assert a is None or float(a.abs().max()) == 0.0
+            continue
+        assert torch.allclose(a, b, atol=1e-10)
+
+
+def test_chunked_fp32_strong_decay_gradients_finite():
+    """Strong decays (exponents past fp32 range above the diagonal) keep finite gradients."""
+    from octopus_b200.ops.recurrence import recurrence_chunked
+
+    ins = [t.float().requires_grad_(True) for t in _rand(80, 2, 8, torch.float64, 3, decay=40.0)]
+    o, fin = recurrence_chunked(*ins[:5], [(0, 80)], 8 ** -0.5, True, ins[5], [0], chunk=64)
+    (o.sum() + fin.sum()).backward()
+    assert all(torch.isfinite(t.grad).all() for t in ins)
+
+
+@pytest.mark.gpu
+def test_chunked_tensor_ops_on_gpu_match_kernel(monkeypatch):
+    """OCTO_RECURRENCE_CHUNKED=1 on CUDA (tensor ops) against the token-serial sm_100a kernel."""
+    dev = torch.device("cuda", 0)
+    q, k, v, g, b = _inputs(70, 2, 128, torch.bfloat16, seed=5, device=dev)
+    init = torch.randn(1, 2, 128, 128, device=dev) * 0.1
+    segs = [(0, 33), (33, 37)]
+    o1, f1 = recurrence(q, k, v, g, b, segs, 128 ** -0.5, True, init_state=init, init_idx=[0, -1])
+    monkeypatch.setenv("OCTO_RECURRENCE_CHUNKED", "1")
+    o2, f2 = recurrence(q, k, v, g, b, segs, 128 ** -0.5, True, init_state=init, init_idx=[0, -1])
+    torch.cuda.synchronize()
+    rel = lambda a, c: float((a.float() - c.float()).norm() / (c.float().norm() + 1e-12))  # noqa: E731
+    assert rel(o2, o1) < 2e-2 and rel(f2, f1) < 2e-2
