@@ -103,12 +103,15 @@ class HybridWeights:
     """Dense weights (embedding, attention layers, head) in the decoder's flat layout plus
     per-linear-layer tensors in a second flat buffer (fp32 conv taps / gates)."""
 
-    def __init__(self, hc: HybridConfig, device, dtype=torch.bfloat16, seed: int = 0, std: float = 0.02):
+    def __init__(self, hc: HybridConfig, device, dtype=torch.bfloat16, seed: int = 0, std: float = 0.02,
+                 grads: bool = True):
+        """grads=False: frozen / serving weights (no gradient buffers, fp32 parameters without
+        requires_grad)."""
         self.hc = hc
         cfg = hc.base
         self.layout = FlatLayout(cfg)
         grad_dt = torch.float64 if dtype == torch.float64 else torch.float32
-        self.grad = torch.zeros(self.layout.total, dtype=grad_dt, device=device)
+        self.grad = torch.zeros(self.layout.total, dtype=grad_dt, device=device) if grads else None
         self.dense = Weights(cfg, init_flat(cfg, self.layout, device, dtype=dtype, seed=seed, std=std), self.layout,
                              self.grad)
         g = torch.Generator(device="cpu").manual_seed(seed + 11)
@@ -125,14 +128,15 @@ class HybridWeights:
                     if init == "ba":
                         w[2 * hc.lin_heads:] = 0.0
                 w = w.to(dtype).to(device)
-                w.main_grad = torch.zeros(shape, dtype=grad_dt, device=device)
+                if grads:
+                    w.main_grad = torch.zeros(shape, dtype=grad_dt, device=device)
                 self.t[name] = w
             C = hc.lin_width
             pd = torch.float64 if dtype == torch.float64 else torch.float32
             for name, val in ((f"layers.{i}.conv_w", torch.randn(3 * C, hc.conv_width, generator=g) * 0.3),
                               (f"layers.{i}.A_log", torch.log(torch.rand(hc.lin_heads, generator=g) * 15 + 1)),
                               (f"layers.{i}.dt_bias", torch.randn(hc.lin_heads, generator=g) * 0.1)):
-                self.fp32[name] = val.to(pd).to(device).requires_grad_(True)
+                self.fp32[name] = val.to(pd).to(device).requires_grad_(grads)
 
     def layer(self, i):
         return self.dense.layer(i)
@@ -143,14 +147,15 @@ def _rmsnorm_heads(o, w, eps):
     return (of * torch.rsqrt(of.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(o.dtype)
 
 
-def linear_layer_forward(x, hw: HybridWeights, i: int, tree):
+def linear_layer_forward(x, hw: HybridWeights, i: int, tree, lora=None):
     """One linear-recurrence layer over the tree rows x [T, H]; tree: (nodes [n, 4], tails [n, 8])."""
     hc, cfg = hw.hc, hw.hc.base
     t = hw.t
     nodes, tails = tree
     h = ops.rmsnorm(x, t[f"layers.{i}.ln1"], cfg.rms_eps, cfg.norm_plus_one)
-    qkv = ops.linear(h, t[f"layers.{i}.lin_qkv"])
-    z = ops.linear(h, t[f"layers.{i}.lin_z"])
+    la = (lambda name: lora.get(f"layers.{i}.{name}")) if lora is not None else (lambda name: None)
+    qkv = ops.linear(h, t[f"layers.{i}.lin_qkv"], lora=la("lin_qkv"))
+    z = ops.linear(h, t[f"layers.{i}.lin_z"], lora=la("lin_z"))
     ba = ops.linear(h, t[f"layers.{i}.lin_ba"])  # [T, ba_rows]: beta logits | gate inputs | zero padding
     bb, aa = ba[:, :hc.lin_heads], ba[:, hc.lin_heads:2 * hc.lin_heads]
     W = hc.conv_width
@@ -176,10 +181,10 @@ def linear_layer_forward(x, hw: HybridWeights, i: int, tree):
                          d ** -0.5, hc.kind == "gdn")
     o = _rmsnorm_heads(o.view(T, Hh, d), t[f"layers.{i}.lin_norm"], cfg.rms_eps).reshape(T, C)
     o = (o.float() * torch.nn.functional.silu(z.float())).to(x.dtype)
-    x = ops.linear(o, t[f"layers.{i}.lin_out"], None, residual=x)
+    x = ops.linear(o, t[f"layers.{i}.lin_out"], None, residual=x, lora=la("lin_out"))
     h2 = ops.rmsnorm(x, t[f"layers.{i}.ln2"], cfg.rms_eps, cfg.norm_plus_one)
-    act = ops.swiglu(ops.linear(h2, t[f"layers.{i}.gu_w"]))
-    return ops.linear(act, t[f"layers.{i}.down_w"], None, residual=x)
+    act = ops.swiglu(ops.linear(h2, t[f"layers.{i}.gu_w"], lora=la("gu_w")))
+    return ops.linear(act, t[f"layers.{i}.down_w"], None, residual=x, lora=la("down_w"))
 
 
 def _tree_recurrence(q, k, v, g, beta, nodes, scale, delta):
@@ -205,17 +210,19 @@ def _tree_recurrence(q, k, v, g, beta, nodes, scale, delta):
     return out
 
 
-def hybrid_forward(hw: HybridWeights, batch, temperature: float = 1.0):
+def hybrid_forward(hw: HybridWeights, batch, temperature: float = 1.0, lora=None):
     """(logp, entropy) of the scored pairs of a prefix-tree micro-batch (TreeBatch with
-    `nodes` / `path_tail`)."""
+    `nodes` / `path_tail`); lora: models.hybrid_lora.HybridLoRA adapters or None."""
     hc, cfg = hw.hc, hw.hc.base
     tree = (batch.nodes, batch.path_tail)
     x = ops.embed(batch.ids, hw.dense["embed"])
+    if torch.is_grad_enabled() and not x.requires_grad:
+        x.requires_grad_(True)  # a graph even when only adapters (plain tensors with main_grad) train
     for i in range(cfg.layers):
         if hc.is_linear(i):
-            x = linear_layer_forward(x, hw, i, tree)
+            x = linear_layer_forward(x, hw, i, tree, lora)
         else:
-            x = layer_forward(x, hw.layer(i), cfg, batch.pos, batch.plan)
+            x = layer_forward(x, hw.layer(i), cfg, batch.pos, batch.plan, lora.layer(i) if lora is not None else None)
     hf = ops.rmsnorm(x, hw.dense["norm"], cfg.rms_eps, cfg.norm_plus_one)
     hp = hf.index_select(0, batch.pair_rows)
     return ops.logprob_head(hp, hw.dense.head, batch.pair_labels, 1.0 / temperature, cfg.vocab_size)

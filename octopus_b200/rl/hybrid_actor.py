@@ -168,4 +168,108 @@ class HybridActor:
         save_file(tensors, os.path.join(path, "hybrid_linear.safetensors"))
 
 
-__all__ = ["HybridActor"]
+class HybridLoRAActor:
+    """LoRA training of a hybrid model (models.hybrid_lora): the base is frozen (no weight
+    gradients, no master or optimizer state for it); AdamW runs on the adapters' flat fp32
+    master; `hw` is the serving copy (base + s B A) the colocated hybrid engine reads,
+    refreshed after every optimizer step."""
+
+    def __init__(self, hc: HybridConfig, device="cuda", *, r: int = 32, alpha: float = 32.0,
+                 optim: OptimConfig | None = None, ppo: PPOConfig | None = None, seed: int = 0, dtype=torch.bfloat16,
+                 ckpt: bool = True, temperature: float = 1.0):
+        from ..models.hybrid_lora import HybridLoRA
+
+        self.cfg, self.hc = hc.base, hc
+        self.device = torch.device(device)
+        self.optim = optim or OptimConfig()
+        self.ppo = ppo or PPOConfig()
+        self.base = HybridWeights(hc, self.device, dtype=dtype, seed=seed, grads=False)   # frozen
+        self.hw = HybridWeights(hc, self.device, dtype=dtype, seed=seed, grads=False)     # serving copy
+        self.lora = HybridLoRA(hc, r, alpha, self.device, dtype, seed)
+        self.weights = self.hw.dense
+        self.layout = self.hw.layout
+        self.master, self.grad = self.lora.master, self.lora.grad
+        self.exp_avg, self.exp_avg_sq = torch.zeros_like(self.master), torch.zeros_like(self.master)
+        self.step_count = 0
+        self.version = 0
+        self.ckpt = ckpt
+        self.temperature = temperature
+        self.optimizer_merge()
+
+    def set_memory(self, ckpt_block: int = 1, act_gpu_bytes=None, chunk_tokens: int = 0, seq_tile: int = 0):
+        if chunk_tokens:
+            raise ValueError("chunk-major training of hybrid LoRA adapters is not supported")
+
+    def zero_grad(self):
+        self.grad.zero_()
+
+    def reload_master(self):
+        """After loading base weights (HF) into `base`: adapters keep their master."""
+        self.optimizer_merge()
+
+    def optimizer_merge(self):
+        """hw <- base with s B A added to every adapted tensor."""
+        with torch.no_grad():
+            self.hw.dense.flat.copy_(self.base.dense.flat)
+            for k, t in self.base.t.items():
+                self.hw.t[k].copy_(t)
+            for k, p in self.base.fp32.items():
+                self.hw.fp32[k].copy_(p)
+            self.lora.merge_into(self.base, self.hw)
+
+    def forward_backward(self, mbs, denom: float | None = None) -> dict:
+        denom = denom if denom is not None else float(sum(mb.pair_w.sum() for mb in mbs))
+        stats = {}
+        for mb in mbs:
+            d = mb.to_device(self.device)
+            logp, ent = hybrid_forward(self.base, d.batch, self.temperature, lora=self.lora)
+            loss, st = ppo_loss(logp, ent, d.adv, d.w, d.behav, None, denom, self.ppo)
+            loss.backward()
+            for k, v in st.items():
+                stats[k] = stats.get(k, 0.0) + v.detach() * (1.0 if k == "tokens" else float(mb.pair_w.sum()))
+            stats["loss"] = stats.get("loss", 0.0) + loss.detach()
+        stats.setdefault("loss", torch.zeros((), device=self.device))
+        tok = float(sum(mb.pair_w.sum() for mb in mbs)) or 1.0
+        return {k: (v if k in ("tokens", "loss") else v / tok) for k, v in stats.items()}
+
+    def optimizer_step(self) -> torch.Tensor:
+        self.step_count += 1
+        o = self.optim
+        sq = torch.zeros(1, dtype=torch.float32, device=self.device)
+        ops.sqnorm_(self.grad, sq)
+        ops.adamw_(self.master, self.grad, self.exp_avg, self.exp_avg_sq, self.lora.flat16, lr=o.lr, betas=o.betas,
+                   eps=o.eps, weight_decay=o.weight_decay, step=self.step_count, sqnorm=sq, max_norm=o.max_grad_norm)
+        self.optimizer_merge()
+        self.version += 1
+        return sq
+
+    def train_step(self, mbs) -> dict:
+        t0 = time.perf_counter()
+        self.zero_grad()
+        stats = self.forward_backward(mbs)
+        sq = self.optimizer_step()
+        stats["grad_norm"] = sq.sqrt()
+        stats["train_s"] = time.perf_counter() - t0
+        return stats
+
+    def extra_state(self) -> dict:
+        return {}
+
+    def load_extra_state(self, st: dict):
+        """After a recover load (adapter master restored): compute copy and serving weights."""
+        self.lora.refresh_compute()
+        self.optimizer_merge()
+
+    def save_hf(self, path: str):
+        """The merged serving weights (dense HF safetensors + hybrid_linear.safetensors)."""
+        from safetensors.torch import save_file
+
+        from ..models.decoder import save_hf
+
+        save_hf(self.weights, path)
+        tensors = {k: v.detach().cpu().contiguous() for k, v in self.hw.t.items()}
+        tensors.update({k: v.detach().cpu().contiguous() for k, v in self.hw.fp32.items()})
+        save_file(tensors, os.path.join(path, "hybrid_linear.safetensors"))
+
+
+__all__ = ["HybridActor", "HybridLoRAActor"]

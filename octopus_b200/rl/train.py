@@ -67,11 +67,16 @@ def build(cfg, device):
                     reuse_train_logp=a.reuse_train_logp)
     dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
     if hc is not None:
-        if a.lora_rank > 0 or cfg.rollout.tp > 1:
-            raise SystemExit("hybrid presets train full-parameter replicas (no LoRA or rollout TP)")
-        from .hybrid_actor import HybridActor
+        if cfg.rollout.tp > 1:
+            raise SystemExit("hybrid presets: no rollout TP")
+        from .hybrid_actor import HybridActor, HybridLoRAActor
 
-        actor = HybridActor(hc, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype, ckpt=a.gradient_checkpointing)
+        if a.lora_rank > 0:
+            actor = HybridLoRAActor(hc, device, r=a.lora_rank, alpha=a.lora_alpha, optim=optim, ppo=ppo, seed=cfg.seed,
+                                    dtype=dtype, ckpt=a.gradient_checkpointing)
+        else:
+            actor = HybridActor(hc, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype,
+                                ckpt=a.gradient_checkpointing)
         if world > 1:  # replicated data parallelism: one all-reduce of every gradient per step
             from ..parallel.dp import DataParallel
 
@@ -98,7 +103,8 @@ def build(cfg, device):
     actor.set_memory(a.ckpt_block, int(a.act_gpu_gb * (1 << 30)) if a.act_gpu_gb >= 0 else None,
                      chunk_tokens=chunk_tokens, seq_tile=a.seq_tile)
     if cfg.model.path:
-        load_hf(getattr(actor, "base", actor.weights), cfg.model.path)
+        base = getattr(actor, "base", actor.weights)
+        load_hf(base.dense if hc is not None and hasattr(base, "dense") else base, cfg.model.path)
         if hc is not None:
             _load_hybrid_linear(actor, cfg.model.path)
         actor.reload_master()
@@ -210,8 +216,9 @@ def _load_hybrid_linear(actor, path):
     st = load_file(f)
     import torch
 
+    hw = actor.base if hasattr(actor, "lora") else actor.hw  # LoRA: the frozen base
     with torch.no_grad():
-        for k, t in list(actor.hw.t.items()) + list(actor.hw.fp32.items()):
+        for k, t in list(hw.t.items()) + list(hw.fp32.items()):
             t.copy_(st[k].to(t.dtype))
 
 

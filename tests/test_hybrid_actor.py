@@ -201,3 +201,48 @@ def test_hybrid_data_parallel_matches_one_process():
             assert np.allclose(lin[k], t.numpy(), rtol=1e-9, atol=1e-12), k
         for k, p in ref.hw.fp32.items():
             assert np.allclose(fp[k], p.detach().numpy(), rtol=1e-9, atol=1e-12), k
+
+
+def test_hybrid_lora_actor():
+    """Hybrid LoRA: only the adapters train (the frozen base has no gradient buffers), the
+    serving copy equals base + s B A, and the hybrid forward on the serving copy equals the
+    base forward with the adapters; the trainer CLI runs a LoRA step on the hybrid preset."""
+    from octopus_b200.rl.hybrid_actor import HybridLoRAActor
+
+    hc = HybridConfig(get_config("tiny", layers=4, vocab_size=512), kind="gdn", pattern="LLAL", lin_heads=2,
+                      lin_dim=32)
+    act = HybridLoRAActor(hc, "cpu", r=4, alpha=8.0, optim=OptimConfig(lr=1e-2), dtype=torch.float64, seed=1)
+    assert act.base.grad is None and not any(hasattr(t, "main_grad") for t in act.base.t.values())
+    base0 = act.base.dense.flat.clone()
+    assert torch.equal(act.hw.dense.flat, base0)  # B = 0: serving = base
+    act.train_step([_mb()])
+    assert torch.equal(act.base.dense.flat, base0) and float(act.lora.grad.abs().sum()) > 0
+    name = "layers.0.lin_qkv"
+    A, B = act.lora.t[f"{name}.A"], act.lora.t[f"{name}.B"]
+    assert float(B.abs().sum()) > 0
+    assert torch.allclose(act.hw.t[name], act.base.t[name] + act.lora.scale * (B @ A), atol=1e-12)
+    mb = _mb(7).to_device("cpu")
+    with torch.no_grad():
+        lp_serve, _ = hybrid_forward(act.hw, mb.batch)
+        lp_lora, _ = hybrid_forward(act.base, mb.batch, lora=act.lora)
+    assert torch.allclose(lp_serve, lp_lora, atol=1e-9)
+
+
+def test_train_cli_hybrid_lora(tmp_path, monkeypatch):
+    from octopus_b200.envs import dag
+    from octopus_b200.rl import train
+
+    orig = dag.DagConfig.__init__
+
+    def small(self, *a, **kw):
+        orig(self, *a, **kw)
+        self.prefix_len, self.turn_len, self.role_len = 32, 8, 4
+
+    monkeypatch.setattr(dag.DagConfig, "__init__", small)
+    args = ["--cpu", "model.preset=tiny-hybrid", "rl.kind=dag", "rl.batch_size=2", "rl.n_samples=2",
+            "rollout.kv_gb=0.05", "rollout.max_batch=16", "actor.mb_tokens=65536", "actor.lora_rank=8",
+            f"checkpoint.dir={tmp_path}", "checkpoint.save_every=1", "total_steps=1"]
+    assert train.main(args) == 0
+    assert train.main(args[:-1] + ["total_steps=2"]) == 0
+    rows = [json.loads(x) for x in open(tmp_path / "octopus-b200" / "run0" / "steps.jsonl")]
+    assert [r["step"] for r in rows] == [1, 2]
