@@ -246,3 +246,22 @@ def test_train_cli_hybrid_lora(tmp_path, monkeypatch):
     assert train.main(args[:-1] + ["total_steps=2"]) == 0
     rows = [json.loads(x) for x in open(tmp_path / "octopus-b200" / "run0" / "steps.jsonl")]
     assert [r["step"] for r in rows] == [1, 2]
+
+
+@__import__("pytest").mark.gpu
+def test_hybrid_lora_actor_gpu_step():
+    """One hybrid LoRA step on the sm_100a kernels (r = 8): the adapters move, the serving copy
+    changes, the engine generates from it."""
+    from octopus_b200.rl.hybrid_actor import HybridLoRAActor
+
+    dev = torch.device("cuda", 0)
+    act = HybridLoRAActor(hybrid_config("hybrid-7b", layers=4), dev, r=8, alpha=16.0, optim=OptimConfig(lr=1e-3),
+                          seed=2)
+    eng = HybridEngine(act.hw, kv_slots=1 << 14, max_batch=8, device=dev)
+    s0 = act.hw.t["layers.0.lin_qkv"].clone()
+    st = act.train_step([_mb(4, V=50000)])
+    torch.cuda.synchronize()
+    assert torch.isfinite(st["loss"]) and float(st["grad_norm"]) > 0
+    assert not torch.equal(act.hw.t["layers.0.lin_qkv"], s0)
+    o = eng.generate([GenInput(list(range(100, 140)), max_new_tokens=4, keep_cursor=False)])[0]
+    assert len(o.output_ids) == 4 and np.isfinite(o.output_logprobs).all()
