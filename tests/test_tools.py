@@ -80,3 +80,29 @@ def test_rollout_and_mount_load_run_on_the_engine():
     rows = [json.loads(x) for x in buf.getvalue().splitlines()]
     assert st["pairs"] == 2 and st["reads"] > 0 and st["mounted_tokens"] > 0 and st["not_found"] == 0
     assert any(r["kind"] == "read" and r["mounted"] > 0 for r in rows)
+
+
+def test_prefix_flops_rules(tmp_path):
+    """Analytic prefix-reuse FLOPs: a thread reuses its previous request, a branch its parent's
+    latest, main's first nothing; the saving is 1 - reuse / no-reuse; logs are read from
+    episode directories; hybrid presets count attention layers only in the quadratic term."""
+    import json
+
+    from octopus_b200.tools.prefix_flops import episode_flops, model_constants, run
+
+    reqs = [{"thread": "main", "prompt_tokens": 100, "completion_tokens": 10},
+            {"thread": "fork0/branch-0", "prompt_tokens": 130, "completion_tokens": 5},
+            {"thread": "main", "prompt_tokens": 150, "completion_tokens": 20}]
+    r = episode_flops(reqs, 1.0, 0.0)
+    # reuse: main 100+10, branch (130-110)+5, main (150-110)+20 ; none: 110 + 135 + 170
+    assert r["flops_reuse"] == 110 + 25 + 60 and r["flops_no_reuse"] == 110 + 135 + 170
+    q = episode_flops(reqs[:1], 0.0, 1.0)
+    assert q["flops_reuse"] == 100 * 100 / 2 + 10 * 100 + 10 * 10 / 2
+    d = tmp_path / "ep"
+    d.mkdir()
+    (d / "requests.jsonl").write_text("".join(json.dumps(x) + "\n" for x in reqs))
+    tot = run([str(tmp_path)], "tiny")
+    assert tot["episodes"] == 1 and 0 < tot["saving"] < 1
+    ct_d, ca_d = model_constants("tiny")
+    ct_h, ca_h = model_constants("tiny-hybrid")
+    assert ca_d > 0 and ca_h == 0 and ct_h > 0  # tiny-hybrid's two layers are both linear (pattern LLLA)
