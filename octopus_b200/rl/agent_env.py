@@ -84,6 +84,9 @@ class AgentEnv:
             y = res["y"] if "y" in res else float(self.grade(self.tasks[ti], tree.get("answer")))
             ep = {"y": y, "requests": res["requests"],
                   "branches": branches, "task": ti}
+            ctl = tree.get("control")
+            if ctl and "answer" in ctl and not self.grade_workspace:  # the main-first control's grade
+                ep["control_y"] = float(self.grade(self.tasks[ti], ctl["answer"]))
             groups.setdefault(ti, []).append(ep)
             out.episodes.append(ep)
             out.rewards.append(ep["y"])

@@ -169,10 +169,14 @@ def plan_group_stats(episodes: list[dict]) -> dict:
         return round(sum(xs) / len(xs), 4) if xs else None
 
     rows = [b for e in episodes for b in e.get("branches") or []]
+    ctl = [e for e in episodes if e.get("control_y") is not None]
     return {"abs_A_main": mean([abs(e["A_main"]) for e in episodes]),
             "abs_A_branch": mean([abs(b["A_branch"]) for b in rows]),
             "y": mean([float(e["y"]) for e in episodes]),
-            "forked": mean([float(bool(e.get("forked"))) for e in episodes])}
+            "forked": mean([float(bool(e.get("forked"))) for e in episodes]),
+            # fork vs its main-first control (OCTOPUS_PLAN_CONTROL): y - y_control
+            "fork_minus_control": mean([float(e["y"]) - float(e["control_y"]) for e in ctl]),
+            "controls": len(ctl)}
 
 
 def has_variance(rewards: list[float]) -> bool:

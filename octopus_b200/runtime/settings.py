@@ -120,6 +120,12 @@ def conflict_by() -> bool:
     return _flag("OCTOPUS_CONFLICT_BY")
 
 
+def plan_control() -> bool:
+    """OCTOPUS_PLAN_CONTROL=1: after a forking episode, a no-fork continuation of main from just
+    before its first fork (the main-first control) is run and graded."""
+    return bool(os.environ.get("OCTOPUS_PLAN_CONTROL"))
+
+
 def read_control() -> bool:
     """OCTOPUS_READ_CONTROL=1: a read's no-mount counterfactual continuation is graded."""
     return _flag("OCTOPUS_READ_CONTROL")

@@ -167,8 +167,12 @@ class CursorRuntime:
     async def _thread_tool(self, thread: str, port: RuntimePort, forks_this_turn: list, name: str, args: dict):
         depth = self.depth(thread)
         if name == "fork":
+            if thread == "control":  # the control runs without forks
+                return FORK_DEPTH_REFUSAL, False
             if forks_this_turn:
                 return ONE_FORK, False
+            if thread == "main" and getattr(self, "_control_snap", None) is None and S.plan_control():
+                self._control_snap = await self.ws.snapshot("main")  # main's workspace at its first fork
             if depth + 1 > S.fork_depth() - 1 + 1 and depth >= S.fork_depth():
                 return FORK_DEPTH_REFUSAL, False
             if depth >= S.fork_depth():
@@ -300,15 +304,48 @@ class CursorRuntime:
         start = {"branch_id": "main", "session_id": self.session_id, "task": task,
                  "messages": [{"role": "system", "content": self.ws.system_prompt(task)},
                               {"role": "user", "content": task}]}
+        self._control_snap = None
         res = await self._run_thread("main", start, 0)
         tree = {"task": task, "tools": self.tool_list("main"), "forks": self.forks.get("main", []),
                 "main_end": self._main_end(res["steps"]),
                 "answer": handed(closing_step(res["steps"])), "requests": len(self.requests),
                 "budget": self.ws.budget(), "used": self.used, "reminded": res["reminded"]}
+        if S.plan_control() and tree["forks"]:
+            tree["control"] = await self._control(task, res)
         if self.log_dir:
             self._write(tree, res)
         await self.ws.close()
         return {"tree": tree, "main": res, "requests": self.requests}
+
+    async def _control(self, task: str, main_res: dict) -> dict:
+        """The main-first control: main's history up to (not including) its first forking
+        reply, continued without forks (fork is refused) in a copy of main's workspace at that
+        point, with the calls main had left; closed by done like main.  Its requests are
+        logged under thread "control" (never trained); the record gives its answer."""
+        msgs = main_res["messages"]
+        pl = int(self.forks["main"][0].get("prefix_len", len(msgs)))
+        idx = max((i for i in range(min(pl, len(msgs))) if msgs[i].get("role") == "assistant"), default=None)
+        if idx is None:
+            return {"kind": "main-first", "error": "no forking reply"}
+        ctrl = [dict(m) for m in msgs[:idx]]
+        calls_before = sum(1 for m in ctrl if m.get("role") == "assistant")
+        try:
+            await self.ws.copy("main", "control")
+            if self._control_snap is not None:
+                await self.ws.restore("control", self._control_snap)
+        except BranchCopyError as e:
+            return {"kind": "main-first", "error": f"copy failed: {e}"}
+        saved = self.max_main_calls
+        if saved is not None:
+            self.max_main_calls = max(1, saved - calls_before)
+        start = {"branch_id": "control", "session_id": f"{self.session_id}/control", "task": task, "messages": ctrl}
+        n0 = len(self.requests)
+        try:
+            res = await self._run_thread("control", start, 0)
+        finally:
+            self.max_main_calls = saved
+        return {"kind": "main-first", "calls_before": calls_before, "answer": handed(closing_step(res["steps"])),
+                "main_end": self._main_end(res["steps"]), "requests": len(self.requests) - n0}
 
     def _main_end(self, steps: list) -> str:
         if any(s.get("name") == "done" and not s.get("rejected") for s in steps):

@@ -148,3 +148,33 @@ def test_fork_task_list_lenient():
     assert core.fork_task_list('["x",\n "y"] trailing') == ["x", "y"]
     msg, _ = core.apply_runtime("fork", {"tasks": ["only one"]})
     assert msg.startswith("fork needs at least two")
+
+
+def test_main_first_control_run(monkeypatch):
+    """OCTOPUS_PLAN_CONTROL=1: after a forking episode, main's history up to its forking reply
+    continues without forks (fork is refused) as thread "control", closed by done; its
+    requests are logged under "control" and the tree records its answer."""
+    monkeypatch.setenv("OCTOPUS_PLAN_CONTROL", "1")
+    chat = Scripted({
+        "control": [("try fork", [call("fork", tasks=["a", "b"])]), ("alone", [call("done", answer="c-ans")])],
+        "branch-0": [("", [call("commit", branch_id="branch-0", summary="s0")])],
+        "branch-1": [("", [call("commit", branch_id="branch-1", summary="s1")])],
+        "ep": [("look", [call("note", text="x")]), ("split", [call("fork", tasks=["a", "b"])]),
+               ("end", [call("done", answer="fork-ans")])],
+    })
+    out = run_episode(WorkspaceProvider(), chat, "t")
+    tree = out["tree"]
+    assert tree["answer"] == "fork-ans" and tree["control"]["answer"] == "c-ans"
+    assert tree["control"]["kind"] == "main-first" and tree["control"]["calls_before"] == 1
+    ctl = [b for b in chat.bodies if b["session_id"].endswith("control")]
+    assert len(ctl) == 2 and all(m.get("content") != "split" for m in ctl[0]["messages"])
+    assert [r["thread"] for r in out["requests"]].count("control") == 2
+
+
+def test_group_stats_fork_minus_control():
+    from octopus_b200.rl.group import plan_group_stats
+
+    eps = [{"y": 1.0, "A_main": 0.5, "control_y": 0.0, "branches": []},
+           {"y": 0.0, "A_main": -0.5, "control_y": 0.0, "branches": []}, {"y": 1.0, "A_main": 0.5, "branches": []}]
+    st = plan_group_stats(eps)
+    assert st["fork_minus_control"] == 0.5 and st["controls"] == 2
