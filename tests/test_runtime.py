@@ -178,3 +178,25 @@ def test_group_stats_fork_minus_control():
            {"y": 0.0, "A_main": -0.5, "control_y": 0.0, "branches": []}, {"y": 1.0, "A_main": 0.5, "branches": []}]
     st = plan_group_stats(eps)
     assert st["fork_minus_control"] == 0.5 and st["controls"] == 2
+
+
+def test_fork_wall_from_logs(tmp_path, monkeypatch):
+    """fork_wall: a logged forking episode with its control gives one pair; the fork's cost is
+    its critical path, the control's its own requests plus main's before the fork."""
+    import json
+
+    from octopus_b200.tools.fork_wall import run
+
+    monkeypatch.setenv("OCTOPUS_PLAN_CONTROL", "1")
+    chat = Scripted({
+        "control": [("alone", [call("done", answer="c")])],
+        "branch-0": [("", [call("commit", branch_id="branch-0", summary="s0")])],
+        "branch-1": [("", [call("commit", branch_id="branch-1", summary="s1")])],
+        "ep": [("split", [call("fork", tasks=["a", "b"])]), ("end", [call("done", answer="f")])],
+    })
+    run_episode(WorkspaceProvider(), chat, "t", log_dir=str(tmp_path / "ep"))
+    (tmp_path / "ep" / "result.json").write_text(json.dumps({"reward": 1.0, "control_reward": 0.0}))
+    out = run([str(tmp_path)], "tokens")
+    # fork: main 2 replies + the longest branch (1 reply) = 3 x 20 tokens; control: 0 before + 1 reply
+    assert out["pairs"] == 1 and out["ratio_median"] == 3.0 and out["fork_cheaper"] == 0.0
+    assert out["gain"] == 1.0 and out["gain_when_not"] == 1.0
