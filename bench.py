@@ -33,7 +33,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "RL step tokens/sec/box (rollout+train+sync), 7B-shape multi-agent, 1/2/4/8 B200"
-BASELINE_VALUE = None  # BASELINE.md publishes no tokens/sec figure for this metric
+BASELINE_VALUE = None  # the reference publishes no tokens/sec figure for this metric
 
 
 def parse():

@@ -239,7 +239,7 @@ def report(items_path, labels_path, out=print) -> int:
             tot = max(1, sum(c.values()))
             out(f"  {ck} {cond}: " + " ".join(f"{k} {c[k] / tot:.2f}" for k in LABELS if c[k]))
     if bad:
-        out(f"\nNO VERDICT: {sum(bad.values())} samples have no valid label; rerun judge")
+        out(f"\nNO DECISION: {sum(bad.values())} samples have no valid label; rerun judge")
         return 1
     out("\ndecision (hijack):")
     hj = score["hijack"]
