@@ -804,11 +804,8 @@ static int dec_smem() {
 
 template <int D>
 static void fwd_impl(const AttnParams& p, int n_tiles, cudaStream_t st) {
-  static bool cfg = false;
-  if (!cfg) {
-    cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, fwd_smem<D>());
-    cfg = true;
-  }
+  static SmemOptIn opt;
+  opt.ensure(attn_fwd_kernel<D>, fwd_smem<D>());
   attn_fwd_kernel<D><<<dim3(n_tiles, p.Hq), 256, fwd_smem<D>(), st>>>(p);
 }
 
@@ -820,12 +817,9 @@ void attn_fwd(const AttnParams& p, int n_tiles, int D, cudaStream_t st) {
 
 template <int D>
 static void bwd_impl(const AttnBwdParams& p, int n_qtiles, int n_ktiles, cudaStream_t st) {
-  static bool cfg = false;
-  if (!cfg) {
-    cudaFuncSetAttribute(attn_bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, dq_smem<D>());
-    cudaFuncSetAttribute(attn_bwd_dkv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, dkv_smem<D>());
-    cfg = true;
-  }
+  static SmemOptIn opt_dq, opt_dkv;
+  opt_dq.ensure(attn_bwd_dq_kernel<D>, dq_smem<D>());
+  opt_dkv.ensure(attn_bwd_dkv_kernel<D>, dkv_smem<D>());
   if (n_qtiles > 0) attn_bwd_dq_kernel<D><<<dim3(n_qtiles, p.Hq), 128, dq_smem<D>(), st>>>(p);
   if (n_ktiles > 0) attn_bwd_dkv_kernel<D><<<dim3(n_ktiles, p.Hkv), 128, dkv_smem<D>(), st>>>(p);
 }
@@ -842,21 +836,30 @@ void attn_bwd(const AttnBwdParams& p, int n_qtiles, int n_ktiles, int D, cudaStr
   else bwd_impl<64>(p, n_qtiles, n_ktiles, st);
 }
 
+// Launches through cudaLaunchKernelEx so that the returned code is this call's own
+// (an error left pending by unrelated earlier work is neither reported nor cleared).
 template <int D>
-static void dec_impl(const DecodeParams& p, int B, cudaStream_t st) {
-  static bool cfg = false;
-  if (!cfg) {
-    cudaFuncSetAttribute(attn_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, dec_smem<D>());
-    cfg = true;
-  }
-  attn_decode_kernel<D><<<dim3(B, p.Hkv, p.num_splits), 128, dec_smem<D>(), st>>>(p);
-  if (p.num_splits > 1) attn_decode_combine_kernel<<<dim3(B, p.Hq), 128, 0, st>>>(p, D);
+static cudaError_t dec_impl(const DecodeParams& p, int B, cudaStream_t st) {
+  static SmemOptIn opt;
+  cudaError_t e = opt.ensure(attn_decode_kernel<D>, dec_smem<D>());
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(B, p.Hkv, p.num_splits);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = dec_smem<D>();
+  cfg.stream = st;
+  e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<D>, p);
+  if (e != cudaSuccess || p.num_splits <= 1) return e;
+  cudaLaunchConfig_t cc{};
+  cc.gridDim = dim3(B, p.Hq);
+  cc.blockDim = dim3(128);
+  cc.stream = st;
+  return cudaLaunchKernelEx(&cc, attn_decode_combine_kernel, p, D);
 }
 
-void attn_decode(const DecodeParams& p, int B, int D, cudaStream_t st) {
-  if (B == 0) return;
-  if (D == 128) dec_impl<128>(p, B, st);
-  else dec_impl<64>(p, B, st);
+cudaError_t attn_decode(const DecodeParams& p, int B, int D, cudaStream_t st) {
+  if (B == 0) return cudaSuccess;
+  return D == 128 ? dec_impl<128>(p, B, st) : dec_impl<64>(p, B, st);
 }
 
 }  // namespace octo

@@ -66,7 +66,7 @@ void attn_fwd(const AttnParams& p, int n_tiles, int D, cudaStream_t st);
 void attn_bwd_delta(const __nv_bfloat16* o, int ldo, const __nv_bfloat16* dO, int lddo, float* delta, int Tq, int Hq,
                     int D, cudaStream_t st);
 void attn_bwd(const AttnBwdParams& p, int n_qtiles, int n_ktiles, int D, cudaStream_t st);
-void attn_decode(const DecodeParams& p, int B, int D, cudaStream_t st);
+cudaError_t attn_decode(const DecodeParams& p, int B, int D, cudaStream_t st);  // this call's launch error
 // tcgen05/TMEM forward (head_dim 128), same contract as attn_fwd with 128-row query tiles
 void attn_fwd_tc(const AttnParams& p, int n_tiles, int* status, cudaStream_t st);
 

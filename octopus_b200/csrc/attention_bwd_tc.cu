@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           t_last = globaltimer_ns();
         } else if (*abort_flag) {
           ok = false;
-        } else if (globaltimer_ns() - t_last > OCTO_WAIT_NS) {
+        } else if (globaltimer_ns() - t_last > wait_budget_ns(status)) {
           *abort_flag = 1;
           record_error(status, kErrMbarTimeout, 930);
           ok = false;
@@ -576,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           t_last = globaltimer_ns();
         } else if (*abort_flag) {
           ok = false;
-        } else if (globaltimer_ns() - t_last > OCTO_WAIT_NS) {
+        } else if (globaltimer_ns() - t_last > wait_budget_ns(status)) {
           *abort_flag = 1;
           record_error(status, kErrMbarTimeout, 980);
           ok = false;
@@ -670,14 +670,9 @@ int attn_bwd_dkv_tc_smem_bytes() { return 2 * kTile + 2 * kQStages * kTile64 + 2
 
 void attn_bwd_tc(const AttnBwdParams& p, const AttnBwdMaps& maps, int n_qtiles, int n_ktiles, int* status,
                  cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         attn_bwd_dq_tc_smem_bytes());
-    cudaFuncSetAttribute(attn_bwd_dkv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         attn_bwd_dkv_tc_smem_bytes());
-    configured = true;
-  }
+  static SmemOptIn opt_dq, opt_dkv;
+  opt_dq.ensure(attn_bwd_dq_tc_kernel, attn_bwd_dq_tc_smem_bytes());
+  opt_dkv.ensure(attn_bwd_dkv_tc_kernel, attn_bwd_dkv_tc_smem_bytes());
   if (n_qtiles > 0)
     attn_bwd_dq_tc_kernel<<<n_qtiles * p.Hq, kThreads, attn_bwd_dq_tc_smem_bytes(), st>>>(maps, p, status);
   if (n_ktiles > 0)

@@ -299,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           t_last = globaltimer_ns();
         } else if (*abort_flag) {
           ok = false;
-        } else if (globaltimer_ns() - t_last > OCTO_WAIT_NS) {
+        } else if (globaltimer_ns() - t_last > wait_budget_ns(status)) {
           *abort_flag = 1;
           record_error(status, kErrMbarTimeout, 830);
           ok = false;
@@ -446,11 +446,8 @@ int attn_fwd_pp_smem_bytes() { return (2 + 2 * kStages) * kTile + 1024 + 256; }
 
 void attn_fwd_pp(const AttnParams& p, const AttnMaps& maps, int n_tiles, int* status, cudaStream_t st) {
   if (n_tiles == 0) return;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attn_fwd_pp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_fwd_pp_smem_bytes());
-    configured = true;
-  }
+  static SmemOptIn opt;
+  opt.ensure(attn_fwd_pp_kernel, attn_fwd_pp_smem_bytes());
   attn_fwd_pp_kernel<<<n_tiles * p.Hq, kThreads, attn_fwd_pp_smem_bytes(), st>>>(maps, p, status);
 }
 

@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_tc_kernel(AttnParams p, 
           t_last = globaltimer_ns();
         } else if (*abort_flag) {
           ok = false;
-        } else if (globaltimer_ns() - t_last > OCTO_WAIT_NS) {
+        } else if (globaltimer_ns() - t_last > wait_budget_ns(status)) {
           *abort_flag = 1;
           record_error(status, kErrMbarTimeout, 610);
           ok = false;
@@ -377,11 +377,8 @@ int attn_fwd_tc_smem_bytes() { return (1 + 2 * kStages) * kTileBytes + 1024 + 25
 
 void attn_fwd_tc(const AttnParams& p, int n_tiles, int* status, cudaStream_t st) {
   if (n_tiles == 0) return;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_fwd_tc_smem_bytes());
-    configured = true;
-  }
+  static SmemOptIn opt;
+  opt.ensure(attn_fwd_tc_kernel, attn_fwd_tc_smem_bytes());
   attn_fwd_tc_kernel<<<dim3(n_tiles, p.Hq), kThreads, attn_fwd_tc_smem_bytes(), st>>>(p, status);
 }
 

@@ -138,9 +138,10 @@ __global__ void peer_barrier_kernel(PeerPtrs flags, int world, int me, int seq, 
     __threadfence_system();
     volatile int* mine = const_cast<volatile int*>(static_cast<const volatile int*>(flags.p[me]));
     const uint64_t t0 = globaltimer_ns();
+    const uint64_t budget = wait_budget_ns(status);
     for (int r = 0; r < world; ++r) {
       while (mine[r] < seq) {
-        if (globaltimer_ns() - t0 > OCTO_WAIT_NS) {
+        if (globaltimer_ns() - t0 > budget) {
           record_error(status, kErrPeerTimeout, 900 + r);
           return;
         }

@@ -11,6 +11,7 @@
 // everywhere (a per-CTA abort flag in shared memory), releases TMEM and returns, so
 // the context stays usable and the host can report the failure.
 #pragma once
+#include <atomic>
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -32,6 +33,11 @@ enum StatusCode : int {
 #define OCTO_WAIT_NS 2000000000ull
 #endif
 
+// Status word layout (int32[4] per device): [0] error code, [1] site of the first
+// error, [2] runtime wait budget in microseconds (0 = OCTO_WAIT_NS), [3] the index a
+// bounds check rejected (debug builds).
+constexpr int kStatusWords = 4;
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -48,6 +54,49 @@ __device__ __forceinline__ void record_error(int* status, int code, int where) {
     atomicCAS(status + 1, 0, where);
   }
 }
+
+// Budget of one primary wait: the runtime value in status[2] (microseconds) when the
+// host set one, else OCTO_WAIT_NS.  Drain waits after a timeout keep OCTO_WAIT_NS.
+__device__ __forceinline__ uint64_t wait_budget_ns(const int* status) {
+  if (status != nullptr) {
+    const int us = *reinterpret_cast<const volatile int*>(status + 2);
+    if (us > 0) return static_cast<uint64_t>(us) * 1000ull;
+  }
+  return OCTO_WAIT_NS;
+}
+
+// Bounds check of an index read from a caller's table (token ids, KV slot ids): true if
+// 0 <= i < n; else records kErrBadIndex with the site and the offending index (first
+// error wins) and the caller skips the access, so a bad table entry never becomes an
+// out-of-bounds load or store.  One compare per row: always on.
+__device__ __forceinline__ bool index_ok(long long i, long long n, int* status, int where) {
+  if (i >= 0 && i < n) return true;
+  if (status != nullptr && atomicCAS(status, 0, kErrBadIndex) == 0) {
+    status[1] = where;
+    status[3] = static_cast<int>(i);
+  }
+  return false;
+}
+
+// ---------------------------------------------------------------- host: kernel attributes
+// A kernel's max-dynamic-shared-memory attribute belongs to its instance in the CURRENT
+// device's context, so a process that launches on several devices must set it on each.
+// One SmemOptIn per kernel instantiation (a function-local static) remembers the devices
+// it has configured (bit per device ordinal < 64; larger ordinals are set on every call).
+struct SmemOptIn {
+  std::atomic<unsigned long long> done{0ull};
+  template <class Kernel>
+  cudaError_t ensure(Kernel* kern, int bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+    if (bit != 0ull && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit != 0ull) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+  }
+};
 
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -105,7 +154,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (((++n) & 63u) == 0u) {
-      if (globaltimer_ns() - t0 > OCTO_WAIT_NS) {
+      if (globaltimer_ns() - t0 > wait_budget_ns(status)) {
         *abort_flag = 1;
         record_error(status, kErrMbarTimeout, where);
         return false;

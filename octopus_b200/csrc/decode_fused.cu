@@ -94,7 +94,7 @@ __global__ void splitk_finish_qkv_kernel(const float* __restrict__ ws, int split
                                          const bf16* __restrict__ bias, const int32_t* __restrict__ pos,
                                          float log2_theta, bf16* __restrict__ q, int ldq,
                                          const int64_t* __restrict__ slots, bf16* __restrict__ kc,
-                                         bf16* __restrict__ vc) {
+                                         bf16* __restrict__ vc, long long n_slots, int* status) {
   grid_dep_launch();
   const int row = blockIdx.x;
   const int half = D / 2, per_head = half / 8;
@@ -140,7 +140,7 @@ __global__ void splitk_finish_qkv_kernel(const float* __restrict__ ws, int split
     return;
   }
   const int64_t slot = slots[row];
-  if (slot < 0) return;
+  if (slot < 0 || !index_ok(slot, n_slots, status, 720)) return;  // negative: not written
   const bool is_k = hd < Hq + Hkv;
   const int kh = is_k ? hd - Hq : hd - Hq - Hkv;
   bf16* dst = (is_k ? kc : vc) + slot * static_cast<int64_t>(Hkv) * D + static_cast<size_t>(kh) * D;
@@ -158,11 +158,11 @@ void splitk_finish_norm(const float* ws, int splits, int M, int N, const bf16* b
 
 void splitk_finish_qkv(const float* ws, int splits, int M, int Hq, int Hkv, int D, const bf16* bias,
                        const int32_t* pos, float theta, bf16* q, int ldq, const int64_t* slots, bf16* kc, bf16* vc,
-                       cudaStream_t st) {
+                       long long n_slots, int* status, cudaStream_t st) {
   if (M == 0) return;
   const int threads = ((Hq + 2 * Hkv) * (D / 16) + 31) / 32 * 32;
   splitk_finish_qkv_kernel<<<M, threads, 0, st>>>(ws, splits, M, Hq, Hkv, D, bias, pos, log2f(theta), q, ldq, slots,
-                                                  kc, vc);
+                                                  kc, vc, n_slots, status);
 }
 
 }  // namespace octo

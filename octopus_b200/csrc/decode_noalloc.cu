@@ -9,6 +9,7 @@
 // is current, and caches them per device.  The kernels are the regular decode kernels
 // of attention.cu, launched through the same host launcher with these addresses as
 // their scratch pointers.
+#include <cstdint>
 #include <cstdio>
 #include <mutex>
 
@@ -77,6 +78,21 @@ extern "C" __attribute__((visibility("default"))) int octo_decode_attention_noal
                  floats, OCTO_NOALLOC_MAX_PARTIAL_FLOATS, rows, OCTO_NOALLOC_MAX_PARTIAL_ROWS);
     return OCTO_NOALLOC_ERR_TOO_LARGE;
   }
+  // The kernel reads K/V rows with 16-byte copies and q / writes o two bf16 at a time:
+  // misaligned pointers or strides would fault on the GPU, so they are refused here.
+  const auto addr = [](const void* p) { return reinterpret_cast<uintptr_t>(p); };
+  const int row = Hq * head_dim;
+  if ((addr(k_cache) | addr(v_cache)) % 16 != 0 || (addr(q) | addr(o)) % 4 != 0 ||
+      (addr(kv_start) | addr(kv_len) | addr(kv_indices)) % 4 != 0 || ldq < row || ldo < row || ldq % 2 != 0 ||
+      ldo % 2 != 0 || q == nullptr || o == nullptr || k_cache == nullptr || v_cache == nullptr ||
+      kv_start == nullptr || kv_len == nullptr || kv_indices == nullptr) {
+    std::fprintf(stderr,
+                 "octo_decode_attention_noalloc: bad pointers or strides (k/v caches must be 16-byte aligned, q, o "
+                 "and the int32 tables 4-byte aligned and non-null, ldq / ldo even and >= Hq * head_dim = %d; got "
+                 "ldq %d, ldo %d)\n",
+                 row, ldq, ldo);
+    return OCTO_NOALLOC_ERR_UNSUPPORTED;
+  }
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return OCTO_NOALLOC_ERR_SETUP;
   float* part_o = nullptr;
@@ -100,8 +116,9 @@ extern "C" __attribute__((visibility("default"))) int octo_decode_attention_noal
   p.Hkv = Hkv;
   p.num_splits = num_splits;
   p.scale = scale;
-  octo::attn_decode(p, B, head_dim, stream);
-  const cudaError_t e = cudaGetLastError();
+  // the launcher returns the error of its own launches only (an unrelated pending error is
+  // left for its owner to see)
+  const cudaError_t e = octo::attn_decode(p, B, head_dim, stream);
   if (e != cudaSuccess) {
     std::fprintf(stderr, "octo_decode_attention_noalloc: launch failed: %s\n", cudaGetErrorString(e));
     return OCTO_NOALLOC_ERR_LAUNCH;

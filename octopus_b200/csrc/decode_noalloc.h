@@ -41,7 +41,8 @@
 
 #define OCTO_NOALLOC_OK 0
 #define OCTO_NOALLOC_ERR_TOO_LARGE (-1)     // sizes exceed the static scratch
-#define OCTO_NOALLOC_ERR_UNSUPPORTED (-2)   // head_dim not 64/128, Hq % Hkv != 0, or GQA group > 16
+#define OCTO_NOALLOC_ERR_UNSUPPORTED (-2)   // head_dim not 64/128, Hq % Hkv != 0, GQA group > 16, or
+                                            // misaligned / null pointers or strides (see below)
 #define OCTO_NOALLOC_ERR_SETUP (-3)         // the scratch address could not be resolved
 #define OCTO_NOALLOC_ERR_LAUNCH (-4)        // a kernel launch failed
 
@@ -56,7 +57,12 @@ extern "C" {
 //   kv_start, kv_len: int32 [B];  kv_indices: int32 slot ids
 //   o:       bf16 [B, Hq * head_dim], row stride ldo (elements)
 //   num_splits: key-range splits per request (1..64); 1 needs no scratch at all
-// Returns OCTO_NOALLOC_OK or one of the OCTO_NOALLOC_ERR_* codes.
+// Alignment: k_cache and v_cache 16-byte aligned; q, o and the int32 tables 4-byte
+// aligned; ldq and ldo even and at least Hq * head_dim.  Other inputs are refused with
+// OCTO_NOALLOC_ERR_UNSUPPORTED before anything is launched.
+// Returns OCTO_NOALLOC_OK or one of the OCTO_NOALLOC_ERR_* codes.  OCTO_NOALLOC_ERR_LAUNCH
+// reports a failure of this call's own launches; an error left pending by earlier,
+// unrelated work is not cleared here and surfaces at the caller's next error check.
 int octo_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, const int32_t* kv_start,
                                   const int32_t* kv_len, const int32_t* kv_indices, void* o, int B, int Hq, int Hkv,
                                   int head_dim, int ldq, int ldo, int num_splits, float scale, cudaStream_t stream);

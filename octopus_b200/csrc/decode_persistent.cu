@@ -304,11 +304,8 @@ __global__ void decode_persistent_combine_kernel(DecodePersistParams p) {
 int decode_persistent_smem_bytes() { return kStages * kTileBytes + 1024 + 2 * kStages * 8 + 16; }
 
 void decode_persistent_launch(const DecodePersistParams& p, int grid, int* status, cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(decode_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_persistent_smem_bytes());
-    configured = true;
-  }
+  static SmemOptIn opt;
+  opt.ensure(decode_persistent_kernel, decode_persistent_smem_bytes());
   decode_persistent_kernel<<<grid, 64, decode_persistent_smem_bytes(), st>>>(p, status);
   if (p.num_splits > 1) decode_persistent_combine_kernel<<<dim3(p.B, p.Hq), 128, 0, st>>>(p);
 }

@@ -116,7 +116,11 @@ __global__ void __launch_bounds__(32 * (1 + kConsumers), 2) decode_shared_kernel
       int n0 = x.k0 + lane < x.k1 ? static_cast<int>(idx[x.k0 + lane]) : first;
       int n1 = x.k0 + 32 + lane < x.k1 ? static_cast<int>(idx[x.k0 + 32 + lane]) : first;
       for (int t0 = x.k0; t0 < x.k1; t0 += kTile) {
-        const int i0 = n0, i1 = n1;
+        int i0 = n0, i1 = n1;
+        if (p.n_slots > 0) {
+          if (!index_ok(i0, p.n_slots, status, 730)) i0 = 0;
+          if (!index_ok(i1, p.n_slots, status, 731)) i1 = 0;
+        }
         if (t0 + kTile < x.k1) {
           const int u = t0 + kTile;
           n0 = u + lane < x.k1 ? static_cast<int>(idx[u + lane]) : first;
@@ -313,12 +317,8 @@ __global__ void decode_shared_combine_kernel(DecodeSharedParams p) {
 int decode_shared_smem_bytes() { return kStages * kTileBytes + 1024 + 2 * kStages * 8 + 16; }
 
 void decode_shared_launch(const DecodeSharedParams& p, int grid, int* status, cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(decode_shared_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         decode_shared_smem_bytes());
-    configured = true;
-  }
+  static SmemOptIn opt;
+  opt.ensure(decode_shared_kernel, decode_shared_smem_bytes());
   decode_shared_kernel<<<grid, 32 * (1 + kConsumers), decode_shared_smem_bytes(), st>>>(p, status);
   decode_shared_combine(p, st);
 }

@@ -31,6 +31,8 @@ struct DecodeSharedParams {
   int max_slots;
   int chunk;                     // largest keys per work item any plan may use (host checks)
   float scale;
+  long long n_slots;             // rows of the K / V caches: slot ids outside [0, n_slots) are reported
+                                 // (kErrBadIndex) and read as slot 0 instead; 0 disables the check
   unsigned long long* trace;     // optional event timestamps of CTA 0 (tcgen05 kernel; debugging)
 };
 

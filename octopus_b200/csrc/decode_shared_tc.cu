@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
             t_last = globaltimer_ns();
           } else if (*abort_flag) {
             ok = false;
-          } else if (globaltimer_ns() - t_last > OCTO_WAIT_NS) {
+          } else if (globaltimer_ns() - t_last > wait_budget_ns(status)) {
             *abort_flag = 1;
             record_error(status, kErrMbarTimeout, 1013);
             ok = false;
@@ -451,11 +451,8 @@ template <int kStages, int kMinBlocks>
 static void launch(const DecodeSharedParams& p, const DecodeSharedMaps& maps, int sms, int* status,
                    cudaStream_t st) {
   auto kern = decode_shared_tc_kernel<kStages, kMinBlocks>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<kStages>());
-    configured = true;
-  }
+  static SmemOptIn opt;
+  opt.ensure(kern, smem_bytes<kStages>());
   kern<<<kMinBlocks * sms, kThreads, smem_bytes<kStages>(), st>>>(maps, p, status);
 }
 

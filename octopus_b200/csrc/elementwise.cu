@@ -276,22 +276,27 @@ void swiglu_bwd(const bf16* gu, const bf16* dout, bf16* dgu, int T, int F, cudaS
 }
 
 // ----------------------------------------------------------------- embedding
+// A token id outside [0, V) is reported (kErrBadIndex, site 700, the id) and its row is
+// written as zeros instead of reading outside the table.
 __global__ void embed_fwd_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ W, bf16* out, int T, int H,
-                                 int V) {
-  const int row = blockIdx.x;
-  if (row >= T) return;
-  int64_t id = ids[row];
-  if (id < 0 || id >= V) id = 0;
-  const uint4* src = reinterpret_cast<const uint4*>(W + static_cast<size_t>(id) * H);
-  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * H);
-  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = src[c];
-}
-__global__ void embed_bwd_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ dout, float* dW, int T,
-                                 int H, int V) {
+                                 int V, int* status) {
   const int row = blockIdx.x;
   if (row >= T) return;
   const int64_t id = ids[row];
-  if (id < 0 || id >= V) return;
+  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * H);
+  if (!index_ok(id, V, status, 700)) {
+    for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(W + static_cast<size_t>(id) * H);
+  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = src[c];
+}
+__global__ void embed_bwd_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ dout, float* dW, int T,
+                                 int H, int V, int* status) {
+  const int row = blockIdx.x;
+  if (row >= T) return;
+  const int64_t id = ids[row];
+  if (!index_ok(id, V, status, 701)) return;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
     float f[8];
     load8(dout + static_cast<size_t>(row) * H + c, f);
@@ -299,23 +304,26 @@ __global__ void embed_bwd_kernel(const int64_t* __restrict__ ids, const bf16* __
     for (int i = 0; i < 8; ++i) atomicAdd(&dW[static_cast<size_t>(id) * H + c + i], f[i]);
   }
 }
-void embed_fwd(const int64_t* ids, const bf16* W, bf16* out, int T, int H, int V, cudaStream_t st) {
+void embed_fwd(const int64_t* ids, const bf16* W, bf16* out, int T, int H, int V, int* status, cudaStream_t st) {
   if (T == 0) return;
-  embed_fwd_kernel<<<T, 128, 0, st>>>(ids, W, out, T, H, V);
+  embed_fwd_kernel<<<T, 128, 0, st>>>(ids, W, out, T, H, V, status);
 }
-void embed_bwd(const int64_t* ids, const bf16* dout, float* dW, int T, int H, int V, cudaStream_t st) {
+void embed_bwd(const int64_t* ids, const bf16* dout, float* dW, int T, int H, int V, int* status, cudaStream_t st) {
   if (T == 0) return;
-  embed_bwd_kernel<<<T, 128, 0, st>>>(ids, dout, dW, T, H, V);
+  embed_bwd_kernel<<<T, 128, 0, st>>>(ids, dout, dW, T, H, V, status);
 }
 
 // ----------------------------------------------------------------- paged KV write
-// cache[slot[t], h, :] = src[t, h, :] for the k and v heads of a fused qkv row.
+// cache[slot[t], h, :] = src[t, h, :] for the k and v heads of a fused qkv row.  A
+// negative slot means "no write"; a slot >= n_slots is reported (kErrBadIndex, site 710)
+// and skipped.
 __global__ void kv_write_kernel(const bf16* __restrict__ qkv, int ld, int Hq, int Hkv, int D,
-                                const int64_t* __restrict__ slots, bf16* kc, bf16* vc, int T) {
+                                const int64_t* __restrict__ slots, bf16* kc, bf16* vc, int T, long long n_slots,
+                                int* status) {
   const int t = blockIdx.x;
   if (t >= T) return;
   const int64_t slot = slots[t];
-  if (slot < 0) return;
+  if (slot < 0 || !index_ok(slot, n_slots, status, 710)) return;
   const int width = Hkv * D;
   const bf16* k = qkv + static_cast<size_t>(t) * ld + static_cast<size_t>(Hq) * D;
   const bf16* v = k + width;
@@ -325,9 +333,9 @@ __global__ void kv_write_kernel(const bf16* __restrict__ qkv, int ld, int Hq, in
   }
 }
 void kv_write(const bf16* qkv, int ld, int Hq, int Hkv, int D, const int64_t* slots, bf16* kc, bf16* vc, int T,
-              cudaStream_t st) {
+              long long n_slots, int* status, cudaStream_t st) {
   if (T == 0) return;
-  kv_write_kernel<<<T, 64, 0, st>>>(qkv, ld, Hq, Hkv, D, slots, kc, vc, T);
+  kv_write_kernel<<<T, 64, 0, st>>>(qkv, ld, Hq, Hkv, D, slots, kc, vc, T, n_slots, status);
 }
 
 // ----------------------------------------------------------------- optimizer

@@ -19,10 +19,12 @@ void rope_apply(__nv_bfloat16* qkv, int ld, const int32_t* pos, int T, int Hq, i
 void swiglu_fwd(const __nv_bfloat16* gu, __nv_bfloat16* out, int T, int F, cudaStream_t st);
 void swiglu_bwd(const __nv_bfloat16* gu, const __nv_bfloat16* dout, __nv_bfloat16* dgu, int T, int F,
                 cudaStream_t st);
-void embed_fwd(const int64_t* ids, const __nv_bfloat16* W, __nv_bfloat16* out, int T, int H, int V, cudaStream_t st);
-void embed_bwd(const int64_t* ids, const __nv_bfloat16* dout, float* dW, int T, int H, int V, cudaStream_t st);
+void embed_fwd(const int64_t* ids, const __nv_bfloat16* W, __nv_bfloat16* out, int T, int H, int V, int* status,
+               cudaStream_t st);
+void embed_bwd(const int64_t* ids, const __nv_bfloat16* dout, float* dW, int T, int H, int V, int* status,
+               cudaStream_t st);
 void kv_write(const __nv_bfloat16* qkv, int ld, int Hq, int Hkv, int D, const int64_t* slots, __nv_bfloat16* kc,
-              __nv_bfloat16* vc, int T, cudaStream_t st);
+              __nv_bfloat16* vc, int T, long long n_slots, int* status, cudaStream_t st);
 void sqnorm_accum(const float* g, long n, float* out, cudaStream_t st);
 // decode_fused.cu: split-K finishes fused with the layer's next element-wise step
 void splitk_finish_norm(const float* ws, int splits, int M, int N, const __nv_bfloat16* bias,
@@ -30,7 +32,7 @@ void splitk_finish_norm(const float* ws, int splits, int M, int N, const __nv_bf
                         float eps, bool plus_one, __nv_bfloat16* h, int ldh, cudaStream_t st);
 void splitk_finish_qkv(const float* ws, int splits, int M, int Hq, int Hkv, int D, const __nv_bfloat16* bias,
                        const int32_t* pos, float theta, __nv_bfloat16* q, int ldq, const int64_t* slots,
-                       __nv_bfloat16* kc, __nv_bfloat16* vc, cudaStream_t st);
+                       __nv_bfloat16* kc, __nv_bfloat16* vc, long long n_slots, int* status, cudaStream_t st);
 void adamw_step(float* p, const float* g, float* m, float* v, __nv_bfloat16* p16, long n, float lr, float b1,
                 float b2, float eps, float wd, int step, const float* sqnorm, float max_norm, float grad_scale,
                 cudaStream_t st);

@@ -15,11 +15,8 @@ template <int BN, bool A_MN, bool B_MN, class Epi, int MT = 1>
 static void launch_one(const GemmLaunch& g, const Epi& epi) {
   using Cfg = GemmCfg<BN, MT>;
   auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, Epi, ALocal<A_MN>, MT>;
-  static bool configured = false;  // attribute is per function, not per device context
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-    configured = true;
-  }
+  static SmemOptIn opt;  // the attribute is set per device context
+  opt.ensure(kern, Cfg::kSmemBytes);
   if (!g.s.pdl) {
     kern<<<g.grid, kGemmThreads, Cfg::kSmemBytes, g.stream>>>(ALocal<A_MN>{g.ta}, g.tb, g.s, epi, g.status);
     return;

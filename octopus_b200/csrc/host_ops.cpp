@@ -24,7 +24,7 @@ static std::vector<torch::Tensor> g_status(64);
 torch::Tensor status_tensor(int device) {
   std::lock_guard<std::mutex> lk(g_status_mu);
   if (!g_status[device].defined()) {
-    g_status[device] = torch::zeros({2}, torch::dtype(torch::kInt32).device(torch::kCUDA, device));
+    g_status[device] = torch::zeros({kStatusWordsHost}, torch::dtype(torch::kInt32).device(torch::kCUDA, device));
   }
   return g_status[device];
 }
@@ -88,6 +88,7 @@ void attn_decode_shared_t(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, t
   p.max_slots = static_cast<int>(max_slots);
   p.chunk = static_cast<int>(chunk);
   p.scale = static_cast<float>(scale);
+  p.n_slots = kc.numel() / (Hkv * 128);
   TORCH_CHECK(row_nslot.numel() >= p.B, "decode_shared: row_nslot too small");
   TORCH_CHECK(part_o.numel() >= static_cast<int64_t>(p.B) * Hq * max_slots * 128 &&
                   part_lse.numel() >= static_cast<int64_t>(p.B) * Hq * max_slots,
@@ -365,14 +366,14 @@ torch::Tensor gemm_qkv_rope_t(torch::Tensor A, torch::Tensor W, c10::optional<to
     auto q = torch::empty({M, Hq * D}, A.options());
     splitk_finish_qkv(ws.data_ptr<float>(), splits, M, Hq, Hkv, D, static_cast<const __nv_bfloat16*>(bp),
                       pos.data_ptr<int32_t>(), static_cast<float>(theta), BF(q), Hq * D, slots.data_ptr<int64_t>(),
-                      BF(kc), BF(vc), g.stream);
+                      BF(kc), BF(vc), kc.numel() / (Hkv * D), g.status, g.stream);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return q;
   }
   auto qkv = torch::empty({M, N}, A.options());
   gemm_out(A, false, W, false, qkv, 1.0, c10::nullopt, bias, false, 0);
   rope_apply(BF(qkv), N, pos.data_ptr<int32_t>(), M, Hq, Hkv, D, static_cast<float>(theta), false, g.stream);
-  kv_write(CBF(qkv), N, Hq, Hkv, D, slots.data_ptr<int64_t>(), BF(kc), BF(vc), M, g.stream);
+  kv_write(CBF(qkv), N, Hq, Hkv, D, slots.data_ptr<int64_t>(), BF(kc), BF(vc), M, kc.numel() / (Hkv * D), g.status, g.stream);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return qkv.narrow(1, 0, Hq * D);
 }
@@ -539,7 +540,7 @@ torch::Tensor embed_fwd_t(torch::Tensor ids, torch::Tensor W) {
   CHECK_CONTIG(W);
   const int T = ids.numel(), V = W.size(0), H = W.size(1);
   auto out = torch::empty({T, H}, W.options());
-  embed_fwd(ids.data_ptr<int64_t>(), CBF(W), BF(out), T, H, V, cur_stream(W));
+  embed_fwd(ids.data_ptr<int64_t>(), CBF(W), BF(out), T, H, V, status_ptr(W.get_device()), cur_stream(W));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }
@@ -549,7 +550,7 @@ void embed_bwd_t(torch::Tensor ids, torch::Tensor dout, torch::Tensor dW) {
   CHECK_F32(dW);
   CHECK_CONTIG(dout);
   embed_bwd(ids.data_ptr<int64_t>(), CBF(dout), dW.data_ptr<float>(), ids.numel(), dW.size(1), dW.size(0),
-            cur_stream(dW));
+            status_ptr(dW.get_device()), cur_stream(dW));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -561,8 +562,9 @@ void kv_write_t(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, torch::Te
   CHECK_CONTIG(kc);
   CHECK_CONTIG(vc);
   TORCH_CHECK(qkv.stride(1) == 1, "kv_write: qkv rows");
+  TORCH_CHECK(kc.numel() == vc.numel() && kc.size(-1) == Hkv * D, "kv_write: k / v cache shapes");
   kv_write(CBF(qkv), qkv.stride(0), Hq, Hkv, D, slots.data_ptr<int64_t>(), BF(kc), BF(vc), slots.numel(),
-           cur_stream(qkv));
+           kc.numel() / (Hkv * D), status_ptr(qkv.get_device()), cur_stream(qkv));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -8,6 +8,10 @@
 
 namespace octo {
 
+// Per-device status word (int32): [0] error code, [1] site, [2] runtime wait budget in
+// microseconds (0: the compiled default), [3] index rejected by a debug bounds check.
+constexpr int kStatusWordsHost = 4;
+
 struct GemmShape {
   int M, N, K;
   int m_tiles, n_tiles, k_blocks, num_tiles;

@@ -15,7 +15,7 @@
 //   barrier      single-CTA bounded barrier on a counter slot.
 //   reshard      strided 2D copies from the trainer's weight layout to TP shards.
 //
-// All waits are bounded by OCTO_WAIT_NS; a timeout records kErrPeerTimeout in the
+// All waits are bounded (status word budget, default OCTO_WAIT_NS); a timeout records kErrPeerTimeout in the
 // status word, raises the CTA abort flag and returns without touching peer data.
 #include <cuda_bf16.h>
 
@@ -40,9 +40,10 @@ __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence
 
 __device__ bool wait_ge(const int* f, int target, volatile int* abort, int* status, int where) {
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t budget = wait_budget_ns(status);
   while (ld_acquire_sys(f) < target) {
     if (abort != nullptr && *abort) return false;
-    if (globaltimer_ns() - t0 > OCTO_WAIT_NS) {
+    if (globaltimer_ns() - t0 > budget) {
       record_error(status, kErrPeerTimeout, where);
       if (abort != nullptr) *abort = 1;
       return false;
@@ -166,9 +167,10 @@ struct AGather {
     const int need = remote_chunks(mb);
     if (need == 0) return true;
     const uint64_t t0 = globaltimer_ns();
+    const uint64_t budget = wait_budget_ns(status);
     while (ld_acquire_gpu(work + 1 + mb) < need) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > OCTO_WAIT_NS) {
+      if (globaltimer_ns() - t0 > budget) {
         record_error(status, kErrPeerTimeout, 940);
         *abort = 1;
         return false;
@@ -274,11 +276,8 @@ template <int BN, class Epi, class ASrc>
 static void launch_tp(const GemmLaunch& g, const Epi& epi, const ASrc& a) {
   using Cfg = GemmCfg<BN>;
   auto kern = gemm_tcgen05_kernel<BN, false, false, Epi, ASrc>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-    configured = true;
-  }
+  static SmemOptIn opt;
+  opt.ensure(kern, Cfg::kSmemBytes);
   kern<<<g.grid, kGemmThreads, Cfg::kSmemBytes, g.stream>>>(a, g.tb, g.s, epi, g.status);
 }
 

@@ -89,16 +89,60 @@ def available() -> bool:
     return _load() is not None
 
 
+ERR_NAMES = {1: "pipeline barrier wait timed out", 2: "peer flag wait timed out", 3: "bounds check failed",
+             4: "TMEM allocation failed"}
+
+
+class KernelError(RuntimeError):
+    """A kernel recorded an error in the device status word (the context is still usable)."""
+
+    def __init__(self, code: int, where: int, index: int):
+        self.code, self.where, self.index = code, where, index
+        extra = f", index {index}" if code == 3 else ""
+        super().__init__(f"octopus_b200 kernel error {code} ({ERR_NAMES.get(code, '?')}) at site {where}{extra}")
+
+
+def read_status(device: int = 0) -> tuple[int, int, int]:
+    """(code, site, rejected index) of the device status word, without clearing it (syncs)."""
+    code, where, _budget, index = (int(x) for x in ext().status_tensor(device).cpu().tolist())
+    return code, where, index
+
+
 def check_status(device: int = 0, reset: bool = True) -> None:
-    """Raise if a kernel on `device` recorded a timeout or bounds error (syncs)."""
-    st = ext().status_tensor(device)
-    code, where = (int(x) for x in st.cpu().tolist())
+    """Raise KernelError if a kernel on `device` recorded a timeout or bounds error (syncs)."""
+    code, where, index = read_status(device)
     if reset and code:
-        st.zero_()
+        st = ext().status_tensor(device)
+        st[0:2].zero_()
+        st[3:4].zero_()
     if code:
-        names = {1: "pipeline barrier wait timed out", 2: "peer flag wait timed out",
-                 3: "bounds check failed", 4: "TMEM allocation failed"}
-        raise RuntimeError(f"octopus_b200 kernel error {code} ({names.get(code, '?')}) at site {where}")
+        raise KernelError(code, where, index)
+
+
+def set_wait_budget(device: int, microseconds: int) -> int:
+    """Set the time limit of every primary device-side wait on `device` (mbarrier phases,
+    peer flags, staging counters); 0 restores the compiled default (2 s).  Returns the
+    previous value.  Stream-ordered: it applies to kernels launched afterwards on the
+    current stream."""
+    st = ext().status_tensor(device)
+    prev = int(st[2].item())
+    st[2:3].fill_(int(microseconds))
+    return prev
+
+
+class wait_budget:
+    """Context: a runtime wait budget (microseconds) for kernels launched inside."""
+
+    def __init__(self, device: int, microseconds: int):
+        self.device, self.us = device, microseconds
+
+    def __enter__(self):
+        self.prev = set_wait_budget(self.device, self.us)
+        return self
+
+    def __exit__(self, *exc):
+        set_wait_budget(self.device, self.prev)
+        return False
 
 
 class pdl_launches:
