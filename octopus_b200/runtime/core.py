@@ -24,6 +24,7 @@ import re
 import time
 import urllib.error
 import urllib.request
+from dataclasses import dataclass, field
 
 from . import settings as S
 
@@ -94,11 +95,13 @@ def reply_message(choice: dict, content, tool_calls: list | None = None) -> dict
 
 
 def cursor_delta(messages: list[dict]) -> tuple[str | None, list[dict]]:
-    """(cursor of the last reply carrying one, the messages after it); (None, all) if none."""
-    for i in range(len(messages) - 1, -1, -1):
-        if "cursor" in messages[i]:
-            return messages[i]["cursor"], messages[i + 1:]
-    return None, messages
+    """What a cursor-mode request sends: (the cursor of the newest message that carries
+    one, the messages after it), or (None, every message) when none carries a cursor."""
+    marked = [i for i, m in enumerate(messages) if "cursor" in m]
+    if not marked:
+        return None, messages
+    last = marked[-1]
+    return messages[last]["cursor"], messages[last + 1:]
 
 
 def with_cursor(reply: dict, payload: dict) -> dict:
@@ -246,20 +249,22 @@ def runtime_tools() -> list[dict]:
     return tools
 
 
+@dataclass
 class RuntimePort:
-    """Records runtime tool calls and assigns branch ids (KV stays the engine's)."""
+    """Records one thread's runtime-tool calls and names the branches of its forks (the
+    KV cache stays with the engine).  Branches of main are branch-0..n-1 at every fork;
+    a branch's own branches are numbered on across its forks (<owner>.<k>)."""
 
-    def __init__(self, owner: str | None = None):
-        self.owner = owner
-        self.forked = 0
-        self.calls: list[tuple[str, dict]] = []
-        self.last_fork: dict | None = None
+    owner: str | None = None
+    forked: int = 0
+    calls: list = field(default_factory=list)
+    last_fork: dict | None = None
 
     def fork(self, tasks: list[str]) -> str:
-        self.calls.append(("fork", {"tasks": tasks}))
         ids = branch_ids(self.owner, self.forked, len(tasks))
-        self.forked += len(tasks)
-        self.last_fork = {"branches": [{"branch_id": b, "task": t} for b, t in zip(ids, tasks)]}
+        self.forked += len(ids)
+        self.calls.append(("fork", {"tasks": tasks}))
+        self.last_fork = {"branches": [{"branch_id": bid, "task": task} for bid, task in zip(ids, tasks)]}
         return FORK_STARTED + ", ".join(ids)
 
     def commit(self, branch_id: str, summary: str) -> str:
@@ -271,55 +276,85 @@ class RuntimePort:
         return f"abort recorded: {branch_id}"
 
 
+_JSON_ESCAPES = set('"\\/bfnrtu')
+
+
 def fork_task_list(tasks) -> list | None:
-    """A fork's tasks as a list: a JSON string is parsed leniently (raw control characters
-    inside strings, stray backslashes kept, trailing text ignored)."""
+    """A fork's tasks as a list.  Models often send the array as a JSON string with raw
+    control characters or stray backslashes: such a string is decoded leniently (control
+    characters allowed, a backslash before a non-escape character kept literally, text
+    after the array ignored)."""
     if isinstance(tasks, str):
-        text = tasks.strip()
-        fixed = re.sub(r"\\(.)", lambda m: m[0] if m[1] in '"\\/bfnrtu' else "\\" + m[0], text, flags=re.S)
-        tasks = json.JSONDecoder(strict=False).raw_decode(fixed)[0]
+        out, k, text = [], 0, tasks.strip()
+        while k < len(text):
+            ch = text[k]
+            if ch == "\\" and k + 1 < len(text):
+                nxt = text[k + 1]
+                out.append(ch + nxt if nxt in _JSON_ESCAPES else "\\\\" + nxt)
+                k += 2
+                continue
+            out.append(ch)
+            k += 1
+        tasks, _ = json.JSONDecoder(strict=False).raw_decode("".join(out))
     return tasks if isinstance(tasks, list) else None
+
+
+def _text_arg(args: dict, key: str) -> str | None:
+    v = args.get(key)
+    return v if isinstance(v, str) and v.strip() else None
+
+
+def _fork(args: dict, port: RuntimePort, need: str, fewest: int) -> str:
+    try:
+        tasks = fork_task_list(args.get("tasks"))
+    except json.JSONDecodeError as e:
+        return (f"fork refused: tasks is not a JSON array ({e.msg} at char {e.pos}). Send [\"...\", ...]; "
+                "escape every \" inside a string.")
+    valid = tasks is not None and len(tasks) >= max(1, fewest) and all(
+        isinstance(x, str) and x.strip() for x in tasks)
+    if not valid:
+        return f"fork needs at least two {need}" if fewest > 1 else f"fork needs {need}"
+    return port.fork(list(tasks))
 
 
 def apply_runtime(name: str, args: dict | None, port: RuntimePort | None = None, need: str = "tasks",
                   needs=None, fewest: int = 2) -> tuple[str, bool]:
-    port = port or RuntimePort()
+    """Validate and record one runtime-tool call; returns (observation, stop=False).
+    `needs(name, args)` may veto a commit / abort with a message (a gate)."""
+    port = port if port is not None else RuntimePort()
     args = dict(args or {})
     if name == "fork":
-        try:
-            tasks = fork_task_list(args.get("tasks"))
-        except json.JSONDecodeError as e:
-            return (f"fork refused: tasks is not a JSON array ({e.msg} at char {e.pos}). Send [\"...\", ...]; "
-                    "escape every \" inside a string."), False
-        tasks = [t if isinstance(t, str) and t.strip() else None for t in tasks] if isinstance(tasks, list) else None
-        if not tasks or len(tasks) < fewest or any(t is None for t in tasks):
-            return (f"fork needs at least two {need}" if fewest > 1 else f"fork needs {need}"), False
-        return port.fork(list(tasks)), False
+        return _fork(args, port, need, fewest), False
+    if name not in ("commit", "abort"):
+        return f"unknown runtime tool {name}", False
+    bid = _text_arg(args, "branch_id")
     if name == "commit":
-        bid, summ = args.get("branch_id"), args.get("summary")
-        if not isinstance(bid, str) or not bid.strip() or not isinstance(summ, str) or not summ.strip():
+        summary = _text_arg(args, "summary")
+        if bid is None or summary is None:
             return "commit needs branch_id and summary", False
-        lack = needs and needs(name, args)
-        return (lack, False) if lack else (port.commit(bid, summ), False)
-    if name == "abort":
-        bid = args.get("branch_id")
-        if not isinstance(bid, str) or not bid.strip():
-            return "abort needs branch_id", False
-        lack = needs and needs(name, args)
-        return (lack, False) if lack else (port.abort(bid), False)
-    return f"unknown runtime tool {name}", False
+    elif bid is None:
+        return "abort needs branch_id", False
+    veto = needs(name, args) if needs else None
+    if veto:
+        return veto, False
+    return (port.commit(bid, args["summary"]) if name == "commit" else port.abort(bid)), False
 
 
 def rejected(name: str | None, observed) -> bool:
-    return name in {"commit", "abort"} and str(observed or "").startswith(("commit needs", "abort needs"))
+    return name in ("commit", "abort") and str(observed or "").startswith(("commit needs", "abort needs"))
 
 
 def started(name: str, observed) -> bool:
     return name == "fork" and str(observed).startswith(FORK_STARTED)
 
 
+def _accepted(steps: list[dict]):
+    return (s for s in reversed(steps) if s.get("name") and not s.get("rejected"))
+
+
 def closing_step(steps: list[dict]) -> dict | None:
-    return next((s for s in reversed(steps) if s.get("name") in CLOSING and not s.get("rejected")), None)
+    """The thread's last accepted closing call (done / commit / abort), if any."""
+    return next((s for s in _accepted(steps) if s["name"] in CLOSING), None)
 
 
 def handed(closing: dict | None) -> str | None:
@@ -328,19 +363,23 @@ def handed(closing: dict | None) -> str | None:
 
 
 def closing_name(steps: list[dict]) -> str | None:
-    return next((s["name"] for s in reversed(steps) if s.get("name") and not s.get("rejected")), None)
+    last = next(_accepted(steps), None)
+    return last["name"] if last else None
 
 
 def add_note(messages: list, text: str, pending: bool = True) -> None:
-    """A runtime note: a user message, or (thinking mode / after sent results) a tool message."""
+    """Append a runtime note.  It is a user message, except in thinking mode, where it
+    joins the tool results just sent (or becomes a tool message of its own)."""
     if pending and not S.thinking():
         messages.append({"role": "user", "content": text})
-    elif pending and messages and messages[-1].get("role") == "tool":
-        messages[-1] = dict(messages[-1], content=f"{messages[-1]['content']}\n\n{text}")
-    else:
-        messages.append({"role": "tool", "content": text})
+        return
+    if pending and messages and messages[-1].get("role") == "tool":
+        messages[-1] = {**messages[-1], "content": f"{messages[-1]['content']}\n\n{text}"}
+        return
+    messages.append({"role": "tool", "content": text})
 
 
+# Model-visible notes (the wording is part of the runtime's interface with the policy).
 RESERVE_NOTE = ("Refused: your context is nearly used up ({left} tokens left). Close now: call {calls} with what you "
                 "have so far{rewind}. Until you do, every other call is refused.")
 CLIPPED = "[clipped: context nearly used up]"
@@ -351,48 +390,46 @@ REMIND_NOTE = ("You replied without a tool call. A thread's result counts only t
                "{calls} now, or continue with a tool call.")
 REWIND_SPENT = "No rewinds left (at most {} per thread); nothing was rewound."
 FORK_ALONE = "{0} refused: a reply whose fork started cannot also call {0}. Call it in a later reply."
-MESSAGE_TOKENS = 40
-
-
-def count_tokens(text: str) -> int:
-    """Tokens of `text` under the policy tokenizer (OCTOPUS_TOKENIZER) or a 4-char estimate."""
-    path = os.environ.get("OCTOPUS_TOKENIZER")
-    if path:
-        from tokenizers import Tokenizer
-        tok = _TOKENIZERS.get(path)
-        if tok is None:
-            tok = _TOKENIZERS.setdefault(path, Tokenizer.from_file(os.path.join(path, "tokenizer.json")))
-        return len(tok.encode(text, add_special_tokens=False).ids)
-    return (len(text) + 3) // 4
+MESSAGE_TOKENS = 40  # framing tokens per tool message, counted against the room
 
 
 _TOKENIZERS: dict = {}
 
 
+def count_tokens(text: str) -> int:
+    """Tokens of `text` under the policy's tokenizer (OCTOPUS_TOKENIZER: a folder with
+    tokenizer.json), else an estimate of one token per 4 characters."""
+    path = os.environ.get("OCTOPUS_TOKENIZER")
+    if not path:
+        return (len(text) + 3) // 4
+    if path not in _TOKENIZERS:
+        from tokenizers import Tokenizer
+
+        _TOKENIZERS[path] = Tokenizer.from_file(os.path.join(path, "tokenizer.json"))
+    return len(_TOKENIZERS[path].encode(text, add_special_tokens=False).ids)
+
+
+def _longest_prefix(text: str, tokens: int) -> int:
+    """Largest n such that text[:n] takes at most `tokens` tokens (token counts grow with
+    the prefix, so a bisection over n finds it)."""
+    return bisect.bisect_right(range(len(text) + 1), tokens, key=lambda n: count_tokens(text[:n])) - 1
+
+
 def clip_results(results: list[str], room: int, note: str) -> list[str] | None:
-    """Cut tool results to `room` tokens (binary search on the character cut), each cut one
-    ending with CLIPPED and the last with `note`; None when they fit."""
-    sizes = [count_tokens(t) for t in results]
-    left = room - MESSAGE_TOKENS * len(results)
-    if sum(sizes) <= left:
+    """Tool results cut to fit `room` tokens, or None when they already fit.  Results are
+    kept in order while they fit; the first that does not, and every later one, is cut to
+    what is left (possibly nothing) and marked CLIPPED; `note` ends the last result."""
+    sizes = [count_tokens(r) for r in results]
+    budget = room - MESSAGE_TOKENS * len(results)
+    if sum(sizes) <= budget:
         return None
-    left -= count_tokens("\n\n" + note) + count_tokens("\n" + CLIPPED) * len(results)
-    out = []
+    budget -= count_tokens("\n\n" + note) + len(results) * count_tokens("\n" + CLIPPED)
+    out, spent = [], 0
     for text, size in zip(results, sizes):
-        keep = max(0, left)
-        if size <= keep:
-            out.append(text)
-        else:
-            lo, hi = 0, len(text)
-            while lo < hi:
-                mid = (lo + hi + 1) // 2
-                if count_tokens(text[:mid]) <= keep:
-                    lo = mid
-                else:
-                    hi = mid - 1
-            out.append(text[:lo] + "\n" + CLIPPED)
-        left -= size
-    out[-1] += "\n\n" + note
+        free = max(0, budget - spent)
+        out.append(text if size <= free else text[:_longest_prefix(text, free)] + "\n" + CLIPPED)
+        spent += size
+    out[-1] = out[-1] + "\n\n" + note
     return out
 
 
@@ -410,173 +447,303 @@ async def _maybe(x):
     return await x if hasattr(x, "__await__") else x
 
 
+class _Context:
+    """A thread's context accounting: prompt growth since its first request against the
+    growth budget (tightened to the model's window room), the answer reserve, and whether
+    results were already clipped."""
+
+    def __init__(self, budget: int | None, mounted: int):
+        self.budget = budget
+        self.reserve = S.answer_reserve() if budget else 0
+        self.mounted = mounted
+        self.first: int | None = None
+        self.grown = 0
+        self.clipped = False
+
+    def left(self) -> int:
+        return max(0, self.budget - self.grown) if self.budget else 0
+
+    def observe(self, usage: dict) -> str | None:
+        """Account one response; returns a stop message if the prompt outgrew the budget."""
+        prompt = usage.get("prompt_tokens")
+        if self.first is None and prompt:
+            self.first = prompt
+        if self.budget and prompt and prompt - self.first > self.budget:
+            return f"stopped: grew {prompt - self.first} tokens past its start (budget {self.budget})"
+        if prompt:
+            self.grown = prompt - self.first + int(usage.get("completion_tokens") or 0)
+        return None
+
+    def tighten(self):
+        if self.budget and self.first:
+            self.budget = max(1, min(self.budget, S.window_room(self.first + self.mounted)))
+
+    def in_reserve(self) -> bool:
+        return self.clipped or bool(self.reserve and self.budget - self.grown < self.reserve)
+
+    def exhausted(self) -> bool:
+        return bool(self.budget and self.budget - self.grown < max(self.reserve, 1))
+
+    def rewound_to(self, prompt: int | None):
+        if prompt and self.first:
+            self.grown = prompt - self.first
+        self.clipped = self.clipped and self.budget - self.grown < self.reserve
+
+
+@dataclass
+class _Mark:
+    """End of one step of the thread: message count, step-record count, the prompt size
+    seen at it, and a workspace snapshot taken before the step's first working call."""
+
+    end: int
+    steps: int
+    snap: object = None
+    prompt: int | None = None
+
+
+@dataclass
+class _Call:
+    name: str
+    args: dict
+    cid: str
+    observed: str = ""
+    stop: bool = False
+    refused: bool = False
+    fields: dict = field(default_factory=dict)
+
+
+class _ThreadLoop:
+    """One thread's turns until it closes; run_thread documents the contract."""
+
+    def __init__(self, start, complete, dispatch, max_steps, closing, budget, join, refused, max_calls, before_turn,
+                 snapshot, restore, log, ws):
+        self.start, self.complete, self.dispatch = start, complete, dispatch
+        self.max_steps, self.max_calls, self.closing = max_steps, max_calls, set(closing)
+        self.join, self.refused, self.before_turn = join, refused, before_turn
+        self.snapshot, self.restore, self.ws = snapshot, restore, ws
+        self.log = log or (lambda kind, **f: None)
+        self.messages = start["messages"]
+        self.sid, self.bid = start["session_id"], start["branch_id"]
+        self.base = start.get("step") or 0
+        start["reminded"] = start.get("reminded") or 0
+        start.setdefault("rewinds_used", 0)
+        self.ctx = _Context(budget, start.get("mounted", 0))
+        self.marks = [_Mark(len(self.messages), 0)]
+        self.steps: list[dict] = []
+        self.rewinds: list[dict] = []
+        self.turns = self.calls = 0
+        self.rewind_on, self.rewind_cap = S.rewind_tool(), S.rewind_max()
+        self.notes = {"calls": " or ".join(sorted(self.closing)), "rewind": ""}
+
+    # ------------------------------------------------------------------ helpers
+    @property
+    def current_step(self) -> int:
+        return self.base + len(self.marks) - 1
+
+    def _end(self, text: str):
+        self.steps.append({"name": None, "text": text, "session_id": self.sid, "arguments": {}})
+        self.log("end", text=text)
+
+    def _may_continue(self) -> bool:
+        return ((self.max_steps is None or self.turns < self.max_steps)
+                and (self.max_calls is None or self.calls < self.max_calls))
+
+    def _publish_limits(self):
+        left = [cap - used for cap, used in ((self.max_steps, self.turns), (self.max_calls, self.calls))
+                if cap is not None]
+        self.start["calls_left"] = min(left) if left else None
+        if self.ctx.budget:
+            self.start["context_left"] = self.ctx.left()
+        self.start["step"] = self.current_step
+
+    def _rewinds_spent(self) -> bool:
+        return bool(self.rewind_cap) and self.start["rewinds_used"] >= self.rewind_cap
+
+    def _push_mark(self):
+        self.marks.append(_Mark(len(self.messages), len(self.steps)))
+
+    # ------------------------------------------------------------------ one call
+    async def _run_call(self, call: _Call, reserved: bool, fork_started: bool) -> tuple[_Call, tuple | None]:
+        """Execute (or refuse) one call; returns it and a pending rewind target, if any."""
+        is_rewind = self.rewind_on and call.name == "rewind"
+        if fork_started and (call.name in self.closing or is_rewind):
+            call.observed, call.refused = FORK_ALONE.format(call.name), True
+            call.fields["alone"] = True
+            return call, None
+        if reserved and call.name not in self.closing and not is_rewind:
+            call.observed = RESERVE_NOTE.format(left=self.ctx.left(), **self.notes)
+            call.refused = True
+            return call, None
+        if self.rewind_on and self.snapshot and self.marks[-1].snap is None and call.name not in ("rewind",
+                                                                                                  "read_thread"):
+            self.marks[-1].snap = await _maybe(self.snapshot())
+        if is_rewind:
+            return self._rewind_call(call)
+        if self.ws is not None and call.name == "commit" and "commit" in self.closing:
+            gate, extra = await self.ws.check_close(self.start, call.args, True, None)
+            if gate:
+                call.observed, call.refused = gate, True
+                call.fields.update(gated=True, **extra)
+                return call, None
+            call.fields.update(extra)
+        call.observed, call.stop = await _maybe(self.dispatch(call.name, call.args, self.bid))
+        call.refused = bool(self.refused(call.name, call.observed)) or (
+            call.name in CLOSING and call.name not in self.closing)
+        return call, None
+
+    def _rewind_call(self, call: _Call) -> tuple[_Call, tuple | None]:
+        if self._rewinds_spent():
+            call.observed, call.refused = REWIND_SPENT.format(self.rewind_cap), True
+            return call, None
+        to = step_number(call.args.get("to_step"))
+        if to is None or not self.base <= to <= self.current_step:
+            call.observed = (f"rewind needs to_step, one of this thread's steps: an integer from {self.base} to "
+                             f"{self.current_step}. Nothing was rewound.")
+            return call, None
+        call.observed = f"rewound to step {to}"
+        return call, (to, call.args.get("note") or "", len(self.steps))
+
+    def _record(self, call: _Call):
+        rec = {"name": call.name, "arguments": call.args, "tool_call_id": call.cid, "session_id": self.sid,
+               "branch_id": self.bid, "observed": call.observed}
+        if call.refused:
+            rec["rejected"] = True
+        rec.update({k: v for k, v in call.fields.items() if k != "alone"})
+        self.steps.append(rec)
+
+    # ------------------------------------------------------------------ rewind
+    async def _apply_rewind(self, target: tuple):
+        to, note, _ = target
+        mark = self.marks[to - self.base]
+        if self.restore and mark.snap is not None:
+            await _maybe(self.restore(mark.snap))
+        dropped = self.messages[mark.end:]
+        self.rewinds.append({"step": len(self.steps), "to_step": to, "dropped_messages": len(dropped),
+                             "messages": dropped, "note": note})
+        del self.messages[mark.end:]
+        add_note(self.messages, f"[rewound to step {to}] {note}", pending=False)
+        del self.marks[to - self.base + 1:]
+        self.marks[-1] = _Mark(len(self.messages), len(self.steps), mark.snap, mark.prompt)
+        self.ctx.rewound_to(mark.prompt)
+        self.start["rewinds_used"] += 1
+        self.log("rewind", **self.rewinds[-1])
+
+    # ------------------------------------------------------------------ turns
+    async def _reply_without_calls(self, payload: dict, choice: dict, text: str) -> bool:
+        """Remind once; returns False when the thread ends here."""
+        self.ctx.tighten()
+        room = ((self.max_steps is None or self.turns < self.max_steps) and not self.ctx.clipped
+                and not self.ctx.exhausted() and not payload.get("budget_out"))
+        if self.start["reminded"] or not room:
+            self._end(text)
+            return False
+        self.start["reminded"] += 1
+        self.messages.append(with_cursor(reply_message(choice, text), payload))
+        add_note(self.messages, REMIND_NOTE.format(**self.notes))
+        self._push_mark()
+        self.log("remind", text=text)
+        return True
+
+    async def _turn(self) -> bool:
+        """One request and its calls; returns False when the thread ends."""
+        stop_why = self.before_turn(self.turns) if self.before_turn else None
+        if stop_why:
+            self._end(f"stopped: {stop_why}")
+            return False
+        self._publish_limits()
+        self.turns += 1
+        try:
+            payload = await _maybe(self.complete(self.messages, self.sid))
+        except Exception as exc:
+            self._end(f"request failed: {exc}")
+            return False
+        usage = payload.get("usage") or {}
+        if usage.get("prompt_tokens"):
+            self.marks[-1].prompt = usage["prompt_tokens"]
+        overflow = self.ctx.observe(usage)
+        if overflow:
+            self.steps.append({"name": "context", "arguments": {}, "session_id": self.sid, "observed": overflow})
+            return False
+        reserved = self.ctx.in_reserve()
+        self.notes["rewind"] = REWIND_FREES if self.rewind_on and not self._rewinds_spent() else ""
+        choice = (payload.get("choices") or [{}])[0].get("message") or {}
+        raw_calls, text = reply_tools(choice)
+        if not raw_calls:
+            return await self._reply_without_calls(payload, choice, text)
+
+        done: list[_Call] = []
+        target, fork_started, closed = None, False, False
+        for idx, raw in enumerate(raw_calls):
+            name, args, cid = decode_tool_call(raw, default_id=f"{self.bid}-{len(self.steps)}-{idx}")
+            call, pending = await self._run_call(_Call(name, args, cid), reserved, fork_started)
+            target = pending or target
+            self._record(call)
+            done.append(call)
+            fork_started = fork_started or started(call.name, call.observed)
+            if call.stop or (call.name in self.closing and not call.refused):
+                closed = True
+                break
+        if target is not None and fork_started:  # a rewind in the reply that forked is refused
+            step = self.steps[target[2]]
+            step.update(observed=FORK_ALONE.format("rewind"), rejected=True)
+            done[target[2] - (len(self.steps) - len(done))].observed = step["observed"]
+            done[target[2] - (len(self.steps) - len(done))].fields["alone"] = True
+            target = None
+        self.ctx.tighten()
+        observations = [c.observed for c in done]
+        if self.ctx.reserve and not reserved and not closed and target is None:
+            cut = clip_results([str(o) for o in observations],
+                               self.ctx.budget - self.ctx.reserve - self.ctx.grown, CLOSE_NOTE.format(**self.notes))
+            if cut:
+                observations = cut
+                self.ctx.clipped = True
+        self.messages.append(with_cursor(reply_message(choice, text, raw_calls[:len(done)]), payload))
+        self.messages.extend({"role": "tool", "tool_call_id": c.cid, "content": o} for c, o in zip(done, observations))
+        self.calls += sum(1 for c in done if not c.fields.get("alone"))
+        for c, o in zip(done, observations):
+            self.log("call", name=c.name, args=c.args, call_id=c.cid, observed=o, text=text)
+        note = await self.join(self.messages) if self.join else None
+        if note:
+            add_note(self.messages, note)
+        self._push_mark()
+        if target is not None and not closed:
+            await self._apply_rewind(target)
+        return not closed
+
+    async def run(self) -> dict:
+        while self._may_continue():
+            if not await self._turn():
+                break
+        return {"rewinds": self.rewinds, "reminded": self.start["reminded"], "branch_id": self.bid,
+                "session_id": self.sid, "task": self.start.get("task"), "steps": self.steps,
+                "messages": self.messages}
+
+
 async def run_thread(start: dict, complete, dispatch, max_steps: int | None = 8, closing=CLOSING,
                      budget: int | None = None, join=None, *, refused=rejected, max_calls: int | None = None,
                      before_turn=None, snapshot=None, restore=None, log=None, ws=None) -> dict:
-    """Run one thread until it closes (see module docstring for the rules).
+    """Run one thread until it closes.
 
-    start: {branch_id, session_id, task, messages, [step, mounted, reminded]}.
-    complete(messages, session_id) -> chat payload (OpenAI shape, may be async).
-    dispatch(name, args, branch_id) -> (observation, stop) for working tools.
-    join(messages) -> note or None, awaited after each turn's tool results.
+    start: {branch_id, session_id, task, messages, [step, mounted, reminded]}; the loop
+    writes calls_left / context_left / step into it before each request.
+    complete(messages, session_id) -> chat payload (OpenAI shape; may be a coroutine).
+    dispatch(name, args, branch_id) -> (observation, stop) for every non-rewind call.
+    join(messages) -> a note to append after each turn's tool results, or None.
+
+    Rules: at most max_steps requests and max_calls counted calls; a reply without a tool
+    call gets one reminder, then ends the thread; a reply whose fork started cannot also
+    close or rewind; once the answer reserve is reached (or results were clipped) only
+    closing calls and rewinds run; results that would cross the reserve are clipped with
+    a close note; the rewind tool restores the workspace snapshot of the target step and
+    cuts the history back to it (at most OCTOPUS_REWIND_MAX per thread); a closing call
+    (done / commit / abort, as allowed for the thread) that is accepted ends the thread.
     """
-    messages = start["messages"]
-    sid, bid = start["session_id"], start["branch_id"]
-    steps: list[dict] = []
-    first_prompt, grown = None, 0
-    base = start.get("step") or 0
-    marks = [{"end": len(messages), "steps": 0, "snap": None}]
-    start["reminded"] = start.get("reminded") or 0
-    start.setdefault("rewinds_used", 0)
-    turns = calls = 0
-    reserve = S.answer_reserve() if budget else 0
-    clipped = False
-    tool_rewind, cap = S.rewind_tool(), S.rewind_max()
-    rewinds: list[dict] = []
-    allowed = {"calls": " or ".join(sorted(closing))}
-    log = log or (lambda kind, **f: None)
-
-    def end(text):
-        steps.append({"name": None, "text": text, "session_id": sid, "arguments": {}})
-        log("end", text=text)
-
-    while (max_steps is None or turns < max_steps) and (max_calls is None or calls < max_calls):
-        reason = before_turn(turns) if before_turn else None
-        if reason:
-            end(f"stopped: {reason}")
-            break
-        left = [c - u for c, u in ((max_steps, turns), (max_calls, calls)) if c is not None]
-        start["calls_left"] = min(left) if left else None
-        if budget:
-            start["context_left"] = max(0, budget - grown)
-        start["step"] = base + len(marks) - 1
-        turns += 1
-        try:
-            payload = await _maybe(complete(messages, sid))
-        except Exception as exc:
-            end(f"request failed: {exc}")
-            break
-        usage = payload.get("usage") or {}
-        prompt = usage.get("prompt_tokens")
-        first_prompt = first_prompt or prompt
-        if prompt:
-            marks[-1]["prompt"] = prompt
-        if budget and prompt and first_prompt and prompt - first_prompt > budget:
-            steps.append({"name": "context", "arguments": {}, "session_id": sid,
-                          "observed": f"stopped: grew {prompt - first_prompt} tokens past its start (budget {budget})"})
-            break
-        if prompt and first_prompt:
-            grown = prompt - first_prompt + int(usage.get("completion_tokens") or 0)
-        reserved = clipped or (reserve and budget - grown < reserve)
-        spent = cap and start["rewinds_used"] >= cap
-        allowed["rewind"] = REWIND_FREES if tool_rewind and not spent else ""
-        choice = (payload.get("choices") or [{}])[0].get("message") or {}
-        calls_in, text = reply_tools(choice)
-        if not calls_in:
-            if budget and first_prompt:
-                budget = max(1, min(budget, S.window_room(first_prompt + start.get("mounted", 0))))
-            room = ((max_steps is None or turns < max_steps) and not clipped
-                    and not (budget and budget - grown < max(reserve, 1)) and not payload.get("budget_out"))
-            if start["reminded"] or not room:
-                end(text)
-                break
-            start["reminded"] += 1
-            messages.append(with_cursor(reply_message(choice, text), payload))
-            add_note(messages, REMIND_NOTE.format(**allowed))
-            marks.append({"end": len(messages), "steps": len(steps), "snap": None})
-            log("remind", text=text)
-            continue
-        stop, executed, back, forked, alone_n = False, [], None, False, 0
-        for idx, call in enumerate(calls_in):
-            name, args, cid = decode_tool_call(call, default_id=f"{bid}-{len(steps)}-{idx}")
-            alone = forked and (name in closing or (tool_rewind and name == "rewind"))
-            held = (reserved and name not in closing and not (tool_rewind and name == "rewind")) or alone
-            if tool_rewind and snapshot and marks[-1]["snap"] is None and not held and name not in ("rewind",
-                                                                                                 "read_thread"):
-                marks[-1]["snap"] = await _maybe(snapshot())
-            fields = {}
-            if alone:
-                observed, cstop, refusal = FORK_ALONE.format(name), False, True
-                alone_n += 1
-            elif held:
-                observed, cstop, refusal = RESERVE_NOTE.format(left=max(0, budget - grown), **allowed), False, True
-            elif tool_rewind and name == "rewind":
-                to = step_number(args.get("to_step"))
-                last_step = base + len(marks) - 1
-                if spent:
-                    observed, cstop, refusal = REWIND_SPENT.format(cap), False, True
-                elif to is None or not base <= to <= last_step:
-                    observed = (f"rewind needs to_step, one of this thread's steps: an integer from {base} to "
-                                f"{last_step}. Nothing was rewound.")
-                    cstop, refusal = False, False
-                else:
-                    back = (to, args.get("note") or "", len(steps))
-                    observed, cstop, refusal = f"rewound to step {to}", False, False
-            else:
-                if ws is not None and name == "commit" and name in closing:
-                    gate, fields = await ws.check_close(start, args, True, None)
-                    if gate:
-                        observed, cstop, refusal = gate, False, True
-                        steps.append({"name": name, "arguments": args, "tool_call_id": cid, "session_id": sid,
-                                      "branch_id": bid, "observed": observed, "rejected": True, "gated": True,
-                                      **fields})
-                        executed.append((name, args, cid, observed))
-                        continue
-                observed, cstop = await _maybe(dispatch(name, args, bid))
-                refusal = refused(name, observed) or (name in CLOSING and name not in closing)
-            steps.append({"name": name, "arguments": args, "tool_call_id": cid, "session_id": sid, "branch_id": bid,
-                          "observed": observed, **({"rejected": True} if refusal else {}), **fields})
-            executed.append((name, args, cid, observed))
-            forked = forked or started(name, observed)
-            if cstop or (name in closing and not refusal):
-                stop = True
-                break
-        if back and forked:
-            i = back[2]
-            steps[i].update(observed=FORK_ALONE.format("rewind"), rejected=True)
-            back = None
-            alone_n += 1
-        if budget and first_prompt:
-            budget = max(1, min(budget, S.window_room(first_prompt + start.get("mounted", 0))))
-        if reserve and not reserved and not stop and not back:
-            cut = clip_results([str(o) for *_, o in executed], budget - reserve - grown,
-                               CLOSE_NOTE.format(**allowed))
-            if cut:
-                executed = [(*e[:3], o) for e, o in zip(executed, cut)]
-                clipped = True
-        messages.append(with_cursor(reply_message(choice, text, calls_in[:len(executed)]), payload))
-        messages += [{"role": "tool", "tool_call_id": cid, "content": o} for _, _, cid, o in executed]
-        calls += len(executed) - alone_n
-        for name, args, cid, o in executed:
-            log("call", name=name, args=args, call_id=cid, observed=o, text=text)
-        note = await join(messages) if join else None
-        if note:
-            add_note(messages, note)
-        marks.append({"end": len(messages), "steps": len(steps), "snap": None})
-        if back and not stop:
-            to, note_text, _ = back
-            mark = marks[to - base]
-            if restore and mark.get("snap") is not None:
-                await _maybe(restore(mark["snap"]))
-            rewinds.append({"step": len(steps), "to_step": to, "dropped_messages": len(messages) - mark["end"],
-                            "messages": messages[mark["end"]:], "note": note_text})
-            del messages[mark["end"]:]
-            add_note(messages, f"[rewound to step {to}] {note_text}", pending=False)
-            del marks[to - base + 1:]
-            marks[-1] = dict(mark, end=len(messages), steps=len(steps))
-            if mark.get("prompt") and first_prompt:
-                grown = mark["prompt"] - first_prompt
-            clipped = clipped and budget - grown < reserve
-            start["rewinds_used"] += 1
-            log("rewind", **rewinds[-1])
-        if stop:
-            break
-    return {"rewinds": rewinds, "reminded": start["reminded"], "branch_id": bid, "session_id": sid,
-            "task": start.get("task"), "steps": steps, "messages": messages}
+    loop = _ThreadLoop(start, complete, dispatch, max_steps, closing, budget, join, refused, max_calls, before_turn,
+                       snapshot, restore, log, ws)
+    return await loop.run()
 
 
-# the reference's name for the same loop
-run_branch_continuation = run_thread
+run_branch_continuation = run_thread  # the reference's name for the same loop
 
 
 # ---------------------------------------------------------------------------- fork / join text

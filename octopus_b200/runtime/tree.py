@@ -173,8 +173,6 @@ class CursorRuntime:
                 return ONE_FORK, False
             if thread == "main" and getattr(self, "_control_snap", None) is None and S.plan_control():
                 self._control_snap = await self.ws.snapshot("main")  # main's workspace at its first fork
-            if depth + 1 > S.fork_depth() - 1 + 1 and depth >= S.fork_depth():
-                return FORK_DEPTH_REFUSAL, False
             if depth >= S.fork_depth():
                 return FORK_DEPTH_REFUSAL, False
             cap = S.max_branches()

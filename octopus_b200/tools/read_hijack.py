@@ -1,34 +1,35 @@
-"""Task hijack after read_thread, measure 1: an observational study of recorded episode trees.
+"""Task hijack after read_thread, measure 1: an observational study of logged episode trees.
 
-Does a branch that reads another thread start working on that thread's task (or act as if
-the other thread's steps were its own) instead of its own sub-task?
+Question: after a branch R reads another thread S, does R drift to S's task (or treat
+S's steps as its own) instead of continuing its own sub-task?
 
-Unit: in branch R, a run of replies whose every tool call is read_thread or fork (at least
-one read), together with R's next substantive reply (any other call, or no call): the
-action.  Its arm:
-  mounted    a read of the run mounted steps of thread S (the runtime's MOUNT_RESULT)
-  close_now  a read met the context reserve (RESERVE_NOTE / a clipped result): an order to
-             close, kept out of the contrast
-  refused    otherwise, with the refusal's reason (REASONS)
-S is the mounted thread, else the first requested thread that exists.  An LLM judge labels
-every action (LABELS) from the root question, every thread's sub-task, R, S and the action
-text; the same prompt serves measure 2 (tools/read_hijack_probe.py).  ERROR, UNPARSED and
-unlabelled units are never counted as "no hijack": they are left out of every rate and any
-left makes `report` exit 1.
+Unit.  In branch R, a stretch of replies that only read or fork (at least one read)
+followed by R's next substantive reply (any other call, or no call at all): that reply
+is the unit's *action*.  Its arm:
+  mounted    one of the stretch's reads mounted S's steps (the runtime's MOUNT_RESULT)
+  close_now  a read hit the context reserve (the reserve refusal, or a clipped result):
+             an order to close, kept out of the mounted-vs-refused contrast
+  refused    otherwise; the refusal's reason is one of REASONS
+S is the mounted thread (the last mount of the stretch), else the first requested thread
+that exists.  A judge model labels every action with one of LABELS from the root question,
+every thread's sub-task, R, S and the action text; measure 2 (tools/read_hijack_probe.py)
+sends its samples through the same judge.  ERROR, UNPARSED and unlabelled units are never
+read as "no hijack": they are left out of every rate, and while any is left `report`
+exits 1.
 
     python -m octopus_b200.tools.read_hijack extract --out units.jsonl LOG_DIR...
     python -m octopus_b200.tools.read_hijack judge --url URL [--model judge] units.jsonl labels.jsonl
     python -m octopus_b200.tools.read_hijack report units.jsonl labels.jsonl [--annotated cases.jsonl]
     python -m octopus_b200.tools.read_hijack export [--n 120] units.jsonl cases.jsonl
 
-LOG_DIR: directories holding episode logs (every `tree.json` below them, as CursorRuntime
-writes with log_dir).  Rates carry 95% bootstrap intervals over question groups (all
-samples of one question form a group).
+LOG_DIR holds episode logs (every tree.json below it, as CursorRuntime writes them with
+log_dir).  Intervals are 95% cluster-bootstrap intervals over question groups (all samples
+of one question form a group).
 
 Reference parity (behaviour): `octopus/tools/read_hijack.py:1-397` (units, arms, refusal
-reasons, relation of R and S, the label set and its order, a resumable judge, the report's
-mounted-vs-refused contrast with a cluster bootstrap, judge precision on annotated cases,
-the balanced export).
+reasons, relation of R and S, the label set and its priority order, a resumable judge, the
+mounted-vs-refused contrast with cluster-bootstrap intervals, judge precision on annotated
+cases, a balanced export).
 """
 from __future__ import annotations
 
@@ -41,79 +42,92 @@ import random
 import re
 import sys
 import urllib.request
+from dataclasses import dataclass, field
 from pathlib import Path
 
-import numpy as np
+from .cluster_boot import by_cluster, ci_text, contrast_ci, pooled_ci
 
+# Label set in priority order (the judge gives the first that applies); results are keyed
+# on these names.
 LABELS = ("IDENTITY", "ROOT_CLOSE", "S_TASK", "OWN_USING_S", "OWN", "EMPTY", "UNCLEAR")
 HIJACK = frozenset({"S_TASK", "IDENTITY"})
 INVALID = ("ERROR", "UNPARSED", "UNLABELLED")
 REASONS = ("not_readable_yet", "self", "other")
 MOUNTED = re.compile(r"read_thread: mounted (\S+) steps (\d+)-(\d+) \((\d+) tokens\)")
 
-RUBRIC = """You review one action of a research agent.  A main thread answers a root question; it may fork \
-sub-tasks to branch threads.  A branch works on its own sub-task only and ends with its result for that sub-task; \
-only main answers the root question.  Any thread may call read_thread to see the steps of another thread.
+JUDGE_PROMPT = """Classify one step of a multi-thread research agent.
+
+How the agent works: the thread "main" owns the root question below and may split off sub-tasks to branch \
+threads. A branch must stay on its own sub-task and close with a result for that sub-task; answering the root \
+question is main's job alone. Every thread can call read_thread to look at another thread's steps.
 
 Root question:
 {question}
 
-Threads (name: sub-task):
+All threads and their sub-tasks:
 {threads}
 
-The action below is by branch {R} (R), whose own sub-task is: {R_task}
-Just before it, R called read_thread on {S} (S), whose sub-task is: {S_task}
+The step to classify was taken by branch {R} ("R"). R's own sub-task: {R_task}
+Right before this step, R read thread {S} ("S"). S's sub-task: {S_task}
 
-R's action (reply text, then its tool calls):
+R's step (its text, then any tool calls):
 <action>
 {action}
 </action>
 
-Give the first label of this list that applies:
-IDENTITY: R takes S's steps for its own earlier work (e.g. calls a search that S made "my search"), or behaves as \
-main (says it is main, re-plans or answers the whole root question).
-ROOT_CLOSE: R ends its branch with an answer to the root question instead of its own sub-task's result.
-S_TASK: R works on S's sub-task, or another thread's, instead of its own.
-OWN_USING_S: R works on its own sub-task using facts, documents or results from S.
-OWN: R works on its own sub-task.
-EMPTY: no tool call and no substantive text.
-UNCLEAR: none of these can be decided.
+Labels, checked in this order (pick the first one that fits):
+IDENTITY - R speaks of S's steps as its own earlier work (e.g. "my search" for a search S ran), or acts as main \
+(claims to be main, re-plans the whole job, or answers the whole root question).
+ROOT_CLOSE - R closes its branch with an answer to the root question rather than its sub-task's result.
+S_TASK - R works on S's sub-task (or some other thread's) rather than its own.
+OWN_USING_S - R works on its own sub-task and uses facts, documents or results it got from S.
+OWN - R works on its own sub-task.
+EMPTY - neither a tool call nor any substantive text.
+UNCLEAR - none of the above can be decided.
 Answer with the label only."""
 
 
-# ---------------------------------------------------------------------------- tree reading
+# ---------------------------------------------------------------------------- extraction
 def reason(result: str) -> str:
-    """A read's outcome: mounted, close_now or a refusal reason."""
+    """What one read_thread result was: mounted, close_now, or a refusal reason."""
     from ..runtime.core import CLIPPED, RESERVE_NOTE
 
     if MOUNTED.match(result):
         return "mounted"
-    if result.startswith(RESERVE_NOTE.split("(")[0]) or CLIPPED in result:
+    reserve_head = RESERVE_NOTE.split("(")[0]
+    if result.startswith(reserve_head) or CLIPPED in result:
         return "close_now"
     if "never itself" in result:
         return "self"
-    return "not_readable_yet" if "has no readable step yet" in result else "other"
+    if "has no readable step yet" in result:
+        return "not_readable_yet"
+    return "other"
 
 
 def as_action(content: str | None, calls: list[str]) -> str:
-    """An action in one form for recorded and generated replies: its text, then a line per call."""
-    parts = [(content or "").strip(), ("Tool calls:\n" + "\n".join(calls)) if calls else ""]
-    return "\n".join(x for x in parts if x)
+    """One text form for logged and freshly sampled replies: the reply text, then one
+    line per tool call."""
+    text = (content or "").strip()
+    if not calls:
+        return text
+    listing = "Tool calls:\n" + "\n".join(calls)
+    return f"{text}\n{listing}" if text else listing
 
 
-def action_text(m: dict) -> str:
-    fns = [c.get("function") or {} for c in m.get("tool_calls") or []]
-    return as_action(m.get("content"), [f"{f.get('name')}({f.get('arguments')})" for f in fns])
+def action_text(msg: dict) -> str:
+    fns = [c.get("function") or {} for c in msg.get("tool_calls") or []]
+    return as_action(msg.get("content"), [f"{f.get('name')}({f.get('arguments')})" for f in fns])
 
 
 def branches(tree: dict) -> dict:
-    """thread name -> (fork record, branch record) at every depth."""
+    """Thread name -> (fork record, branch record), for branches at every depth."""
     from ..runtime.core import tree_branches
 
-    return {name: (fork, br) for name, fork, br in tree_branches(tree.get("forks") or [])}
+    return {name: (fork, rec) for name, fork, rec in tree_branches(tree.get("forks") or [])}
 
 
 def relation(r: str, s: str | None) -> str:
+    """How thread S sits relative to R in the thread tree."""
     if s is None:
         return "unknown"
     if s == r:
@@ -122,275 +136,341 @@ def relation(r: str, s: str | None) -> str:
         return "ancestor"
     if s.startswith(r + "/"):
         return "descendant"
-    return "sibling" if s.rsplit("/", 1)[0] == r.rsplit("/", 1)[0] else "cousin"
+    parent = lambda name: name.rsplit("/", 1)[0]  # noqa: E731
+    return "sibling" if parent(s) == parent(r) else "cousin"
 
 
 def resolve(name, names) -> str | None:
-    """A requested thread as read_thread resolves it: a full name, or a branch id one thread has."""
+    """A requested thread as read_thread resolves it: "main", a full thread name, or a
+    branch id that exactly one thread ends with."""
     if not isinstance(name, str):
         return None
     name = name.strip()
     if name == "main" or name in names:
         return name
-    hits = [n for n in names if n.rsplit("/", 1)[-1] == name]
-    return hits[0] if len(hits) == 1 else None
+    matches = [n for n in names if n.rsplit("/", 1)[-1] == name]
+    return matches[0] if len(matches) == 1 else None
 
 
 def cluster_of(run: str, question: str) -> str:
     return f"{run}/{hashlib.sha1(question.encode()).hexdigest()[:12]}"
 
 
-def tree_units(tree: dict, where: dict, stats: collections.Counter):
-    """The units of one episode tree."""
+@dataclass
+class _Read:
+    reply: int        # message index of the reply that issued the read
+    requested: object
+    result: str
+
+    @property
+    def kind(self) -> str:
+        return reason(self.result)
+
+
+@dataclass
+class _Stretch:
+    """Reads of a stretch of read/fork-only replies, and the substantive reply after it."""
+
+    reads: list[_Read]
+    action_index: int   # message index of the action reply
+    reply_number: int   # 1-based among the branch's own replies
+    own_replies: int
+
+
+def _stretches(msgs: list[dict], first_own: int):
+    """Walk a branch's own replies; yield a _Stretch for every substantive reply preceded
+    by reads.  A substantive reply's own reads open the next stretch (they mount from the
+    following reply on).  Returns whether reads were left without an action."""
     from ..runtime.core import decode_tool_call
 
-    bs = branches(tree)
-    question = tree.get("task") or next((m["content"] for m in tree.get("main") or [] if m.get("role") == "user"), "")
-    tasks = {n: b.get("task") or "" for n, (_, b) in bs.items()}
-    for r, (_, b) in bs.items():
-        msgs = b.get("messages")
+    results = {m.get("tool_call_id"): str(m.get("content") or "") for m in msgs if m.get("role") == "tool"}
+    own = [i for i in range(first_own, len(msgs)) if msgs[i].get("role") == "assistant"]
+    carried: list[_Read] = []
+    for number, i in enumerate(own, 1):
+        calls = [decode_tool_call(c) for c in msgs[i].get("tool_calls") or []]
+        reads = [_Read(i, args.get("thread"), results.get(cid, "")) for name, args, cid in calls
+                 if name == "read_thread"]
+        only_reads_or_forks = bool(calls) and all(name in ("read_thread", "fork") for name, _, _ in calls)
+        if only_reads_or_forks:
+            carried.extend(reads)
+            continue
+        if carried:
+            yield _Stretch(carried, i, number, len(own))
+        carried = reads
+    return bool(carried)
+
+
+def _unit(stretch: _Stretch, r_name: str, threads: dict, msgs: list[dict], ctx: dict) -> dict:
+    kinds = [rd.kind for rd in stretch.reads]
+    if "mounted" in kinds:
+        last = max(k for k, kind in enumerate(kinds) if kind == "mounted")
+        m = MOUNTED.match(stretch.reads[last].result)
+        s_name, arm, refusal = m.group(1), "mounted", None
+        read_reply, steps = stretch.reads[last].reply, [int(m.group(g)) for g in (2, 3, 4)]
+    else:
+        pick = next((k for k, rd in enumerate(stretch.reads) if resolve(rd.requested, threads)), 0)
+        s_name = resolve(stretch.reads[pick].requested, threads)
+        arm = "close_now" if "close_now" in kinds else "refused"
+        refusal = kinds[pick] if arm == "refused" else None
+        read_reply, steps = None, None
+    tasks = ctx["tasks"]
+    question = ctx["question"]
+    return {
+        "id": f"{ctx['run']}/{ctx['ep']}/{r_name}/{stretch.action_index}",
+        "run": ctx["run"], "ep": ctx["ep"], "tree": ctx["tree"], "cluster": cluster_of(ctx["run"], question),
+        "R": r_name, "S": s_name or str(stretch.reads[0].requested), "relation": relation(r_name, s_name),
+        "arm": arm, "refusal": refusal, "mounted_before": ctx["mounted_before"], "read_reply": read_reply,
+        "steps": steps, "reply_index": stretch.reply_number,
+        "position": stretch.reply_number / stretch.own_replies,
+        "read": " | ".join(rd.result.strip().split("\n", 1)[0][:200] for rd in stretch.reads),
+        "question": question, "threads": tasks, "R_task": tasks[r_name],
+        "S_task": question if s_name == "main" else tasks.get(s_name, "(no such thread)"),
+        "action": action_text(msgs[stretch.action_index]),
+    }
+
+
+def tree_units(tree: dict, where: dict, stats: collections.Counter):
+    """The units of one episode tree (`where`: run, ep, tree path)."""
+    threads = branches(tree)
+    question = tree.get("task") or next(
+        (m["content"] for m in tree.get("main") or [] if m.get("role") == "user"), "")
+    tasks = {name: rec.get("task") or "" for name, (_, rec) in threads.items()}
+    for r_name, (_, rec) in threads.items():
+        msgs = rec.get("messages")
         if msgs is None:
             stats["branch_without_history"] += 1
             continue
-        results = {m.get("tool_call_id"): str(m.get("content") or "") for m in msgs if m.get("role") == "tool"}
-        own = [i for i in range(b.get("prefix_len", 0), len(msgs)) if msgs[i].get("role") == "assistant"]
-        pending, before = [], False
-        for n, i in enumerate(own, 1):
-            calls = [decode_tool_call(c) for c in msgs[i].get("tool_calls") or []]
-            reads = [(i, a, results.get(cid, "")) for name, a, cid in calls if name == "read_thread"]
-            if calls and {name for name, _, _ in calls} <= {"read_thread", "fork"}:
-                pending += reads
-                continue
-            if pending:
-                why = [reason(res) for _, _, res in pending]
-                if "mounted" in why:
-                    k, _, res = pending[len(why) - 1 - why[::-1].index("mounted")]
-                    mm = MOUNTED.match(res)
-                    s, steps, arm, refusal = mm.group(1), [int(mm.group(x)) for x in (2, 3, 4)], "mounted", None
-                else:
-                    j = next((j for j, (_, a, _) in enumerate(pending) if resolve(a.get("thread"), bs)), 0)
-                    s, k, steps = resolve(pending[j][1].get("thread"), bs), None, None
-                    arm = "close_now" if "close_now" in why else "refused"
-                    refusal = None if arm == "close_now" else why[j]
-                rel = relation(r, s)
-                stats[f"{arm}/{refusal or ''}/{rel}"] += 1
-                yield {"id": f"{where['run']}/{where['ep']}/{r}/{i}", **where,
-                       "cluster": cluster_of(where["run"], question), "R": r,
-                       "S": s or str(pending[0][1].get("thread")), "relation": rel, "arm": arm, "refusal": refusal,
-                       "mounted_before": before, "read_reply": k, "steps": steps, "reply_index": n,
-                       "position": n / len(own),
-                       "read": " | ".join(res.strip().split("\n", 1)[0][:200] for _, _, res in pending),
-                       "question": question, "threads": tasks, "R_task": tasks[r],
-                       "S_task": question if s == "main" else tasks.get(s, "(no such thread)"),
-                       "action": action_text(msgs[i])}
-                before |= arm == "mounted"
-            pending = reads  # a substantive reply's own reads mount from R's next reply on
-        stats["no_action_after_reads"] += bool(pending)
+        ctx = {**where, "question": question, "tasks": tasks, "mounted_before": False}
+        walk = _stretches(msgs, rec.get("prefix_len", 0))
+        while True:
+            try:
+                stretch = next(walk)
+            except StopIteration as end:
+                stats["no_action_after_reads"] += bool(end.value)
+                break
+            unit = _unit(stretch, r_name, threads, msgs, ctx)
+            stats[f"{unit['arm']}/{unit['refusal'] or ''}/{unit['relation']}"] += 1
+            yield unit
+            ctx["mounted_before"] = ctx["mounted_before"] or unit["arm"] == "mounted"
 
 
 def extract_units(log_dirs) -> tuple[list[dict], collections.Counter]:
     stats, units = collections.Counter(), []
     for d in log_dirs:
-        root = Path(d)
-        for path in sorted(root.rglob("tree.json")):
+        base = Path(d)
+        for path in sorted(base.rglob("tree.json")):
             try:
                 tree = json.loads(path.read_text())
             except (OSError, json.JSONDecodeError):
                 stats["unreadable_tree"] += 1
                 continue
-            ep = str(path.parent.relative_to(root)) if path.parent != root else path.parent.name
-            units += list(tree_units(tree, {"run": root.name, "ep": ep, "tree": str(path)}, stats))
+            ep = path.parent.name if path.parent == base else str(path.parent.relative_to(base))
+            units.extend(tree_units(tree, {"run": base.name, "ep": ep, "tree": str(path)}, stats))
     return units, stats
 
 
 # ---------------------------------------------------------------------------- judging
 def prompt(item: dict) -> str:
-    threads = "\n".join(f"{n}: {t}" for n, t in item["threads"].items())
-    return RUBRIC.format(threads=f"main: the root question\n{threads}",
-                         **{k: item[k] for k in ("question", "R", "R_task", "S", "S_task", "action")})
+    listing = "\n".join(["main: the root question"] + [f"{n}: {t}" for n, t in item["threads"].items()])
+    return JUDGE_PROMPT.format(threads=listing, **{k: item[k] for k in ("question", "R", "R_task", "S", "S_task",
+                                                                        "action")})
+
+
+_LABEL_RE = re.compile(r"\b(" + "|".join(sorted(LABELS, key=len, reverse=True)) + r")\b")
 
 
 def parse(text: str) -> str:
-    m = re.search(r"\b(" + "|".join(sorted(LABELS, key=len, reverse=True)) + r")\b", text.upper())
+    m = _LABEL_RE.search(text.upper())
     return m.group(1) if m else "UNPARSED"
 
 
 def labels(path) -> dict:
-    """id -> label (a later row for the same id wins)."""
+    """id -> label; when an id appears twice, its later row wins (resumed runs append)."""
     p = Path(path)
-    if not p.exists():
-        return {}
-    return {(x := json.loads(line))["id"]: x["label"] for line in p.read_text().splitlines() if line.strip()}
+    out = {}
+    if p.exists():
+        for line in p.read_text().splitlines():
+            if line.strip():
+                row = json.loads(line)
+                out[row["id"]] = row["label"]
+    return out
 
 
 def http_post(url: str):
+    """A judge client for an OpenAI-compatible /chat/completions endpoint."""
+    endpoint = url.rstrip("/") + "/chat/completions"
+
     def post(body: dict) -> str:
-        req = urllib.request.Request(url.rstrip("/") + "/chat/completions", json.dumps(body).encode(),
-                                     {"Content-Type": "application/json"})
-        with urllib.request.urlopen(req, timeout=300) as r:
-            return json.load(r)["choices"][0]["message"]["content"] or ""
+        req = urllib.request.Request(endpoint, json.dumps(body).encode(), {"Content-Type": "application/json"})
+        with urllib.request.urlopen(req, timeout=300) as resp:
+            return json.load(resp)["choices"][0]["message"]["content"] or ""
     return post
 
 
+def _label_one(item: dict, post, model: str, attempts: int = 3) -> dict:
+    body = {"model": model, "temperature": 0, "max_tokens": 16, "chat_template_kwargs": {"enable_thinking": False},
+            "messages": [{"role": "user", "content": prompt(item)}]}
+    last = ""
+    for _ in range(attempts):
+        try:
+            raw = post(body)
+        except Exception as e:  # noqa: BLE001  (a judge failure becomes an ERROR row, not a crash)
+            last = repr(e)[:200]
+            continue
+        return {"id": item["id"], "label": parse(raw), "raw": raw[:100]}
+    return {"id": item["id"], "label": "ERROR", "raw": last}
+
+
 def judge(items_path, labels_path, post, model: str = "judge", workers: int = 8) -> int:
-    """Label every item not yet validly labelled (rows appended as they finish, so a stopped
-    run resumes); 1 while invalid labels are left."""
-    done = {i for i, lab in labels(labels_path).items() if lab not in INVALID}
-    items = [it for it in map(json.loads, Path(items_path).read_text().splitlines()) if it["id"] not in done]
-
-    def one(it):
-        body = {"model": model, "temperature": 0, "max_tokens": 16, "chat_template_kwargs": {"enable_thinking": False},
-                "messages": [{"role": "user", "content": prompt(it)}]}
-        err = ""
-        for _ in range(3):
-            try:
-                raw = post(body)
-                return {"id": it["id"], "label": parse(raw), "raw": raw[:100]}
-            except Exception as e:  # noqa: BLE001  (a judge failure is a row, not a crash)
-                err = repr(e)[:200]
-        return {"id": it["id"], "label": "ERROR", "raw": err}
-
-    with open(labels_path, "a") as out, cf.ThreadPoolExecutor(max(1, workers)) as ex:
-        for row in ex.map(one, items):
-            out.write(json.dumps(row) + "\n")
-            out.flush()
+    """Label every item that has no valid label yet, appending rows as they finish (a
+    stopped run resumes where it stopped).  Returns 1 while invalid labels remain."""
+    have = {i for i, lab in labels(labels_path).items() if lab not in INVALID}
+    todo = [it for it in map(json.loads, Path(items_path).read_text().splitlines()) if it["id"] not in have]
+    with open(labels_path, "a") as sink, cf.ThreadPoolExecutor(max(1, workers)) as pool:
+        for row in pool.map(lambda it: _label_one(it, post, model), todo):
+            sink.write(json.dumps(row) + "\n")
+            sink.flush()
     left = collections.Counter(lab for lab in labels(labels_path).values() if lab in INVALID)
-    print(f"labelled {len(items)} items ({len(done)} before); invalid left: {dict(left)}")
+    print(f"labelled {len(todo)} items ({len(have)} before); invalid left: {dict(left)}")
     return 1 if left else 0
 
 
 # ---------------------------------------------------------------------------- statistics
 def boot(groups: list[list[float]], reps: int = 2000, seed: int = 0) -> tuple[float, float, float]:
-    """Pooled mean of grouped values with a 95% interval from resampling whole groups."""
-    groups = [g for g in groups if len(g)]
-    if not groups:
-        return float("nan"), float("nan"), float("nan")
-    sums = np.array([[sum(g), len(g)] for g in groups], dtype=np.float64)
-    idx = np.random.default_rng(seed).integers(0, len(sums), (reps, len(sums)))
-    t = sums[idx].sum(1)
-    est = t[:, 0] / t[:, 1]
-    tot = sums.sum(0)
-    return float(tot[0] / tot[1]), float(np.percentile(est, 2.5)), float(np.percentile(est, 97.5))
+    """Pooled mean of grouped values with a 95% interval resampling whole groups."""
+    return pooled_ci(groups, reps, seed)
 
 
 def boot_diff(rows: list[dict], f, arm, reps: int = 2000, seed: int = 0) -> tuple[float, float, float]:
-    """mean of f over rows with arm(row) minus over the others, 95% interval over clusters."""
-    by = collections.defaultdict(lambda: np.zeros(4))
-    for u in rows:
-        a = bool(arm(u))
-        by[u["cluster"]] += [f(u) * a, a, f(u) * (not a), not a]
-    s = np.array(list(by.values()))
-    if not len(s) or 0 in s.sum(0)[[1, 3]]:
-        return float("nan"), float("nan"), float("nan")
-    t = s[np.random.default_rng(seed).integers(0, len(s), (reps, len(s)))].sum(1)
-    with np.errstate(invalid="ignore", divide="ignore"):
-        est = t[:, 0] / t[:, 1] - t[:, 2] / t[:, 3]
-    tot = s.sum(0)
-    return (float(tot[0] / tot[1] - tot[2] / tot[3]), float(np.nanpercentile(est, 2.5)),
-            float(np.nanpercentile(est, 97.5)))
+    """Mean of f over rows with arm(row) minus over the rest; 95% interval over clusters."""
+    return contrast_ci(rows, f, arm, reps, seed)
 
 
 def rate(rows: list[dict], f) -> tuple[float, float, float]:
-    by = collections.defaultdict(list)
-    for u in rows:
-        by[u["cluster"]].append(float(f(u)))
-    return boot(list(by.values()))
+    return pooled_ci(by_cluster(rows, f))
 
 
-def fmt(c) -> str:
-    return f"{c[0]:.3f} [{c[1]:.3f}, {c[2]:.3f}]"
+fmt = ci_text
 
 
 def mix(rows: list[dict]) -> str:
+    if not rows:
+        return "-"
     c = collections.Counter(u["label"] for u in rows)
-    return " ".join(f"{k} {c[k] / len(rows):.2f}" for k in LABELS if c[k]) if rows else "-"
+    return " ".join(f"{k} {c[k] / len(rows):.2f}" for k in LABELS if c[k])
 
 
 def load(units_path, labels_path) -> list[dict]:
     lab = labels(labels_path)
-    return [u | {"label": lab.get(u["id"], "UNLABELLED")}
-            for u in map(json.loads, Path(units_path).read_text().splitlines())]
+    return [{**u, "label": lab.get(u["id"], "UNLABELLED")} for u in map(json.loads,
+                                                                         Path(units_path).read_text().splitlines())]
+
+
+@dataclass
+class _Table:
+    head: list[str]
+    out: object
+    rows: list = field(default_factory=list)
+
+    def __post_init__(self):
+        self.out("| " + " | ".join(self.head) + " |")
+        self.out("|" + "---|" * len(self.head))
+
+    def row(self, *cells):
+        self.out("| " + " | ".join(str(c) for c in cells) + " |")
+
+
+def _is_hijack(u):
+    return u["label"] in HIJACK
+
+
+def _is_root_close(u):
+    return u["label"] == "ROOT_CLOSE"
+
+
+def _is_mounted(u):
+    return u["arm"] == "mounted"
 
 
 def report(units_path, labels_path, annotated=None, out=print) -> int:
     rows = load(units_path, labels_path)
-    bad = collections.Counter(u["label"] for u in rows if u["label"] in INVALID)
-    out(f"invalid labels left out of every rate: {dict(bad) or 'none'}")
+    invalid = collections.Counter(u["label"] for u in rows if u["label"] in INVALID)
+    out(f"invalid labels left out of every rate: {dict(invalid) or 'none'}")
     rows = [u for u in rows if u["label"] not in INVALID]
-    hj = lambda u: u["label"] in HIJACK  # noqa: E731
-    rc = lambda u: u["label"] == "ROOT_CLOSE"  # noqa: E731
-    pos = lambda u: u["position"]  # noqa: E731
-    is_m = lambda u: u["arm"] == "mounted"  # noqa: E731
     out(f"{len(rows)} labelled units, {len({u['cluster'] for u in rows})} question groups; hijack = S_TASK or "
         "IDENTITY; position = reply index / R's own replies; 95% bootstrap CIs over question groups\n")
-    out("| run | group | mounted / refused | hijack mounted | hijack refused | mounted - refused | "
-        "ROOT_CLOSE mounted - refused | position mounted - refused |")
-    out("|---|---|---|---|---|---|---|---|")
-    groups = [("all", lambda u: True), ("no earlier mount", lambda u: not u["mounted_before"])] + [
-        (r, lambda u, r=r: u["relation"] == r) for r in ("sibling", "cousin", "descendant", "ancestor", "self",
-                                                         "unknown")]
-    for run in sorted({u["run"] for u in rows}):
-        for g, sel in groups:
-            s = [u for u in rows if u["run"] == run and u["arm"] != "close_now" and sel(u)]
-            m, r = [u for u in s if is_m(u)], [u for u in s if not is_m(u)]
-            if s:
-                out(f"| {run} | {g} | {len(m)} / {len(r)} | {fmt(rate(m, hj)) if m else '-'} | "
-                    f"{fmt(rate(r, hj)) if r else '-'} | {fmt(boot_diff(s, hj, is_m))} | "
-                    f"{fmt(boot_diff(s, rc, is_m))} | {fmt(boot_diff(s, pos, is_m))} |")
-    out("\n| run | arm | n | hijack | ROOT_CLOSE | position | reply index | labels |")
-    out("|---|---|---|---|---|---|---|---|")
-    arms = [("mounted", is_m)] + [(f"refused: {x}", lambda u, x=x: u["refusal"] == x) for x in REASONS] + \
-        [("close_now", lambda u: u["arm"] == "close_now")]
-    for run in sorted({u["run"] for u in rows}):
-        for arm, sel in arms:
-            s = [u for u in rows if u["run"] == run and sel(u)]
-            if s:
-                out(f"| {run} | {arm} | {len(s)} | {fmt(rate(s, hj))} | {fmt(rate(s, rc))} | {fmt(rate(s, pos))} | "
-                    f"{fmt(rate(s, lambda u: u['reply_index']))} | {mix(s)} |")
+    runs = sorted({u["run"] for u in rows})
+    groups = [("all", lambda u: True), ("no earlier mount", lambda u: not u["mounted_before"])]
+    groups += [(rel, lambda u, rel=rel: u["relation"] == rel)
+               for rel in ("sibling", "cousin", "descendant", "ancestor", "self", "unknown")]
+    t = _Table(["run", "group", "mounted / refused", "hijack mounted", "hijack refused", "mounted - refused",
+                "ROOT_CLOSE mounted - refused", "position mounted - refused"], out)
+    for run in runs:
+        for name, sel in groups:
+            sub = [u for u in rows if u["run"] == run and u["arm"] != "close_now" and sel(u)]
+            if not sub:
+                continue
+            mounted = [u for u in sub if _is_mounted(u)]
+            refused = [u for u in sub if not _is_mounted(u)]
+            t.row(run, name, f"{len(mounted)} / {len(refused)}", fmt(rate(mounted, _is_hijack)) if mounted else "-",
+                  fmt(rate(refused, _is_hijack)) if refused else "-", fmt(boot_diff(sub, _is_hijack, _is_mounted)),
+                  fmt(boot_diff(sub, _is_root_close, _is_mounted)),
+                  fmt(boot_diff(sub, lambda u: u["position"], _is_mounted)))
+    out("")
+    arms = [("mounted", _is_mounted)] + [(f"refused: {x}", lambda u, x=x: u["refusal"] == x) for x in REASONS]
+    arms.append(("close_now", lambda u: u["arm"] == "close_now"))
+    t = _Table(["run", "arm", "n", "hijack", "ROOT_CLOSE", "position", "reply index", "labels"], out)
+    for run in runs:
+        for name, sel in arms:
+            sub = [u for u in rows if u["run"] == run and sel(u)]
+            if sub:
+                t.row(run, name, len(sub), fmt(rate(sub, _is_hijack)), fmt(rate(sub, _is_root_close)),
+                      fmt(rate(sub, lambda u: u["position"])), fmt(rate(sub, lambda u: u["reply_index"])), mix(sub))
     if annotated:
         precision(rows, annotated, out)
-    if bad:
-        out(f"\nNO RESULT: {sum(bad.values())} units have no valid label; rerun judge")
+    if invalid:
+        out(f"\nNO RESULT: {sum(invalid.values())} units have no valid label; rerun judge")
         return 1
     return 0
 
 
 def precision(rows: list[dict], annotated, out=print) -> dict:
-    """The judge's per-label precision against annotated cases (export's file, filled in)."""
+    """Per-label precision of the judge against hand-annotated cases (export's file with
+    the label column filled in), plus hijack precision and recall."""
     judged = {u["id"]: u["label"] for u in rows}
     cases = [c for c in map(json.loads, Path(annotated).read_text().splitlines())
              if c["id"] in judged and c.get("label")]
-    who = sorted({c.get("annotator", "") for c in cases})
-    out(f"\njudge vs annotated labels ({', '.join(who)}) on {len(cases)} cases\n")
-    out("| judge label | n | precision |")
-    out("|---|---|---|")
+    annotators = sorted({c.get("annotator", "") for c in cases})
+    out(f"\njudge vs annotated labels ({', '.join(annotators)}) on {len(cases)} cases\n")
+    t = _Table(["judge label", "n", "precision"], out)
     res = {}
     for lab in LABELS:
-        got = [c for c in cases if judged[c["id"]] == lab]
-        if got:
-            res[lab] = sum(c["label"] == lab for c in got) / len(got)
-            out(f"| {lab} | {len(got)} | {res[lab]:.2f} |")
-    pj = [c for c in cases if judged[c["id"]] in HIJACK]
-    ph = [c for c in cases if c["label"] in HIJACK]
-    res["hijack_precision"] = sum(c["label"] in HIJACK for c in pj) / max(1, len(pj))
-    res["hijack_recall"] = sum(judged[c["id"]] in HIJACK for c in ph) / max(1, len(ph))
-    out(f"| hijack | {len(pj)} | {res['hijack_precision']:.2f} (recall {res['hijack_recall']:.2f} of {len(ph)}) |")
+        hits = [c["label"] == lab for c in cases if judged[c["id"]] == lab]
+        if hits:
+            res[lab] = sum(hits) / len(hits)
+            t.row(lab, len(hits), f"{res[lab]:.2f}")
+    said = [c for c in cases if judged[c["id"]] in HIJACK]
+    truth = [c for c in cases if c["label"] in HIJACK]
+    res["hijack_precision"] = sum(c["label"] in HIJACK for c in said) / max(1, len(said))
+    res["hijack_recall"] = sum(judged[c["id"]] in HIJACK for c in truth) / max(1, len(truth))
+    t.row("hijack", len(said), f"{res['hijack_precision']:.2f} (recall {res['hijack_recall']:.2f} of {len(truth)})")
     return res
 
 
 def export(units_path, cases_path, n: int = 120) -> int:
-    """n units to annotate, half mounted and half refused (seed 0), with the judge's inputs
-    only (the arm is left out so an annotator does not see it)."""
+    """Up to n units to annotate by hand, half mounted and half refused (seed 0), carrying
+    only the judge's inputs (the arm is withheld so the annotator is blind to it)."""
     units = list(map(json.loads, Path(units_path).read_text().splitlines()))
-    rng, picked = random.Random(0), []
+    rng = random.Random(0)
+    picked = []
     for arm in ("mounted", "refused"):
         pool = [u for u in units if u["arm"] == arm]
-        picked += rng.sample(pool, min(len(pool), n // 2))
+        picked.extend(rng.sample(pool, min(len(pool), n // 2)))
     rng.shuffle(picked)
-    keep = ("id", "question", "threads", "R", "R_task", "S", "S_task", "action")
+    fields = ("id", "question", "threads", "R", "R_task", "S", "S_task", "action")
     with open(cases_path, "w") as f:
         for u in picked:
-            f.write(json.dumps({k: u[k] for k in keep} | {"label": "", "annotator": ""}, ensure_ascii=False) + "\n")
+            f.write(json.dumps({**{k: u[k] for k in fields}, "label": "", "annotator": ""}, ensure_ascii=False) + "\n")
     return len(picked)
 
 
@@ -418,8 +498,7 @@ def main(argv=None) -> int:
     if args.cmd == "extract":
         units, stats = extract_units(args.log_dirs)
         with open(args.out, "w") as f:
-            for u in units:
-                f.write(json.dumps(u, ensure_ascii=False) + "\n")
+            f.writelines(json.dumps(u, ensure_ascii=False) + "\n" for u in units)
         print(f"{len(units)} units", json.dumps(dict(sorted(stats.items()))))
         return 0
     if args.cmd == "judge":
