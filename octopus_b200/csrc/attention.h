@@ -68,7 +68,6 @@ void attn_bwd_delta(const __nv_bfloat16* o, int ldo, const __nv_bfloat16* dO, in
 void attn_bwd(const AttnBwdParams& p, int n_qtiles, int n_ktiles, int D, cudaStream_t st);
 cudaError_t attn_decode(const DecodeParams& p, int B, int D, cudaStream_t st);  // this call's launch error
 // tcgen05/TMEM forward (head_dim 128), same contract as attn_fwd with 128-row query tiles
-void attn_fwd_tc(const AttnParams& p, int n_tiles, int* status, cudaStream_t st);
 
 // TMA maps of the two-query-tile forward: q [Tq, Hq*D] box 64 x 128; k, v [rows, Hkv*D]
 // box 64 x 64 (one producer warp's rows), all 128-byte swizzled.

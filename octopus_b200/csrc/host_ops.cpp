@@ -115,14 +115,6 @@ void attn_decode_shared_t(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, t
 static bool g_pdl = false;
 void set_pdl(bool on) { g_pdl = on; }
 
-// L2 prefetch depth of B (K-blocks ahead of the TMA loads) for decode-sized GEMMs.  Off by
-// default: on the 7B decode shapes (M = 256) depths 8 and 16 measured 0-10% slower than none
-// (the weight stream is not bound by the latency of its loads); OCTO_GEMM_PF sets it.
-int gemm_prefetch_depth(int M) {
-  if (M > 256) return 0;
-  const char* e = std::getenv("OCTO_GEMM_PF");
-  return e != nullptr ? std::atoi(e) : 0;
-}
 
 int pick_bn(int M, int N, int sms, int hint) {
   if (hint == 64 || hint == 128 || hint == 256) return hint;
@@ -172,7 +164,7 @@ static GemmLaunch make_launch(const torch::Tensor& A, bool a_mn, const torch::Te
   g.alpha = 1.f;
   g.vocab_limit = N;
   g.s.pdl = g_pdl ? 1 : 0;
-  g.s.b_prefetch = gemm_prefetch_depth(M);
+  g.s.b_prefetch = 0;  // L2 prefetch of B only in PDL launches (see gemm_sm100.cuh)
   return g;
 }
 
@@ -647,10 +639,8 @@ std::vector<torch::Tensor> attn_fwd_t(torch::Tensor q, torch::Tensor k, torch::T
     maps.k = make_tmap_bf16_2d(k.data_ptr(), Hkv * D, k.size(0), k.stride(0), 64, 64);
     maps.v = make_tmap_bf16_2d(v.data_ptr(), Hkv * D, v.size(0), v.stride(0), 64, 64);
     attn_fwd_pp(p, maps, tiles.numel() / 2, status_ptr(q.get_device()), cur_stream(q));
-  } else if (use_tc) {
-    TORCH_CHECK(D == 128, "attention: the tcgen05 forward needs head_dim 128");
-    attn_fwd_tc(p, tiles.numel() / 2, status_ptr(q.get_device()), cur_stream(q));
   } else {
+    TORCH_CHECK(use_tc == 0, "attention: kernel mode must be 2 (tcgen05, head_dim 128) or 0 (mma.sync)");
     attn_fwd(p, tiles.numel() / 2, D, cur_stream(q));
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -56,7 +56,7 @@ static GemmLaunch base_launch(int M, const torch::Tensor& W, int bn_hint) {
   g.stream = at::cuda::getCurrentCUDAStream(dev).stream();
   g.alpha = 1.f;
   g.vocab_limit = N;
-  g.s.b_prefetch = gemm_prefetch_depth(M);
+  g.s.b_prefetch = 0;
   return g;
 }
 

@@ -52,7 +52,6 @@ inline int num_sms(int device) {
 
 // GEMM N-tile width for an M x N problem on `sms` SMs (hint 64/128/256 forces it).
 int pick_bn(int M, int N, int sms, int hint);
-int gemm_prefetch_depth(int M);
 // Split count of `k_blocks` K blocks into about `want` splits with none empty (the kernel
 // gives split s the blocks [s * per, s * per + per) with per = ceil(k_blocks / splits)).
 inline int nonempty_splits(int k_blocks, int want) {

@@ -1,11 +1,13 @@
 // Tensor-parallel fused kernels over NVLink peer memory (sm_100a).
 //
-//   AG -> GEMM   the persistent tcgen05 GEMM with an A source that TMA-loads each
-//                128-row block of the sequence-sharded activation straight from the
-//                rank that owns it (plain tiled TMA loads of peer memory, no staging copy).  Every
-//                CTA publishes "my shard is ready" to the peers when it starts and waits
-//                (bounded) for a peer's publication before its first load from that peer,
-//                so the transfer overlaps the MMAs tile by tile.
+//   AG -> GEMM   the persistent tcgen05 GEMM with an A source that gathers the
+//                sequence-sharded activation into a LOCAL staging buffer: the epilogue
+//                warps copy each remote row over NVLink once with plain 16-byte peer loads
+//                (after a bounded wait for the owner's "shard ready" signal) and publish
+//                per-128-row-block readiness counters, while the producer starts on the
+//                rank's own rows.  The producer's TMA loads read local memory only (the
+//                rank's own shard or the staging buffer, after the block's counter is
+//                complete), so the transfer overlaps the MMAs block by block.
 //   GEMM -> RS   the same GEMM with an epilogue that stores each accumulator row as bf16
 //                into the receive buffer of the rank owning that row (peer stores), then
 //                signals; the owner's reduce kernel sums the tp partials in rank order

@@ -30,21 +30,16 @@ CPU_VOCAB_CHUNK = 1024  # vocab columns per chunk of the CPU head (online log-su
 
 
 def use_tc_attention(D: int) -> int:
-    """Attention forward kernel: 2 = tcgen05/TMEM with two query tiles per CTA (head_dim 128,
-    the default), 1 = tcgen05 with one query tile per CTA, 0 = mma.sync (OCTO_ATTN_TC)."""
-    import os
-
-    if D != 128:
-        return 0
-    return int(os.environ.get("OCTO_ATTN_TC", "2"))
+    """Attention forward kernel: 2 = tcgen05/TMEM with two query tiles per CTA (head_dim
+    128: every BASELINE model), 0 = the mma.sync kernel for other head dims (the tiny
+    test models use 64)."""
+    return 2 if D == 128 else 0
 
 
 def use_tc_bwd(D: int) -> int:
-    """Attention backward kernels: 1 = tcgen05/TMEM (head_dim 128, the default), 0 = mma.sync
-    (OCTO_ATTN_BWD_TC=0)."""
-    import os
-
-    return int(D == 128 and os.environ.get("OCTO_ATTN_BWD_TC", "1") != "0")
+    """Attention backward kernels: 1 = tcgen05/TMEM (head_dim 128), 0 = mma.sync (other
+    head dims)."""
+    return int(D == 128)
 
 
 def _is_cuda(t: torch.Tensor) -> bool:

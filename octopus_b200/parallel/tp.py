@@ -14,7 +14,7 @@ Between the row- and column-parallel GEMMs the residual stream is sequence-shard
 rank r keeps rows [r rows_s, (r+1) rows_s) of h.  One layer on rank r:
 
   x_r  = rmsnorm(h_r)                      (written into r's IPC activation buffer)
-  qkv  = AG(x_0..x_tp-1) @ qkv_w_r^T       ag_gemm: TMA loads of peer shards, tcgen05 MMA
+  qkv  = AG(x_0..x_tp-1) @ qkv_w_r^T       ag_gemm: peer rows copied into local staging, tcgen05 MMA
   o    = attention(rope(qkv)) on r's heads  local KV cache holds r's KV heads
   h_r += RS(o @ o_w_r^T)                   gemm_rs: epilogue peer stores + tp_reduce
   x_r  = rmsnorm(h_r)                      (fused into tp_reduce)

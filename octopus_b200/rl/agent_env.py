@@ -20,6 +20,7 @@ from dataclasses import dataclass, field
 
 from ..runtime.core import branch_key, tree_branches
 from ..runtime.tree import CursorRuntime
+from .group import read_outcomes
 from .workflow import TrainRow, plan_group_rewards, rows_to_microbatches
 
 
@@ -87,12 +88,15 @@ class AgentEnv:
             ctl = tree.get("control")
             if ctl and "answer" in ctl and not self.grade_workspace:  # the main-first control's grade
                 ep["control_y"] = float(self.grade(self.tasks[ti], ctl["answer"]))
+            if tree.get("read_controls"):  # OCTOPUS_READ_CONTROL counterfactuals (credit on the read reply)
+                ep["read_controls"] = [{k: v for k, v in c.items() if k != "result"} for c in tree["read_controls"]]
             groups.setdefault(ti, []).append(ep)
             out.episodes.append(ep)
             out.rewards.append(ep["y"])
             out.generated_tokens += sum(int(r["completion_tokens"]) for r in res["requests"])
         for eps in groups.values():
-            rows: list[TrainRow] = plan_group_rewards(eps, out.records, self.branch_credit, self.gate, self.filter)
+            rows: list[TrainRow] = plan_group_rewards(eps, out.records, self.branch_credit, self.gate, self.filter,
+                                                      read_rewards=read_outcomes)
             if rows:
                 out.units.append(rows)
         for rid in list(engine.records):

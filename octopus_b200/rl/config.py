@@ -42,6 +42,8 @@ class RolloutSection:
     max_tokens: int = 262144
     tool_call_parser: str = "qwen3_coder"
     tp: int = 1
+    push_hosts: str = ""        # comma list of remote rollout hosts to push each weight version to ("" = off)
+    push_dir: str = ""          # destination folder on those hosts (one v<version> subfolder per push)
 
 
 @dataclass

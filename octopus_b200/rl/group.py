@@ -48,6 +48,12 @@ def group_step(episodes: list[dict], branch_credit: str = "outcome", gate=None, 
     return episodes
 
 
+def read_outcomes(episode: dict, control: dict, branch: dict) -> tuple[float, float]:
+    """Default read-control rewards: 1 for a branch (the reader, or its control) that closed
+    with commit, else 0.  Environments that grade branch results can pass their own."""
+    return float(branch.get("ended_with") == "commit"), float(control.get("end") == "commit")
+
+
 def read_values(episode: dict, read_rewards) -> dict:
     """Read-control counterfactual: {reader reply id: {calls, call, v = r_reader - r_control}}."""
     out = {}

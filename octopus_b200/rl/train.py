@@ -245,6 +245,23 @@ def _swe_env(cfg, engine, rep, replicas):
                          timeout=cfg.rl.swe_timeout, filter_zero_variance=cfg.rl.filter_zero_variance)
 
 
+def _push_weights(actor, cfg, run_dir: str) -> dict:
+    """Weight sync to remote rollout hosts (rollout.push_hosts): the adapter (LoRA actors)
+    or the HF weights of this version, written under run_dir/push/v<version> and copied
+    to <push_dir>/v<version> on every host (rl.adapter_push: tar over ssh with retries)."""
+    from ..models.decoder import save_hf
+    from .adapter_push import push_adapter
+
+    src = os.path.join(run_dir, "push", f"v{actor.version}")
+    if hasattr(actor, "lora"):
+        actor.lora.save_peft(src, base_model=cfg.model.path)
+    else:
+        save_hf(actor.weights, src)
+    hosts = [h.strip() for h in cfg.rollout.push_hosts.split(",") if h.strip()]
+    dest = os.path.join(cfg.rollout.push_dir or "octopus_weights", f"v{actor.version}")
+    return push_adapter(src, hosts, dest)
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="python -m octopus_b200.rl.train")
     ap.add_argument("--config", default=DEFAULT_CONFIG)
@@ -299,6 +316,8 @@ def main(argv=None) -> int:
             print(line, flush=True)
             log.write(line + "\n")
             log.flush()
+        if cfg.rollout.push_hosts and rank == 0:
+            _push_weights(actor, cfg, run_dir)
         if cfg.checkpoint.recover_every and (step + 1) % cfg.checkpoint.recover_every == 0:
             checkpoint.save(actor, run_dir, step + 1, {"step": step + 1}, spool=spool)
         if cfg.checkpoint.save_every and (step + 1) % cfg.checkpoint.save_every == 0 and rank == 0:

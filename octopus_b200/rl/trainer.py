@@ -25,14 +25,16 @@ import torch
 from ..envs.dag import instance_microbatches
 from ..utils.iostats import d2h
 from .actor import Actor, build_microbatch
+from .dp_balance import longest_first
 
 
 @dataclass
 class TrainerConfig:
     mb_tokens: int = 32768      # prefix-tree tokens per micro-batch (flat estimate)
     sync_every: int = 1
-    # (index, count): train every count-th micro-batch starting at index.  Ranks of one
-    # tensor-parallel rollout group hold the same rollout and split its training this way.
+    # (index, count): this rank's share of the micro-batches when `count` ranks hold the same
+    # rollout (the ranks of one tensor-parallel rollout group split its training): the
+    # micro-batches are assigned largest-first by prefix-tree tokens (rl.dp_balance).
     mb_shard: tuple = (0, 1)
 
 
@@ -52,8 +54,8 @@ class RLTrainer:
         else:
             mbs = instance_microbatches(ro, self.cfg.mb_tokens, build_microbatch)
         k, n = self.cfg.mb_shard
-        if n > 1:
-            mbs = mbs[k::n]
+        if n > 1:  # this rank's share: micro-batches assigned longest-first by tree tokens
+            mbs = [mbs[i] for i in sorted(longest_first([mb.n_tree for mb in mbs], n)[k])]
         stats = self.actor.train_step(mbs)
         stats["micro_batches"] = len(mbs)
         stats["tree_tokens"] = sum(mb.n_tree for mb in mbs)

@@ -12,16 +12,27 @@ time since the last step line) and returns an action:
   * a traceback inside octopus_b200 code -> NEEDS-MAIN: stop, a human must look
   * otherwise               -> continue
 
-The policy (`decide`) is pure and testable; `Watchdog.poll` gathers the facts and
-`apply` edits the live env file.  Restarting processes is the launcher's job: the
-watchdog returns the action.
+The policy (`decide`) is pure and testable; `Watchdog.step` gathers the facts, applies
+the micro-batch cut to the live env file and returns the action.  `supervise` (the
+command line below) is the launcher: it runs the training command in its own process
+group with OCTOPUS_LIVE_ENV pointing at the live env file (the trainer re-reads it every
+step and resumes from its recover checkpoint on restart), polls, and stops / restarts it
+as decided:
+
+    python -m octopus_b200.rl.watchdog --log run.log --live-env live.env [--poll 60] -- \
+        python -m octopus_b200.rl.train --config grpo.yaml ...
 
 Reference parity (behaviour): `scripts/rl_env/rl_watchdog.sh:1-80`.
 """
 from __future__ import annotations
 
+import argparse
+import json
 import os
 import re
+import signal
+import subprocess
+import sys
 import time
 from dataclasses import dataclass, field
 
@@ -109,6 +120,11 @@ class Watchdog:
         self.live_env_path = live_env_path
         self.stall_s = stall_s
         self.counts: dict[str, int] = {}
+        self.offset = 0  # log bytes written before the current run of the command (ignored)
+
+    def mark_restart(self):
+        """Ignore what earlier runs wrote to the log (the next facts read only the new run)."""
+        self.offset = os.path.getsize(self.log_path) if os.path.exists(self.log_path) else 0
 
     def facts(self, running: bool, exit_code: int | None = None) -> Facts:
         tail = ""
@@ -117,7 +133,7 @@ class Watchdog:
             with open(self.log_path, "rb") as f:
                 f.seek(0, 2)
                 n = f.tell()
-                f.seek(max(0, n - 65536))
+                f.seek(max(self.offset, n - 65536))
                 tail = f.read().decode("utf-8", "replace")
             last = os.path.getmtime(self.log_path)
         mem = 0.0
@@ -138,3 +154,71 @@ class Watchdog:
             if d.mb_tokens_factor != 1.0 and self.live_env_path:
                 cut_mb_tokens(self.live_env_path, d.mb_tokens_factor)
         return d
+
+
+def _stop_group(proc, grace_s: float = 30.0) -> int:
+    """SIGTERM the child's process group, SIGKILL it after `grace_s`; returns its exit code."""
+    if proc.poll() is None:
+        try:
+            os.killpg(proc.pid, signal.SIGTERM)
+            proc.wait(timeout=grace_s)
+        except subprocess.TimeoutExpired:
+            os.killpg(proc.pid, signal.SIGKILL)
+            proc.wait()
+        except ProcessLookupError:
+            pass
+    return proc.returncode
+
+
+EXIT_CODES = {"finished": 0, "needs_main": 2}
+
+
+def supervise(cmd: list[str], log_path: str, live_env: str, poll_s: float = 60.0, stall_s: float = STALL_S,
+              sleep=time.sleep, report=print) -> int:
+    """Run `cmd` under the watchdog until it finishes or the policy gives up.
+    Returns 0 when the run finished, 2 when a traceback in this package needs a person,
+    1 when it stopped for another reason."""
+    wd = Watchdog(log_path, live_env, stall_s)
+    env = dict(os.environ, OCTOPUS_LIVE_ENV=os.path.abspath(live_env))
+
+    def launch():
+        wd.mark_restart()
+        with open(log_path, "ab") as log:
+            return subprocess.Popen(cmd, stdout=log, stderr=subprocess.STDOUT, env=env, start_new_session=True)
+
+    proc, restarts = launch(), 0
+    while True:
+        sleep(poll_s)
+        code = proc.poll()
+        d = wd.step(code is None, code)
+        if d.action == "continue":
+            continue
+        if code is None:
+            code = _stop_group(proc)
+        report(json.dumps({"t": round(time.time(), 1), "action": d.action, "reason": d.reason, "exit_code": code,
+                           "restarts": restarts, "counts": wd.counts}))
+        if d.action == "resume":
+            restarts += 1
+            proc = launch()
+            continue
+        if d.action == "needs_main":
+            return EXIT_CODES["needs_main"]
+        return EXIT_CODES["finished"] if d.reason == "finished" else 1
+
+
+def main(argv=None) -> int:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    if "--" not in argv:
+        raise SystemExit("usage: python -m octopus_b200.rl.watchdog --log LOG --live-env FILE [--poll S] -- CMD ...")
+    k = argv.index("--")
+    ap = argparse.ArgumentParser(prog="python -m octopus_b200.rl.watchdog")
+    ap.add_argument("--log", required=True, help="the run's log file (the child's stdout / stderr go here)")
+    ap.add_argument("--live-env", required=True, help="live env file (MB_TOKENS=...) the trainer re-reads")
+    ap.add_argument("--poll", type=float, default=60.0)
+    ap.add_argument("--stall", type=float, default=STALL_S, help="seconds without a log write that count as a stall")
+    args = ap.parse_args(argv[:k])
+    return supervise(argv[k + 1:], args.log, args.live_env, args.poll, args.stall)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

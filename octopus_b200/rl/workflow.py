@@ -99,6 +99,11 @@ def episode_rows(episode: dict, records: dict) -> list[TrainRow]:
                     beh[a:b] = rr["logprobs"][: b - a]
         for a, b, d in own["spans"]:
             adv[a:b] += d
+        read_adv = episode.get("read_adv") or {}
+        for rid in chain:  # a read reply with a read control: its completion gets r_reader - r_control more
+            if rid in read_adv:
+                rr = records[rid]
+                adv[rr["prompt_len"]: rr["prompt_len"] + rr["completion"]] += read_adv[rid]["v"]
         # mounted rows are placeholders in the engine's sequence; the prefix tree takes the
         # sequence without them plus (at, source, s0, s1) mounts in that coordinate system
         toks = rec["tokens"]
@@ -125,7 +130,7 @@ def _source_range(src: str, s0: int, s1: int, records: dict) -> tuple[int, int]:
 
 
 def plan_group_rewards(episodes: list[dict], records: dict, branch_credit: str = "outcome", gate=None,
-                       filter_zero_variance: bool = True) -> list[TrainRow]:
+                       filter_zero_variance: bool = True, read_rewards=None) -> list[TrainRow]:
     """Rows of one group (episodes of the same task); [] when the group is filtered."""
     if filter_zero_variance and not has_variance([float(e["y"]) for e in episodes]):
         return []
@@ -136,7 +141,7 @@ def plan_group_rewards(episodes: list[dict], records: dict, branch_credit: str =
             if th != "main" and not th.startswith("readctl/") and th != "control" and branch_key(th) not in have:
                 e.setdefault("branches", []).append({"key": branch_key(th)})
                 have.add(branch_key(th))
-    group_step(episodes, branch_credit=branch_credit, gate=gate)
+    group_step(episodes, branch_credit=branch_credit, gate=gate, read_rewards=read_rewards)
     return [row for e in episodes for row in episode_rows(e, records)]
 
 

@@ -27,8 +27,8 @@ import time
 from pathlib import Path
 
 from . import settings as S
-from .core import (CLOSING, DONE_TOOL, READ_TOOL, RUNTIME_NAMES, RuntimePort, apply_runtime, branch_task_message,
-                   closing_name, closing_step, cursor_delta, handed, join_note, run_thread, runtime_tools,
+from .core import (CLOSING, DONE_TOOL, READ_TOOL, RUNTIME_NAMES, RuntimePort, apply_runtime, branch_key,
+                   branch_task_message, closing_name, closing_step, cursor_delta, handed, join_note, run_thread, runtime_tools,
                    thread_name, without_cursors)
 
 FORK_DEPTH_REFUSAL = "Forking is not available at this depth; finish this task yourself."
@@ -117,6 +117,7 @@ class CursorRuntime:
         self.used = 0  # completion tokens against the shared budget
         self.budget_out = False
         self.pending_mounts: dict[str, list] = {}
+        self._read_caps: dict[str, dict] = {}  # OCTOPUS_READ_CONTROL: branch -> state before its mount request
         self._ids = itertools.count()
 
     # ------------------------------------------------------------------ transport
@@ -131,6 +132,8 @@ class CursorRuntime:
                     body["audit_messages"] = without_cursors(messages)
         if self.pending_mounts.get(thread):
             body["mount"] = list(self.pending_mounts[thread])
+            if S.read_control() and self._is_branch(thread) and thread not in self._read_caps:
+                await self._capture_read(thread, messages)
         t0 = time.time()
         payload = self._complete_fn(body)
         if hasattr(payload, "__await__"):
@@ -167,7 +170,7 @@ class CursorRuntime:
     async def _thread_tool(self, thread: str, port: RuntimePort, forks_this_turn: list, name: str, args: dict):
         depth = self.depth(thread)
         if name == "fork":
-            if thread == "control":  # the control runs without forks
+            if thread == "control" or thread.startswith("readctl/"):  # controls run without forks
                 return FORK_DEPTH_REFUSAL, False
             if forks_this_turn:
                 return ONE_FORK, False
@@ -194,6 +197,8 @@ class CursorRuntime:
                 return MAIN_CLOSE.format(name), False
             return apply_runtime(name, args, port)
         if name == "read_thread":
+            if thread.startswith("readctl/"):  # a read control runs without the mount it replaces
+                return "read_thread: not available in this thread", False
             return self._read(thread, args), False
         return await self.ws.dispatch(name, args, thread)
 
@@ -224,7 +229,7 @@ class CursorRuntime:
         self.pending_mounts.setdefault(reader, []).append((cursor, start_tok, end_tok))
         return MOUNT_RESULT.format(src=src, a=a, b=b, n=end_tok - start_tok)
 
-    async def _run_thread(self, thread: str, start: dict, depth: int) -> dict:
+    async def _run_thread(self, thread: str, start: dict, depth: int, max_steps_left: int | None = None) -> dict:
         port = RuntimePort(owner=None if thread == "main" else start["branch_id"])
         forks_this_turn: list = []
         my_forks = self.forks.setdefault(thread, [])
@@ -284,6 +289,8 @@ class CursorRuntime:
 
         closing = self.ws.closing(depth)
         max_steps = None if depth == 0 else self.branch_turns
+        if max_steps_left is not None:
+            max_steps = max_steps_left if max_steps is None else min(max_steps, max_steps_left)
         max_calls = self.max_main_calls if depth == 0 else None
         budget = S.thread_budget()
 
@@ -294,7 +301,7 @@ class CursorRuntime:
                                join=join, max_calls=max_calls, before_turn=before_turn,
                                snapshot=lambda: self.ws.snapshot(thread),
                                restore=lambda snap: self.ws.restore(thread, snap), ws=self.ws)
-        self.threads.setdefault(thread, {"replies": []})["steps"] = res["steps"]
+        self.threads.setdefault(thread, {"replies": []}).update(steps=res["steps"], messages=res["messages"])
         return res
 
     # ------------------------------------------------------------------ episode
@@ -310,6 +317,8 @@ class CursorRuntime:
                 "budget": self.ws.budget(), "used": self.used, "reminded": res["reminded"]}
         if S.plan_control() and tree["forks"]:
             tree["control"] = await self._control(task, res)
+        if S.read_control() and self._read_caps:
+            tree["read_controls"] = [await self._read_control(task, th, cap) for th, cap in self._read_caps.items()]
         if self.log_dir:
             self._write(tree, res)
         await self.ws.close()
@@ -344,6 +353,57 @@ class CursorRuntime:
             self.max_main_calls = saved
         return {"kind": "main-first", "calls_before": calls_before, "answer": handed(closing_step(res["steps"])),
                 "main_end": self._main_end(res["steps"]), "requests": len(self.requests) - n0}
+
+    # ------------------------------------------------------------------ read controls
+    @staticmethod
+    def _is_branch(thread: str) -> bool:
+        return thread not in ("main", "control") and not thread.startswith("readctl/")
+
+    async def _capture_read(self, thread: str, messages: list) -> None:
+        """OCTOPUS_READ_CONTROL: the state just before a branch's first request that carries a
+        mount: its history, its workspace, the reply whose read_thread call mounted and the
+        turns it had used.  _read_control continues from here without the mount."""
+        reply = next((m for m in reversed(messages) if m.get("role") == "assistant"), {})
+        names = [(c.get("function") or {}).get("name") for c in reply.get("tool_calls") or []]
+        results = [str(m.get("content") or "") for m in messages if m.get("role") == "tool"][-len(names):] \
+            if names else []
+        reads = [k for k, n in enumerate(names) if n == "read_thread"]
+        mounted = [j for j, k in enumerate(reads) if k < len(results) and results[k].startswith("read_thread: mounted")]
+        replies = self.threads.get(thread, {}).get("replies") or []
+        self._read_caps[thread] = {
+            "messages": [dict(m) for m in messages], "snap": await self.ws.snapshot(thread),
+            "read_rid": replies[-1][0] if replies else None, "read_calls": names,
+            "read_call": mounted[0] if mounted else 0, "turns": len(replies), "history": len(messages)}
+
+    async def _read_control(self, task: str, thread: str, cap: dict) -> dict:
+        """One read control: the reader's state before its mount request continued without the
+        mount (forks and reads refused), in a copy of the reader's workspace restored to that
+        point, with the turns the reader had left.  Its requests are logged under thread
+        readctl/<reader> (never trained); the record names the reader (`of`, the branch key),
+        the read reply and call, how the control ended and its result for grading."""
+        name = f"readctl/{thread}"
+        rec = {"of": branch_key(thread), "thread": thread, "read_rid": cap["read_rid"], "read_calls": cap["read_calls"],
+               "read_call": cap["read_call"]}
+        later = (self.threads.get(thread, {}).get("messages") or [])[cap["history"]:]
+        rec["forked_after"] = any((c.get("function") or {}).get("name") == "fork"
+                                  for m in later if m.get("role") == "assistant" for c in m.get("tool_calls") or [])
+        try:
+            await self.ws.copy(thread, name)
+            if cap["snap"] is not None:
+                await self.ws.restore(name, cap["snap"])
+        except BranchCopyError as e:
+            return {**rec, "error": f"copy failed: {e}"}
+        bid = thread.rsplit("/", 1)[-1]
+        start = {"branch_id": bid, "session_id": f"{self.session_id}/{name}", "task": task,
+                 "messages": [dict(m) for m in cap["messages"]]}
+        left = None if self.branch_turns is None else max(1, self.branch_turns - cap["turns"])
+        n0 = len(self.requests)
+        res = await self._run_thread(name, start, self.depth(thread), max_steps_left=left)
+        closing = closing_step(res["steps"])
+        rec.update(end=closing_name(res["steps"]) if closing else "stopped", summary=handed(closing),
+                   control_forked=any(s.get("name") == "fork" for s in res["steps"]),
+                   requests=len(self.requests) - n0, result=await self.ws.capture(name))
+        return rec
 
     def _main_end(self, steps: list) -> str:
         if any(s.get("name") == "done" and not s.get("rejected") for s in steps):

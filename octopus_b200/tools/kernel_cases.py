@@ -7,8 +7,7 @@ Cases (inputs sized above L2 where DRAM behaviour matters, a few GB at most):
   gemm_wgrad_7b      dY^T X for the down projection (MN-major operands)
   attn_fwd_pp        tree attention forward, tcgen05 kernel with two query tiles per CTA
                      (8 x 2048 own + 2048 prefix)
-  attn_fwd_tc        same, tcgen05 kernel with one query tile per CTA
-  attn_fwd_mma       same on the mma.sync kernel
+  attn_fwd_mma       same on the mma.sync kernel (the path of head dims other than 128)
   attn_bwd           tree attention backward (dq + dkv kernels)
   decode_splitk      paged decode, 256 requests x 3000 keys (split-K kernel)
   decode_persistent  same on the persistent producer/consumer kernel
@@ -120,10 +119,10 @@ def build(case: str, dev):
         X = torch.randn(16384, 18944, device=dev).bfloat16()
         G = torch.zeros(3584, 18944, device=dev)
         return lambda: ops.gemm(dY, X, a_mn=True, b_mn=True, out=G, accumulate=True)
-    if case in ("attn_fwd_pp", "attn_fwd_tc", "attn_fwd_mma"):
+    if case in ("attn_fwd_pp", "attn_fwd_mma"):
         plan, qkv, Hq, Hkv, D = tree_case(dev)
         q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
-        mode = {"attn_fwd_pp": 2, "attn_fwd_tc": 1, "attn_fwd_mma": 0}[case]
+        mode = {"attn_fwd_pp": 2, "attn_fwd_mma": 0}[case]
         return lambda: ops.ext().attn_fwd(q, k, v, plan.cu_q, plan.cu_k, plan.key_idx, plan.tiles_for(mode), Hq, Hkv,
                                           D, D ** -0.5, True, True, mode)
     if case == "attn_bwd":

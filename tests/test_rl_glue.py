@@ -1,4 +1,5 @@
 """Spool crash semantics, DP balance, run config, recover checkpoints, watchdog policy (CPU)."""
+import json
 import os
 import time
 
@@ -110,3 +111,68 @@ def test_group_credit():
     reqs = [{"thread": "main", "completion_tokens": 5}, {"thread": "fork0/branch-0", "completion_tokens": 7},
             {"thread": "fork0/branch-1", "completion_tokens": 9}, {"thread": "main", "completion_tokens": 3}]
     assert critical_path(reqs) == 17
+
+
+def test_watchdog_supervise_restarts_after_oom(tmp_path):
+    """A child that fails with a CUDA OOM is restarted with MB_TOKENS cut by 10% in the live
+    env file (which it sees through OCTOPUS_LIVE_ENV); its second run finishes."""
+    import sys
+
+    log, live, marker = tmp_path / "run.log", tmp_path / "live.env", tmp_path / "ran_once"
+    live.write_text("MB_TOKENS=100000\n")
+    child = (f"import os, sys, pathlib\n"
+             f"m = pathlib.Path({str(marker)!r})\n"
+             f"print('live', open(os.environ['OCTOPUS_LIVE_ENV']).read().strip(), flush=True)\n"
+             f"if not m.exists():\n"
+             f"    m.write_text('1'); print('torch.OutOfMemoryError: CUDA out of memory', flush=True); sys.exit(1)\n"
+             f"print('step 1 done', flush=True)\n")
+    reports = []
+    rc = watchdog.supervise([sys.executable, "-c", child], str(log), str(live), poll_s=1.0, report=reports.append)
+    assert rc == 0
+    assert "MB_TOKENS=89088" in live.read_text()  # 100000 * 0.9, rounded down to a multiple of 1024
+    text = log.read_text()
+    assert "out of memory" in text and "MB_TOKENS=89088" in text and "step 1 done" in text
+    acts = [json.loads(r)["action"] for r in reports]
+    assert acts == ["resume", "stop"]
+
+
+def test_trainer_split_is_longest_first():
+    from octopus_b200.rl.trainer import RLTrainer, TrainerConfig
+
+    class MB:
+        def __init__(self, n):
+            self.n_tree, self.n_flat = n, n
+
+    class FakeActor:
+        def train_step(self, mbs):
+            self.got = mbs
+            return {"loss": 0.0}
+
+    mbs = [MB(n) for n in (10, 900, 20, 800, 30)]
+
+    class Ro:
+        def microbatches(self, cap, build):
+            return mbs
+
+    shares = []
+    for k in range(2):
+        a = FakeActor()
+        RLTrainer(a, None, None, TrainerConfig(mb_shard=(k, 2))).train_on(Ro())
+        shares.append(sorted(m.n_tree for m in a.got))
+    assert shares == [[900], [10, 20, 30, 800]]  # 900 | 800 + 30 + 20 + 10
+
+
+def test_push_weights_after_a_step(tmp_path, monkeypatch):
+    """rollout.push_hosts: each weight version is written under the run folder and handed
+    to the tar-over-ssh push for every host (the push itself is faked here)."""
+    from octopus_b200.rl import adapter_push, train
+
+    calls = []
+    monkeypatch.setattr(adapter_push, "push_adapter", lambda src, hosts, dest: calls.append((src, hosts, dest)) or {})
+    cfg = config.load(None, ["rollout.push_hosts=h1, h2", "rollout.push_dir=/srv/w"])
+    actor = Actor(get_config("tiny", layers=1), "cpu", dtype=torch.float32)
+    actor.version = 3
+    train._push_weights(actor, cfg, str(tmp_path))
+    (src, hosts, dest), = calls
+    assert hosts == ["h1", "h2"] and dest == "/srv/w/v3" and src.endswith("push/v3")
+    assert any(f.endswith(".safetensors") for f in os.listdir(src))

@@ -200,3 +200,38 @@ def test_fork_wall_from_logs(tmp_path, monkeypatch):
     # fork: main 2 replies + the longest branch (1 reply) = 3 x 20 tokens; control: 0 before + 1 reply
     assert out["pairs"] == 1 and out["ratio_median"] == 3.0 and out["fork_cheaper"] == 0.0
     assert out["gain"] == 1.0 and out["gain_when_not"] == 1.0
+
+
+def test_read_control_continues_without_the_mount(monkeypatch):
+    """OCTOPUS_READ_CONTROL: a branch whose read mounted gets a continuation from the state
+    before its mount request, without the mount; forks and reads are refused there; the
+    record names the reader, its read reply and how the control ended."""
+    monkeypatch.setenv("OCTOPUS_READ_TOOL", "1")
+    monkeypatch.setenv("OCTOPUS_READ_CONTROL", "1")
+    chat = Scripted({
+        "readctl/fork0/branch-1": [("", [call("fork", tasks=["x", "y"]), call("read_thread", thread="branch-0")]),
+                                   ("", [call("abort", branch_id="branch-1")])],
+        "ep": [("", [call("fork", tasks=["a", "b"])]), ("", [call("done", answer="q")])],
+        "branch-0": [("", [call("commit", branch_id="branch-0", summary="s0")])],
+        "branch-1": [("", [call("read_thread", thread="branch-0")]),
+                     ("", [call("commit", branch_id="branch-1", summary="s1")])],
+    })
+    out = run_episode(WorkspaceProvider(), chat, "t")
+    (rc,) = out["tree"]["read_controls"]
+    assert rc["of"] == "fork0-branch-1" and rc["read_calls"] == ["read_thread"] and rc["read_call"] == 0
+    assert rc["end"] == "abort" and not rc["forked_after"] and rc["control_forked"]
+    reader = [b for b in chat.bodies if b["session_id"] == "ep/fork0/branch-1"]
+    ctl = [b for b in chat.bodies if "readctl" in b["session_id"]]
+    assert reader[1].get("mount") and not any(b.get("mount") for b in ctl)
+    # the control started from the reader's history as it stood at the mount request
+    tools = [str(m["content"]) for m in ctl[0]["messages"] if m.get("role") == "tool"]
+    assert tools[-4].startswith("read_thread: mounted")  # the reader's read, then the control's own turns:
+    assert tools[-3].startswith("Forking is not available") and "not available in this thread" in tools[-2]
+    assert rc["read_rid"] == next(r["id"] for r in out["requests"] if r["thread"] == "fork0/branch-1")
+    assert all(r["thread"] == "readctl/fork0/branch-1" for r in out["requests"][-2:])
+    # credit: the reader committed, its control aborted -> +1 on the read reply
+    from octopus_b200.rl.group import read_outcomes, read_values
+    branches = [{"key": "fork0-branch-1", "ended_with": "commit"}]
+    assert read_values({"read_controls": [rc], "branches": branches}, read_outcomes) == {}  # it tried to fork
+    clean = {**rc, "control_forked": False}
+    assert read_values({"read_controls": [clean], "branches": branches}, read_outcomes)[rc["read_rid"]]["v"] == 1.0
