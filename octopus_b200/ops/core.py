@@ -642,8 +642,10 @@ def sample(h, W, temperature: float = 1.0, seed: int = 0, row_stream=None, vocab
     z = (ref._f(h) @ ref._f(W).t()) * alpha
     if vocab_limit is not None:
         z = z[:, :vocab_limit]
-    gen = torch.Generator().manual_seed(int(seed))
-    u = torch.rand(z.shape, generator=gen, dtype=z.dtype).clamp_(1e-7, 1 - 1e-7)
+    # counter-based noise of (seed, row stream, token): a row's sample does not depend on
+    # which other rows share its batch (as on the GPU)
+    rs = row_stream.cpu() if row_stream is not None else torch.arange(z.shape[0])
+    u = _uniform(seed, rs, z.shape[1]).to(z.dtype)
     tok = (z - torch.log(-torch.log(u))).argmax(-1)
     lp = torch.log_softmax(z, -1).gather(1, tok[:, None])[:, 0]
     return tok, lp.float()

@@ -634,6 +634,122 @@ class Engine:
             self.stats["decode_steps"] += steps
         return out_t, out_l
 
+    # ------------------------------------------------------------------ continuous batching
+    # (serving.scheduler drives these: requests join after a prefill, decode in chunks of a
+    # few steps together with every live request, and leave when they stop)
+    @property
+    def supports_continuous(self) -> bool:
+        return self.mount_layers is None  # layer-subset mounts keep a second key list per row
+
+    @torch.no_grad()
+    def admit(self, inputs: list[GenInput]) -> list:
+        """Resolve, allocate and prefill `inputs` (one sampling setting); per input either a
+        live request (its first sampled token in out_tok / out_lp) or the exception that
+        failed it alone (unknown cursor, bad mount, no KV room)."""
+        live, out = [], []
+        for inp in inputs:
+            try:
+                r = self._resolve(inp)
+            except Exception as e:  # noqa: BLE001  (this request fails, the others go on)
+                out.append(e)
+                continue
+            try:
+                r.own_slots = self._alloc(len(r.new_tokens) + (0 if inp.prefill_only else inp.max_new_tokens))
+            except OutOfKV as e:
+                self._abandon(r)
+                out.append(e)
+                continue
+            live.append(r)
+            out.append(r)
+        if live:
+            self._filter = (float(live[0].inp.top_p), int(live[0].inp.top_k))
+            t0 = time.perf_counter()
+            tok, lp = self._prefill(live, live[0].inp.temperature)
+            self.stats["prefill_s"] += time.perf_counter() - t0
+            for r, a, b in zip(live, tok, lp):
+                r.out_tok, r.out_lp = [int(a)], [float(b)]
+        return out
+
+    def _abandon(self, r: _Req):
+        """Release what a resolved request holds when it does not run to the end."""
+        if r.own_slots is not None and len(r.own_slots):
+            self.pool.decref(r.own_slots)
+            r.own_slots = None
+        for ex in r.extra_slots:
+            self.pool.decref(ex)
+        r.extra_slots = []
+        if r.radix_handle >= 0:
+            self.radix.unlock(r.radix_handle)
+            self.radix.release_handle(r.radix_handle)
+            r.radix_handle = -1
+
+    def layout_rows(self, rows: list[_Req], tail: int) -> int:
+        """Place live requests in decode rows 0..n-1 of a batch bucket for the next decode
+        chunks of at most `tail` steps: each row's key list is [context | own slots | tail
+        null slots] (steps past a request's end write the null slot) and its state continues
+        from its last sampled token.  Returns the bucket size B."""
+        n = len(rows)
+        B = self._bucket(n)
+        regions, off = [], 0
+        starts, lens = np.zeros(B, np.int32), np.zeros(B, np.int32)
+        tok, pos, stream = np.zeros(B, np.int64), np.zeros(B, np.int32), np.zeros(B, np.int64)
+        final = np.zeros(n, np.int64)
+        for k, r in enumerate(rows):
+            g = len(r.out_tok)
+            region = np.concatenate([r.ctx_slots, r.own_slots, np.full(tail, self.null_slot, np.int64)])
+            regions.append(region)
+            starts[k] = off
+            lens[k] = len(r.ctx_slots) + len(r.new_tokens) + g - 1
+            off += len(region)
+            tok[k] = r.out_tok[-1]
+            pos[k] = r.first_pos + len(r.new_tokens) + g - 1
+            stream[k] = (r.rid << 32) | (int(pos[k]) + 1)
+            final[k] = len(r.ctx_slots) + len(r.new_tokens) + r.inp.max_new_tokens + 1  # (steps past it: discarded)
+        for k in range(n, B):
+            regions.append(np.full(1 + tail, self.null_slot, np.int64))
+            starts[k] = off
+            off += 1 + tail
+        if off > self.kv_index_capacity:
+            raise OutOfKV("kv index capacity exceeded; lower the batch or raise kv_index_capacity")
+        dev = self.device
+        self.kv_indices[:off].copy_(h2d(np.concatenate(regions).astype(np.int32), dev))
+        for dst, src in ((self.s_start, starts), (self.s_len, lens), (self.s_tok, tok), (self.s_pos, pos),
+                         (self.s_stream, stream)):
+            dst[:B].copy_(h2d(src, dev))
+        self._shared_active = False
+        if self.shared_decode is not None:
+            ctx = np.asarray([len(r.ctx_slots) for r in rows], np.int64)
+            self._shared_active = self.shared_decode.plan(regions[:n], starts, ctx, final, B)
+        return B
+
+    @torch.no_grad()
+    def decode_chunk(self, n: int, B: int, steps: int, temperature: float) -> tuple[np.ndarray, np.ndarray]:
+        """`steps` decode steps of the laid-out batch; host (tokens, logprobs) [n, steps]."""
+        self._ensure_out(steps)
+        self.s_step.zero_()
+        # padding rows restart at their null region each chunk (their key count would
+        # otherwise grow past it when a layout is reused for several chunks)
+        self.s_len[n:B].zero_()
+        t0 = time.perf_counter()
+        if self.use_graphs:
+            g = self._graph(B, temperature)
+            for _ in range(steps):
+                g.replay()
+            ops.add_launches(self._graph_kernels[self._graph_key(B, temperature)] * steps)
+        else:
+            for _ in range(steps):
+                self._decode_step(B, temperature)
+        out_t = d2h(self.s_out_tok[:n, :steps]).numpy()
+        out_l = d2h(self.s_out_lp[:n, :steps]).numpy()
+        self.stats["decode_s"] += time.perf_counter() - t0
+        self.stats["decode_steps"] += steps
+        return out_t, out_l
+
+    def finish(self, r: _Req) -> GenOutput:
+        """Close a live request with what it generated (at most max_new_tokens)."""
+        mx = 0 if r.inp.prefill_only else r.inp.max_new_tokens
+        return self._finish(r, r.out_tok[:mx], r.out_lp[:mx])
+
     # ------------------------------------------------------------------ public API
     @torch.no_grad()
     def generate(self, inputs: list[GenInput]) -> list[GenOutput]:
@@ -654,63 +770,72 @@ class Engine:
         self.stats["decode_s"] += time.perf_counter() - t1
         outs = []
         for j, r in enumerate(reqs):
-            n_new = len(r.new_tokens)
             mx = 0 if r.inp.prefill_only else r.inp.max_new_tokens
             toks = ([int(first_tok[j])] + [int(x) for x in out_t[j]])[:mx]
             lps = ([float(first_lp[j])] + [float(x) for x in out_l[j]])[:mx]
-            reason = "length"
-            if r.inp.stop_ids:
-                for k, t in enumerate(toks):
-                    if t in r.inp.stop_ids:
-                        toks, lps, reason = toks[:k + 1], lps[:k + 1], "stop"
-                        break
-            # generated rows with KV: all but the last sampled token (its KV is not written)
-            n_kv_gen = max(0, len(toks) - 1)
-            used = n_new + n_kv_gen
-            cid = None
-            if r.inp.keep_cursor:
-                cid = r.inp.cursor_id or self.new_cursor_id()
-                gen_pos = np.arange(r.first_pos + n_new, r.first_pos + n_new + len(toks))
-                slots = np.concatenate([r.ctx_slots, r.own_slots[:used], np.full(len(toks) - n_kv_gen, -1, np.int64)])
-                cur = Cursor(cid, np.concatenate([r.ctx_tokens, r.new_tokens, np.asarray(toks, np.int32)]), slots,
-                             np.concatenate([r.ctx_pos, np.arange(r.first_pos, r.first_pos + n_new), gen_pos]),
-                             prompt_len=len(r.ctx_tokens) + n_new,
-                             mounted=np.concatenate([r.ctx_mounted, np.zeros(n_new + len(toks), bool)]),
-                             version=self.version)
-                held = cur.slots[cur.slots >= 0]
-                self.cursors.put(Cursor(cid, cur.tokens, cur.slots, cur.positions, cur.prompt_len, cur.mounted,
-                                        cur.version), take_ref=False)
-                self._on_cursor(r, cid)
-                # the store's reference: ctx slots are borrowed (incref); own used slots transfer ownership
-                if len(r.ctx_slots):
-                    self.pool.incref(r.ctx_slots)
-                del held
-            if r.inp.cursor is None and not r.inp.mount and len(r.new_tokens) and self._use_radix:
-                full = np.concatenate([r.ctx_tokens, r.new_tokens]).astype(np.int32)
-                sl = np.concatenate([r.ctx_slots, r.own_slots[:n_new]]).astype(np.int64)
-                self.radix.insert(self.version, full, sl)
-            # release what this request owns and did not hand to a cursor
-            if not r.inp.keep_cursor:
-                self.pool.decref(r.own_slots)
-            elif len(r.own_slots) > used:
-                self.pool.decref(r.own_slots[used:])
-            for ex in r.extra_slots:  # K3 copies: a kept cursor holds its own reference
-                self.pool.decref(ex)
-            if r.radix_handle >= 0:
-                self.radix.unlock(r.radix_handle)
-                self.radix.release_handle(r.radix_handle)
-            if self.record_interactions and cid is not None:
-                prompt = np.concatenate([r.ctx_tokens, r.new_tokens]).astype(np.int32)
-                self.records[cid] = {"tokens": np.concatenate([prompt, np.asarray(toks, np.int32)]),
-                                     "prompt_len": len(prompt), "completion": len(toks),
-                                     "logprobs": np.asarray(lps, np.float32), "parent": r.inp.cursor,
-                                     "mounts": [(at, m[0], int(m[1]), int(m[2]))
-                                                for at, m in zip(r.mount_at, r.inp.mount)],
-                                     "version": self.version}
-            self.stats["cached_tokens"] += r.cached
-            self.stats["requests"] += 1
-            outs.append(GenOutput(toks, lps, cid, n_new, r.cached, r.first_pos, reason))
+            outs.append(self._finish(r, toks, lps))
         return outs
+
+    @staticmethod
+    def _cut_at_stop(inp: GenInput, toks: list, lps: list) -> tuple[list, list, str]:
+        """Tokens through the first stop token (finish reason "stop"), else all ("length")."""
+        if inp.stop_ids:
+            for k, t in enumerate(toks):
+                if t in inp.stop_ids:
+                    return toks[:k + 1], lps[:k + 1], "stop"
+        return toks, lps, "length"
+
+    def _finish(self, r: _Req, toks: list, lps: list) -> GenOutput:
+        """Close one request: cut at its stop token, keep its reply as a cursor (or release
+        its slots), insert its prompt into the radix cache, record the interaction."""
+        toks, lps, reason = self._cut_at_stop(r.inp, toks, lps)
+        n_new = len(r.new_tokens)
+        # generated rows with KV: all but the last sampled token (its KV is not written)
+        n_kv_gen = max(0, len(toks) - 1)
+        used = n_new + n_kv_gen
+        cid = None
+        if r.inp.keep_cursor:
+            cid = r.inp.cursor_id or self.new_cursor_id()
+            gen_pos = np.arange(r.first_pos + n_new, r.first_pos + n_new + len(toks))
+            slots = np.concatenate([r.ctx_slots, r.own_slots[:used], np.full(len(toks) - n_kv_gen, -1, np.int64)])
+            cur = Cursor(cid, np.concatenate([r.ctx_tokens, r.new_tokens, np.asarray(toks, np.int32)]), slots,
+                         np.concatenate([r.ctx_pos, np.arange(r.first_pos, r.first_pos + n_new), gen_pos]),
+                         prompt_len=len(r.ctx_tokens) + n_new,
+                         mounted=np.concatenate([r.ctx_mounted, np.zeros(n_new + len(toks), bool)]),
+                         version=self.version)
+            held = cur.slots[cur.slots >= 0]
+            self.cursors.put(Cursor(cid, cur.tokens, cur.slots, cur.positions, cur.prompt_len, cur.mounted,
+                                    cur.version), take_ref=False)
+            self._on_cursor(r, cid)
+            # the store's reference: ctx slots are borrowed (incref); own used slots transfer ownership
+            if len(r.ctx_slots):
+                self.pool.incref(r.ctx_slots)
+            del held
+        if r.inp.cursor is None and not r.inp.mount and len(r.new_tokens) and self._use_radix:
+            full = np.concatenate([r.ctx_tokens, r.new_tokens]).astype(np.int32)
+            sl = np.concatenate([r.ctx_slots, r.own_slots[:n_new]]).astype(np.int64)
+            self.radix.insert(self.version, full, sl)
+        # release what this request owns and did not hand to a cursor
+        if not r.inp.keep_cursor:
+            self.pool.decref(r.own_slots)
+        elif len(r.own_slots) > used:
+            self.pool.decref(r.own_slots[used:])
+        for ex in r.extra_slots:  # K3 copies: a kept cursor holds its own reference
+            self.pool.decref(ex)
+        if r.radix_handle >= 0:
+            self.radix.unlock(r.radix_handle)
+            self.radix.release_handle(r.radix_handle)
+        if self.record_interactions and cid is not None:
+            prompt = np.concatenate([r.ctx_tokens, r.new_tokens]).astype(np.int32)
+            self.records[cid] = {"tokens": np.concatenate([prompt, np.asarray(toks, np.int32)]),
+                                 "prompt_len": len(prompt), "completion": len(toks),
+                                 "logprobs": np.asarray(lps, np.float32), "parent": r.inp.cursor,
+                                 "mounts": [(at, m[0], int(m[1]), int(m[2]))
+                                            for at, m in zip(r.mount_at, r.inp.mount)],
+                                 "version": self.version}
+        self.stats["cached_tokens"] += r.cached
+        self.stats["requests"] += 1
+        return GenOutput(toks, lps, cid, n_new, r.cached, r.first_pos, reason)
 
     def release_cursor(self, cid: str):
         self.cursors.pop(cid)

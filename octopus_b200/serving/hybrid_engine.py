@@ -229,6 +229,8 @@ class HybridEngine(Engine):
         return y
 
     # ------------------------------------------------------------------ cursors
+    supports_continuous = False  # recurrent states follow the static batch layout of generate
+
     def generate(self, inputs):
         self._sweep()
         try:

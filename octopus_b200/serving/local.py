@@ -1,4 +1,5 @@
-"""In-process chat service over the engine: request batching, chat rendering with the
+"""In-process chat service over the engine: request scheduling (continuous batching, or
+static windows for engines without it), chat rendering with the
 cursor protocol (only the messages after the cursor's reply are rendered), tool-call
 parsing, and the template terminator kept on the reply's cursor.  The HTTP server wraps
 it; the RL agent environment calls it directly as the runtime's completion function
@@ -34,16 +35,42 @@ def mounts_of(body: dict) -> list:
 
 
 class BatchingQueue:
-    """Collects concurrent requests for `window` seconds and runs them as one engine batch."""
+    """Static batching for engines without continuous batching (hybrid and tensor-parallel
+    engines): collects concurrent requests for `window` seconds and runs them as one engine
+    batch per sampling setting.  A failing batch is retried request by request, so one bad
+    request (unknown cursor, bad mount) fails alone."""
 
     def __init__(self, engine: Engine, window: float = 0.005, max_batch: int | None = None):
         self.engine = engine
         self.window = window
         self.max_batch = max_batch or engine.max_batch
-        self.lock = threading.Lock()
         self.pending: list = []
         self.inflight = 0
         self.run_lock = asyncio.Lock()
+
+    @property
+    def n_waiting(self) -> int:
+        return len(self.pending)
+
+    @property
+    def n_running(self) -> int:
+        return self.inflight
+
+    async def _run_group(self, loop, items):
+        try:
+            outs = await loop.run_in_executor(None, self.engine.generate, [i for i, _ in items])
+        except Exception:  # noqa: BLE001  (isolate the failing request)
+            if len(items) == 1:
+                raise
+            for item in items:
+                try:
+                    await self._run_group(loop, [item])
+                except Exception as e:  # noqa: BLE001
+                    if not item[1].done():
+                        item[1].set_exception(e)
+            return
+        for (_, f), o in zip(items, outs):
+            f.set_result(o)
 
     async def submit(self, inp: GenInput):
         loop = asyncio.get_running_loop()
@@ -62,10 +89,8 @@ class BatchingQueue:
                     groups.setdefault((float(i.temperature), float(i.top_p), int(i.top_k)), []).append((i, f))
                 for items in groups.values():
                     try:
-                        outs = await loop.run_in_executor(None, self.engine.generate, [i for i, _ in items])
-                        for (_, f), o in zip(items, outs):
-                            f.set_result(o)
-                    except Exception as e:  # per-request errors (404 cursor, bad mount) fail the whole group
+                        await self._run_group(loop, items)
+                    except Exception as e:  # noqa: BLE001
                         for _, f in items:
                             if not f.done():
                                 f.set_exception(e)
@@ -74,6 +99,37 @@ class BatchingQueue:
         finally:
             self.inflight -= 1
 
+
+class ContinuousQueue:
+    """The engine's continuous-batching scheduler (serving.scheduler) behind an async API."""
+
+    def __init__(self, engine: Engine):
+        from .scheduler import Scheduler
+
+        self.engine = engine
+        self.sched = Scheduler(engine)
+
+    @property
+    def n_waiting(self) -> int:
+        return self.sched.pending
+
+    @property
+    def n_running(self) -> int:
+        return self.sched.running
+
+    async def submit(self, inp: GenInput):
+        return await asyncio.wrap_future(self.sched.submit(inp))
+
+    def close(self):
+        self.sched.close()
+
+
+def make_queue(engine: Engine, window: float = 0.005):
+    """Continuous batching where the engine supports it (OCTOPUS_STATIC_BATCHING=1: static
+    windows everywhere), else static windows."""
+    if getattr(engine, "supports_continuous", False) and os.environ.get("OCTOPUS_STATIC_BATCHING", "0") != "1":
+        return ContinuousQueue(engine)
+    return BatchingQueue(engine, window)
 
 
 def _top_k(v) -> int:
@@ -91,7 +147,7 @@ class ChatService:
         self.engine, self.tok, self.model_name = engine, tokenizer, model_name
         # the tool-call markup the model emits: given, else the chat template's family
         self.tool_format = tool_format or detect_format(tokenizer.template_src)
-        self.q = BatchingQueue(engine, window)
+        self.q = make_queue(engine, window)
         self._audit_lock = threading.Lock()
 
     async def chat(self, body: dict) -> dict:

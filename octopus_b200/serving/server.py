@@ -75,7 +75,7 @@ def create_app(engine: Engine, tokenizer: ChatTokenizer | None = None, model_nam
     async def loads():
         st = engine.load_stats()
         return {"token_usage": st["token_usage"], "num_used_tokens": st["num_used_slots"],
-                "num_waiting_reqs": len(q.pending), "num_running_reqs": q.inflight, "cursors": st["cursors"]}
+                "num_waiting_reqs": q.n_waiting, "num_running_reqs": q.n_running, "cursors": st["cursors"]}
 
     @app.get("/get_server_info")
     async def server_info():

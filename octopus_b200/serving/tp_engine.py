@@ -28,6 +28,7 @@ from .engine import Engine
 
 
 class TPEngine(Engine):
+    supports_continuous = False  # every rank must take the same batching decisions: static batches
     def __init__(self, cfg, weights, *, group, max_batch: int = 256, prefill_chunk: int = 16384, **kw):
         import torch.distributed as dist
 

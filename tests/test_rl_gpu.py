@@ -89,3 +89,37 @@ def test_filtered_sampling_graph_and_eager():
     assert bool((z.topk(8).indices == t5[:, None]).any(-1).all())
     assert torch.isfinite(lp1).all()
     ops.check_status(0)
+
+
+def test_continuous_batching_on_graphs():
+    """The scheduler on the CUDA-graph decode with the shared-prefix kernel: rows with a
+    common 256-token prefix join and leave between chunks; each reply follows the same
+    request's solo run (same sampling streams) and the KV pool balances afterwards."""
+    from octopus_b200.serving.scheduler import Scheduler
+
+    cfg, actor, eng = _setup()
+    _, _, solo = _setup()
+    rng = np.random.default_rng(5)
+    prefix = rng.integers(1, cfg.vocab_size, 256).tolist()
+    reqs = [GenInput(prefix + rng.integers(1, cfg.vocab_size, 8 + 3 * k).tolist(), max_new_tokens=m, rid=300 + k,
+                     keep_cursor=False) for k, m in enumerate([40, 9, 25, 3, 33, 17])]
+    free0 = eng.pool.free_count()
+    sched = Scheduler(eng, chunk=8)
+    try:
+        futs = [sched.submit(r) for r in reqs]
+        outs = [f.result(timeout=300) for f in futs]
+    finally:
+        sched.close()
+    torch.cuda.synchronize()
+    ops.check_status(0)
+    agree = total = 0
+    for r, o in zip(reqs, outs):
+        ref = solo.generate([GenInput(r.input_ids, max_new_tokens=r.max_new_tokens, rid=r.rid, keep_cursor=False)])[0]
+        assert len(o.output_ids) == r.max_new_tokens
+        n = next((i for i, (a, b) in enumerate(zip(o.output_ids, ref.output_ids)) if a != b), len(ref.output_ids))
+        agree, total = agree + n, total + len(ref.output_ids)
+        assert np.allclose(o.output_logprobs[:n], ref.output_logprobs[:n], atol=5e-2)
+    assert agree >= 0.9 * total, (agree, total)  # bf16 batch layouts may flip a near-tie late in a reply
+    assert sched.stats["relayouts"] >= 3
+    eng.reset()
+    assert eng.pool.free_count() == free0
