@@ -7,7 +7,9 @@ row, and which rows are mounted (placeholders of another thread's segment).  A
 continuation request sends only the new messages (``cursor`` + delta ids), and a
 ``mount`` splices a range of another cursor's rows into the context without copying
 KV.  Entries live in an LRU under a byte budget (``OCTOPUS_CURSOR_BYTES``, default
-2 GiB of host metadata); evicting an entry releases its slot references.
+2 GiB of host metadata); evicting an entry releases its slot references.  Under KV-pool
+pressure the engine may instead *spill* a cursor (drop its KV, keep the entry and the
+recipe that rebuilds it: ``Engine._spill`` / ``Engine._rebuild``).
 
 Reference parity: `octopus/serving/cursor_store.py:27-81` (LRU cursor store under a
 byte budget, position breakpoints, put_reply) and the placeholder convention of
@@ -83,6 +85,16 @@ class CursorStore:
             if c is not None:
                 self._d.move_to_end(cid)
             return c
+
+    def peek(self, cid: str) -> Cursor | None:
+        """The cursor without marking it recently used."""
+        with self._lock:
+            return self._d.get(cid)
+
+    def oldest_first(self) -> list[str]:
+        """Cursor ids from least to most recently used."""
+        with self._lock:
+            return list(self._d)
 
     def put(self, cur: Cursor, take_ref: bool = True) -> None:
         """Insert a cursor.  With take_ref the store adds its own reference to the slots."""

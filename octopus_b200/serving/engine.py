@@ -114,6 +114,7 @@ class _Req:
     out_lp: list = field(default_factory=list)
     mount_at: list = field(default_factory=list)
     extra_slots: list = field(default_factory=list)  # K3 relocated copies this request allocated
+    pinned: bool = False  # holds one reference on ctx_slots while it runs (spills cannot free them)
 
 
 class Engine:
@@ -196,6 +197,8 @@ class Engine:
             sc = self.cursors.get(src)
             if sc is None:
                 raise CursorNotFound(src)
+            if sc.meta.get("spilled"):
+                self._rebuild(src)
             a, b = int(a), int(b)
             if not (0 <= a < b <= sc.length) or (sc.slots[a:b] < 0).any():
                 raise ValueError(f"mount range [{a}, {b}) invalid for cursor {src} of length {sc.length}")
@@ -255,8 +258,80 @@ class Engine:
             self.radix.evict(n - self.pool.free_count() + 1024)
             s = self.pool.alloc(n)
             if len(s) < n:
-                raise OutOfKV(f"KV pool exhausted: need {n}, free {self.pool.free_count()}")
+                self._spill(n)
+                s = self.pool.alloc(n)
+                if len(s) < n:
+                    raise OutOfKV(f"KV pool exhausted: need {n}, free {self.pool.free_count()}")
         return np.asarray(s, dtype=np.int64)
+
+    # ------------------------------------------------------------------ KV pressure: spill / rebuild
+    _spillable = True  # (the hybrid engine's cursors also carry recurrent states: not spilled)
+
+    def _spill(self, need: int) -> int:
+        """Drop the KV of least-recently-used cursors until `need` slots are free.  A spilled
+        cursor keeps its tokens, positions and recipe (the requests that built it); the
+        next request that continues or mounts it rebuilds its KV first (_rebuild).  Slots a
+        running request or another holder still references are not freed by a spill.
+        Returns the number of cursors spilled."""
+        if not self._spillable:
+            return 0
+        spilled = 0
+        for cid in self.cursors.oldest_first():
+            if self.pool.free_count() >= need:
+                break
+            cur = self.cursors.peek(cid)
+            if cur is None or cur.meta.get("spilled") or cur.meta.get("recipe") is None:
+                continue
+            held = cur.held_slots()
+            if not len(held):
+                continue
+            cur.meta["spilled"] = True
+            cur.meta["kv_rows"] = int(np.argmin(cur.slots >= 0)) if not (cur.slots >= 0).all() else cur.length
+            cur.slots = np.full(cur.length, -1, np.int64)
+            self.pool.decref(held)
+            spilled += 1
+        self.stats["spills"] = self.stats.get("spills", 0) + spilled
+        return spilled
+
+    def _rebuild(self, cid: str, depth: int = 0) -> None:
+        """Recompute a spilled cursor's KV by replaying its recipe as prefill-only requests
+        with the same tokens, mounts and mount rules (hence the same K2 positions); mount
+        sources that are spilled themselves are rebuilt first."""
+        cur = self.cursors.peek(cid)
+        if cur is None:
+            raise CursorNotFound(cid)
+        if not cur.meta.get("spilled"):
+            return
+        if depth > 64:
+            raise RuntimeError(f"cursor {cid}: rebuild recursion too deep")
+        recording, self.record_interactions = self.record_interactions, False
+        tmp_ids, prev, mounts = [], None, []
+        try:
+            for seg in cur.meta["recipe"]:
+                if seg[0] == "mount":
+                    self._rebuild(seg[1], depth + 1)
+                    mounts.append(seg)
+                    continue
+                tid = f"{cid}#rebuild{len(tmp_ids)}"
+                rule = mounts[0][4] if mounts else "K2"
+                self.generate([GenInput(list(seg[1]), cursor=prev, mount=[m[1:4] for m in mounts], mount_rule=rule,
+                                        max_new_tokens=0, prefill_only=True, cursor_id=tid)])
+                tmp_ids.append(tid)
+                prev, mounts = tid, []
+            built = self.cursors.peek(prev) if prev is not None else None
+            n = cur.meta.get("kv_rows", cur.length)
+            if built is None or built.length != n or not np.array_equal(built.tokens, cur.tokens[:n]) or \
+                    not np.array_equal(built.positions, cur.positions[:n]):
+                raise RuntimeError(f"cursor {cid}: its recipe does not rebuild its rows")
+            slots = built.slots.copy()
+            self.pool.incref(slots[slots >= 0])
+            cur.slots = np.concatenate([slots, np.full(cur.length - n, -1, np.int64)])
+            cur.meta["spilled"] = False
+            self.stats["rebuilds"] = self.stats.get("rebuilds", 0) + 1
+        finally:
+            self.record_interactions = recording
+            for tid in tmp_ids:
+                self.cursors.pop(tid)
 
     def bump_version(self) -> int:
         """New weight version: cached KV of older versions is no longer matched."""
@@ -275,6 +350,8 @@ class Engine:
             cur = self.cursors.get(inp.cursor)
             if cur is None:
                 raise CursorNotFound(inp.cursor)
+            if cur.meta.get("spilled"):
+                self._rebuild(inp.cursor)
             # rows without KV (a template terminator appended at put) are re-prefilled
             has_kv = cur.slots >= 0
             ok = int(np.argmin(has_kv)) if not has_kv.all() else cur.length
@@ -286,7 +363,9 @@ class Engine:
                 new = np.concatenate([cur.tokens[ok:], new])
             next_pos = int(cur.positions[ok - 1]) + 1 if ok else 0
             cached = ok
-        elif len(new) > 1 and self._use_radix:
+        elif len(new) > 1 and self._use_radix and not inp.mount:
+            # (a request that mounts puts the mounted rows before its prompt, so its prompt
+            # is not a prefix of the cached sequences)
             ln, slots, handle = self.radix.match(self.version, new[:-1])
             ln = int(ln)
             if ln > 0:
@@ -318,7 +397,11 @@ class Engine:
         r.mount_at = mount_at
         r.extra_slots = extra
         if len(new) == 0:
+            self._abandon(r)
             raise ValueError("request has no new tokens to prefill")
+        if len(r.ctx_slots):  # pin the context: spills during this request cannot free it
+            self.pool.incref(r.ctx_slots)
+            r.pinned = True
         return r
 
     # ------------------------------------------------------------------ model-family hooks
@@ -672,6 +755,9 @@ class Engine:
 
     def _abandon(self, r: _Req):
         """Release what a resolved request holds when it does not run to the end."""
+        if r.pinned:
+            self.pool.decref(r.ctx_slots)
+            r.pinned = False
         if r.own_slots is not None and len(r.own_slots):
             self.pool.decref(r.own_slots)
             r.own_slots = None
@@ -785,6 +871,25 @@ class Engine:
                     return toks[:k + 1], lps[:k + 1], "stop"
         return toks, lps, "length"
 
+    def _recipe(self, r: _Req, gen_kv: list):
+        """How to recompute this request's cursor rows with KV: its parent's recipe (a cursor
+        continuation) or its radix prefix, its mounts, then its prompt and generated tokens.
+        None when the parent cannot be rebuilt."""
+        inp = r.inp
+        if inp.cursor is not None:
+            parent = self.cursors.peek(inp.cursor)
+            base = None if parent is None else parent.meta.get("recipe")
+            if base is None:
+                return None
+            steps = list(base)
+        elif r.cached:
+            steps = [("tokens", np.asarray(r.ctx_tokens[:r.cached], np.int32))]
+        else:
+            steps = []
+        steps += [("mount", src, int(a), int(b), inp.mount_rule) for src, a, b in inp.mount]
+        steps.append(("tokens", np.concatenate([r.new_tokens, np.asarray(gen_kv, np.int32)]).astype(np.int32)))
+        return steps
+
     def _finish(self, r: _Req, toks: list, lps: list) -> GenOutput:
         """Close one request: cut at its stop token, keep its reply as a cursor (or release
         its slots), insert its prompt into the radix cache, record the interaction."""
@@ -803,14 +908,17 @@ class Engine:
                          prompt_len=len(r.ctx_tokens) + n_new,
                          mounted=np.concatenate([r.ctx_mounted, np.zeros(n_new + len(toks), bool)]),
                          version=self.version)
-            held = cur.slots[cur.slots >= 0]
-            self.cursors.put(Cursor(cid, cur.tokens, cur.slots, cur.positions, cur.prompt_len, cur.mounted,
-                                    cur.version), take_ref=False)
+            cur.meta["recipe"] = self._recipe(r, toks[:n_kv_gen])
+            # the store's reference: the request's pin on the ctx slots and its used own slots
+            # move to the cursor
+            self.cursors.put(cur, take_ref=False)
             self._on_cursor(r, cid)
-            # the store's reference: ctx slots are borrowed (incref); own used slots transfer ownership
-            if len(r.ctx_slots):
+            if len(r.ctx_slots) and not r.pinned:
                 self.pool.incref(r.ctx_slots)
-            del held
+            r.pinned = False
+        elif r.pinned:
+            self.pool.decref(r.ctx_slots)
+            r.pinned = False
         if r.inp.cursor is None and not r.inp.mount and len(r.new_tokens) and self._use_radix:
             full = np.concatenate([r.ctx_tokens, r.new_tokens]).astype(np.int32)
             sl = np.concatenate([r.ctx_slots, r.own_slots[:n_new]]).astype(np.int64)

@@ -230,6 +230,7 @@ class HybridEngine(Engine):
 
     # ------------------------------------------------------------------ cursors
     supports_continuous = False  # recurrent states follow the static batch layout of generate
+    _spillable = False  # a cursor's recurrent-state snapshots are not rebuilt from its recipe
 
     def generate(self, inputs):
         self._sweep()
