@@ -33,6 +33,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "RL step tokens/sec/box (rollout+train+sync), 7B-shape multi-agent, 1/2/4/8 B200"
+METRIC_GRPO = "RL step tokens/sec/box (rollout+train+sync), 1.5B-shape single-agent GRPO"
 BASELINE_VALUE = None  # the reference publishes no tokens/sec figure for this metric
 
 
@@ -42,7 +43,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="octopus", choices=["octopus", "reference"])
-    ap.add_argument("--model", default="qwen2.5-7b")
+    ap.add_argument("--config", default="dag7b", choices=["dag7b", "grpo1.5b"],
+                    help="dag7b: BASELINE config 3 (the headline); grpo1.5b: config 2 (1.5B single-agent GRPO, "
+                         "64 prompts x 8 samples x 1024 tokens, TP=1 replicas)")
+    ap.add_argument("--model", default="")
     ap.add_argument("--instances", type=int, default=32)
     ap.add_argument("--samples", type=int, default=4)
     ap.add_argument("--prefix", type=int, default=2048)
@@ -148,8 +152,10 @@ def main():
     n_gpus = world
 
     over = {"layers": args.layers} if args.layers else {}
+    grpo = args.config == "grpo1.5b"
+    args.model = args.model or ("qwen2.5-1.5b" if grpo else "qwen2.5-7b")
     cfg = get_config(args.model, **over)
-    tp = args.tp or (2 if world % 2 == 0 else 1)
+    tp = 1 if grpo else (args.tp or (2 if world % 2 == 0 else 1))
     if world % tp:
         raise SystemExit(f"--tp {tp} must divide the {world} GPUs")
     replicas = world // tp
@@ -160,18 +166,29 @@ def main():
             g = dist.new_group(list(range(r * tp, (r + 1) * tp)))
             if r == rep:
                 tp_group = g
-    # strong scaling: this replica's share of the DAG instances
-    inst = [i for i in range(args.instances) if i % replicas == rep]
-    dcfg = DagConfig(instances=args.instances, samples=args.samples, prefix_len=args.prefix, turn_len=args.turn,
-                     role_len=args.role, seed=1000 + rep)
-    env = MultiAgentDag(cfg.vocab_size, dcfg)
+    # strong scaling: this replica's share of the DAG instances (or GRPO prompts)
+    if grpo:
+        from octopus_b200.envs.grpo import GrpoConfig, SingleAgentGrpo
+
+        gcfg = GrpoConfig(seed=1000 + rep)
+        inst = [i for i in range(gcfg.prompts) if i % replicas == rep]
+        env = SingleAgentGrpo(cfg.vocab_size, gcfg)
+    else:
+        inst = [i for i in range(args.instances) if i % replicas == rep]
+        dcfg = DagConfig(instances=args.instances, samples=args.samples, prefix_len=args.prefix, turn_len=args.turn,
+                         role_len=args.role, seed=1000 + rep)
+        env = MultiAgentDag(cfg.vocab_size, dcfg)
     sharded = world > 1 and args.actor == "sharded"
     actor = ShardedActor(cfg, dev, seed=0) if sharded else Actor(cfg, dev, seed=0)
-    per_inst = args.prefix + args.samples * (4 * (args.turn + args.role) + 2)
+    if grpo:
+        per_inst = gcfg.prompt_len + gcfg.samples * (gcfg.response_len + 1)
+    else:
+        per_inst = args.prefix + args.samples * (4 * (args.turn + args.role) + 2)
     kv_slots = int(len(inst) * per_inst * 1.15) + 8192
     if args.kv_gb:
         kv_slots = int(args.kv_gb * (1 << 30) / (4 * cfg.layers * cfg.kv_width // tp))
-    max_batch = max(8 * tp, 1 << (len(inst) * args.samples * 2 - 1).bit_length())
+    rows = len(inst) * (gcfg.samples if grpo else args.samples * 2)
+    max_batch = max(8 * tp, 1 << (rows - 1).bit_length())
     if tp > 1:
         engine = TPEngine(cfg, actor.weights, group=tp_group, kv_slots=kv_slots, max_batch=max_batch, device=dev,
                           use_graphs=not args.no_graphs)
@@ -237,23 +254,33 @@ def main():
         h2d_b, d2h_b = float(io["h2d"]), float(io["d2h"])
     value = gen / (ms / 1000.0)
     e2e = gen / wall_s
+    par = (f"rollout tp{tp} x {replicas} replicas" + (" (fused AG->GEMM / GEMM->RS)" if tp > 1 else "")
+           + f", actor {'zero-sharded fused' if sharded else 'replicated'} over {n_gpus}"
+           if n_gpus > 1 else "single GPU (rollout engine + actor colocated)")
+    if grpo:
+        metric = METRIC_GRPO
+        run_config = {"model": args.model + (f"-L{args.layers}" if args.layers else ""), "config": "BASELINE config 2",
+                      "global_batch": gcfg.prompts * gcfg.samples, "seq_len": gcfg.prompt_len + gcfg.response_len,
+                      "parallelism": par, "prompts": gcfg.prompts, "samples": gcfg.samples,
+                      "response_len": gcfg.response_len, "tokens_counted": "generated (= trained) tokens per RL step",
+                      "l2": "inputs larger than L2 (KV > 10 GB per step)"}
+    else:
+        metric = METRIC
+        run_config = {"model": args.model + (f"-L{args.layers}" if args.layers else ""),
+                      "global_batch": args.instances * args.samples,
+                      "seq_len": args.prefix + 4 * (args.turn + args.role), "parallelism": par,
+                      "dag": "planner->2 solvers->verifier, prefix mounted zero-copy",
+                      "instances": args.instances, "samples": args.samples, "prefix": args.prefix,
+                      "turn": args.turn, "tokens_counted": "generated (= trained) tokens per RL step",
+                      "l2": "inputs larger than L2 (7B weights 15 GB, KV > 10 GB per step)"}
     if rank == 0:
         s0 = stats[-1]
         out = {
-            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": n_gpus, "steps": args.steps,
+            "metric": metric, "value": round(value, 2), "unit": "tokens/s", "n_gpus": n_gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 2), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
             "dtype": "bf16", "data": "synthetic (uniform random tokens, random-init weights, Bernoulli(0.5) rewards)",
-            "config": {"model": args.model + (f"-L{args.layers}" if args.layers else ""),
-                       "global_batch": args.instances * args.samples,
-                       "seq_len": args.prefix + 4 * (args.turn + args.role),
-                       "parallelism": (f"rollout tp{tp} x {replicas} replicas (fused AG->GEMM / GEMM->RS), "
-                                       f"actor {'zero-sharded fused' if sharded else 'replicated'} over {n_gpus}"
-                                       if n_gpus > 1 else "single GPU (rollout engine + actor colocated)"),
-                       "dag": "planner->2 solvers->verifier, prefix mounted zero-copy",
-                       "instances": args.instances, "samples": args.samples, "prefix": args.prefix,
-                       "turn": args.turn, "tokens_counted": "generated (= trained) tokens per RL step",
-                       "l2": "inputs larger than L2 (7B weights 15 GB, KV > 10 GB per step)"},
+            "config": run_config,
             "clocks": clk,
             "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d_b / args.steps),
                     "d2h_bytes_per_step": int(d2h_b / args.steps),

@@ -563,18 +563,27 @@ def logprob_head(h, W, labels, alpha: float = 1.0, vocab_limit: int | None = Non
 
 
 # ---------------------------------------------------------------------------- sampling
-def _uniform(seed: int, stream: torch.Tensor, V: int) -> torch.Tensor:
-    """Counter-based uniforms in (0, 1), [rows, V]: a 32-bit integer hash (Wellons' "lowbias32"
-    finaliser) of (seed, row stream, token), so a row's draws do not depend on the batch."""
+def _lowbias32(x: torch.Tensor) -> torch.Tensor:
+    """Wellons' "lowbias32" 32-bit integer finaliser on int64 tensors holding 32-bit values."""
     M32 = 0xFFFFFFFF
-    tok = torch.arange(V, device=stream.device, dtype=torch.int64)
-    x = ((stream.to(torch.int64)[:, None] * 0x9E3779B1 + (int(seed) & M32) * 0x85EBCA77) & M32)
-    x = (x ^ ((tok[None, :] * 0xC2B2AE3D) & M32)) & M32
     x = x ^ (x >> 16)
     x = (x * 0x7FEB352D) & M32
     x = x ^ (x >> 15)
     x = (x * 0x846CA68B) & M32
-    x = x ^ (x >> 16)
+    return x ^ (x >> 16)
+
+
+def _uniform(seed: int, stream: torch.Tensor, V: int) -> torch.Tensor:
+    """Counter-based uniforms in (0, 1), [rows, V]: a 32-bit integer hash of (seed, row
+    stream, token), so a row's draws do not depend on the batch.  All 64 bits of the
+    stream (request id << 32 | position) enter the row key."""
+    M32 = 0xFFFFFFFF
+    s = stream.to(torch.int64)
+    lo, hi = s & M32, (s >> 32) & M32
+    key = _lowbias32(((hi * 0x9E3779B1) & M32) ^ ((int(seed) & M32) * 0x85EBCA77 & M32))
+    key = _lowbias32(((lo * 0x27D4EB2F) & M32) ^ key)
+    tok = torch.arange(V, device=stream.device, dtype=torch.int64)
+    x = _lowbias32((key[:, None] ^ ((tok[None, :] * 0xC2B2AE3D) & M32)) & M32)
     return (x.to(torch.float64) + 0.5) / 4294967296.0
 
 

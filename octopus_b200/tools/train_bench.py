@@ -1,0 +1,219 @@
+"""Prefix-tree training benchmark with a reference arm.
+
+    python -m octopus_b200.tools.train_bench [--impl octopus|reference] [--depth 4 --branch 4 --seg 256]
+        [--layers N] [--steps K] [--warmup W] [--flat]
+
+The batch: a tree of `depth` levels under a virtual root, `branch` children per node and
+`seg` random tokens per node (4 x 4 x 256: 256 leaves, 87,040 tree tokens), trained as one
+micro-batch; with --flat the same 256 sequences of depth * seg tokens are trained with no
+prefix sharing (262,144 rows).  One step = forward + backward of every sequence's
+next-token logprobs under a policy-gradient loss (random per-sequence advantages) and one
+AdamW update.  Timed with CUDA events after `warmup` steps; reports trained (flat) tokens
+per second, tree rows per second, the chunked head's own forward+backward time on the
+tree's scored rows (152,064 vocab, 4096-row chunks), and peak memory above the weights and
+optimizer state.
+
+--impl reference runs the reference's own stock trainer path from baseline/_ref (a copy
+of the reference package): a Hugging Face Qwen2 model (random init, bf16, gradient
+checkpointing, FlashAttention-2) with `octopus.rl.prefix_tree.patch_attention` /
+`tree_inputs` (tree attention as one FlashAttention varlen call per node with its
+ancestors' keys gathered) and `octopus.rl.lm_head.bind_head` (the chunked head), and
+torch AdamW.  It prints one JSON line per arm; a failure prints {"unavailable": reason}.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def tree_sequences(depth: int, branch: int, seg: int, vocab: int, seed: int = 0):
+    """Flat sequences of a full tree: every root-to-leaf path (depth segments of seg tokens)."""
+    rng = np.random.default_rng(seed)
+    level = [np.empty(0, np.int64)]
+    for _ in range(depth):
+        level = [np.concatenate([p, rng.integers(1, vocab, seg)]) for p in level for _ in range(branch)]
+    return level
+
+
+def _clock_note():
+    import torch
+
+    return {"device": torch.cuda.get_device_name(0)}
+
+
+def run_octopus(args) -> dict:
+    import torch
+
+    from octopus_b200 import ops
+    from octopus_b200.models.config import get_config
+    from octopus_b200.rl.actor import Actor, build_microbatch
+
+    dev = torch.device("cuda", 0)
+    cfg = get_config(args.model, **({"layers": args.layers} if args.layers else {}))
+    seqs = tree_sequences(args.depth, args.branch, args.seg, cfg.vocab_size)
+    flat = np.concatenate(seqs)
+    cu = np.concatenate([[0], np.cumsum([len(s) for s in seqs])])
+    rng = np.random.default_rng(1)
+    adv = np.repeat(rng.standard_normal(len(seqs)), [len(s) for s in seqs]).astype(np.float32)
+    mask = np.ones(len(flat), np.float32)
+    mask[cu[:-1]] = 0.0  # a sequence's first token has no prediction
+    mb = build_microbatch(flat, list(cu), None, mask, adv, np.zeros(len(flat), np.float32), share=not args.flat)
+    actor = Actor(cfg, dev, seed=0)
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated(dev)
+    for _ in range(args.warmup):
+        actor.train_step([mb])
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        actor.train_step([mb])
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    peak = torch.cuda.max_memory_allocated(dev) - base
+    ops.check_status(0)
+    # the fused head alone on the tree's scored (row, label) pairs
+    P = len(mb.pair_row)
+    h = (torch.randn(P, cfg.hidden, device=dev) * 0.5).bfloat16().requires_grad_(True)
+    W = actor.weights.head
+    lab = torch.as_tensor(mb.pair_label, device=dev)
+
+    def head():
+        lp, ent = ops.logprob_head(h, W, lab)
+        lp.sum().backward()
+
+    for _ in range(2):
+        head()
+    torch.cuda.synchronize()
+    a.record()
+    head()
+    b.record()
+    torch.cuda.synchronize()
+    return {"impl": "octopus", "ms_per_step": round(ms, 2), "tree_rows": int(mb.n_tree), "flat_tokens": int(mb.n_flat),
+            "trained_tokens_per_s": round(mb.n_flat / ms * 1e3, 1), "tree_rows_per_s": round(mb.n_tree / ms * 1e3, 1),
+            "head_ms": round(a.elapsed_time(b), 2), "head_rows": P, "peak_activation_gb": round(peak / 2**30, 2)}
+
+
+def run_reference(args) -> dict:
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "octopus")):
+        return {"impl": "reference", "unavailable": "baseline/_ref/octopus missing (copy of the reference package)"}
+    sys.path.insert(0, ref)
+    import torch
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from octopus_b200.models.config import get_config
+
+    try:
+        from octopus.rl.lm_head import bind_head
+        from octopus.rl.prefix_tree import patch_attention, tree_inputs
+    except Exception as e:  # noqa: BLE001
+        return {"impl": "reference", "unavailable": f"reference trainer modules do not import: {e!r}"[:300]}
+    dev = torch.device("cuda", 0)
+    cfg = get_config(args.model, **({"layers": args.layers} if args.layers else {}))
+    hf = Qwen2Config(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden, intermediate_size=cfg.ffn,
+                     num_hidden_layers=cfg.layers, num_attention_heads=cfg.heads, num_key_value_heads=cfg.kv_heads,
+                     max_position_embeddings=32768, rope_theta=cfg.rope_theta, rms_norm_eps=cfg.rms_eps,
+                     tie_word_embeddings=cfg.tie_embeddings, torch_dtype="bfloat16")
+    hf._attn_implementation = "flash_attention_2"
+    try:
+        torch.manual_seed(0)
+        with torch.device(dev):
+            model = Qwen2ForCausalLM(hf).to(torch.bfloat16)
+        model.config._attn_implementation = "flash_attention_2"
+        model.gradient_checkpointing_enable(gradient_checkpointing_kwargs={"use_reentrant": False})
+        model.train()
+        patch_attention()
+        bind_head(model, 1.0)
+    except Exception as e:  # noqa: BLE001
+        return {"impl": "reference", "unavailable": f"model setup failed: {e!r}"[:300]}
+    seqs = tree_sequences(args.depth, args.branch, args.seg, cfg.vocab_size)
+    flat = np.concatenate(seqs)
+    lens = [len(s) for s in seqs]
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+    ids = torch.as_tensor(flat, device=dev)[None]
+    rng = np.random.default_rng(1)
+    adv = torch.as_tensor(np.repeat(rng.standard_normal(len(seqs)), lens), dtype=torch.float32, device=dev)
+    labels = torch.roll(ids[0], -1)
+    mask = torch.ones(len(flat), device=dev)
+    mask[cu[1:] - 1] = 0.0  # a sequence's last token has no label
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-6, fused=True)
+    head = model.get_output_embeddings()
+
+    def step():
+        if args.flat:
+            kwargs = {"input_ids": ids, "position_ids": torch.cat([torch.arange(n, device=dev) for n in lens])[None],
+                      "use_cache": False}
+            head.octopus_tree = None
+            head.octopus_labels = labels
+            head.octopus_scored = None
+        else:
+            meta, kwargs = tree_inputs(ids, cu, None, None)
+            head.octopus_tree = meta
+        out = model(**kwargs).logits  # [1, T_flat, 2]: (logprob of the next token, entropy)
+        lp = out[0, :, 0]
+        loss = -(lp * adv * mask).sum() / mask.sum()
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+
+    try:
+        torch.cuda.synchronize()
+        base = torch.cuda.memory_allocated(dev)
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        torch.cuda.reset_peak_memory_stats(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+    except Exception as e:  # noqa: BLE001
+        return {"impl": "reference", "unavailable": f"reference training step failed on this GPU: {e!r}"[:400]}
+    ms = a.elapsed_time(b) / args.steps
+    peak = torch.cuda.max_memory_allocated(dev) - base
+    tree_rows = len(flat) if args.flat else int(tree_inputs(ids, cu, None, None)[1]["input_ids"].shape[1])
+    return {"impl": "reference", "ms_per_step": round(ms, 2), "tree_rows": tree_rows, "flat_tokens": len(flat),
+            "trained_tokens_per_s": round(len(flat) / ms * 1e3, 1), "tree_rows_per_s": round(tree_rows / ms * 1e3, 1),
+            "peak_activation_gb": round(peak / 2**30, 2),
+            "path": "HF Qwen2 + FlashAttention-2 varlen per tree node (octopus.rl.prefix_tree) + chunked head "
+                    "(octopus.rl.lm_head, torch.compile'd softmax) + torch fused AdamW"}
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(prog="python -m octopus_b200.tools.train_bench")
+    ap.add_argument("--impl", default="octopus", choices=["octopus", "reference"])
+    ap.add_argument("--model", default="qwen2.5-7b")
+    ap.add_argument("--layers", type=int, default=0)
+    ap.add_argument("--depth", type=int, default=4)
+    ap.add_argument("--branch", type=int, default=4)
+    ap.add_argument("--seg", type=int, default=256)
+    ap.add_argument("--flat", action="store_true", help="train the same sequences with no prefix sharing")
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=2)
+    args = ap.parse_args(argv)
+    if ROOT not in sys.path:
+        sys.path.insert(0, ROOT)
+    t0 = time.time()
+    res = run_octopus(args) if args.impl == "octopus" else run_reference(args)
+    res.update(config={"model": args.model + (f"-L{args.layers}" if args.layers else ""), "depth": args.depth,
+                       "branch": args.branch, "seg": args.seg, "flat": args.flat, "steps": args.steps,
+                       "warmup": args.warmup, "dtype": "bf16", "data": "synthetic random tokens, random init"},
+               wall_s=round(time.time() - t0, 1))
+    print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

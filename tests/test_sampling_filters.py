@@ -77,3 +77,16 @@ def test_service_fields():
     assert _top_k(None) == 0 and _top_k(-1) == 0 and _top_k(20) == 20
     g = generate_input({"input_ids": [1, 2], "sampling_params": {"max_new_tokens": 4, "top_p": 0.95, "top_k": 20}})
     assert g.top_p == pytest.approx(0.95) and g.top_k == 20
+
+
+def test_noise_depends_on_the_whole_row_stream():
+    """Row streams are (request id << 32 | position): two requests at the same position must
+    draw different noise (the high 32 bits enter the row key)."""
+    import torch
+
+    from octopus_b200.ops.core import _uniform
+
+    s = torch.tensor([(7 << 32) | 100, (8 << 32) | 100, (7 << 32) | 101], dtype=torch.int64)
+    u = _uniform(3, s, 64)
+    assert not torch.equal(u[0], u[1]) and not torch.equal(u[0], u[2])
+    assert float(u.min()) > 0.0 and float(u.max()) < 1.0
