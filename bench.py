@@ -60,8 +60,10 @@ def parse():
     ap.add_argument("--profile-step", default="",
                     help="after the timed steps, run one more step under the PyTorch CUDA trace and write rank 0's "
                          "per-kernel breakdown (JSON) here; not part of the timed value")
-    ap.add_argument("--actor", default="sharded", choices=["sharded", "dp"],
-                    help="N > 1 actor: ZeRO-sharded with fused peer-memory kernels, or replicated + NCCL all-reduce")
+    ap.add_argument("--actor", default="sharded", choices=["sharded", "fsdp", "dp"],
+                    help="N > 1 actor: sharded (ZeRO: fp32 master / optimizer sharded, fused peer-memory RS + AdamW + "
+                         "all-gather), fsdp (full shard: per-layer peer-memory gather and reduce-scatter), or dp "
+                         "(replicated + NCCL all-reduce)")
     return ap.parse_args()
 
 
@@ -178,8 +180,13 @@ def main():
         dcfg = DagConfig(instances=args.instances, samples=args.samples, prefix_len=args.prefix, turn_len=args.turn,
                          role_len=args.role, seed=1000 + rep)
         env = MultiAgentDag(cfg.vocab_size, dcfg)
-    sharded = world > 1 and args.actor == "sharded"
-    actor = ShardedActor(cfg, dev, seed=0) if sharded else Actor(cfg, dev, seed=0)
+    sharded = world > 1 and args.actor in ("sharded", "fsdp")
+    if world > 1 and args.actor == "fsdp":
+        from octopus_b200.parallel.fsdp import FSDPActor
+
+        actor = FSDPActor(cfg, dev, seed=0)
+    else:
+        actor = ShardedActor(cfg, dev, seed=0) if sharded else Actor(cfg, dev, seed=0)
     if grpo:
         per_inst = gcfg.prompt_len + gcfg.samples * (gcfg.response_len + 1)
     else:
@@ -255,7 +262,8 @@ def main():
     value = gen / (ms / 1000.0)
     e2e = gen / wall_s
     par = (f"rollout tp{tp} x {replicas} replicas" + (" (fused AG->GEMM / GEMM->RS)" if tp > 1 else "")
-           + f", actor {'zero-sharded fused' if sharded else 'replicated'} over {n_gpus}"
+           + f", actor {dict(sharded='zero-sharded fused', fsdp='full-shard fused', dp='replicated')[args.actor]}"
+           + f" over {n_gpus}"
            if n_gpus > 1 else "single GPU (rollout engine + actor colocated)")
     if grpo:
         metric = METRIC_GRPO

@@ -13,6 +13,8 @@
 //                  buffer of every rank (P2P stores), which is also the rollout engine's
 //                  weight buffer — the trainer -> rollout weight sync.
 //   bcast_bf16:    plain shard broadcast (initial weight replication).
+//   peer_gather_bf16 / peer_rs_acc:  the full-shard (FSDP) actor's per-layer all-gather of
+//                  bf16 weight shards and reduce-scatter (accumulate) of fp32 gradients.
 //   peer_barrier:  bounded flag barrier across ranks (sequence-numbered flags in peer
 //                  memory, each wait limited by a time budget; on timeout the kernel
 //                  records kErrPeerTimeout and returns).
@@ -128,7 +130,8 @@ __global__ void bcast_bf16_kernel(const __nv_bfloat16* __restrict__ src, PeerPtr
 // flags: each rank's flag array (int32[kMaxRanks]) in its own IPC buffer.  Rank `me`
 // writes `seq` into slot `me` of every rank's array, then waits (bounded) until its own
 // array holds `seq` in every slot.
-__global__ void peer_barrier_kernel(PeerPtrs flags, int world, int me, int seq, int* status) {
+__global__ void peer_barrier_kernel(PeerPtrs flags, int world, int me, int seq, int* status,
+                                    unsigned long long budget_ns) {
   if (threadIdx.x == 0) {
     __threadfence_system();
     for (int r = 0; r < world; ++r) {
@@ -138,7 +141,7 @@ __global__ void peer_barrier_kernel(PeerPtrs flags, int world, int me, int seq, 
     __threadfence_system();
     volatile int* mine = const_cast<volatile int*>(static_cast<const volatile int*>(flags.p[me]));
     const uint64_t t0 = globaltimer_ns();
-    const uint64_t budget = wait_budget_ns(status);
+    const uint64_t budget = budget_ns ? budget_ns : wait_budget_ns(status);
     for (int r = 0; r < world; ++r) {
       while (mine[r] < seq) {
         if (globaltimer_ns() - t0 > budget) {
@@ -148,6 +151,45 @@ __global__ void peer_barrier_kernel(PeerPtrs flags, int world, int me, int seq, 
       }
     }
     __threadfence_system();
+  }
+}
+
+// FSDP all-gather of one unit: dst[r * n + j] = shard_r[j] (16-byte peer loads; n % 8 == 0).
+__global__ void peer_gather_bf16_kernel(PeerPtrs src, int world, size_t n, __nv_bfloat16* __restrict__ dst) {
+  const size_t n8 = n / 8;
+  const size_t total = n8 * static_cast<size_t>(world);
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / n8);
+    const size_t j = i - static_cast<size_t>(r) * n8;
+    const uint4 u = reinterpret_cast<const uint4*>(src.p[r])[j];
+    reinterpret_cast<uint4*>(dst)[i] = u;
+  }
+}
+
+// FSDP reduce-scatter of one unit's gradient: acc[j] += sum_r part_r[j] in rank order
+// (part_r = this rank's slice of rank r's gradient slot; 16-byte peer loads; n % 4 == 0).
+__global__ void peer_rs_acc_kernel(PeerPtrs src, int world, size_t n, float* __restrict__ acc) {
+  const size_t n4 = n / 4;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    float4 s = reinterpret_cast<const float4*>(acc)[i];
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r < world) {
+        const float4 v = reinterpret_cast<const float4*>(src.p[r])[i];
+        t.x += v.x;
+        t.y += v.y;
+        t.z += v.z;
+        t.w += v.w;
+      }
+    }
+    s.x += t.x;
+    s.y += t.y;
+    s.z += t.z;
+    s.w += t.w;
+    reinterpret_cast<float4*>(acc)[i] = s;
   }
 }
 
@@ -184,8 +226,19 @@ void bcast_bf16(const __nv_bfloat16* src, const int64_t* dst_ptrs, int world, si
   bcast_bf16_kernel<<<grid_for(n, 8), 256, 0, st>>>(src, to_peers(dst_ptrs, world), world, off, n);
 }
 
-void peer_barrier(const int64_t* flag_ptrs, int world, int me, int seq, int* status, cudaStream_t st) {
-  peer_barrier_kernel<<<1, 32, 0, st>>>(to_peers(flag_ptrs, world), world, me, seq, status);
+void peer_gather_bf16(const int64_t* src_ptrs, int world, size_t n, __nv_bfloat16* dst, cudaStream_t st) {
+  if (n == 0) return;
+  peer_gather_bf16_kernel<<<grid_for(n * world, 8), 256, 0, st>>>(to_peers(src_ptrs, world), world, n, dst);
+}
+
+void peer_rs_acc(const int64_t* src_ptrs, int world, size_t n, float* acc, cudaStream_t st) {
+  if (n == 0) return;
+  peer_rs_acc_kernel<<<grid_for(n, 4), 256, 0, st>>>(to_peers(src_ptrs, world), world, n, acc);
+}
+
+void peer_barrier(const int64_t* flag_ptrs, int world, int me, int seq, int* status, cudaStream_t st,
+                  unsigned long long budget_ns) {
+  peer_barrier_kernel<<<1, 32, 0, st>>>(to_peers(flag_ptrs, world), world, me, seq, status, budget_ns);
 }
 
 }  // namespace octo

@@ -79,11 +79,37 @@ void bcast_bf16_t(torch::Tensor src, std::vector<int64_t> dst_ptrs, int64_t off)
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void peer_barrier_t(std::vector<int64_t> flag_ptrs, int64_t me, int64_t seq, int64_t device) {
+// dst[r * n + j] = rank r's bf16 buffer[off + j] (the FSDP per-layer all-gather)
+void peer_gather_bf16_t(std::vector<int64_t> ptrs, int64_t off, int64_t n, torch::Tensor dst) {
+  c10::cuda::CUDAGuard guard(dst.get_device());
+  TORCH_CHECK(dst.scalar_type() == torch::kBFloat16 && dst.is_contiguous(), "peer_gather: bf16 contiguous dst");
+  TORCH_CHECK(n % 8 == 0 && off % 8 == 0 && dst.numel() >= n * static_cast<int64_t>(ptrs.size()),
+              "peer_gather: n and off multiples of 8, dst holds world * n");
+  auto p = ptr_list(ptrs);
+  for (auto& x : p) x += off * 2;
+  peer_gather_bf16(p.data(), static_cast<int>(p.size()), static_cast<size_t>(n),
+                   reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()), at::cuda::getCurrentCUDAStream().stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// acc[j] += sum_r rank r's fp32 buffer[off + j] (the FSDP per-layer reduce-scatter)
+void peer_rs_acc_t(std::vector<int64_t> ptrs, int64_t off, torch::Tensor acc) {
+  c10::cuda::CUDAGuard guard(acc.get_device());
+  TORCH_CHECK(acc.scalar_type() == torch::kFloat32 && acc.is_contiguous(), "peer_rs_acc: fp32 contiguous acc");
+  TORCH_CHECK(acc.numel() % 4 == 0 && off % 4 == 0, "peer_rs_acc: sizes multiples of 4");
+  auto p = ptr_list(ptrs);
+  for (auto& x : p) x += off * 4;
+  peer_rs_acc(p.data(), static_cast<int>(p.size()), static_cast<size_t>(acc.numel()), acc.data_ptr<float>(),
+              at::cuda::getCurrentCUDAStream().stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void peer_barrier_t(std::vector<int64_t> flag_ptrs, int64_t me, int64_t seq, int64_t device, int64_t budget_us) {
   c10::cuda::CUDAGuard guard(static_cast<int>(device));
   auto f = ptr_list(flag_ptrs);
   peer_barrier(f.data(), static_cast<int>(f.size()), static_cast<int>(me), static_cast<int>(seq),
-               status_ptr(static_cast<int>(device)), at::cuda::getCurrentCUDAStream().stream());
+               status_ptr(static_cast<int>(device)), at::cuda::getCurrentCUDAStream().stream(),
+               static_cast<unsigned long long>(budget_us > 0 ? budget_us : 0) * 1000ull);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -95,7 +121,10 @@ void register_comm(py::module& m) {
   m.def("rs_sum_sq", &rs_sum_sq_t);
   m.def("adamw_bcast", &adamw_bcast_t);
   m.def("bcast_bf16", &bcast_bf16_t);
-  m.def("peer_barrier", &peer_barrier_t);
+  m.def("peer_barrier", &peer_barrier_t, py::arg("flag_ptrs"), py::arg("me"), py::arg("seq"), py::arg("device"),
+        py::arg("budget_us") = 0);
+  m.def("peer_gather_bf16", &peer_gather_bf16_t);
+  m.def("peer_rs_acc", &peer_rs_acc_t);
 }
 
 }  // namespace octo

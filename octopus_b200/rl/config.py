@@ -61,6 +61,7 @@ class ActorSection:
     mb_tokens: int = 262144     # prefix-tree tokens per micro-batch
     gradient_checkpointing: bool = True
     sharded: bool = True        # ZeRO-sharded optimizer state over ranks
+    full_shard: bool = False    # FSDP: weights, gradients and optimizer state sharded per layer (parallel.fsdp.FSDPActor)
     fused_collectives: bool = True
     lora_rank: int = 0          # > 0: train LoRA adapters on a frozen base (single-replica actor)
     lora_alpha: float = 32.0

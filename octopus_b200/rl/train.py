@@ -92,6 +92,11 @@ def build(cfg, device):
             from ..parallel.dp import DataParallel
 
             DataParallel(actor).attach_actor()
+    elif world > 1 and a.full_shard:
+        from ..parallel.fsdp import FSDPActor
+
+        actor = FSDPActor(mcfg, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype,
+                          fused=a.fused_collectives and device.type == "cuda")
     elif world > 1 and a.sharded:
         actor = ShardedActor(mcfg, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype,
                              ckpt=a.gradient_checkpointing, fused=a.fused_collectives and device.type == "cuda")

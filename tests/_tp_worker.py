@@ -117,6 +117,7 @@ def main():
     if os.environ.get("TP_ENGINE", "1") == "1":
         engine_check(dev, local)
     fsdp_check(dev, local)
+    fullshard_check(dev, local)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -214,6 +215,38 @@ def fsdp_check(dev, local):
     w1, w0 = res[True][1].float(), res[False][1].float()
     err = ((w1 - w0).abs().max() / w0.abs().max()).item()
     check("fsdp fused weights", err < 1e-2, f"rel_err={err:.2e}")
+
+
+def fullshard_check(dev, local):
+    """Full-shard actor: per-layer peer-memory gather / reduce-scatter on side streams vs the
+    same actor on NCCL collectives, two steps, unequal micro-batch counts per rank."""
+    from octopus_b200 import ops
+    from octopus_b200.models.config import get_config
+    from octopus_b200.parallel.fsdp import FSDPActor
+    from octopus_b200.rl.actor import OptimConfig
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from test_fsdp_full_gloo import CFG, _data, _mb
+
+    rank = dist.get_rank()
+    cfg = get_config("tiny", **CFG)
+    seqs, adv = _data()
+    split = {0: [[0, 1], [2]], 1: [[3, 4, 5]]}[rank % 2]
+    res = {}
+    for fused in (True, False):
+        a = FSDPActor(cfg, dev, seed=5, optim=OptimConfig(lr=1e-3), fused=fused)
+        for _ in range(2):
+            a.train_step([_mb(i, seqs, adv) for i in split])
+        torch.cuda.synchronize()
+        ops.check_status(local)
+        res[fused] = (a.master.clone(), a.serve16.clone())
+        a.close()
+    m1, m0 = res[True][0], res[False][0]
+    err = ((m1 - m0).abs().max() / m0.abs().max()).item()
+    check("fsdp full-shard master", err < 1e-3, f"rel_err={err:.2e}")
+    w1, w0 = res[True][1].float(), res[False][1].float()
+    err = ((w1 - w0).abs().max() / w0.abs().max()).item()
+    check("fsdp full-shard weights", err < 1e-2, f"rel_err={err:.2e}")
 
 
 if __name__ == "__main__":

@@ -30,5 +30,6 @@ def test_tp_fused_kernels_and_engine():
     print(out[-4000:])
     assert p.returncode == 0, out[-4000:]
     for name in ("ag rows_s=8", "ag rows_s=512", "rs rows_s=256", "rs-norm rows_s=16", "sample", "engine forward",
-                 "engine generate", "engine reshard", "fsdp fused master", "fsdp fused weights"):
+                 "engine generate", "engine reshard", "fsdp fused master", "fsdp fused weights",
+                 "fsdp full-shard master", "fsdp full-shard weights"):
         assert f"TP_OK {name}" in out, name
