@@ -15,16 +15,34 @@ from .bm25 import BM25Index
 
 
 class Retrieval:
-    """In-process retrieval with the same contract as the HTTP service."""
+    """In-process retrieval with the same contract as the HTTP service.  backend "bm25"
+    (default) ranks with the in-process BM25 index; "dense" ranks by inner product of the
+    query embedding (`encode(query) -> vector`) with document embeddings (`dense`: a
+    DenseIndex whose docids name documents of `docs`)."""
 
-    def __init__(self, docs: list[dict], snippet_words: int = 64, page_words: int = 512):
+    def __init__(self, docs: list[dict], snippet_words: int = 64, page_words: int = 512, backend: str = "bm25",
+                 dense=None, encode=None):
         self.index = BM25Index(docs)
         self.snippet_words = snippet_words
         self.page_words = page_words
+        self.backend = backend
+        if backend == "dense":
+            if dense is None or encode is None:
+                raise ValueError("the dense backend needs a DenseIndex and a query encoder")
+            self.dense, self.encode = dense, encode
+            self._dense_rows = [self.index.by_id.get(d) for d in dense.docids]
+        elif backend != "bm25":
+            raise ValueError(f"backend {backend!r}: bm25 or dense")
+
+    def _ranked(self, query: str, k: int):
+        if self.backend == "bm25":
+            return self.index.search(query, k)
+        hits = self.dense.search(self.encode(query), k)
+        return [(self._dense_rows[r], s) for r, s in hits if self._dense_rows[r] is not None]
 
     def search(self, query: str, k: int = 10) -> list[dict]:
         out = []
-        for i, s in self.index.search(query, k):
+        for i, s in self._ranked(query, k):
             d = self.index.docs[i]
             words = d.get("text", "").split()
             out.append({"docid": d["docid"], "title": d.get("title", ""),
@@ -50,7 +68,7 @@ def create_app(retrieval: Retrieval):
 
     @app.get("/health")
     async def health():
-        return {"ok": True, "docs": len(retrieval.index.docs)}
+        return {"ok": True, "docs": len(retrieval.index.docs), "backend": retrieval.backend}
 
     @app.post("/search")
     async def search(body: dict):
@@ -84,3 +102,41 @@ class HTTPRetrieval:
 
     def open(self, docid: str, page: int = 0):
         return self._post("/open", {"docid": docid, "page": page})
+
+
+def make_retrieval(docs: list[dict], backend: str = "bm25", embeddings: str = "", encoder: str = "",
+                   device: str = "cpu") -> Retrieval:
+    """A Retrieval over `docs`: BM25, or dense with document embeddings from `embeddings`
+    (a glob of (reps, docids) pickles) and the query encoder at local path `encoder`."""
+    if backend != "dense":
+        return Retrieval(docs)
+    from .dense import DenseIndex, QueryEncoder, load_embeddings
+
+    reps, ids = load_embeddings(embeddings)
+    return Retrieval(docs, backend="dense", dense=DenseIndex(reps, ids, device), encode=QueryEncoder(encoder, device))
+
+
+def main(argv=None) -> int:
+    import argparse
+    import json
+
+    ap = argparse.ArgumentParser(prog="python -m octopus_b200.envs.search.service")
+    ap.add_argument("--docs", required=True, help="JSONL corpus: one {docid, title, text} per line")
+    ap.add_argument("--backend", default="bm25", choices=["bm25", "dense"])
+    ap.add_argument("--embeddings", default="", help="dense: glob of (reps, docids) pickles")
+    ap.add_argument("--encoder", default="", help="dense: local path of the query embedding model")
+    ap.add_argument("--device", default="cpu")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    args = ap.parse_args(argv)
+    with open(args.docs) as f:
+        docs = [json.loads(line) for line in f if line.strip()]
+    import uvicorn
+
+    uvicorn.run(create_app(make_retrieval(docs, args.backend, args.embeddings, args.encoder, args.device)),
+                host=args.host, port=args.port)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

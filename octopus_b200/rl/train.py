@@ -162,7 +162,7 @@ def build(cfg, device):
 def _search_env(cfg, engine, rep, replicas):
     from ..envs.search.agent import SearchWorkspace, search_defaults
     from ..envs.search.reward import search_outcome
-    from ..envs.search.service import Retrieval
+    from ..envs.search.service import make_retrieval
     from ..rl.group import search_gate
     from ..serving.chat import ChatTokenizer
     from ..serving.local import ChatService
@@ -175,7 +175,12 @@ def _search_env(cfg, engine, rep, replicas):
     corpus_path = os.environ.get("OCTOPUS_SEARCH_CORPUS", "")
     corpus = [json.loads(x) for x in open(corpus_path)] if corpus_path else [
         {"docid": r["qid"], "title": r["question"], "text": str(r.get("context", ""))} for r in rows]
-    retrieval = Retrieval(corpus)
+    # OCTOPUS_SEARCH_BACKEND=dense: document embeddings OCTOPUS_SEARCH_EMBEDDINGS (glob of pickles), query
+    # encoder OCTOPUS_SEARCH_ENCODER (local checkpoint path)
+    retrieval = make_retrieval(corpus, os.environ.get("OCTOPUS_SEARCH_BACKEND", "bm25"),
+                               os.environ.get("OCTOPUS_SEARCH_EMBEDDINGS", ""),
+                               os.environ.get("OCTOPUS_SEARCH_ENCODER", ""),
+                               os.environ.get("OCTOPUS_SEARCH_DEVICE", "cpu"))
     search_defaults()
     tok = ChatTokenizer.from_dir(cfg.model.path) if cfg.model.path else ChatTokenizer.tiny()
     svc = ChatService(engine, tok)

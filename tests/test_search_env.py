@@ -40,3 +40,33 @@ def test_dry_run_episode_forks_and_answers():
     assert len(out["tree"]["forks"][0]["branches"]) == 2
     assert all(b["ended_with"] == "done" for b in out["tree"]["forks"][0]["branches"])
     assert grade("q", out["tree"]["answer"], "three")["correct"]
+
+
+def test_dense_backend_ranks_by_inner_product(tmp_path):
+    """Dense retrieval: document vectors from (reps, docids) pickles, normalised fp16,
+    exact top-k by inner product with the encoded query; same result contract as BM25."""
+    import pickle
+
+    import numpy as np
+
+    from octopus_b200.envs.search.dense import DenseIndex, load_embeddings
+    from octopus_b200.envs.search.service import Retrieval
+
+    docs = [{"docid": f"d{i}", "title": f"t{i}", "text": f"document number {i} " * 5} for i in range(50)]
+    rng = np.random.default_rng(0)
+    reps = rng.normal(size=(50, 16)).astype(np.float32)
+    for k, part in enumerate((slice(0, 30), slice(30, 50))):
+        with open(tmp_path / f"emb{k}.pkl", "wb") as f:
+            pickle.dump((reps[part], [f"d{i}" for i in range(50)][part]), f)
+    r, ids = load_embeddings(str(tmp_path / "emb*.pkl"))
+    assert r.shape == (50, 16) and ids[31] == "d31"
+    idx = DenseIndex(r, ids, block=7)  # host search in row blocks with a running top-k
+    q = reps[17] + 0.01 * rng.normal(size=16)
+    enc = {"find seventeen": q}
+    ret = Retrieval(docs, backend="dense", dense=idx, encode=lambda s: enc[s])
+    hits = ret.search("find seventeen", k=3)
+    assert hits[0]["docid"] == "d17" and len(hits) == 3
+    norm = reps / np.linalg.norm(reps, axis=1, keepdims=True)
+    want = np.argsort(-(norm @ (q / np.linalg.norm(q))))[:3]
+    assert [h["docid"] for h in hits] == [f"d{i}" for i in want]
+    assert ret.open("d17")["docid"] == "d17"
