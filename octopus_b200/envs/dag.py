@@ -50,6 +50,9 @@ class DagRollout:
     generated_tokens: int = 0
     rewards: list = field(default_factory=list)
 
+    def microbatches(self, token_cap: int, build):
+        return instance_microbatches(self, token_cap, build)
+
 
 class MultiAgentDag:
     def __init__(self, vocab_size: int, cfg: DagConfig | None = None):

@@ -228,16 +228,5 @@ def hybrid_forward(hw: HybridWeights, batch, temperature: float = 1.0, lora=None
     return ops.logprob_head(hp, hw.dense.head, batch.pair_labels, 1.0 / temperature, cfg.vocab_size)
 
 
-def hybrid_sequence_reference(hw: HybridWeights, tokens: np.ndarray):
-    """Next-token logprobs of one sequence run alone (the oracle for tree training)."""
-    from ..rl.actor import build_microbatch
-
-    n = len(tokens)
-    mb = build_microbatch(tokens, [0, n], None, np.ones(n, np.float32), np.zeros(n, np.float32),
-                          np.zeros(n, np.float32), pad_to=8)
-    d = mb.to_device(hw.dense.flat.device)
-    return hybrid_forward(hw, d.batch)[0], mb
-
-
 __all__ = ["FAMILIES", "HybridConfig", "HybridWeights", "family_kind", "hybrid_config", "hybrid_forward",
            "linear_layer_forward"]

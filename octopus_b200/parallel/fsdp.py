@@ -35,37 +35,10 @@ import torch
 import torch.distributed as dist
 
 from .. import ops
+from .peer import PeerBuffers  # noqa: F401  (re-exported: the sharded actors' IPC buffers)
 from ..models.decoder import FlatLayout, Weights, init_flat
 from ..rl.actor import Actor, OptimConfig
 from ..rl.loss import PPOConfig, ppo_loss
-
-
-class PeerBuffers:
-    """One IPC-capable buffer per rank, mapped into every rank (device pointers)."""
-
-    def __init__(self, nbytes: int, device: torch.device, group=None):
-        C = ops.ext()
-        self.local = C.symm_alloc(nbytes, device.index)
-        handle = C.ipc_handle(self.local)
-        world = dist.get_world_size(group)
-        rank = dist.get_rank(group)
-        handles = [None] * world
-        dist.all_gather_object(handles, handle, group=group)
-        self.ptrs = []
-        self._opened = []
-        for r, h in enumerate(handles):
-            if r == rank:
-                self.ptrs.append(self.local.data_ptr())
-            else:
-                p = C.ipc_open(h, device.index)
-                self.ptrs.append(p)
-                self._opened.append(p)
-
-    def close(self):
-        C = ops.ext()
-        for p in self._opened:
-            C.ipc_close(p)
-        self._opened = []
 
 
 class ShardedActor(Actor):

@@ -196,7 +196,7 @@ class TPGroup:
     """IPC buffers and fused kernels of one TP group (one process per GPU)."""
 
     def __init__(self, group, device, *, max_rows: int, hidden: int, max_n: int, max_sample_rows: int):
-        from .fsdp import PeerBuffers
+        from .peer import PeerBuffers
 
         self.group = group
         self.tp = dist.get_world_size(group)

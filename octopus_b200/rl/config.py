@@ -85,6 +85,8 @@ class RLSection:
     swe_bundle: int = 0         # > 1: bundles of this many tasks of one repository per episode
     swe_timeout: float = 120.0  # seconds per tool / test command
     episodes_per_server: int = 8
+    dag_prefix: int = 2048      # kind=dag: the shared task prefix every agent mounts
+    dag_turn: int = 512         # kind=dag: tokens per agent turn
 
 
 @dataclass

@@ -140,6 +140,7 @@ def build(cfg, device):
     if cfg.rl.kind == "dag":
         inst = [i for i in range(cfg.rl.batch_size) if i % replicas == rep]
         dag = MultiAgentDag(mcfg.vocab_size, DagConfig(instances=cfg.rl.batch_size, samples=cfg.rl.n_samples,
+                                                       prefix_len=cfg.rl.dag_prefix, turn_len=cfg.rl.dag_turn,
                                                        temperature=cfg.rollout.temperature,
                                                        seed=cfg.seed * 1000 + rep))
 

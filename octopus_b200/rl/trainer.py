@@ -22,7 +22,6 @@ from dataclasses import dataclass
 
 import torch
 
-from ..envs.dag import instance_microbatches
 from ..utils.iostats import d2h
 from .actor import Actor, build_microbatch
 from .dp_balance import longest_first
@@ -49,10 +48,7 @@ class RLTrainer:
         return self.env.rollout(self.engine)
 
     def train_on(self, ro) -> dict:
-        if hasattr(ro, "microbatches"):
-            mbs = ro.microbatches(self.cfg.mb_tokens, build_microbatch)
-        else:
-            mbs = instance_microbatches(ro, self.cfg.mb_tokens, build_microbatch)
+        mbs = ro.microbatches(self.cfg.mb_tokens, build_microbatch)
         k, n = self.cfg.mb_shard
         if n > 1:  # this rank's share: micro-batches assigned longest-first by tree tokens
             mbs = [mbs[i] for i in sorted(longest_first([mb.n_tree for mb in mbs], n)[k])]

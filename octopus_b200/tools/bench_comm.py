@@ -19,6 +19,9 @@ bandwidth (770 GB/s per direction).  Cases (7B shapes):
             baseline: reduce_scatter_tensor + norm
   adamw_bcast  AdamW on the owned shard + peer stores of the new bf16 weights to every rank;
             baseline: AdamW + all_gather_into_tensor
+  fsdp_layer_gather / fsdp_layer_reduce_scatter  the full-shard actor's per-layer all-gather of
+            one 7B decoder layer's bf16 shards and reduce-scatter-accumulate of its fp32
+            gradient; baseline: all_gather_into_tensor / reduce_scatter_tensor + add
 """
 from __future__ import annotations
 
@@ -77,7 +80,7 @@ def main(argv=None) -> int:
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     from octopus_b200 import ops
-    from octopus_b200.parallel.fsdp import PeerBuffers
+    from octopus_b200.parallel.peer import PeerBuffers
     from octopus_b200.parallel.tp import TPGroup
 
     rank, world = dist.get_rank(), dist.get_world_size()
@@ -196,8 +199,49 @@ def main(argv=None) -> int:
     emit({"kernel": "adamw_bcast", "world": world, "elements": total, "fused_ms": round(tf, 3),
           "nccl_ms": round(tb, 3), "link_bytes": link, "link_gbs": round(link / tf / 1e6, 1),
           "roofline_ms": round(roof, 3), "frac_of_roofline": round(roof / tf, 3), "speedup_vs_nccl": round(tb / tf, 2)})
+    # ------------------------------------------------------------------ full-shard actor: one 7B layer unit
+    unit = 233_046_016 // (world * 8) * (world * 8)  # elements of one decoder layer unit (padded to world * 8)
+    su = unit // world
+    shards = PeerBuffers(su * 2, dev)
+    shards.local.view(torch.bfloat16).normal_()
+    slot = torch.empty(unit, dtype=torch.bfloat16, device=dev)
+    gslots = PeerBuffers(unit * 4, dev)
+    gsl = gslots.local.view(torch.float32)
+    gsl.normal_()
+    acc = torch.zeros(su, device=dev)
+    mine = shards.local.view(torch.bfloat16)[:su]
+
+    def ag_fused():
+        C.peer_gather_bf16(shards.ptrs, 0, su, slot)
+
+    def ag_base():
+        dist.all_gather_into_tensor(slot, mine)
+
+    tf, tb = timed(ag_fused, 10, 2), timed(ag_base, 10, 2)
+    link = (world - 1) * su * 2.0
+    roof = roofline_ms(0.0, link, pk)
+    emit({"kernel": "fsdp_layer_gather", "world": world, "elements": unit, "fused_ms": round(tf, 3),
+          "nccl_ms": round(tb, 3), "link_bytes": link, "link_gbs": round(link / tf / 1e6, 1),
+          "roofline_ms": round(roof, 3), "frac_of_roofline": round(roof / tf, 3), "speedup_vs_nccl": round(tb / tf, 2)})
+    red = torch.empty(su, device=dev)
+
+    def rsl_fused():
+        C.peer_rs_acc(gslots.ptrs, rank * su, acc)
+
+    def rsl_base():
+        dist.reduce_scatter_tensor(red, gsl)
+        acc.add_(red)
+
+    tf, tb = timed(rsl_fused, 10, 2), timed(rsl_base, 10, 2)
+    link = (world - 1) * su * 4.0
+    roof = roofline_ms(0.0, link, pk)
+    emit({"kernel": "fsdp_layer_reduce_scatter", "world": world, "elements": unit, "fused_ms": round(tf, 3),
+          "nccl_ms": round(tb, 3), "link_bytes": link, "link_gbs": round(link / tf / 1e6, 1),
+          "roofline_ms": round(roof, 3), "frac_of_roofline": round(roof / tf, 3), "speedup_vs_nccl": round(tb / tf, 2)})
     torch.cuda.synchronize()
     dist.barrier()
+    shards.close()
+    gslots.close()
     grads.close()
     weights.close()
     ops.check_status(local)
