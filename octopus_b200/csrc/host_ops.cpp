@@ -154,13 +154,15 @@ static GemmLaunch make_launch(const torch::Tensor& A, bool a_mn, const torch::Te
   g.s.n_tiles = (N + BN - 1) / BN;
   g.s.k_blocks = (K + 63) / 64;
   g.s.num_tiles = g.s.m_tiles * g.s.n_tiles;
+  g.status = status_ptr(device);
+  g.stream = cur_stream(A);
+  TORCH_CHECK(K > 0 || M == 0 || N == 0, "gemm: K must be positive");
+  if (M == 0 || N == 0) return g;  // empty product: callers return before launching; no tensor maps
   g.ta = a_mn ? make_tmap_bf16_2d(A.data_ptr(), M, K, A.stride(0), 64, 64)
               : make_tmap_bf16_2d(A.data_ptr(), K, M, A.stride(0), 64, 128);
   g.tb = b_mn ? make_tmap_bf16_2d(B.data_ptr(), N, K, B.stride(0), 64, 64)
               : make_tmap_bf16_2d(B.data_ptr(), K, N, B.stride(0), 64, BN);
-  g.status = status_ptr(device);
   g.grid = std::min(g.s.num_tiles, sms);
-  g.stream = cur_stream(A);
   g.alpha = 1.f;
   g.vocab_limit = N;
   g.s.pdl = g_pdl ? 1 : 0;

@@ -26,6 +26,7 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
 inline CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
                                      uint32_t box_inner, uint32_t box_outer,
                                      CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  TORCH_CHECK(ptr != nullptr && inner > 0 && outer > 0, "TMA map of an empty tensor");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15u) == 0, "TMA base must be 16-byte aligned");
   TORCH_CHECK((row_stride_elems * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
   CUtensorMap m;

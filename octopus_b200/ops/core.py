@@ -498,6 +498,10 @@ class _Head(torch.autograd.Function):
     def forward(ctx, h, W, labels, alpha, vocab_limit):
         M = h.shape[0]
         ctx.alpha, ctx.vocab_limit = alpha, vocab_limit
+        if M == 0:  # no trained pair (an empty micro-batch that keeps the ranks' collectives paired)
+            z = torch.zeros(0, dtype=torch.float32, device=h.device)
+            ctx.save_for_backward(h, W, labels, z, z)
+            return z, z.clone()
         if _is_cuda(h):
             pad = (-M) % 8
             hp = torch.cat([h, h.new_zeros(pad, h.shape[1])]) if pad else h
@@ -523,6 +527,8 @@ class _Head(torch.autograd.Function):
         g_ent = g_ent.float().contiguous()
         mg = getattr(W, "main_grad", None)
         frozen = mg is None and not ctx.needs_input_grad[1]
+        if M == 0:
+            return torch.zeros_like(h), (None if (mg is not None or frozen) else torch.zeros_like(W)), None, None, None
         if _is_cuda(h):
             dh = torch.empty_like(h)
             dW = mg if mg is not None else (None if frozen else

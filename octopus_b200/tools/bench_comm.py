@@ -87,7 +87,7 @@ def main(argv=None) -> int:
     pk = _peaks()
     H, F, QKV = 3584, 18944, 4608
     rows_list = (64, 128, 2048)
-    comm = TPGroup(dist.group.WORLD, dev, max_rows=max(rows_list), hidden=H, max_n=H, max_sample_rows=256)
+    comm = TPGroup(dist.group.WORLD, dev, max_rows=world * max(rows_list), hidden=H, max_n=H, max_sample_rows=256)
     out = []
 
     def emit(rec):

@@ -202,6 +202,22 @@ def test_logprob_head_fwd_bwd():
     assert rel_err(W.main_grad, Wr.grad) < 3e-2
 
 
+def test_empty_rows_head_and_gemm():
+    """Zero-row operands (a rank's empty micro-batch) return empty results and zero gradients
+    without building a tensor map or launching a kernel."""
+    H, V = 512, 1024
+    h = torch.zeros(0, H, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    W = (torch.randn(V, H, device=dev) * 0.05).bfloat16().requires_grad_(True)
+    lp, ent = ops.logprob_head(h, W, torch.zeros(0, dtype=torch.int64, device=dev), 1.0, V)
+    assert lp.shape == (0,) and ent.shape == (0,)
+    (lp.sum() + ent.sum()).backward()
+    assert h.grad.shape == (0, H) and float(W.grad.float().abs().sum()) == 0.0
+    y = ops.gemm(torch.zeros(0, H, device=dev, dtype=torch.bfloat16), W.detach())
+    assert y.shape == (0, V)
+    torch.cuda.synchronize()
+    ops.check_status(0)
+
+
 def test_sampling_distribution():
     torch.manual_seed(9)
     H, V = 64, 256
