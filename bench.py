@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--profile-step", default="",
                     help="after the timed steps, run one more step under the PyTorch CUDA trace and write rank 0's "
                          "per-kernel breakdown (JSON) here; not part of the timed value")
+    ap.add_argument("--fsdp-gather", action="store_true",
+                    help="--actor fsdp: gather each layer's weights from the shards (default: read the serving copy)")
     ap.add_argument("--actor", default="sharded", choices=["sharded", "fsdp", "dp"],
                     help="N > 1 actor: sharded (ZeRO: fp32 master / optimizer sharded, fused peer-memory RS + AdamW + "
                          "all-gather), fsdp (full shard: per-layer peer-memory gather and reduce-scatter), or dp "
@@ -184,7 +186,7 @@ def main():
     if world > 1 and args.actor == "fsdp":
         from octopus_b200.parallel.fsdp import FSDPActor
 
-        actor = FSDPActor(cfg, dev, seed=0)
+        actor = FSDPActor(cfg, dev, seed=0, gather_weights=args.fsdp_gather)
     else:
         actor = ShardedActor(cfg, dev, seed=0) if sharded else Actor(cfg, dev, seed=0)
     if grpo:

@@ -160,7 +160,9 @@ class _StagedWeights(Weights):
     (norm + head) into staging of their own; every view's main_grad points into the
     matching gradient staging."""
 
-    def __init__(self, cfg, layout: FlatLayout, wslots, gslots, edge_w: dict, edge_g: dict):
+    def __init__(self, cfg, layout: FlatLayout, wslots, gslots, edge_w: dict, edge_g: dict, full=None):
+        # full: the complete bf16 flat buffer (the serving copy); when given, weight views point
+        # into it and only the gradient views are staged
         self.cfg, self.layout, self.flat = cfg, layout, None
         self.t = {}
         last = len(layout.units) - 1
@@ -169,9 +171,11 @@ class _StagedWeights(Weights):
             o = layout.offsets[s.name] - u0
             n = math.prod(s.shape)
             if 0 < s.unit < last:
-                wb, gb = wslots[(s.unit - 1) % 2], gslots[(s.unit - 1) % 2]
+                wb, gb = (None if full is not None else wslots[(s.unit - 1) % 2]), gslots[(s.unit - 1) % 2]
             else:
-                wb, gb = edge_w[s.unit], edge_g[s.unit]
+                wb, gb = (None if full is not None else edge_w[s.unit]), edge_g[s.unit]
+            if wb is None:
+                wb = full[u0:]
             v = wb[o: o + n].view(s.shape)
             v.main_grad = gb[o: o + n].view(s.shape)
             self.t[s.name] = v
@@ -181,9 +185,14 @@ class FSDPActor(Actor):
     """Full-shard (FSDP) actor over the flat layout.
 
     Each rank holds 1/W of every unit: bf16 weights (`shard16`), fp32 master, AdamW
-    moments and the reduced fp32 gradient (`grad_shard`).  A training micro-batch:
+    moments and the reduced fp32 gradient (`grad_shard`).  The colocated engine keeps the
+    full bf16 serving copy (`serve16`) resident, and it equals the gathered shards for the
+    whole of a training step (it is re-gathered right after each optimizer step), so by
+    default the layers read their weights from it and only gradients are staged per layer;
+    with `gather_weights=True` (a deployment whose serving copy lives elsewhere) every
+    layer's weights are gathered from the shards as below.  A training micro-batch:
 
-    * forward: before layer i the layer's unit is all-gathered into staging slot i % 2
+    * forward (gather_weights): before layer i the layer's unit is all-gathered into staging slot i % 2
       (peer loads of every rank's bf16 slice on a gather stream, the next layer prefetched
       while this one computes); the embedding and the norm + head unit are gathered once
       per step into staging of their own;
@@ -212,7 +221,7 @@ class FSDPActor(Actor):
 
     def __init__(self, cfg, device="cuda", *, optim: OptimConfig | None = None, ppo: PPOConfig | None = None,
                  seed: int = 0, dtype=torch.bfloat16, temperature: float = 1.0, group=None,
-                 fused: bool | None = None, wait_budget_us: int = 60_000_000):
+                 fused: bool | None = None, wait_budget_us: int = 60_000_000, gather_weights: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         self.optim = optim or OptimConfig()
@@ -223,6 +232,7 @@ class FSDPActor(Actor):
         self.layout = FlatLayout(cfg, pad_multiple=self.world)
         self.us = UnitShards(self.layout, self.world, self.rank)
         self.fused = (self.device.type == "cuda") if fused is None else fused
+        self.gather_weights = bool(gather_weights)
         self.ckpt, self.ckpt_block, self.chunk_tokens, self.host_acts, self.seq_tile = True, 1, 0, None, 0
         self.temperature, self.version, self.step_count = temperature, 0, 0
         gdt = torch.float64 if dtype == torch.float64 else torch.float32
@@ -250,10 +260,14 @@ class FSDPActor(Actor):
         for u in range(n_units):
             self.shard16[us.local(u)].copy_(full[us.owned(u)])
         self.gslots = [gsl[:layer_n], gsl[layer_n:]]
-        self.wslots = [torch.empty(layer_n, dtype=dtype, device=dev) for _ in range(2)]
-        self.edge_w = {u: torch.empty(us.size[u], dtype=dtype, device=dev) for u in (0, self.last_unit)}
+        if self.gather_weights:
+            self.wslots = [torch.empty(layer_n, dtype=dtype, device=dev) for _ in range(2)]
+            self.edge_w = {u: torch.empty(us.size[u], dtype=dtype, device=dev) for u in (0, self.last_unit)}
+        else:
+            self.wslots, self.edge_w = [], {}
         self.edge_g = edge_g
-        self.tw = _StagedWeights(cfg, self.layout, self.wslots, self.gslots, self.edge_w, self.edge_g)
+        self.tw = _StagedWeights(cfg, self.layout, self.wslots, self.gslots, self.edge_w, self.edge_g,
+                                 full=None if self.gather_weights else full)
         # the serving copy: full bf16 weights the colocated engine reads
         self.serve16 = full
         self.weights = Weights(cfg, self.serve16, self.layout)
@@ -300,6 +314,8 @@ class FSDPActor(Actor):
     # ------------------------------------------------------------------ staging
     def _gather_layer(self, u: int, prefetch: bool):
         """Unit u (a layer) into weight slot (u - 1) % 2 unless it is there already."""
+        if not self.gather_weights:
+            return
         s = (u - 1) % 2
         if self._slot_unit[s] == u:
             return
@@ -324,7 +340,7 @@ class FSDPActor(Actor):
             torch.cuda.current_stream(self.device).wait_event(self._gather_ev.pop(u))
 
     def _stage_edges(self):
-        if self._edges_ready:
+        if self._edges_ready or not self.gather_weights:
             return
         for u in (0, self.last_unit):
             self._gather_into(u, self.edge_w[u])

@@ -62,6 +62,7 @@ class ActorSection:
     gradient_checkpointing: bool = True
     sharded: bool = True        # ZeRO-sharded optimizer state over ranks
     full_shard: bool = False    # FSDP: weights, gradients and optimizer state sharded per layer (parallel.fsdp.FSDPActor)
+    gather_weights: bool = False  # FSDP: gather each layer from the shards instead of reading the serving copy
     fused_collectives: bool = True
     lora_rank: int = 0          # > 0: train LoRA adapters on a frozen base (single-replica actor)
     lora_alpha: float = 32.0

@@ -96,7 +96,7 @@ def build(cfg, device):
         from ..parallel.fsdp import FSDPActor
 
         actor = FSDPActor(mcfg, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype,
-                          fused=a.fused_collectives and device.type == "cuda")
+                          fused=a.fused_collectives and device.type == "cuda", gather_weights=a.gather_weights)
     elif world > 1 and a.sharded:
         actor = ShardedActor(mcfg, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype,
                              ckpt=a.gradient_checkpointing, fused=a.fused_collectives and device.type == "cuda")

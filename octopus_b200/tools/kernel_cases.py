@@ -19,6 +19,7 @@ Cases (inputs sized above L2 where DRAM behaviour matters, a few GB at most):
   decode_gemms       the four GEMMs of one 7B decoder layer at 256 decode rows (OCTO_SPLITK=0: no split-K,
                      OCTO_GEMM_MT=1: one M-tile per CTA)
   decode_gemm_{qkv,o,gu,down}  one of them, over weight copies > 2x L2 (time / copies = per GEMM)
+  decode_sweep       the four decode GEMMs at 16..256 rows: time, HBM rate, roofline fraction
   head_fwd           fused logprob head, 4096 rows x 152064 vocab
   sample_head        fused sampling head, 256 rows x 152064 vocab
 """
@@ -213,6 +214,63 @@ def main(argv=None):
     print(f"{args.case}: {a.elapsed_time(b) / args.reps:.3f} ms/iter")
 
 
+def decode_sweep(rows=(16, 32, 64, 128, 256), reps=20):
+    """The four decode GEMMs of a 7B layer at several decode batch sizes: CUDA-graph replays over
+    weight copies that together exceed 2x L2 (cold weights), per-GEMM time, achieved HBM bandwidth
+    and the fraction of the roofline max(weight bytes / HBM copy rate, FLOPs / bf16 GEMM rate)
+    (MEASURED_PEAKS.json when present, else 6.65 TB/s and 1.59 PFLOP/s)."""
+    import json
+    import os
+
+    dev = torch.device("cuda", 0)
+    hbm, tflops = 6650.0, 1590.0
+    peaks = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    if os.path.exists(peaks):
+        with open(peaks) as f:
+            pk = json.load(f)
+        hbm, tflops = float(pk.get("hbm_gbs", hbm)), float(pk.get("bf16_tflops", tflops))
+    H, F = 3584, 18944
+    shapes = {"qkv": (4608, H), "o": (H, 3584), "gu": (2 * F, H), "down": (H, F)}
+    for name, (n, k) in shapes.items():
+        copies = max(2, -(-(300 << 20) // (n * k * 2)))
+        ws = [(torch.randn(n, k, device=dev) * 0.02).bfloat16() for _ in range(copies)]
+        for M in rows:
+            x = torch.randn(M, k, device=dev).bfloat16()
+            outs = [torch.empty(M, n, device=dev, dtype=torch.bfloat16) for _ in ws]
+
+            def fn():
+                for w, o in zip(ws, outs):
+                    ops.gemm(x, w, out=o)
+
+            fn()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                fn()
+            torch.cuda.current_stream().wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            for _ in range(3):
+                g.replay()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(reps):
+                g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            ops.check_status(0)
+            us = a.elapsed_time(b) * 1e3 / (reps * copies)
+            byts = n * k * 2 + M * (n + k) * 2
+            roof = max(byts / (hbm * 1e3), 2.0 * M * n * k / (tflops * 1e6))  # microseconds
+            print(json.dumps({"gemm": name, "M": M, "N": n, "K": k, "us": round(us, 2),
+                              "tb_s": round(byts / us / 1e6, 2), "roofline_us": round(roof, 2),
+                              "frac_of_roofline": round(roof / us, 3)}), flush=True)
+            del g
+        del ws
+
+
 def trace_attn_tc():
     """Per-event timeline (microseconds from CTA start) of CTA (0, 0) of the tcgen05 attention."""
     dev = torch.device("cuda", 0)
@@ -237,5 +295,7 @@ if __name__ == "__main__":
     import sys
     if len(sys.argv) > 1 and sys.argv[1] == "trace_attn_tc":
         trace_attn_tc()
+    elif len(sys.argv) > 1 and sys.argv[1] == "decode_sweep":
+        decode_sweep()
     else:
         main()

@@ -233,20 +233,22 @@ def fullshard_check(dev, local):
     seqs, adv = _data()
     split = {0: [[0, 1], [2]], 1: [[3, 4, 5]]}[rank % 2]
     res = {}
-    for fused in (True, False):
-        a = FSDPActor(cfg, dev, seed=5, optim=OptimConfig(lr=1e-3), fused=fused)
-        for _ in range(2):
-            a.train_step([_mb(i, seqs, adv) for i in split])
-        torch.cuda.synchronize()
-        ops.check_status(local)
-        res[fused] = (a.master.clone(), a.serve16.clone())
-        a.close()
-    m1, m0 = res[True][0], res[False][0]
-    err = ((m1 - m0).abs().max() / m0.abs().max()).item()
-    check("fsdp full-shard master", err < 1e-3, f"rel_err={err:.2e}")
-    w1, w0 = res[True][1].float(), res[False][1].float()
-    err = ((w1 - w0).abs().max() / w0.abs().max()).item()
-    check("fsdp full-shard weights", err < 1e-2, f"rel_err={err:.2e}")
+    for gather in (True, False):
+        for fused in (True, False):
+            a = FSDPActor(cfg, dev, seed=5, optim=OptimConfig(lr=1e-3), fused=fused, gather_weights=gather)
+            for _ in range(2):
+                a.train_step([_mb(i, seqs, adv) for i in split])
+            torch.cuda.synchronize()
+            ops.check_status(local)
+            res[gather, fused] = (a.master.clone(), a.serve16.clone())
+            a.close()
+    m0, w0 = res[False, False][0], res[False, False][1].float()
+    for key in ((True, True), (True, False), (False, True)):
+        tag = ("gathered" if key[0] else "serving-copy") + (" fused" if key[1] else " nccl")
+        err = ((res[key][0] - m0).abs().max() / m0.abs().max()).item()
+        check(f"fsdp full-shard master {tag}", err < 1e-3, f"rel_err={err:.2e}")
+        err = ((res[key][1].float() - w0).abs().max() / w0.abs().max()).item()
+        check(f"fsdp full-shard weights {tag}", err < 1e-2, f"rel_err={err:.2e}")
 
 
 if __name__ == "__main__":

@@ -2,10 +2,13 @@
 gathered into rotating staging slots layer by layer, gradients are reduce-scattered per
 layer during the backward, the embedding and head once per step.  One step on two ranks
 (each its own micro-batches, unequal counts) must equal one single-process Actor step
-over all of them; the serving copy must equal the updated weights on every rank."""
+over all of them; the serving copy must equal the updated weights on every rank.  Both
+weight sources are checked over two steps: layers gathered from the shards, and layers read
+from the serving copy (re-gathered after each optimizer step)."""
 import os
 
 import numpy as np
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -39,11 +42,15 @@ def _reference():
     cfg = get_config("tiny", **CFG)
     actor = Actor(cfg, "cpu", seed=5, dtype=torch.float64, ckpt=True, optim=OptimConfig(lr=1e-3))
     seqs, adv = _data()
-    st = actor.train_step([_mb(i, seqs, adv) for part in SPLIT.values() for i in part])
+    for _ in range(STEPS):
+        st = actor.train_step([_mb(i, seqs, adv) for part in SPLIT.values() for i in part])
     return actor, float(st["grad_norm"])
 
 
-def _worker(rank, world, port, q):
+STEPS = 2
+
+
+def _worker(rank, world, port, q, gather):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     from datetime import timedelta
@@ -53,19 +60,22 @@ def _worker(rank, world, port, q):
         from octopus_b200.parallel.fsdp import FSDPActor
 
         cfg = get_config("tiny", **CFG)
-        actor = FSDPActor(cfg, "cpu", seed=5, dtype=torch.float64, optim=OptimConfig(lr=1e-3), fused=False)
+        actor = FSDPActor(cfg, "cpu", seed=5, dtype=torch.float64, optim=OptimConfig(lr=1e-3), fused=False,
+                          gather_weights=gather)
         seqs, adv = _data()
-        st = actor.train_step([_mb(i, seqs, adv) for i in SPLIT[rank]])
+        for _ in range(STEPS):
+            st = actor.train_step([_mb(i, seqs, adv) for i in SPLIT[rank]])
         q.put((rank, actor.serve16.numpy().copy(), float(st["grad_norm"])))
     finally:
         dist.destroy_process_group()
 
 
-def test_fsdp_full_shard_two_ranks_matches_single_process():
+@pytest.mark.parametrize("gather", [False, True])
+def test_fsdp_full_shard_two_ranks_matches_single_process(gather):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29400 + os.getpid() % 200
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    port = 29400 + os.getpid() % 200 + (7 if gather else 0)
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, gather)) for r in range(2)]
     for p in procs:
         p.start()
     got = dict((r, (w, g)) for r, w, g in (q.get(timeout=300) for _ in range(2)))
