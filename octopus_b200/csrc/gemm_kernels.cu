@@ -75,6 +75,10 @@ void gemm_launch(const GemmLaunch& g) {
   } else if (g.epi == kEpiSplitK) {
     EpiSplitK e{reinterpret_cast<float*>(g.C), g.s.M, g.s.N, nullptr};
     by_bn(g, e);
+  } else if (g.epi == kEpiSwiGLU) {
+    EpiSwiGLU e{reinterpret_cast<__nv_bfloat16*>(g.C), g.ldc};
+    if (g.mt == 2) launch_one<256, false, false, EpiSwiGLU, 2>(g, e);
+    else launch_one<256, false, false>(g, e);
   } else if (g.epi == kEpiSample) {
     EpiSample e{g.partial, g.s.n_tiles, g.bn, g.alpha, g.vocab_limit, g.seed, g.row_offset, g.col_base};
     if (g.bn == 256) launch_one<256, false, false>(g, e);

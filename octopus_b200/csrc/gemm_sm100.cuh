@@ -23,6 +23,9 @@
 // Each epilogue thread owns one accumulator row per tile; rows >= M are skipped.
 #pragma once
 #include <cuda.h>
+
+#include <type_traits>
+
 #include "common.cuh"
 #include "octo_api.h"
 
@@ -78,6 +81,14 @@ __device__ __forceinline__ void gemm_tile_coords(const GemmShape& s, int tile, i
   nb = r / gm;
   if (s.m_shift) mb = (mb + s.m_shift) % s.m_tiles;
 }
+
+// An epilogue with `static constexpr bool kPaired = true` takes the two halves of a paired
+// B tile (shape.b_pair > 0) together: apply_pair(row, col0, nvalid, lo[32], hi[32]) per
+// 32-column chunk of the tile's BN / 2 output columns.
+template <class E, class = void>
+struct EpiPaired : std::false_type {};
+template <class E>
+struct EpiPaired<E, std::void_t<decltype(E::kPaired)>> : std::bool_constant<E::kPaired> {};
 
 // ---------------------------------------------------------------- A-operand sources
 //
@@ -174,7 +185,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       auto pf_step = [&]() {  // prefetch one K-block of B, then advance the cursor
         if (pf_tile >= shape.num_tiles) return;
         if constexpr (!B_MN) {
-          tma_prefetch_l2_2d(&tmB, pf_kb * kGemmBK, pf_nb * BN);
+          if (shape.b_pair > 0) {
+            tma_prefetch_l2_2d(&tmB, pf_kb * kGemmBK, pf_nb * (BN / 2));
+            tma_prefetch_l2_2d(&tmB, pf_kb * kGemmBK, shape.b_pair + pf_nb * (BN / 2));
+          } else {
+            tma_prefetch_l2_2d(&tmB, pf_kb * kGemmBK, pf_nb * BN);
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < BN / 64; ++j) tma_prefetch_l2_2d(&tmB, pf_nb * BN + 64 * j, pf_kb * kGemmBK);
@@ -219,7 +235,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int mt = 0; mt < MT; ++mt) asrc.load(a_dst + mt * Cfg::kATileBytes, &full_bar[stage], k0, MT * mb + mt);
           }
           if constexpr (!B_MN) {
-            tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, n0);
+            if (shape.b_pair > 0) {  // two half-height boxes (the map's box is BN / 2 rows)
+              const int r0 = nb * (BN / 2);
+              tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, r0);
+              tma_load_2d(b_dst + (BN / 2) * kGemmBK * 2, &tmB, &full_bar[stage], k0, shape.b_pair + r0);
+            } else {
+              tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, n0);
+            }
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full_bar[stage], n0 + 64 * j, k0);
@@ -335,18 +357,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int row = (MT * mb + mt) * kGemmBM + quarter * 32 + lane;
         epi.begin_split(ks);
         epi.begin_tile();
+        if constexpr (EpiPaired<Epi>::value) {
+          // paired tile: TMEM columns [0, BN/2) hold the first half, [BN/2, BN) the second
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols + mt * BN + c * 32), r);
-          tmem_wait_ld();
-          const int col0 = n0 + c * 32;
-          if (row < shape.M && col0 < shape.N) {
-            float v[32];
+          for (int c = 0; c < BN / 64; ++c) {
+            uint32_t r[32], r2[32];
+            const uint32_t cb = tmem_base + lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols + mt * BN + c * 32);
+            tmem_ld_32x32b_x32(cb, r);
+            tmem_ld_32x32b_x32(cb + BN / 2, r2);
+            tmem_wait_ld();
+            const int col0 = nb * (BN / 2) + c * 32;
+            if (row < shape.M && col0 < shape.N) {
+              float lo[32], hi[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = empty_k ? 0.f : __uint_as_float(r[i]);
-            const int nvalid = shape.N - col0 < 32 ? shape.N - col0 : 32;
-            epi.apply(row, col0, nvalid, v, nb);
+              for (int i = 0; i < 32; ++i) {
+                lo[i] = empty_k ? 0.f : __uint_as_float(r[i]);
+                hi[i] = empty_k ? 0.f : __uint_as_float(r2[i]);
+              }
+              const int nvalid = shape.N - col0 < 32 ? shape.N - col0 : 32;
+              epi.apply_pair(row, col0, nvalid, lo, hi);
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols + mt * BN + c * 32), r);
+            tmem_wait_ld();
+            const int col0 = n0 + c * 32;
+            if (row < shape.M && col0 < shape.N) {
+              float v[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = empty_k ? 0.f : __uint_as_float(r[i]);
+              const int nvalid = shape.N - col0 < 32 ? shape.N - col0 : 32;
+              epi.apply(row, col0, nvalid, v, nb);
+            }
           }
         }
         if (mt == MT - 1) {  // accumulator drained: the MMA warp may reuse it
@@ -452,6 +497,42 @@ struct EpiF32 {
       }
     }
   }
+  __device__ __forceinline__ void begin_split(int) {}
+  __device__ __forceinline__ void begin_tile() {}
+  __device__ __forceinline__ void end_tile(int, int) {}
+  __device__ __forceinline__ void finish() const {}
+};
+
+// Gated MLP: C (bf16 [M, N], row stride ldc) = silu(gate) * up, where the paired tile's first
+// half is the gate projection and its second half the up projection of the same N columns.
+// Gate and up are rounded to bf16 first, so the result equals the unfused GEMM (bf16 output)
+// followed by swiglu_fwd_kernel.
+struct EpiSwiGLU {
+  static constexpr bool kPaired = true;
+  __nv_bfloat16* C;
+  int ldc;
+  __device__ __forceinline__ void apply_pair(int row, int col0, int nvalid, float (&g)[32], float (&u)[32]) {
+    __nv_bfloat16* dst = C + static_cast<size_t>(row) * ldc + col0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (q * 8 < nvalid) {
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float gb = __bfloat162float(__float2bfloat16(g[q * 8 + i]));
+          const float ub = __bfloat162float(__float2bfloat16(u[q * 8 + i]));
+          o[i] = gb / (1.f + __expf(-gb)) * ub;
+        }
+        uint4 w;
+        w.x = pack_bf16x2(o[0], o[1]);
+        w.y = pack_bf16x2(o[2], o[3]);
+        w.z = pack_bf16x2(o[4], o[5]);
+        w.w = pack_bf16x2(o[6], o[7]);
+        *reinterpret_cast<uint4*>(dst + q * 8) = w;
+      }
+    }
+  }
+  __device__ __forceinline__ void apply(int, int, int, float (&)[32], int) {}
   __device__ __forceinline__ void begin_split(int) {}
   __device__ __forceinline__ void begin_tile() {}
   __device__ __forceinline__ void end_tile(int, int) {}

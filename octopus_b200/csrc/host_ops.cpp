@@ -282,6 +282,38 @@ void gemm_out(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, torch::Ten
 //   (x, h) = (A W^T + bias + residual, RMSNorm(x) * norm_w)
 // Split-K launches (every decode-sized o / down projection) finish in one kernel that also
 // normalises; other shapes run the GEMM and the norm separately.
+// Gated MLP projection fused with its activation: act[M, F] = silu(A W_gate^T) * (A W_up^T),
+// W = [W_gate; W_up] ([2F, K], the checkpoint's gate_up layout).  Each tile pairs 128 gate
+// rows with the matching 128 up rows (two TMA boxes into one 256-row B stage), so the
+// epilogue holds both halves of its 128 output columns; no [M, 2F] intermediate is written.
+// F must be a multiple of 128 (callers fall back to GEMM + swiglu otherwise).
+torch::Tensor gemm_swiglu_t(torch::Tensor A, torch::Tensor W) {
+  c10::cuda::CUDAGuard guard(A.get_device());
+  TORCH_CHECK(W.dim() == 2 && W.size(0) % 256 == 0, "gemm_swiglu: W rows must be 2F with F a multiple of 128");
+  GemmLaunch g = make_launch(A, false, W, false, 256);
+  const int M = g.s.M, F = g.s.N / 2;
+  auto out = torch::empty({M, F}, A.options());
+  if (M == 0) return out;
+  const int sms = num_sms(A.get_device());
+  g.bn = 256;
+  g.s.N = F;
+  g.s.n_tiles = F / 128;
+  g.s.b_pair = F;
+  g.s.k_splits = 0;
+  g.tb = make_tmap_bf16_2d(W.data_ptr(), g.s.K, 2 * static_cast<int64_t>(F), W.stride(0), 64, 128);
+  // decode-sized M (129..256 rows): both 128-row M-blocks in one CTA when the tiles fill the GPU
+  g.mt = (M > 128 && M <= 256 && g.s.n_tiles * 4 >= sms * 3) ? 2 : 1;
+  g.s.m_tiles = g.mt == 2 ? 1 : (M + 127) / 128;
+  g.s.num_tiles = g.s.m_tiles * g.s.n_tiles;
+  g.grid = std::min(g.s.num_tiles, sms);
+  g.epi = kEpiSwiGLU;
+  g.C = out.data_ptr();
+  g.ldc = F;
+  gemm_launch(g);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
 std::vector<torch::Tensor> gemm_res_norm_t(torch::Tensor A, torch::Tensor W, torch::Tensor residual,
                                            torch::Tensor norm_w, double eps, bool plus_one,
                                            c10::optional<torch::Tensor> bias) {
@@ -813,6 +845,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_fwd", &embed_fwd_t);
   m.def("embed_bwd", &embed_bwd_t);
   m.def("kv_write", &kv_write_t);
+  m.def("gemm_swiglu", &gemm_swiglu_t);
   m.def("gemm_res_norm", &gemm_res_norm_t, py::arg("A"), py::arg("W"), py::arg("residual"), py::arg("norm_w"),
         py::arg("eps"), py::arg("plus_one"), py::arg("bias") = py::none());
   m.def("gemm_qkv_rope", &gemm_qkv_rope_t, py::arg("A"), py::arg("W"), py::arg("bias"), py::arg("pos"),

@@ -19,6 +19,8 @@ struct GemmShape {
   int k_splits; // split-K factor (0 or 1: none); tiles = k_splits x m_tiles x n_tiles
   int pdl;      // launched as a programmatic dependent: prefetch weights to L2, then wait for the predecessor
   int b_prefetch;  // > 0: the producer keeps L2 prefetches of B this many K-blocks ahead of its loads
+  int b_pair;      // > 0: paired B tiles (gated MLP): B rows [nb*BN/2, +BN/2) and [b_pair + nb*BN/2, +BN/2)
+                   // form tile nb; the epilogue gets each output chunk's two halves together
 };
 
 enum GemmEpiKind : int {
@@ -28,6 +30,7 @@ enum GemmEpiKind : int {
   kEpiSample = 3,   // per (row, n-tile) partial (max, sumexp, best gumbel score, argmax)
   kEpiHeadGrad = 4, // C bf16 = d(loss)/d(logit) of the logprob head, recomputed from lse/entropy
   kEpiSplitK = 5,   // fp32 partial of one K split -> workspace[split][M][N] (then splitk_finish)
+  kEpiSwiGLU = 6,   // C bf16 [M, N] = silu(gate) * up from paired B tiles (b_pair = N)
 };
 
 struct GemmLaunch {

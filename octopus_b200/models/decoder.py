@@ -164,9 +164,16 @@ def layer_forward(x, w, cfg: ModelConfig, pos, plan, lw=None):
     a = ops.attention(qkv, plan, cfg.heads, cfg.kv_heads, cfg.head_dim)
     x = ops.linear(a, o_w, None, residual=x, lora=la[1])
     h2 = ops.rmsnorm(x, ln2, cfg.rms_eps, cfg.norm_plus_one)
-    gu = ops.linear(h2, gu_w, lora=la[2])
-    act = ops.swiglu(gu)
+    act = _mlp_act(h2, gu_w, la[2])
     return ops.linear(act, down_w, None, residual=x, lora=la[3])
+
+
+def _mlp_act(h2, gu_w, lora):
+    """swiglu(h2 gu_w^T): without autograd (checkpointed forwards) one GEMM with the
+    activation in its epilogue; with autograd the projection is kept for the backward."""
+    if lora is None and not torch.is_grad_enabled():
+        return ops.gemm_swiglu(h2, gu_w)
+    return ops.swiglu(ops.linear(h2, gu_w, lora=lora))
 
 
 def _mlp_part(x, a, w, cfg, lw):
@@ -176,7 +183,7 @@ def _mlp_part(x, a, w, cfg, lw):
     la = lw if lw is not None else (None, None, None, None)
     x = ops.linear(a, o_w, None, residual=x, lora=la[1])
     h2 = ops.rmsnorm(x, ln2, cfg.rms_eps, cfg.norm_plus_one)
-    act = ops.swiglu(ops.linear(h2, gu_w, lora=la[2]))
+    act = _mlp_act(h2, gu_w, la[2])
     return ops.linear(act, down_w, None, residual=x, lora=la[3])
 
 

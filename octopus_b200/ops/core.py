@@ -267,6 +267,26 @@ def swiglu(gu):
     return _SwiGLU.apply(gu)
 
 
+def gemm_swiglu_ok(x, gu_w) -> bool:
+    """Whether gemm_swiglu runs as one fused GEMM for these operands."""
+    return (_is_cuda(x) and x.dim() == 2 and gu_w.shape[0] % 256 == 0 and x.shape[0] % 8 == 0
+            and x.shape[1] % 8 == 0 and x.stride(1) == 1 and gu_w.stride(1) == 1)
+
+
+def gemm_swiglu(x, gu_w):
+    """swiglu(x gu_w^T) with gu_w = [W_gate; W_up] ([2F, K]), forward only (no autograd).
+
+    On CUDA (F a multiple of 128) one tcgen05 GEMM pairs each 128-row gate tile with its
+    up tile and applies silu(gate) * up in the epilogue: the [M, 2F] projection is never
+    written.  The result equals the unfused GEMM + swiglu (gate and up rounded to bf16
+    before the activation).  Otherwise: the GEMM, then swiglu."""
+    if gemm_swiglu_ok(x, gu_w):
+        return ext().gemm_swiglu(x, gu_w)
+    if _is_cuda(x):
+        return ext().swiglu_fwd(gemm(x, gu_w))
+    return ref.swiglu(ref.linear(x, gu_w, None, None).to(x.dtype)).to(x.dtype)
+
+
 # ---------------------------------------------------------------------------- embedding
 class _Embed(torch.autograd.Function):
     # `anchor` (an empty tensor that requires grad) records the op in the graph when the

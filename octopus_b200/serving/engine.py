@@ -431,8 +431,7 @@ class Engine:
         o = attn(qkv[:, : cfg.q_width], i)
         x = ops.gemm(o, o_w, residual=x).to(x.dtype)
         h2 = sv.rms(x, ln2, cfg.rms_eps, cfg.norm_plus_one)
-        gu = ops.gemm(h2, gu_w).to(x.dtype)
-        act = sv.swiglu(gu)
+        act = ops.gemm_swiglu(h2, gu_w)
         return ops.gemm(act, down_w, residual=x).to(x.dtype)
 
     def _layer_decode(self, x, h, i, pos, slots, attn):
@@ -446,7 +445,7 @@ class Engine:
                            self.kc[i], self.vc[i])
         o = attn(q, i)
         x, h2 = sv.gemm_res_norm(o, o_w, x, ln2, cfg.rms_eps, cfg.norm_plus_one)
-        act = sv.swiglu(ops.gemm(h2, gu_w).to(x.dtype))
+        act = ops.gemm_swiglu(h2, gu_w)  # gate / up GEMM with the activation in its epilogue
         return sv.gemm_res_norm(act, down_w, x, nxt, cfg.rms_eps, cfg.norm_plus_one)
 
     def _final(self, x):

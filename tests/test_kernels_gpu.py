@@ -218,6 +218,27 @@ def test_empty_rows_head_and_gemm():
     ops.check_status(0)
 
 
+@pytest.mark.parametrize("M,F,K", [(8, 512, 256), (40, 1024, 512), (200, 1024, 512), (256, 18944, 3584),
+                                   (1000, 1536, 768)])
+def test_gemm_swiglu_matches_gemm_then_swiglu(M, F, K):
+    """The gate / up GEMM with SwiGLU in its epilogue (paired 128-row gate and up tiles,
+    decode-sized and large M) against the GEMM followed by the swiglu kernel, and against
+    an fp32 reference."""
+    torch.manual_seed(11)
+    x = torch.randn(M, K, device=dev).bfloat16()
+    W = (torch.randn(2 * F, K, device=dev) * K ** -0.5).bfloat16()
+    fused = ops.gemm_swiglu(x, W)
+    unfused = ops.swiglu(ops.gemm(x, W))
+    torch.cuda.synchronize()
+    ops.check_status(0)
+    assert fused.shape == (M, F)
+    assert (fused.float() - unfused.float()).abs().max().item() <= 1e-2 * unfused.float().abs().max().item()
+    gu = x.float() @ W.float().t()
+    g, u = gu[:, :F], gu[:, F:]
+    want = g * torch.sigmoid(g) * u
+    assert rel_err(fused, want) < 1e-2
+
+
 def test_sampling_distribution():
     torch.manual_seed(9)
     H, V = 64, 256
