@@ -79,6 +79,11 @@ void gemm_launch(const GemmLaunch& g) {
     EpiSwiGLU e{reinterpret_cast<__nv_bfloat16*>(g.C), g.ldc};
     if (g.mt == 2) launch_one<256, false, false, EpiSwiGLU, 2>(g, e);
     else launch_one<256, false, false>(g, e);
+  } else if (g.epi == kEpiQKVRope) {
+    EpiQKVRope e{reinterpret_cast<__nv_bfloat16*>(g.C), g.ldc, reinterpret_cast<const __nv_bfloat16*>(g.bias), g.pos,
+                 g.rope_log2_theta, g.rope_heads, g.bn};
+    if (g.bn == 128) launch_one<128, false, false>(g, e);
+    else launch_one<64, false, false>(g, e);
   } else if (g.epi == kEpiSample) {
     EpiSample e{g.partial, g.s.n_tiles, g.bn, g.alpha, g.vocab_limit, g.seed, g.row_offset, g.col_base};
     if (g.bn == 256) launch_one<256, false, false>(g, e);

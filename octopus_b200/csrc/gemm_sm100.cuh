@@ -539,6 +539,74 @@ struct EpiSwiGLU {
   __device__ __forceinline__ void finish() const {}
 };
 
+// QKV projection with the rotary embedding (training forward): tile nb is head nb (BN = head
+// dim D), so the paired halves of a chunk are the rotary pairs (i, i + D/2) of one head.
+// C (bf16, row stride ldc) = acc + bias, rounded to bf16, then rotated by pos[row] on the
+// q and k heads in fp32 and rounded again - the unfused GEMM (bf16 output) + rope_kernel.
+struct EpiQKVRope {
+  static constexpr bool kPaired = true;
+  __nv_bfloat16* C;
+  int ldc;
+  const __nv_bfloat16* bias;
+  const int32_t* pos;
+  float log2_theta;
+  int rot_heads;
+  int D;
+  __device__ __forceinline__ void apply_pair(int row, int col0, int, float (&lo)[32], float (&hi)[32]) {
+    const int half = D >> 1;
+    const int h = col0 / half;          // head (= tile)
+    const int i0 = col0 - h * half;     // rotary index of lo[0]
+    const int clo = h * D + i0, chi = clo + half;
+    if (bias != nullptr) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float bl[8], bh[8];
+        load8(bias + clo + q * 8, bl);
+        load8(bias + chi + q * 8, bh);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          lo[q * 8 + i] += bl[i];
+          hi[q * 8 + i] += bh[i];
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      lo[i] = __bfloat162float(__float2bfloat16(lo[i]));
+      hi[i] = __bfloat162float(__float2bfloat16(hi[i]));
+    }
+    if (h < rot_heads) {
+      const int p = pos[row];
+#pragma unroll 4
+      for (int i = 0; i < 32; ++i) {
+        float sn, cs;
+        rope_sincos(p, i0 + i, D, log2_theta, sn, cs);
+        const float a = lo[i], b = hi[i];
+        lo[i] = a * cs - b * sn;
+        hi[i] = b * cs + a * sn;
+      }
+    }
+    __nv_bfloat16* dl = C + static_cast<size_t>(row) * ldc + clo;
+    __nv_bfloat16* dh = C + static_cast<size_t>(row) * ldc + chi;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float tl[8], th[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        tl[i] = lo[q * 8 + i];
+        th[i] = hi[q * 8 + i];
+      }
+      store8(dl + q * 8, tl);
+      store8(dh + q * 8, th);
+    }
+  }
+  __device__ __forceinline__ void apply(int, int, int, float (&)[32], int) {}
+  __device__ __forceinline__ void begin_split(int) {}
+  __device__ __forceinline__ void begin_tile() {}
+  __device__ __forceinline__ void end_tile(int, int) {}
+  __device__ __forceinline__ void finish() const {}
+};
+
 // fp32 partial of K split `ks` -> ws[ks][row][col] (row stride N); a finish kernel sums the splits
 struct EpiSplitK {
   float* ws;

@@ -314,6 +314,37 @@ torch::Tensor gemm_swiglu_t(torch::Tensor A, torch::Tensor W) {
   return out;
 }
 
+// Training QKV projection with the rotary embedding in the GEMM epilogue:
+//   out = rope(A W^T + bias) on the Hq + Hkv q / k heads (v heads unrotated), head dim 64 or 128.
+// One N tile per head, so each epilogue thread holds both rotary halves of its row's head.
+torch::Tensor gemm_rope_t(torch::Tensor A, torch::Tensor W, c10::optional<torch::Tensor> bias, torch::Tensor pos,
+                          double theta, int64_t Hq, int64_t Hkv, int64_t D) {
+  c10::cuda::CUDAGuard guard(A.get_device());
+  TORCH_CHECK(D == 64 || D == 128, "gemm_rope: head_dim 64 or 128");
+  GemmLaunch g = make_launch(A, false, W, false, static_cast<int>(D));
+  const int M = g.s.M, N = g.s.N;
+  TORCH_CHECK(N == (Hq + 2 * Hkv) * D, "gemm_rope: W rows must be (Hq + 2 Hkv) * D");
+  CHECK_I32(pos);
+  CHECK_CONTIG(pos);
+  TORCH_CHECK(pos.numel() >= M, "gemm_rope: one position per row");
+  auto out = torch::empty({M, N}, A.options());
+  if (M == 0) return out;
+  if (bias.has_value() && bias->defined()) {
+    CHECK_BF16(*bias);
+    TORCH_CHECK(bias->is_contiguous() && bias->numel() == N, "gemm_rope: bias must have N elements");
+    g.bias = bias->data_ptr();
+  }
+  g.epi = kEpiQKVRope;
+  g.C = out.data_ptr();
+  g.ldc = N;
+  g.pos = pos.data_ptr<int32_t>();
+  g.rope_log2_theta = log2f(static_cast<float>(theta));
+  g.rope_heads = static_cast<int>(Hq + Hkv);
+  gemm_launch(g);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
 std::vector<torch::Tensor> gemm_res_norm_t(torch::Tensor A, torch::Tensor W, torch::Tensor residual,
                                            torch::Tensor norm_w, double eps, bool plus_one,
                                            c10::optional<torch::Tensor> bias) {
@@ -846,6 +877,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd", &embed_bwd_t);
   m.def("kv_write", &kv_write_t);
   m.def("gemm_swiglu", &gemm_swiglu_t);
+  m.def("gemm_rope", &gemm_rope_t, py::arg("A"), py::arg("W"), py::arg("bias"), py::arg("pos"), py::arg("theta"),
+        py::arg("Hq"), py::arg("Hkv"), py::arg("D"));
   m.def("gemm_res_norm", &gemm_res_norm_t, py::arg("A"), py::arg("W"), py::arg("residual"), py::arg("norm_w"),
         py::arg("eps"), py::arg("plus_one"), py::arg("bias") = py::none());
   m.def("gemm_qkv_rope", &gemm_qkv_rope_t, py::arg("A"), py::arg("W"), py::arg("bias"), py::arg("pos"),

@@ -31,6 +31,7 @@ enum GemmEpiKind : int {
   kEpiHeadGrad = 4, // C bf16 = d(loss)/d(logit) of the logprob head, recomputed from lse/entropy
   kEpiSplitK = 5,   // fp32 partial of one K split -> workspace[split][M][N] (then splitk_finish)
   kEpiSwiGLU = 6,   // C bf16 [M, N] = silu(gate) * up from paired B tiles (b_pair = N)
+  kEpiQKVRope = 7,  // C bf16 = acc + bias with the rotary embedding on the q / k heads (BN = head dim)
 };
 
 struct GemmLaunch {
@@ -58,6 +59,9 @@ struct GemmLaunch {
   const float* ent;        // head grad: per-row entropy
   const float* g_lp;       // head grad: d loss / d logp per row
   const float* g_ent;      // head grad: d loss / d entropy per row
+  const int32_t* pos;      // rope epilogue: per-row position
+  float rope_log2_theta;   // rope epilogue: log2(rope theta)
+  int rope_heads;          // rope epilogue: rotated heads (q + k); later heads are stored unrotated
   int* status;
   int grid;
   cudaStream_t stream;

@@ -153,14 +153,22 @@ class TreeBatch:
     pair_labels: torch.Tensor  # [M] int64 label of each pair
 
 
+def qkv_rope(h, qkv_w, qkv_b, pos, cfg: ModelConfig, lora=None):
+    """The fused q / k / v projection with the rotary embedding on q and k: one GEMM with
+    the rotation in its epilogue, or (LoRA adapters) the projection, then rope_."""
+    if lora is None:
+        return ops.linear_rope(h, qkv_w, qkv_b, pos, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.rope_theta)
+    qkv = ops.linear(h, qkv_w, qkv_b, lora=lora)
+    return ops.rope_(qkv, pos, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.rope_theta)
+
+
 def layer_forward(x, w, cfg: ModelConfig, pos, plan, lw=None):
     """One decoder layer; lw: the layer's LoRA adapters (qkv, o, gu, down), each
     (A, B, scale) or None."""
     ln1, qkv_w, qkv_b, o_w, ln2, gu_w, down_w = w
     la = lw if lw is not None else (None, None, None, None)
     h = ops.rmsnorm(x, ln1, cfg.rms_eps, cfg.norm_plus_one)
-    qkv = ops.linear(h, qkv_w, qkv_b, lora=la[0])
-    qkv = ops.rope_(qkv, pos, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.rope_theta)
+    qkv = qkv_rope(h, qkv_w, qkv_b, pos, cfg, la[0])
     a = ops.attention(qkv, plan, cfg.heads, cfg.kv_heads, cfg.head_dim)
     x = ops.linear(a, o_w, None, residual=x, lora=la[1])
     h2 = ops.rmsnorm(x, ln2, cfg.rms_eps, cfg.norm_plus_one)
@@ -216,8 +224,7 @@ def layer_forward_tiled(x, w, cfg: ModelConfig, pos, plan, lw=None, tile: int = 
     ln1, qkv_w, qkv_b = w[0], w[1], w[2]
     la = lw if lw is not None else (None, None, None, None)
     h = ops.rmsnorm(x, ln1, cfg.rms_eps, cfg.norm_plus_one)
-    qkv = ops.linear(h, qkv_w, qkv_b, lora=la[0])
-    qkv = ops.rope_(qkv, pos, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.rope_theta)
+    qkv = qkv_rope(h, qkv_w, qkv_b, pos, cfg, la[0])
     a = ops.attention(qkv, plan, cfg.heads, cfg.kv_heads, cfg.head_dim)
     T = x.shape[0]
     tile = max(8, tile // 8 * 8)

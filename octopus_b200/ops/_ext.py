@@ -28,7 +28,7 @@ def _load():
 KERNELS_PER_CALL = {
     "gemm_out": 1, "head_fwd": 2, "head_grad_logits": 1, "sample_head": 2, "rmsnorm_fwd": 1, "rmsnorm_bwd": 1,
     "rope": 1, "swiglu_fwd": 1, "swiglu_bwd": 1, "embed_fwd": 1, "embed_bwd": 1, "kv_write": 1,
-    "sqnorm_accum": 1, "adamw": 1, "attn_fwd": 1, "attn_bwd": 3, "attn_decode": 2, "gemm_swiglu": 1, "attn_decode_persistent": 2,
+    "sqnorm_accum": 1, "adamw": 1, "attn_fwd": 1, "attn_bwd": 3, "attn_decode": 2, "gemm_swiglu": 1, "gemm_rope": 1, "attn_decode_persistent": 2,
     "attn_decode_shared": 2, "recur_fwd": 1, "recur_bwd": 1, "conv_fwd": 1, "conv_bwd": 1,
     "rs_sum_sq": 1, "adamw_bcast": 1, "bcast_bf16": 1, "peer_barrier": 1, "peer_gather_bf16": 1, "peer_rs_acc": 1,
 }

@@ -106,24 +106,31 @@ class _Linear(torch.autograd.Function):
         x, w = ctx.saved_tensors
         dy = dy.contiguous()
         dres = dy if ctx.has_res else None
-        db = None
-        if ctx.bias is not None:
-            db = _accum_wgrad(ctx.bias, dy.float().sum(0) if dy.dtype != torch.float64 else dy.sum(0))
-        mg = getattr(w, "main_grad", None)
-        frozen = mg is None and not ctx.needs_input_grad[1]  # (LoRA base weights: no weight gradient)
-        if _is_cuda(x):
-            dx = gemm(dy, w, b_mn=True)  # dy [M,N] @ w [N,K]
-            if frozen:
-                dw = None
-            elif mg is not None:
-                gemm(dy, x, a_mn=True, b_mn=True, out=mg, accumulate=True)
-                dw = None
-            else:
-                dw = gemm(dy, x, a_mn=True, b_mn=True, out_dtype=torch.float32).to(w.dtype)
-        else:
-            dx = (ref._f(dy) @ ref._f(w)).to(x.dtype)
-            dw = None if frozen else _accum_wgrad(w, ref._f(dy).t() @ ref._f(x))
+        dx, dw, db = _linear_grads(x, w, ctx.bias, dy, ctx.needs_input_grad[1])
         return dx, dw, db, dres
+
+
+def _linear_grads(x, w, bias, dy, w_needs_grad):
+    """(dx, dw, db) of y = x W^T + b: the weight gradient accumulates into W.main_grad (fp32)
+    when W has one (then dw is None), the bias gradient likewise."""
+    db = None
+    if bias is not None:
+        db = _accum_wgrad(bias, dy.float().sum(0) if dy.dtype != torch.float64 else dy.sum(0))
+    mg = getattr(w, "main_grad", None)
+    frozen = mg is None and not w_needs_grad  # (LoRA base weights: no weight gradient)
+    if _is_cuda(x):
+        dx = gemm(dy, w, b_mn=True)  # dy [M,N] @ w [N,K]
+        if frozen:
+            dw = None
+        elif mg is not None:
+            gemm(dy, x, a_mn=True, b_mn=True, out=mg, accumulate=True)
+            dw = None
+        else:
+            dw = gemm(dy, x, a_mn=True, b_mn=True, out_dtype=torch.float32).to(w.dtype)
+    else:
+        dx = (ref._f(dy) @ ref._f(w)).to(x.dtype)
+        dw = None if frozen else _accum_wgrad(w, ref._f(dy).t() @ ref._f(x))
+    return dx, dw, db
 
 
 def linear(x, w, b=None, residual=None, lora=None):
@@ -240,6 +247,36 @@ def _rope_inplace(qkv, pos, Hq, Hkv, D, theta, inverse):
 
 def rope_(qkv, pos, Hq, Hkv, D, theta):
     return _Rope.apply(qkv, pos, Hq, Hkv, D, theta)
+
+
+class _LinearRope(torch.autograd.Function):
+    """qkv = rope(x W^T + b) in one tcgen05 GEMM (the rotary embedding in its epilogue);
+    backward: the inverse rotation of the gradient, then the linear layer's gradients."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, pos, Hq, Hkv, D, theta):
+        ctx.meta = (Hq, Hkv, D, theta)
+        ctx.bias = b
+        ctx.save_for_backward(x, w, pos)
+        return ext().gemm_rope(x, w, b, pos, theta, Hq, Hkv, D)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, pos = ctx.saved_tensors
+        Hq, Hkv, D, theta = ctx.meta
+        g = dy.contiguous().clone()
+        _rope_inplace(g, pos, Hq, Hkv, D, theta, inverse=True)
+        dx, dw, db = _linear_grads(x, w, ctx.bias, g, ctx.needs_input_grad[1])
+        return dx, dw, db, None, None, None, None, None
+
+
+def linear_rope(x, w, b, pos, Hq, Hkv, D, theta):
+    """rope(x W^T + b) on the q / k heads of the fused qkv projection: one GEMM with the
+    rotation in its epilogue on CUDA (head_dim 64 / 128), else linear then rope_."""
+    if (_is_cuda(x) and D in (64, 128) and x.shape[0] % 8 == 0 and x.shape[1] % 8 == 0 and x.stride(1) == 1
+            and w.stride(1) == 1 and pos.dtype == torch.int32):
+        return _LinearRope.apply(x, w, b, pos.contiguous(), Hq, Hkv, D, theta)
+    return rope_(linear(x, w, b), pos, Hq, Hkv, D, theta)
 
 
 # ---------------------------------------------------------------------------- SwiGLU

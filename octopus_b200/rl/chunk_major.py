@@ -40,6 +40,7 @@ import numpy as np
 import torch
 
 from .. import ops
+from ..models.decoder import qkv_rope
 
 
 @dataclass
@@ -349,8 +350,7 @@ def _chunk_layer(x, k_ext, v_ext, w, cfg, pos, plan, own, lw):
     la = lw if lw is not None else (None, None, None, None)
     Hq, Hkv, D = cfg.heads, cfg.kv_heads, cfg.head_dim
     h = ops.rmsnorm(x, ln1, cfg.rms_eps, cfg.norm_plus_one)
-    qkv = ops.linear(h, qkv_w, qkv_b, lora=la[0])
-    qkv = ops.rope_(qkv, pos, Hq, Hkv, D, cfg.rope_theta)
+    qkv = qkv_rope(h, qkv_w, qkv_b, pos, cfg, la[0])
     q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
     if k_ext is not None:
         ka, va = torch.cat([k, k_ext]), torch.cat([v, v_ext])

@@ -239,6 +239,33 @@ def test_gemm_swiglu_matches_gemm_then_swiglu(M, F, K):
     assert rel_err(fused, want) < 1e-2
 
 
+@pytest.mark.parametrize("M,Hq,Hkv,D,bias", [(64, 4, 2, 64, True), (1000, 28, 4, 128, True), (264, 8, 8, 128, False)])
+def test_linear_rope_matches_linear_then_rope(M, Hq, Hkv, D, bias):
+    """The qkv projection with the rotary embedding in its epilogue: forward equals the GEMM
+    followed by the rope kernel; gradients of x, W and the bias match the unfused ops."""
+    torch.manual_seed(12)
+    K, N = 256, (Hq + 2 * Hkv) * D
+    x = torch.randn(M, K, device=dev).bfloat16().requires_grad_(True)
+    W = (torch.randn(N, K, device=dev) * K ** -0.5).bfloat16().requires_grad_(True)
+    b = (torch.randn(N, device=dev) * 0.1).bfloat16().requires_grad_(True) if bias else None
+    pos = torch.randint(0, 4000, (M,), device=dev, dtype=torch.int32)
+    y = ops.linear_rope(x, W, b, pos, Hq, Hkv, D, 1e6)
+    x2 = x.detach().clone().requires_grad_(True)
+    W2 = W.detach().clone().requires_grad_(True)
+    b2 = b.detach().clone().requires_grad_(True) if bias else None
+    y2 = ops.rope_(ops.linear(x2, W2, b2), pos, Hq, Hkv, D, 1e6)
+    assert (y.float() - y2.float()).abs().max().item() <= 1e-2 * y2.float().abs().max().item()
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    y2.backward(gy)
+    torch.cuda.synchronize()
+    ops.check_status(0)
+    assert rel_err(x.grad, x2.grad) < 1e-2
+    assert rel_err(W.grad, W2.grad) < 1e-2
+    if bias:
+        assert rel_err(b.grad, b2.grad) < 1e-2
+
+
 def test_sampling_distribution():
     torch.manual_seed(9)
     H, V = 64, 256
