@@ -33,25 +33,29 @@ namespace octo_native {
 
 class SlotPool {
  public:
-  explicit SlotPool(int64_t capacity) : cap_(capacity), ref_(capacity, 0) {
-    free_.reserve(capacity);
-    for (int64_t s = capacity - 1; s >= 0; --s) free_.push_back(s);
+  // Free slots are kept as coalesced runs [start, start + len) ordered by address, and
+  // alloc(n) takes the lowest-addressed run that holds all n (else the lowest runs in
+  // turn), so a request's slots come out ascending and, while the pool is not fragmented,
+  // consecutive: the decode kernels then stream a sequence's keys with tiled TMA copies.
+  explicit SlotPool(int64_t capacity) : cap_(capacity), ref_(capacity, 0), free_n_(capacity) {
+    if (capacity > 0) runs_.emplace(0, capacity);
   }
   int64_t capacity() const { return cap_; }
-  int64_t free_count() const { return static_cast<int64_t>(free_.size()); }
-  int64_t used_count() const { return cap_ - free_count(); }
+  int64_t free_count() const { return free_n_; }
+  int64_t used_count() const { return cap_ - free_n_; }
 
   // Allocate n slots with refcount 1; returns an empty vector if not enough are free.
   std::vector<int64_t> alloc(int64_t n) {
     std::vector<int64_t> out;
-    if (n <= 0) return out;
-    if (n > free_count()) return out;
-    out.resize(n);
-    for (int64_t i = 0; i < n; ++i) {
-      const int64_t s = free_.back();
-      free_.pop_back();
-      ref_[s] = 1;
-      out[i] = s;
+    if (n <= 0 || n > free_n_) return out;
+    out.reserve(n);
+    auto it = runs_.begin();
+    for (; it != runs_.end(); ++it)
+      if (it->second >= n) break;
+    if (it != runs_.end()) {
+      take(it, n, out);
+    } else {
+      while (static_cast<int64_t>(out.size()) < n) take(runs_.begin(), n - static_cast<int64_t>(out.size()), out);
     }
     return out;
   }
@@ -64,28 +68,40 @@ class SlotPool {
   }
   // Returns how many slots became free.
   int64_t decref(const int64_t* s, int64_t n) {
-    int64_t freed = 0;
+    std::vector<int64_t> freed;
     for (int64_t i = 0; i < n; ++i) {
       check(s[i]);
       if (ref_[s[i]] <= 0) throw std::runtime_error("double free of slot " + std::to_string(s[i]));
-      if (--ref_[s[i]] == 0) {
-        free_.push_back(s[i]);
-        ++freed;
-      }
+      if (--ref_[s[i]] == 0) freed.push_back(s[i]);
     }
-    return freed;
+    std::sort(freed.begin(), freed.end());
+    for (size_t i = 0; i < freed.size();) {  // consecutive freed slots go back as one run
+      size_t j = i + 1;
+      while (j < freed.size() && freed[j] == freed[j - 1] + 1) ++j;
+      give(freed[i], static_cast<int64_t>(j - i));
+      i = j;
+    }
+    return static_cast<int64_t>(freed.size());
   }
   int32_t refcount(int64_t s) const {
     check(s);
     return ref_[s];
   }
-  // Invariant check: every slot is either free (ref 0, on the free list once) or held.
+  // Invariant check: every slot is either free (ref 0, in exactly one run) or held, and
+  // runs are disjoint, non-adjacent and counted.
   bool check_invariants() const {
     std::vector<uint8_t> seen(cap_, 0);
-    for (int64_t s : free_) {
-      if (s < 0 || s >= cap_ || seen[s] || ref_[s] != 0) return false;
-      seen[s] = 1;
+    int64_t total = 0, prev_end = -1;
+    for (const auto& r : runs_) {
+      if (r.second <= 0 || r.first < 0 || r.first + r.second > cap_ || r.first <= prev_end) return false;
+      for (int64_t s = r.first; s < r.first + r.second; ++s) {
+        if (seen[s] || ref_[s] != 0) return false;
+        seen[s] = 1;
+      }
+      prev_end = r.first + r.second;
+      total += r.second;
     }
+    if (total != free_n_) return false;
     for (int64_t s = 0; s < cap_; ++s)
       if (!seen[s] && ref_[s] <= 0) return false;
     return true;
@@ -95,9 +111,41 @@ class SlotPool {
   void check(int64_t s) const {
     if (s < 0 || s >= cap_) throw std::out_of_range("slot id out of range " + std::to_string(s));
   }
+  // up to `want` slots from the front of run `it`
+  void take(std::map<int64_t, int64_t>::iterator it, int64_t want, std::vector<int64_t>& out) {
+    const int64_t start = it->first, len = it->second;
+    const int64_t k = std::min(want, len);
+    for (int64_t s = start; s < start + k; ++s) {
+      ref_[s] = 1;
+      out.push_back(s);
+    }
+    runs_.erase(it);
+    if (k < len) runs_.emplace(start + k, len - k);
+    free_n_ -= k;
+  }
+  // return [start, start + len) to the free runs, merging with its neighbours
+  void give(int64_t start, int64_t len) {
+    free_n_ += len;
+    auto next = runs_.lower_bound(start);
+    if (next != runs_.begin()) {
+      auto prev = std::prev(next);
+      if (prev->first + prev->second == start) {
+        start = prev->first;
+        len += prev->second;
+        runs_.erase(prev);
+      }
+    }
+    next = runs_.lower_bound(start);
+    if (next != runs_.end() && next->first == start + len) {
+      len += next->second;
+      runs_.erase(next);
+    }
+    runs_.emplace(start, len);
+  }
   int64_t cap_;
   std::vector<int32_t> ref_;
-  std::vector<int64_t> free_;
+  std::map<int64_t, int64_t> runs_;  // free runs: start -> length
+  int64_t free_n_;
 };
 
 struct RNode {

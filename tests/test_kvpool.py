@@ -83,3 +83,29 @@ def test_zero_copy_fuzz_pool_balance():
         p.decref(s)
     r.evict(1 << 40)
     assert p.free_count() == 5000
+
+
+def test_slot_runs_come_out_ascending_and_consecutive():
+    """Freed slots coalesce into address-ordered runs; an allocation takes the lowest run
+    that holds it whole, so a request's slots are consecutive and ascending (the decode
+    kernels' tiled copies need that), and a fragmented pool still hands out ascending
+    pieces of the lowest runs."""
+    from octopus_b200._native import SlotPool
+
+    p = SlotPool(64)
+    a, b, c = p.alloc(8), p.alloc(8), p.alloc(8)
+    assert list(a) == list(range(8)) and list(c) == list(range(16, 24))
+    p.decref(np.asarray(b[::-1]))          # freed in any order: one run [8, 16)
+    p.decref(np.asarray(a))                # merges into [0, 16)
+    d = p.alloc(12)
+    assert list(d) == list(range(12))
+    e = p.alloc(10)                        # [12, 16) is too short: the run after c
+    assert list(e) == list(range(24, 34))
+    assert len(p.alloc(35)) == 0           # 34 free
+    f = p.alloc(34)                        # no single run holds it: [12, 16), then [34, 64)
+    assert list(f) == [12, 13, 14, 15] + list(range(34, 64))
+    assert p.free_count() == 0 and p.check_invariants()
+    for x in (c, d, e, f):
+        p.decref(np.asarray(x))
+    assert p.free_count() == 64 and p.check_invariants()
+    assert list(p.alloc(64)) == list(range(64))
