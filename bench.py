@@ -57,6 +57,10 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke tests only)")
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--tp", type=int, default=0, help="rollout tensor parallelism (0: 2 when N is even, else 1)")
+    ap.add_argument("--mode", default="colocated", choices=["colocated", "disagg"],
+                    help="N > 1: colocated (every GPU rolls out, then trains) or disagg (half of the GPUs roll out "
+                         "while the other half trains on the previous rollout, rl.disagg)")
+    ap.add_argument("--rollout-gpus", type=int, default=0, help="--mode disagg: rollout GPUs (0: half, rounded up)")
     ap.add_argument("--profile-step", default="",
                     help="after the timed steps, run one more step under the PyTorch CUDA trace and write rank 0's "
                          "per-kernel breakdown (JSON) here; not part of the timed value")
@@ -155,6 +159,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
     n_gpus = world
 
+    if world > 1 and args.mode == "disagg":
+        return run_disagg(args, world, rank, local, dev)
     over = {"layers": args.layers} if args.layers else {}
     grpo = args.config == "grpo1.5b"
     args.model = args.model or ("qwen2.5-1.5b" if grpo else "qwen2.5-7b")
@@ -328,6 +334,140 @@ def main():
             actor.close()
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+def run_disagg(args, world, rank, local, dev):
+    """--mode disagg: ranks [0, R) roll out (one engine replica each, TP 1), ranks [R, N) train
+    the previous iteration's rollouts (full-shard actor over the trainer ranks); rollouts and
+    weights are exchanged between iterations (octopus_b200.rl.disagg)."""
+    import torch
+    import torch.distributed as dist
+
+    from octopus_b200 import ops
+    from octopus_b200.envs.dag import DagConfig, MultiAgentDag
+    from octopus_b200.models.config import get_config
+    from octopus_b200.rl.actor import Actor
+    from octopus_b200.rl.disagg import DisaggRLTrainer, make_groups, rollout_weights, split_roles
+    from octopus_b200.serving.engine import Engine
+    from octopus_b200.utils import iostats
+
+    if args.config != "dag7b":
+        raise SystemExit("--mode disagg runs the dag7b config")
+    over = {"layers": args.layers} if args.layers else {}
+    args.model = args.model or "qwen2.5-7b"
+    cfg = get_config(args.model, **over)
+    n_roll = split_roles(world, args.rollout_gpus)
+    n_train = world - n_roll
+    train_group, push = make_groups(world, n_roll)
+    role = "rollout" if rank < n_roll else "train"
+    if role == "rollout":
+        inst = [i for i in range(args.instances) if i % n_roll == rank]
+        dcfg = DagConfig(instances=args.instances, samples=args.samples, prefix_len=args.prefix, turn_len=args.turn,
+                         role_len=args.role, seed=1000 + rank)
+        env = MultiAgentDag(cfg.vocab_size, dcfg)
+        w = rollout_weights(cfg, dev, n_train, seed=0)
+        per_inst = args.prefix + args.samples * (4 * (args.turn + args.role) + 2)
+        kv_slots = int(len(inst) * per_inst * 1.15) + 8192
+        if args.kv_gb:
+            kv_slots = int(args.kv_gb * (1 << 30) / (4 * cfg.layers * cfg.kv_width))
+        rows = len(inst) * args.samples * 2
+        engine = Engine(cfg, w, kv_slots=kv_slots, max_batch=max(8, 1 << (rows - 1).bit_length()), device=dev,
+                        use_graphs=not args.no_graphs)
+
+        class _Env:
+            def rollout(self, eng):
+                return env.rollout(eng, inst)
+
+        trainer = DisaggRLTrainer("rollout", n_rollout=n_roll, flat=w.flat, push_group=push, engine=engine,
+                                  env=_Env(), mb_tokens=args.mb_tokens)
+    else:
+        engine = None
+        if n_train > 1:
+            from octopus_b200.parallel.fsdp import FSDPActor
+
+            actor = FSDPActor(cfg, dev, seed=0, group=train_group)
+            flat = actor.serve16
+        else:
+            actor = Actor(cfg, dev, seed=0)
+            flat = actor.flat16
+        trainer = DisaggRLTrainer("train", n_rollout=n_roll, flat=flat, push_group=push, actor=actor,
+                                  mb_tokens=args.mb_tokens)
+    for _ in range(args.warmup):
+        trainer.step()
+    torch.cuda.synchronize()
+    ops.check_status(local)
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    e0 = dict(engine.stats) if engine is not None else {}
+    clocks.start()
+    iostats.reset()
+    l0 = ops.launches()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gen, wall, stats = 0, [], []
+    start.record()
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        st = trainer.step()
+        torch.cuda.synchronize()
+        wall.append(time.perf_counter() - t0)
+        gen += st["generated_tokens"]
+        stats.append(st)
+    end.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    io = iostats.snapshot()
+    launches = ops.launches() - l0
+    ms = start.elapsed_time(end)
+    ops.check_status(local)
+    s0 = stats[-1]
+    t = torch.tensor([ms, sum(wall), s0.get("rollout_s", 0.0), s0.get("train_s", 0.0), s0["sync_s"]],
+                     dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    sm = torch.tensor([float(gen), float(launches), io["h2d"], io["d2h"], float(s0.get("tree_tokens") or 0),
+                       float(s0.get("trained_tokens") or 0)], dtype=torch.float64, device=dev)
+    dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    ms, wall_s = float(t[0]), float(t[1])
+    gen = float(sm[0])
+    value, e2e = gen / (ms / 1000.0), gen / wall_s
+    if rank == 0:
+        par = (f"disaggregated, one step asynchronous: {n_roll} rollout GPUs (tp1 replicas) + {n_train} trainer GPUs "
+               f"(actor {'full-shard fused' if n_train > 1 else 'single GPU'}); rollout k overlaps training on "
+               f"rollout k-1")
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 2), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
+            "dtype": "bf16", "data": "synthetic (uniform random tokens, random-init weights, Bernoulli(0.5) rewards)",
+            "config": {"model": args.model + (f"-L{args.layers}" if args.layers else ""),
+                       "global_batch": args.instances * args.samples,
+                       "seq_len": args.prefix + 4 * (args.turn + args.role), "parallelism": par,
+                       "dag": "planner->2 solvers->verifier, prefix mounted zero-copy",
+                       "instances": args.instances, "samples": args.samples, "prefix": args.prefix,
+                       "turn": args.turn, "staleness": "each rollout trained once, one weight version behind",
+                       "tokens_counted": "generated tokens per iteration (each trained once, one iteration later)",
+                       "l2": "inputs larger than L2 (7B weights 15 GB, KV > 10 GB per step)"},
+            "clocks": clk,
+            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": int(float(sm[2]) / args.steps),
+                    "d2h_bytes_per_step": int(float(sm[3]) / args.steps),
+                    "api": "octopus_b200.rl.disagg.DisaggRLTrainer.step"},
+            "gpu_launches": int(sm[1]),
+            "phases_s": {"rollout": round(float(t[2]), 3), "train": round(float(t[3]), 3),
+                         "exchange": round(float(t[4]), 4)},
+            "engine_per_step": {k: round((engine.stats[k] - e0[k]) / args.steps, 3)
+                                for k in ("prefill_s", "decode_s", "decode_steps", "prefill_tokens", "cached_tokens")},
+            "trained_tokens_last_step": int(sm[5]), "tree_tokens_last_step": int(sm[4]),
+        }
+        print(json.dumps(out), flush=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    if role == "train" and n_train > 1:
+        actor.close()
+    dist.barrier()
+    dist.destroy_process_group()
     return 0
 
 
