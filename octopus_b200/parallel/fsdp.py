@@ -474,6 +474,14 @@ class FSDPActor(Actor):
         self._slot_unit = [-1, -1]
         self._edges_ready = False
 
+    def after_load(self):
+        """After a recover checkpoint filled the serving copy and the fp32 shards: this rank's
+        bf16 weight shards from the serving copy."""
+        for u in range(len(self.us.units)):
+            self.shard16[self.us.local(u)].copy_(self.serve16[self.us.owned(u)])
+        self._slot_unit = [-1, -1]
+        self._edges_ready = False
+
     def reload_master(self):
         """After a checkpoint load into the serving copy: shards <- it, master <- shards."""
         for u in range(len(self.us.units)):

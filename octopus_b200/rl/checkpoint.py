@@ -43,10 +43,12 @@ def _dist():
     return dist if dist.is_available() and dist.is_initialized() else None
 
 
-def save(actor, root: str, step: int, dataloader_state: dict | None = None, spool=None) -> str:
+def save(actor, root: str, step: int, dataloader_state: dict | None = None, spool=None, group=None) -> str:
+    """Write a recover checkpoint; `group`: the process group that holds the actor (default:
+    every rank), whose first rank writes the weights and the state."""
     dist = _dist()
-    rank = dist.get_rank() if dist else 0
-    world = dist.get_world_size() if dist else 1
+    rank = dist.get_rank(group) if dist else 0
+    world = dist.get_world_size(group) if dist else 1
     tmp = os.path.join(root, "recover.tmp")
     final = os.path.join(root, "recover")
     if rank == 0:
@@ -54,14 +56,14 @@ def save(actor, root: str, step: int, dataloader_state: dict | None = None, spoo
         os.makedirs(tmp, exist_ok=True)
         save_hf(actor.weights, os.path.join(tmp, "weights"))
     if dist:
-        dist.barrier()
+        dist.barrier(group)
     opt = {"master": actor.master.cpu(), "exp_avg": actor.exp_avg.cpu(), "exp_avg_sq": actor.exp_avg_sq.cpu(),
            "step_count": actor.step_count, "layout": _layout_hash(actor)}
     if hasattr(actor, "extra_state"):  # parameters and optimizer state outside the flat layout (hybrid layers)
         opt["extra"] = actor.extra_state()
     torch.save(opt, os.path.join(tmp, f"optim-rank{rank}.pt"))
     if dist:
-        dist.barrier()
+        dist.barrier(group)
     if rank == 0:
         state = {"step": step, "version": actor.version, "world": world,
                  "rng": {"python": repr(random.getstate()), "numpy": np.random.get_state()[1].tolist()[:8],
@@ -78,14 +80,14 @@ def save(actor, root: str, step: int, dataloader_state: dict | None = None, spoo
         if spool is not None:
             spool.commit()
     if dist:
-        dist.barrier()
+        dist.barrier(group)
     return final
 
 
-def load(actor, root: str) -> dict:
+def load(actor, root: str, group=None) -> dict:
     dist = _dist()
-    rank = dist.get_rank() if dist else 0
-    world = dist.get_world_size() if dist else 1
+    rank = dist.get_rank(group) if dist else 0
+    world = dist.get_world_size(group) if dist else 1
     d = os.path.join(root, "recover")
     with open(os.path.join(d, "state.json")) as f:
         state = json.load(f)
@@ -102,6 +104,8 @@ def load(actor, root: str) -> dict:
         actor.load_extra_state(opt["extra"])
     actor.step_count = int(opt["step_count"])
     actor.version = int(state["version"])
+    if hasattr(actor, "after_load"):  # derived buffers (e.g. full-shard bf16 weight shards)
+        actor.after_load()
     return state
 
 

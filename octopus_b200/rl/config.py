@@ -88,6 +88,8 @@ class RLSection:
     episodes_per_server: int = 8
     dag_prefix: int = 2048      # kind=dag: the shared task prefix every agent mounts
     dag_turn: int = 512         # kind=dag: tokens per agent turn
+    disaggregate: bool = False  # > 1 GPU: rollout GPUs and trainer GPUs run one step apart (rl.disagg)
+    rollout_gpus: int = 0       # disaggregate: rollout GPUs (0: half, rounded up)
 
 
 @dataclass

@@ -40,7 +40,7 @@ class DisaggRLTrainer:
     first trainer rank and every rollout rank (the weight broadcast)."""
 
     def __init__(self, role: str, *, n_rollout: int, flat: torch.Tensor, push_group, engine=None, env=None,
-                 actor=None, mb_tokens: int = 32768):
+                 actor=None, mb_tokens: int = 32768, report: bool = False):
         assert role in ("rollout", "train")
         self.role = role
         self.rank, self.world = dist.get_rank(), dist.get_world_size()
@@ -50,6 +50,7 @@ class DisaggRLTrainer:
         self.flat, self.push_group = flat, push_group
         self.engine, self.env, self.actor = engine, env, actor
         self.mb_tokens = mb_tokens
+        self.report = report
         self.pending = []    # trainer: rollouts received, not trained yet
         self.steps = 0
         self.version = 0     # weight version this rank holds
@@ -75,11 +76,15 @@ class DisaggRLTrainer:
                 box = [None]
                 dist.recv_object_list(box, src=src)
                 self.pending.append(box[0])
+        self.push_weights()
+        self.version = self.steps
+
+    def push_weights(self):
+        """The first trainer rank's bf16 weights -> every rollout rank (each of these ranks calls it)."""
         if self.role == "rollout" or self.rank == self.n_rollout:
             dist.broadcast(self.flat, src=self.n_rollout, group=self.push_group)
         if self.role == "rollout":
             self.engine.bump_version()  # cached prefixes of the old weights are not reused
-        self.version = self.steps
 
     # ------------------------------------------------------------------ one iteration
     def step(self) -> dict:
@@ -109,6 +114,15 @@ class DisaggRLTrainer:
         self.steps += 1
         t2 = time.perf_counter()
         out.update(sync_s=t2 - t1, step_s=t2 - t0, version=self.version)
+        if self.report:  # the first trainer rank's numbers travel to rank 0 (the run's log)
+            if self.rank == self.n_rollout:
+                dist.send_object_list([out], dst=0)
+            elif self.rank == 0:
+                box = [None]
+                dist.recv_object_list(box, src=self.n_rollout)
+                own = ("trained_tokens", "loss", "tree_tokens", "flat_tokens", "micro_batches", "train_s")
+                out.update({k if k in own else f"train_{k}": v for k, v in box[0].items()
+                            if k not in ("role", "generated_tokens")})
         return out
 
 

@@ -38,12 +38,82 @@ def _dist_init(device):
     return world
 
 
+def build_disagg(cfg, device, world: int, rank: int):
+    """(trainer, actor or None, engine or None, spool, trainer group) of a disaggregated run (dense model,
+    rollout TP 1, no LoRA): rollout ranks get an engine over their own weight copy and their
+    share of the environment, trainer ranks the actor (full-shard over the trainer ranks)."""
+    import torch
+
+    from ..models.config import get_config
+    from ..serving.engine import Engine
+    from .actor import Actor, OptimConfig
+    from .disagg import DisaggRLTrainer, make_groups, rollout_weights, split_roles
+    from .loss import PPOConfig
+    from .spool import Spool
+
+    a = cfg.actor
+    if cfg.rollout.tp > 1 or a.lora_rank > 0 or cfg.model.path:
+        raise SystemExit("rl.disaggregate: dense random-init models, rollout.tp 1, no LoRA")
+    mcfg = get_config(cfg.model.preset, **({"layers": cfg.model.layers} if cfg.model.layers else {}))
+    dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
+    n_roll = split_roles(world, cfg.rl.rollout_gpus)
+    n_train = world - n_roll
+    train_group, push = make_groups(world, n_roll)
+    spool = Spool(cfg.rl.spool) if cfg.rl.spool else None
+    if rank < n_roll:
+        w = rollout_weights(mcfg, device, n_train, dtype=dtype, seed=cfg.seed)
+        kv_slots = int(cfg.rollout.kv_gb * (1 << 30) / (4 * mcfg.layers * mcfg.kv_width))
+        engine = Engine(mcfg, w, kv_slots=kv_slots, max_batch=cfg.rollout.max_batch, device=device)
+        env = _make_env(cfg, mcfg, engine, rank, n_roll)
+        tr = DisaggRLTrainer("rollout", n_rollout=n_roll, flat=w.flat, push_group=push, engine=engine, env=env,
+                             mb_tokens=a.mb_tokens, report=True)
+        return tr, None, engine, spool, train_group
+    optim = OptimConfig(lr=a.lr, betas=(a.beta1, a.beta2), eps=a.eps, weight_decay=a.weight_decay,
+                        max_grad_norm=a.gradient_clipping)
+    ppo = PPOConfig(eps_clip=a.eps_clip, eps_clip_higher=a.eps_clip_higher, behav_imp_weight_cap=a.behav_imp_weight_cap,
+                    reuse_train_logp=a.reuse_train_logp)
+    if n_train > 1:
+        from ..parallel.fsdp import FSDPActor
+
+        actor = FSDPActor(mcfg, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype, group=train_group,
+                          fused=a.fused_collectives and device.type == "cuda")
+        flat = actor.serve16
+    else:
+        actor = Actor(mcfg, device, optim=optim, ppo=ppo, seed=cfg.seed, dtype=dtype, ckpt=a.gradient_checkpointing)
+        flat = actor.flat16
+    tr = DisaggRLTrainer("train", n_rollout=n_roll, flat=flat, push_group=push, actor=actor, mb_tokens=a.mb_tokens,
+                         report=True)
+    return tr, actor, None, spool, train_group
+
+
+def _make_env(cfg, mcfg, engine, rep: int, replicas: int):
+    """The environment of rollout replica `rep` of `replicas` (its share of the tasks)."""
+    from ..envs.dag import DagConfig, MultiAgentDag
+
+    if cfg.rl.kind == "dag":
+        inst = [i for i in range(cfg.rl.batch_size) if i % replicas == rep]
+        dag = MultiAgentDag(mcfg.vocab_size, DagConfig(instances=cfg.rl.batch_size, samples=cfg.rl.n_samples,
+                                                       prefix_len=cfg.rl.dag_prefix, turn_len=cfg.rl.dag_turn,
+                                                       temperature=cfg.rollout.temperature,
+                                                       seed=cfg.seed * 1000 + rep))
+
+        class _Env:
+            def rollout(self, eng):
+                return dag.rollout(eng, inst)
+
+        return _Env()
+    if cfg.rl.kind == "search":
+        return _search_env(cfg, engine, rep, replicas)
+    if cfg.rl.kind == "swe":
+        return _swe_env(cfg, engine, rep, replicas)
+    raise SystemExit(f"rl.kind {cfg.rl.kind!r}: dag, search or swe")
+
+
 def build(cfg, device):
     """(trainer, actor, engine, env, spool, tp_rank) for a run config."""
     import torch
     import torch.distributed as dist
 
-    from ..envs.dag import DagConfig, MultiAgentDag
     from ..models.config import get_config
     from ..models.decoder import load_hf
     from ..parallel.fsdp import ShardedActor
@@ -137,24 +207,7 @@ def build(cfg, device):
         engine = Engine(mcfg, actor.weights, kv_slots=kv_slots, max_batch=cfg.rollout.max_batch, device=device)
     replicas = world // tp
     spool = Spool(cfg.rl.spool) if cfg.rl.spool else None
-    if cfg.rl.kind == "dag":
-        inst = [i for i in range(cfg.rl.batch_size) if i % replicas == rep]
-        dag = MultiAgentDag(mcfg.vocab_size, DagConfig(instances=cfg.rl.batch_size, samples=cfg.rl.n_samples,
-                                                       prefix_len=cfg.rl.dag_prefix, turn_len=cfg.rl.dag_turn,
-                                                       temperature=cfg.rollout.temperature,
-                                                       seed=cfg.seed * 1000 + rep))
-
-        class _Env:
-            def rollout(self, eng):
-                return dag.rollout(eng, inst)
-
-        env = _Env()
-    elif cfg.rl.kind == "search":
-        env = _search_env(cfg, engine, rep, replicas)
-    elif cfg.rl.kind == "swe":
-        env = _swe_env(cfg, engine, rep, replicas)
-    else:
-        raise SystemExit(f"rl.kind {cfg.rl.kind!r}: dag, search or swe")
+    env = _make_env(cfg, mcfg, engine, rep, replicas)
     trainer = RLTrainer(actor, engine, env, TrainerConfig(mb_tokens=a.mb_tokens, mb_shard=(tp_rank, tp)),
                         sync_fn=engine.sync_weights if tp > 1 else None)
     return trainer, actor, engine, env, spool, tp_rank
@@ -301,6 +354,8 @@ def main(argv=None) -> int:
         C.save_settings(os.path.join(run_dir, "episode_settings.json"))
         with open(os.path.join(run_dir, "config.json"), "w") as f:
             json.dump(cfg.to_dict(), f, indent=1)
+    if world > 1 and cfg.rl.disaggregate:
+        return _main_disagg(cfg, device, world, rank, run_dir)
     trainer, actor, engine, env, spool, tp_rank = build(cfg, device)
     step0 = 0
     if checkpoint.exists(run_dir):
@@ -342,6 +397,52 @@ def main(argv=None) -> int:
         if hasattr(actor, "close"):
             actor.close()
         dist.destroy_process_group()
+    return 0
+
+
+def _main_disagg(cfg, device, world: int, rank: int, run_dir: str) -> int:
+    """Training loop of a disaggregated run: every rank steps the loop; trainer ranks keep the
+    recover checkpoints, the first trainer rank writes HF weights, rank 0 the step log (its
+    rollout numbers plus the first trainer rank's, prefixed train_ where both have a key)."""
+    import torch
+    import torch.distributed as dist
+
+    from . import checkpoint
+    from ..models.decoder import save_hf
+
+    trainer, actor, engine, spool, group = build_disagg(cfg, device, world, rank)
+    n_roll = trainer.n_rollout
+    step0 = 0
+    if actor is not None and checkpoint.exists(run_dir):
+        step0 = int(checkpoint.load(actor, run_dir, group=group)["step"])
+    s = torch.tensor([step0], dtype=torch.int64, device=device)
+    dist.broadcast(s, src=n_roll)  # every rank resumes at the trainer's step
+    step0 = int(s.item())
+    if step0:
+        trainer.push_weights()  # the rollout ranks start from the restored weights
+    log = open(os.path.join(run_dir, "steps.jsonl"), "a") if rank == 0 else None
+    for step in range(step0, cfg.total_steps):
+        t0 = time.time()
+        st = trainer.step()
+        if rank == 0:
+            row = {"step": step + 1, "time": round(time.time() - t0, 3),
+                   **{k: (round(v, 6) if isinstance(v, float) else v) for k, v in st.items()
+                      if isinstance(v, (int, float))}}
+            line = json.dumps(row)
+            print(line, flush=True)
+            log.write(line + "\n")
+            log.flush()
+        if actor is not None:
+            if cfg.checkpoint.recover_every and (step + 1) % cfg.checkpoint.recover_every == 0:
+                checkpoint.save(actor, run_dir, step + 1, {"step": step + 1}, spool=spool, group=group)
+            if cfg.checkpoint.save_every and (step + 1) % cfg.checkpoint.save_every == 0 and rank == n_roll:
+                save_hf(actor.weights, os.path.join(run_dir, f"hf-step{step + 1}"))
+    dist.barrier()
+    if engine is not None and hasattr(engine, "close"):
+        engine._graphs.clear()
+    if hasattr(actor, "close"):
+        actor.close()
+    dist.destroy_process_group()
     return 0
 
 

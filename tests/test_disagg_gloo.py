@@ -19,6 +19,14 @@ MB = 10 ** 6
 ITERS = 3
 
 
+def _free_port():
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 def _engine(w):
     from octopus_b200.serving.engine import Engine
 
@@ -73,7 +81,7 @@ def _sequential():
 def test_disaggregated_two_ranks_match_sequential_schedule():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + os.getpid() % 200
+    port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
