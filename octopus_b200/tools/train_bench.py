@@ -65,17 +65,29 @@ def run_octopus(args) -> dict:
     mask = np.ones(len(flat), np.float32)
     mask[cu[:-1]] = 0.0  # a sequence's first token has no prediction
     mb = build_microbatch(flat, list(cu), None, mask, adv, np.zeros(len(flat), np.float32), share=not args.flat)
+    mbs = [mb]
+    if args.flat:
+        # the flattened batch is 3x the tree's rows: trained as micro-batches (gradient accumulation) of at
+        # most the tree's row count, so its activations fit beside the optimizer state as the tree's do
+        tree_rows = build_microbatch(flat, list(cu), None, mask, adv, np.zeros(len(flat), np.float32)).n_tree
+        mbs, part = [], []
+        for i in range(len(seqs)):
+            if part and (cu[i + 1] - cu[part[0]]) > tree_rows:
+                mbs.append(_sub_mb(part, cu, flat, mask, adv, build_microbatch))
+                part = []
+            part.append(i)
+        mbs.append(_sub_mb(part, cu, flat, mask, adv, build_microbatch))
     actor = Actor(cfg, dev, seed=0)
     torch.cuda.synchronize()
     base = torch.cuda.memory_allocated(dev)
     for _ in range(args.warmup):
-        actor.train_step([mb])
+        actor.train_step(mbs)
     torch.cuda.synchronize()
     torch.cuda.reset_peak_memory_stats(dev)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
-        actor.train_step([mb])
+        actor.train_step(mbs)
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / args.steps
@@ -100,7 +112,15 @@ def run_octopus(args) -> dict:
     torch.cuda.synchronize()
     return {"impl": "octopus", "ms_per_step": round(ms, 2), "tree_rows": int(mb.n_tree), "flat_tokens": int(mb.n_flat),
             "trained_tokens_per_s": round(mb.n_flat / ms * 1e3, 1), "tree_rows_per_s": round(mb.n_tree / ms * 1e3, 1),
-            "head_ms": round(a.elapsed_time(b), 2), "head_rows": P, "peak_activation_gb": round(peak / 2**30, 2)}
+            "head_ms": round(a.elapsed_time(b), 2), "head_rows": P, "peak_activation_gb": round(peak / 2**30, 2),
+            "micro_batches": len(mbs)}
+
+
+def _sub_mb(idx, cu, flat, mask, adv, build):
+    """A flat (no prefix sharing) micro-batch of sequences idx (consecutive)."""
+    a, b = cu[idx[0]], cu[idx[-1] + 1]
+    sub_cu = [int(c - a) for c in cu[idx[0]: idx[-1] + 2]]
+    return build(flat[a:b], sub_cu, None, mask[a:b], adv[a:b], np.zeros(b - a, np.float32), share=False)
 
 
 def run_reference(args) -> dict:
@@ -180,7 +200,11 @@ def run_reference(args) -> dict:
         b.record()
         torch.cuda.synchronize()
     except Exception as e:  # noqa: BLE001
-        return {"impl": "reference", "unavailable": f"reference training step failed on this GPU: {e!r}"[:400]}
+        import traceback
+
+        traceback.print_exc()  # the whole error on stderr (the JSON line keeps its start)
+        return {"impl": "reference", "unavailable": f"reference training step failed on this GPU: {e!r}"[:400],
+                "inductor_failed": "Inductor" in repr(e)}
     ms = a.elapsed_time(b) / args.steps
     peak = torch.cuda.max_memory_allocated(dev) - base
     tree_rows = len(flat) if args.flat else int(tree_inputs(ids, cu, None, None)[1]["input_ids"].shape[1])
@@ -207,6 +231,23 @@ def main(argv=None) -> int:
         sys.path.insert(0, ROOT)
     t0 = time.time()
     res = run_octopus(args) if args.impl == "octopus" else run_reference(args)
+    if res.pop("inductor_failed", False) and os.environ.get("OCTOPUS_COMPILE", "1") != "0":
+        # the reference's element-wise blocks are torch.compile'd by default; when Inductor cannot
+        # build them here, run the reference again with its own documented switch for eager blocks
+        import subprocess
+
+        env = dict(os.environ, OCTOPUS_COMPILE="0")
+        p = subprocess.run([sys.executable, "-m", "octopus_b200.tools.train_bench", *(argv or sys.argv[1:])], env=env,
+                           capture_output=True, text=True)
+        sys.stderr.write(p.stderr[-4000:])
+        lines = [x for x in p.stdout.splitlines() if x.startswith("{")]
+        if lines:
+            res = json.loads(lines[-1])
+            res.pop("config", None)
+            res["compile"] = "OCTOPUS_COMPILE=0 (the stock torch.compile run failed in Inductor on this box)"
+    if args.impl == "reference":
+        res.setdefault("compile", "OCTOPUS_COMPILE=0" if os.environ.get("OCTOPUS_COMPILE", "1") == "0"
+                       else "torch.compile (stock)")
     res.update(config={"model": args.model + (f"-L{args.layers}" if args.layers else ""), "depth": args.depth,
                        "branch": args.branch, "seg": args.seg, "flat": args.flat, "steps": args.steps,
                        "warmup": args.warmup, "dtype": "bf16", "data": "synthetic random tokens, random init"},

@@ -9,6 +9,7 @@ attention's, within bf16 tolerance) on consecutive calls that reuse that scratch
 it must take no device memory from the PyTorch allocator.
 """
 import ctypes
+import gc
 
 import pytest
 import torch
@@ -78,12 +79,20 @@ def test_noalloc_matches_regular_decode_two_calls(D, splits):
         ref32 = _fp32_reference(q, kc, vc, start, lens, idx, Hq, Hkv, D)
         ref = ops.DecodeAttention(Hq, Hkv, D, B, splits, dev)(q, kc, vc, start, idx, kv_len=lens)
         out = torch.empty_like(q)
-        torch.cuda.synchronize()
-        alloc, reserved = torch.cuda.memory_allocated(dev), torch.cuda.memory_reserved(dev)
-        rc = _call(fn, q, kc, vc, start, lens, idx, out, Hq, Hkv, D, splits)
-        torch.cuda.synchronize()
+        # (earlier tests' tensors held in reference cycles must not be collected while the
+        # counters are compared: collect them now and keep the collector off meanwhile)
+        gc.collect()
+        gc.disable()
+        try:
+            torch.cuda.synchronize()
+            alloc, reserved = torch.cuda.memory_allocated(dev), torch.cuda.memory_reserved(dev)
+            rc = _call(fn, q, kc, vc, start, lens, idx, out, Hq, Hkv, D, splits)
+            torch.cuda.synchronize()
+            after = torch.cuda.memory_allocated(dev), torch.cuda.memory_reserved(dev)
+        finally:
+            gc.enable()
         assert rc == 0
-        assert torch.cuda.memory_allocated(dev) == alloc and torch.cuda.memory_reserved(dev) == reserved
+        assert after == (alloc, reserved)
         assert _rel(out, ref) < 2e-2
         assert _rel(out, ref32) < 2e-2
 
